@@ -1,0 +1,235 @@
+/*
+ * wnw_b200.h -- C ABI of the B200-native WnW decode hot path.
+ *
+ * One shared library (libwnw_b200.so, sm_100a) exports everything below.
+ * All entry points take plain pointers, sizes and a cudaStream_t passed as
+ * void*; none allocates device memory (the caller owns every buffer) and none
+ * aborts: each returns a wnw_status, with a message from wnw_last_error().
+ *
+ * Every entry point names the reference interface it replaces
+ * (paths relative to the XMUDeepLIT/WnW project root).
+ */
+#ifndef WNW_B200_H_
+#define WNW_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define WNW_ABI_VERSION 1
+
+typedef enum wnw_status {
+  WNW_OK = 0,
+  WNW_ERR_INVALID = 1,     /* bad argument (size, alignment, dtype, null)   */
+  WNW_ERR_CUDA = 2,        /* a CUDA runtime call failed                    */
+  WNW_ERR_CAPACITY = 3,    /* a plan or buffer exceeds its stated capacity  */
+  WNW_ERR_STATE = 4,       /* call out of order / inconsistent state        */
+  WNW_ERR_TIMEOUT = 5,     /* a bounded wait ran out (device or host)       */
+  WNW_ERR_UNSUPPORTED = 6  /* shape or dtype not compiled in                */
+} wnw_status;
+
+typedef enum wnw_dtype { WNW_F32 = 0, WNW_F16 = 1, WNW_BF16 = 2 } wnw_dtype;
+
+/* Device error codes written by kernels into the caller's err word. */
+#define WNW_DEVERR_MBAR_TIMEOUT 1   /* a TMA mbarrier wait ran out           */
+#define WNW_DEVERR_LEN_MISMATCH 2   /* rebuild plan disagrees with seg_len   */
+#define WNW_DEVERR_CAPACITY 4       /* a segment would exceed its slot       */
+
+int wnw_abi_version(void);
+const char* wnw_status_string(wnw_status s);
+/* Last error message of the calling thread ("" when none). */
+const char* wnw_last_error(void);
+
+/* ------------------------------------------------------------------ *
+ * Decode attention (replaces src/common/kv/fused_attn.py:9-156,
+ * q1_decode_attn / q1_decode_attn_score, and the varlen_attn call of
+ * src/algorithms/wnw/code/session.py:90-106).
+ *
+ * Segment s (= b * num_kv_heads + h) holds seg_len[s] rows starting at row
+ * seg_base[s] of k_store / v_store ([rows, head_dim], row-major).  When
+ * new_k/new_v are given, the step's new token is attended as row seg_len[s]
+ * and written there (fused append; src/common/kv/kernels.py:7-73), so the
+ * caller advances seg_len by one afterwards (wnw_advance_lengths).
+ * Work is split into `split_rows`-row pieces grouped into clusters of
+ * `cluster_size` CTAs; `work` lists (segment, cluster index within the
+ * segment) pairs covering every cluster a segment may need
+ * (wnw_build_work_table).  Outputs o[s, g, :] = softmax(q.K^T*scale).V in the
+ * q dtype with fp32 accumulation.  For segments with score_slot[s] >= 0 the
+ * kernel also stores the base-2 logits of the audio rows
+ * [audio_start[b], audio_end[b]) into logits + logits_off[slot] ([t][g]) and
+ * the merged per-head softmax statistics into stats[s] ([2][group]: max, sum),
+ * from which wnw_score_finalize forms the class-A scores.
+ * ------------------------------------------------------------------ */
+typedef struct wnw_decode_attn_args {
+  int dtype;           /* wnw_dtype of q, k/v stores, new_k/new_v and out   */
+  int head_dim;        /* 16, 32, 64 or 128                                  */
+  int group;           /* q heads per kv head, 1..8                          */
+  int num_segs;        /* batch * num_kv_heads                               */
+  int num_kv_heads;
+  const void* q;       /* [num_segs, group, head_dim]                        */
+  const void* new_k;   /* [num_segs, head_dim] or NULL (no append)           */
+  const void* new_v;
+  void* k_store;       /* [rows, head_dim]                                   */
+  void* v_store;
+  const int64_t* seg_base;  /* [num_segs] first row of each segment          */
+  const int32_t* seg_len;   /* [num_segs] rows stored before this step       */
+  const int32_t* seg_cap;   /* [num_segs] slot capacity or NULL (unchecked)  */
+  const int32_t* work;      /* [n_clusters][2] (segment, cluster-in-segment) */
+  int n_clusters;
+  int cluster_size;         /* 1, 2, 4 or 8                                  */
+  int split_rows;           /* rows per CTA; wnw_split_rows()                */
+  void* out;                /* [num_segs, group, head_dim]                   */
+  float scale;
+  /* class-A scoring (all NULL when unused) */
+  const int32_t* score_slot;     /* [num_segs] -1 or slot index              */
+  const int32_t* audio_start;    /* [batch] audio rows within a segment      */
+  const int32_t* audio_end;
+  float* logits;                 /* base-2 logits, see above                 */
+  const int64_t* logits_off;     /* [n_slots] element offset of each slot    */
+  float* stats;                  /* [num_segs][2][group] or NULL             */
+  /* scratch: partials [n_clusters][group][head_dim + 2] fp32, counters
+     [num_segs] int32 (zero before first use; kernels leave them zero) */
+  float* partials;
+  int32_t* counters;
+  int32_t* err;                  /* device error word (WNW_DEVERR_* bits)    */
+} wnw_decode_attn_args;
+
+wnw_status wnw_decode_attn(const wnw_decode_attn_args* a, void* stream);
+
+/* Rows per CTA used by wnw_decode_attn for a dtype / head_dim. */
+int wnw_split_rows(int dtype, int head_dim);
+
+/* Build the cluster work table on the host from per-segment row capacities
+ * (a segment needs ceil((cap+1)/split_rows) splits).  Writes up to max_clusters
+ * pairs and the count (work == NULL with max_clusters == 0 only counts);
+ * WNW_ERR_CAPACITY when max_clusters is too small. */
+wnw_status wnw_build_work_table(const int32_t* seg_cap, int num_segs, int split_rows,
+                                int cluster_size, int32_t* work, int max_clusters,
+                                int* n_clusters);
+
+/* seg_len[i] += 1 for i < n (device), after a step's fused appends. */
+wnw_status wnw_advance_lengths(int32_t* seg_len, int64_t n, void* stream);
+
+/* ------------------------------------------------------------------ *
+ * Class-A score finalisation + chunk scoring + top-k
+ * (replaces the accumulation of src/common/kv/fused_attn.py:107-121 and
+ * src/algorithms/wnw/code/kernels.py:302-370, and the selection of
+ * src/algorithms/wnw/code/cache.py:632-649 /
+ * src/algorithms/wnw_cpp/code/cache.py:160-171).
+ * ------------------------------------------------------------------ */
+/* Term table: for sample b, terms [term_off[b], term_off[b+1]) in order;
+ * term i reads logits at logits + logit_off[i] ([t][group]) and statistics at
+ * stats + stat_off[i] ([2][group]) and sums heads set in qmask[i].
+ * acc[score_off[b] + t] = sum_i sum_{g in qmask[i]} 2^(x - max_g) / sum_g. */
+wnw_status wnw_score_finalize(const float* logits, const float* stats, const int64_t* logit_off,
+                              const int64_t* stat_off, const uint32_t* qmask,
+                              const int32_t* term_off, int group, int batch,
+                              const int32_t* score_off, int max_audio, float* acc,
+                              void* stream);
+
+/* Chunk scores + top-k per sample from a class-A score vector.
+ * Chunk c of sample b spans segments [c, min(c+segs_per_chunk, n_seg_b)) with
+ * segments of `stride` rows over audio_len[b] = score_off[b+1]-score_off[b].
+ * score = (P[end]-P[start]) / max(1, end-start) with P the fp32-rounded
+ * prefix sum (accumulated in fp64, like torch's CPU cumsum).  Writes
+ * topk[b*top_k + j] (descending score, ties -> lower index; -1 padding) and
+ * chunk_scores (optional, [sum of chunk counts] at chunk_off[b]).  max_audio
+ * bounds every sample's audio length (it sizes shared memory). */
+wnw_status wnw_chunk_topk(const float* acc, const int32_t* score_off, int batch, int max_audio,
+                          int stride, int segs_per_chunk, int top_k, int32_t* topk,
+                          float* chunk_scores, const int32_t* chunk_off, void* stream);
+
+/* ------------------------------------------------------------------ *
+ * In-place layout maintenance
+ * ------------------------------------------------------------------ */
+/* Compaction + splice of the changed segments of one layer (replaces
+ * rebuild_append_kv, src/algorithms/wnw/code/kernels.py:375-473, and
+ * WnWCache._apply_chunk_update_to_layer, cache.py:891-1010).  `plan_blob` is
+ * the blob written by wnw_planner_device_plan and `layer` selects its record;
+ * one CTA per changed segment (max_changed >= the record's count); rows are moved inside each
+ * segment's slot (evicted ranges removed, later rows shifted down), then
+ * `landing` rows are spliced after the kept rows and seg_len is set. */
+wnw_status wnw_rebuild_segments(int dtype, int head_dim, void* k_store, void* v_store,
+                                const int64_t* seg_base, int32_t* seg_len, const int32_t* seg_cap,
+                                const void* k_landing, const void* v_landing,
+                                const int32_t* plan_blob, int layer, int max_changed,
+                                int32_t* err, void* stream);
+
+/* Copy rows [0, len[s]) of every segment from src (+src_base[s]) to dst
+ * (+dst_base[s]); src and dst must not overlap.  Used to pack a slot layout
+ * into the reference's flat layout and back, and to grow slots. */
+wnw_status wnw_copy_segments(int dtype, int head_dim, const void* src_k, const void* src_v,
+                             const int64_t* src_base, void* dst_k, void* dst_v,
+                             const int64_t* dst_base, const int32_t* len, int num_segs,
+                             void* stream);
+
+/* Reference-layout append (out-of-place, src/common/kv/kernels.py:7-73):
+ * out segment s = old[cu_old[s]:cu_old[s+1]] ++ new_tokens[s]. */
+wnw_status wnw_interleave_append(int dtype, int head_dim, const void* old, const void* new_tokens,
+                                 const int32_t* cu_old, int num_segs, void* out, void* stream);
+
+/* ------------------------------------------------------------------ *
+ * Planner (replaces the pybind11 class Planner,
+ * src/algorithms/wnw_cpp/code/planner.cpp:19-341; same method names and
+ * argument meaning, int32 host arrays instead of CPU tensors).
+ * ------------------------------------------------------------------ */
+typedef struct wnw_planner wnw_planner;
+
+wnw_status wnw_planner_create(int num_layers, int num_kv_heads, int batch_size, int num_kv_groups,
+                              wnw_planner** out);
+void wnw_planner_destroy(wnw_planner* p);
+wnw_status wnw_planner_set_config(wnw_planner* p, int top_k_chunks, int eviction_lag);
+wnw_status wnw_planner_set_seg_count(wnw_planner* p, const int32_t* seg_count, int n);
+wnw_status wnw_planner_set_chunk_to_segs(wnw_planner* p, int b, const int32_t* flat_segs, int n_flat,
+                                         const int32_t* offsets, int n_offsets);
+wnw_status wnw_planner_set_class_b(wnw_planner* p, int layer, const int32_t* kv_heads, int n);
+/* Flattened [L][num_segs][seg_count[b]] (planner.cpp:53-80). */
+wnw_status wnw_planner_set_restore_meta(wnw_planner* p, const int32_t* cpu_s, const int32_t* cpu_e,
+                                        const int32_t* gpu_s, const int32_t* gpu_e, int64_t n);
+wnw_status wnw_planner_set_loaded(wnw_planner* p, int b, const int32_t* segs, int n);
+wnw_status wnw_planner_set_seq_lens(wnw_planner* p, const int32_t* seq_lens, int64_t n);
+wnw_status wnw_planner_get_loaded_segments(const wnw_planner* p, int b, int32_t* out, int cap,
+                                           int* n_out);
+/* planner.cpp:124-306.  Output arrays as in the reference ([L,nseg],
+ * [L,nseg+1], [L], [L+1]); they are written only when *any_change is 1. */
+wnw_status wnw_planner_compute_and_prepare(wnw_planner* p, const int32_t* topk_idx,
+                                           const int32_t* topk_off, int32_t* load_starts_2d,
+                                           int32_t* load_lens_2d, int32_t* cu_new_2d,
+                                           int32_t* new_lens_2d, int32_t* evict_offsets_2d,
+                                           int32_t* evict_max, int32_t* evict_layer_ptr,
+                                           int* any_change, int* total_tokens);
+/* Results of the last compute_and_prepare (the tuple's ev_starts, ev_ends,
+ * cpu_ranges).  *n receives the count; arrays are copied when cap suffices. */
+wnw_status wnw_planner_get_evictions(const wnw_planner* p, int32_t* starts, int32_t* ends, int cap,
+                                     int* n);
+wnw_status wnw_planner_get_cpu_ranges(const wnw_planner* p, int32_t* ranges, int cap_pairs,
+                                      int* n_pairs);
+/* Transfer-row offset of each layer's loads in the gathered order ([L+1]). */
+wnw_status wnw_planner_get_layer_transfer(const wnw_planner* p, int32_t* layer_rows);
+/* Per-sample to_load / to_evict of the last call (sorted segment ids). */
+wnw_status wnw_planner_get_changes(const wnw_planner* p, int b, int32_t* to_load, int cap_load,
+                                   int* n_load, int32_t* to_evict, int cap_evict, int* n_evict);
+/* Device-plan blob for wnw_rebuild_segments: int32 [L+1] layer offsets, then
+ * per layer {n_chg, seg[n], old_len[n], new_len[n], load_src[n], load_len[n],
+ * ev_off[n+1], ev_s[m], ev_e[m]} with lengths EXCLUDING the step's new token. */
+wnw_status wnw_planner_device_plan(const wnw_planner* p, int32_t* blob, int64_t cap, int64_t* used);
+
+/* Gather the planned CPU ranges (cpu_ranges order) of row_bytes-wide rows from
+ * src_k/src_v into dst_k/dst_v (pinned staging), using up to n_threads host
+ * threads (planner.cpp:104-122). */
+wnw_status wnw_gather_rows(const void* src_k, const void* src_v, int64_t row_bytes,
+                           const int32_t* ranges, int n_pairs, void* dst_k, void* dst_v,
+                           int n_threads);
+
+/* Async H2D copy of n bytes for K and V on `stream`, then record `event`
+ * (cudaEvent_t as void*, may be NULL) -- one per layer. */
+wnw_status wnw_h2d_async(void* dst_k, void* dst_v, const void* src_k, const void* src_v,
+                         int64_t bytes, void* stream, void* event);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* WNW_B200_H_ */

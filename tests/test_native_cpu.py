@@ -1,0 +1,125 @@
+"""CPU checks of libwnw_b200.so: it loads, exports every declared symbol, and
+its host-side planner / gather match the oracle and the reference planner's
+recorded outputs bit for bit (no GPU compute here)."""
+import ctypes
+import os
+import re
+
+import numpy as np
+import pytest
+
+from oracle import kernels as K
+from oracle.planner import OraclePlanner
+from tests.golden.scenario import PLANNER_SCENARIOS, make_planner_inputs
+from tests.test_oracle_golden import _planner_from
+
+N = pytest.importorskip("wnw_b200.native")
+
+
+def test_library_exports_every_header_symbol():
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    hdr = open(os.path.join(root, "include", "wnw_b200.h")).read()
+    declared = set(re.findall(r"\b(wnw_[a-z0-9_]+)\s*\(", hdr)) - {"wnw_status", "wnw_dtype"}
+    for name in declared:
+        assert hasattr(N.lib, name), name
+    assert declared == set(N.EXPORTS)
+    assert N.lib.wnw_abi_version() == 1
+    assert N.lib.wnw_split_rows(N.BF16, 128) == 128 and N.lib.wnw_split_rows(N.F32, 128) == 64
+
+
+def test_status_and_error_reporting():
+    from wnw_b200.planner import Planner
+    assert N.lib.wnw_status_string(3) == b"capacity exceeded"
+    with pytest.raises(N.WnwError, match="dimensions must be positive"):
+        Planner(0, 1, 1)
+    p = Planner(2, 2, 1)
+    with pytest.raises(N.WnwError, match="set_seg_count must come first"):
+        p.set_loaded(0, [1])
+    with pytest.raises(N.WnwError, match="seg_count must have batch_size entries"):
+        p.set_seg_count([3, 4])
+
+
+@pytest.mark.parametrize("i", range(len(PLANNER_SCENARIOS)))
+def test_native_planner_matches_reference_planner(golden_dir, i):
+    from wnw_b200.planner import Planner
+    pz = np.load(os.path.join(golden_dir, "planner.npz"), allow_pickle=True)
+    ps = PLANNER_SCENARIOS[i]
+    inp = make_planner_inputs(ps)
+    P = _planner_from(ps, inp, Planner)
+    O = _planner_from(ps, inp, OraclePlanner)
+    L, S = ps["L"], ps["B"] * ps["H"]
+    for step, (tk, toff) in enumerate(inp["steps"]):
+        bufs = [np.full((L, S), -7, np.int32), np.full((L, S), -7, np.int32), np.full((L, S + 1), -7, np.int32),
+                np.full((L, S), -7, np.int32), np.full((L, S + 1), -7, np.int32), np.full(L, -7, np.int32),
+                np.full(L + 1, -7, np.int32)]
+        ch, tot, evs, eve, rng = P.compute_and_prepare(tk, toff, *bufs)
+        r = O.compute_and_prepare(tk, toff)
+        pre = f"p{i}_s{step}_"
+        assert ch == int(pz[pre + "change"]) == r["any_change"]
+        assert tot == int(pz[pre + "total"])
+        if ch:
+            for name, buf in zip(("load_starts", "load_lens", "cu_new", "new_lens", "evict_offsets", "evict_max",
+                                  "evict_layer_ptr"), bufs):
+                assert np.array_equal(buf, pz[pre + name]), name
+        assert np.array_equal(evs, pz[pre + "ev_starts"]) and np.array_equal(eve, pz[pre + "ev_ends"])
+        assert np.array_equal(rng.reshape(-1, 2), pz[pre + "cpu_ranges"].reshape(-1, 2))
+        for b in range(ps["B"]):
+            assert P.get_loaded_segments(b) == list(pz[pre + "loaded"][b])
+            assert P.changes(b) == (r["to_load"][b], r["to_evict"][b])
+        if ch:
+            _check_device_plan(P, bufs, evs, eve, L, S)
+
+
+def _check_device_plan(P, bufs, evs, eve, L, S):
+    """The rebuild blob restates the reference outputs per changed segment."""
+    blob = P.device_plan()
+    ls, ll, _, nl, eo, _, elp = bufs
+    for l in range(L):
+        o = int(blob[l])
+        n = int(blob[o])
+        segs = blob[o + 1:o + 1 + n]
+        new_len = blob[o + 1 + 2 * n:o + 1 + 3 * n]
+        lsrc = blob[o + 1 + 3 * n:o + 1 + 4 * n]
+        llen = blob[o + 1 + 4 * n:o + 1 + 5 * n]
+        ev_off = blob[o + 1 + 5 * n:o + 2 + 6 * n]
+        ne = int(ev_off[-1])
+        es = blob[o + 2 + 6 * n:o + 2 + 6 * n + ne]
+        ee = blob[o + 2 + 6 * n + ne:o + 2 + 6 * n + 2 * ne]
+        for i, fi in enumerate(segs):
+            assert new_len[i] == nl[l, fi] - 1
+            assert llen[i] == ll[l, fi]
+            if llen[i]:
+                assert lsrc[i] == ls[l, fi]
+            r0 = elp[l] + eo[l, fi]
+            r1 = elp[l] + eo[l, fi + 1]
+            assert list(es[ev_off[i]:ev_off[i + 1]]) == list(evs[r0:r1])
+            assert list(ee[ev_off[i]:ev_off[i + 1]]) == list(eve[r0:r1])
+
+
+def test_gather_rows_matches_oracle():
+    from wnw_b200.planner import gather_rows
+    rng = np.random.default_rng(0)
+    for rows, n_ranges, dtype in ((500, 40, np.float32), (70000, 300, np.float16)):
+        ck = rng.standard_normal((rows, 64)).astype(dtype)
+        cv = rng.standard_normal((rows, 64)).astype(dtype)
+        starts = rng.integers(0, rows - 60, n_ranges)
+        ranges = np.stack([starts, starts + rng.integers(0, 60, n_ranges)], 1).astype(np.int32)
+        ek, ev = K.gather_restore(ck, cv, ranges)
+        dk = np.zeros_like(ek)
+        dv = np.zeros_like(ev)
+        gather_rows(ck, cv, ranges, dk, dv, n_threads=4)
+        assert np.array_equal(dk, ek) and np.array_equal(dv, ev)
+
+
+def test_work_table_covers_capacity():
+    from wnw_b200.kernels import build_work_table
+    cap = np.array([0, 127, 128, 1000, 5000], np.int32)
+    w = build_work_table(cap, 128, 4)
+    for s, c in enumerate(cap):
+        nsplit = -(-(int(c) + 1) // 128)
+        ncl = max(1, -(-nsplit // 4))
+        assert sorted(j for seg, j in w.tolist() if seg == s) == list(range(ncl))
+    n = ctypes.c_int()
+    out = np.zeros((2, 2), np.int32)
+    st = N.lib.wnw_build_work_table(N.ptr(cap), cap.size, 128, 4, N.ptr(out), 2, ctypes.byref(n))
+    assert st == 3 and n.value == w.shape[0]

@@ -1,0 +1,633 @@
+"""``B200WnWCache``: drop-in replacement for the reference ``WnWCache`` /
+``WnWCppCache`` (src/algorithms/wnw/code/cache.py, src/algorithms/wnw_cpp/
+code/cache.py) whose decode path runs on the sm_100a kernels of
+``libwnw_b200.so``.
+
+Same constructor arguments, ``setup_audio`` and hook methods, so the
+reference ``WnWSession`` (or ``wnw_b200.session.WnWSession``) and
+``model.generate(past_key_values=cache)`` drive it unchanged.
+
+Device layout (per layer): K and V stores ``[rows, head_dim]`` in the model
+dtype; every (sample, kv head) segment ``s = b * num_kv_heads + h`` owns the
+slot ``[seg_base[s], seg_base[s] + seg_cap[s])`` and its first ``seg_len[s]``
+rows hold exactly the rows of the reference's flat segment, in the same
+order.  Appends write one row into the slot; a chunk update moves rows only
+inside the changed slots.  ``packed_layer`` materialises the reference's flat
+``[total_tokens, head_dim]`` + ``cu_seqlens`` view.
+
+Per decode step:
+  layer l:  [wait for layer l's H2D rows] rebuild changed slots (if a plan is
+            pending) -> one decode-attention launch (attention + append +
+            class-A logits)
+  end:      advance lengths -> class-A score finalisation -> chunk top-k ->
+            (host) planner -> device plan + per-layer H2D of fetched rows on
+            a copy stream, each layer with its own event.
+"""
+from __future__ import annotations
+
+import math
+from itertools import accumulate
+
+import numpy as np
+import torch
+
+from wnw_b200 import kernels as Kx
+from wnw_b200 import native as N
+from wnw_b200.flat_cache import FlatVarlenCache
+from wnw_b200.planner import Planner, gather_rows
+
+
+def compute_segments(num_audio, stride):
+    """Audio segments of ``stride`` tokens (cache.py:1092-1094)."""
+    return [(i * stride, min(i * stride + stride, num_audio)) for i in range(math.ceil(num_audio / stride))]
+
+
+def compute_chunks(segments, chunk_size, stride):
+    """Chunk c = segments [c, c + ceil(chunk/stride)) (cache.py:1097-1101)."""
+    spc = math.ceil(chunk_size / stride)
+    n = len(segments)
+    return [list(range(i, min(i + spc, n))) for i in range(n)]
+
+
+def topk_keep_per_segment(scores, seg_ranges, ratio):
+    """Prefill audio selection per segment (cache.py:1114-1138): keep
+    ``max(1, int(len * ratio))`` highest-scoring tokens of every segment."""
+    n = scores.shape[0]
+    kept = torch.zeros(n, dtype=torch.bool, device=scores.device)
+    if not seg_ranges:
+        return kept
+    stride = seg_ranges[0][1] - seg_ranges[0][0]
+    full = len(seg_ranges) if seg_ranges[-1][1] - seg_ranges[-1][0] == stride else len(seg_ranges) - 1
+    if full:
+        k = max(1, int(stride * ratio))
+        idx = scores[:full * stride].view(full, stride).topk(k, dim=1).indices
+        idx = idx + torch.arange(full, device=scores.device).unsqueeze(1) * stride
+        kept[idx.reshape(-1)] = True
+    if full < len(seg_ranges):
+        a, b = seg_ranges[-1]
+        kept[scores[a:b].topk(max(1, int((b - a) * ratio))).indices + a] = True
+    return kept
+
+
+def topk_keep_global(scores, seg_ranges, ratio):
+    """Prefill audio selection over the whole span (cache.py:1141-1150)."""
+    n = scores.shape[0]
+    k = min(n, sum(max(1, int((b - a) * ratio)) for a, b in seg_ranges))
+    kept = torch.zeros(n, dtype=torch.bool, device=scores.device)
+    kept[scores.topk(k).indices] = True
+    return kept
+
+
+class B200WnWCache(FlatVarlenCache):
+    """WnW KV cache on the B200 slot layout.
+
+    Extra keyword arguments (all optional):
+      max_decode_tokens -- decode rows reserved per slot (grown on demand);
+      fetch_threads     -- host threads for gathering offloaded rows.
+    """
+
+    def __init__(self, config, num_layers, num_kv_heads, num_q_heads, head_dim, device, adapter=None, *,
+                 max_decode_tokens=256, fetch_threads=8):
+        super().__init__(num_layers, num_kv_heads, num_q_heads, head_dim, device, adapter)
+        if self.device.type != "cuda":
+            raise RuntimeError("B200WnWCache needs a CUDA device; the CPU oracle lives in the test suite")
+        if head_dim not in (16, 32, 64, 128):
+            raise ValueError(f"head_dim {head_dim} not supported (16, 32, 64 or 128)")
+        if not 1 <= self.num_kv_groups <= 8:
+            raise ValueError(f"GQA group {self.num_kv_groups} not supported (1..8)")
+        self.config = config
+        self.max_decode_tokens = int(max_decode_tokens)
+        self.fetch_threads = int(fetch_threads)
+        self._class_b_heads_by_layer = [config.get_layer_class_b(l) for l in range(num_layers)]
+        self.batch_size = 0
+        self.prefilled = False
+        self._copy_stream = None
+
+    # ------------------------------------------------------------- set-up
+    def setup_audio(self, audio_starts, audio_ends, attention_mask=None):
+        """cache.py:144-250: segments, chunks, score buffers, fresh state."""
+        super().setup_audio(audio_starts, audio_ends, attention_mask)
+        a_s = [int(x) for x in audio_starts.tolist()]
+        a_e = [int(x) for x in audio_ends.tolist()]
+        pad = [int(x) for x in self.pad_lens.tolist()]
+        B = self.batch_size = len(a_s)
+        self._raw_audio_starts, self._raw_audio_ends, self.pad_lens_list = a_s, a_e, pad
+        self._audio_starts_list = [s - p for s, p in zip(a_s, pad)]
+        self._audio_ends_list = [e - p for e, p in zip(a_e, pad)]
+        stride = self.config.stride_tokens
+        self.segment_ranges = [compute_segments(self._audio_ends_list[b] - self._audio_starts_list[b], stride)
+                               for b in range(B)]
+        self.chunk_to_segs = [compute_chunks(self.segment_ranges[b], self.config.chunk_size_tokens, stride)
+                              for b in range(B)]
+        self.segs_per_chunk = math.ceil(self.config.chunk_size_tokens / stride)
+        audio_lens = [self._audio_ends_list[b] - self._audio_starts_list[b] for b in range(B)]
+        self._score_offsets_list = [0] + list(accumulate(audio_lens))
+        self.max_audio = max(audio_lens) if audio_lens else 0
+        dev = self.device
+        self.score_offsets = torch.tensor(self._score_offsets_list, dtype=torch.int32, device=dev)
+        self.score_accumulator = torch.zeros(self._score_offsets_list[-1], dtype=torch.float32, device=dev)
+        self._prefill_scores = [[] for _ in range(B)]
+        self.loaded_segments = [set() for _ in range(B)]
+        L = self.num_layers
+        self._pk = [None] * L          # packed prefill K / V (until the slot layout is built)
+        self._pv = [None] * L
+        self.seq_lens = [None] * L     # reference semantics: rows incl. this step's token once appended
+        self._offload = []             # (layer, b, kv, seg, k_rows_cpu, v_rows_cpu)
+        self.restore_meta = None
+        self._pending = False
+        self._decode_step = 0
+        self.prefilled = False
+
+    # ------------------------------------------------------------ prefill
+    def prefill_before_attn(self, layer_idx):
+        self.stats.record_prefill_before(self._snapshot_cache_stats)
+
+    def prefill_after_attn(self, layer_idx, class_a_scores, per_head_scores, key_states, value_states):
+        """cache.py:257-349: class-A heads keep everything after the padding;
+        other heads keep the non-audio rows plus a top-``ratio`` subset of every
+        audio segment; class-B heads offload the rest to host memory."""
+        cfg = self.config
+        for b in range(self.batch_size):
+            if class_a_scores[b] is not None:
+                self._prefill_scores[b].append(class_a_scores[b].float())
+        kp, vp, lens = [], [], []
+        for b in range(self.batch_size):
+            r0, r1, pad = self._raw_audio_starts[b], self._raw_audio_ends[b], self.pad_lens_list[b]
+            for h in range(self.num_kv_heads):
+                kf, vf = key_states[b, h], value_states[b, h]
+                if cfg.is_class_a_kv_head(layer_idx, h):
+                    kp.append(kf[pad:])
+                    vp.append(vf[pad:])
+                    lens.append(kf.shape[0] - pad)
+                    continue
+                ratio = cfg.get_retention(layer_idx, h)
+                pick = topk_keep_global if cfg.prefill_global_topk else topk_keep_per_segment
+                kept = pick(per_head_scores[b][h], self.segment_ranges[b], ratio)
+                audio_k, audio_v = kf[r0:r1], vf[r0:r1]
+                kp.append(torch.cat([kf[pad:r0], kf[r1:], audio_k[kept]]))
+                vp.append(torch.cat([vf[pad:r0], vf[r1:], audio_v[kept]]))
+                lens.append((r0 - pad) + (kf.shape[0] - r1) + int(kept.sum()))
+                if cfg.is_class_b(layer_idx, h):
+                    idx = (~kept).nonzero(as_tuple=True)[0]
+                    if idx.numel():
+                        rk = audio_k.index_select(0, idx).cpu()
+                        rv = audio_v.index_select(0, idx).cpu()
+                        self.stats.record_cpu_gpu_transfer(b, g2c_tokens=int(idx.numel()),
+                                                           g2c_bytes=int(rk.numel() + rv.numel()) * rk.element_size())
+                        counts = torch.bincount(idx // cfg.stride_tokens,
+                                                minlength=len(self.segment_ranges[b])).tolist()
+                        off = 0
+                        for si, n in enumerate(counts):
+                            if n:
+                                self._offload.append((layer_idx, b, h, si, rk[off:off + n], rv[off:off + n]))
+                                off += n
+        self._pk[layer_idx] = torch.cat(kp)
+        self._pv[layer_idx] = torch.cat(vp)
+        self.seq_lens[layer_idx] = lens
+
+    def prefill_all_layers_done(self):
+        """cache.py:351-390: host restore store, initial chunk selection and
+        load, then the slot layout, the scoring tables and the planner."""
+        L, H, B, D, G = self.num_layers, self.num_kv_heads, self.batch_size, self.head_dim, self.num_kv_groups
+        S = B * H
+        dt = self._pk[0].dtype
+        self.dtype = dt
+        # --- host restore store + metadata (flat, planner layout)
+        self.seg_count = [len(self.segment_ranges[b]) for b in range(B)]
+        self._meta_base = np.zeros((L, S), np.int64)
+        acc = 0
+        for l in range(L):
+            for fi in range(S):
+                self._meta_base[l, fi] = acc
+                acc += self.seg_count[fi // H]
+        self._meta = {k: np.full(acc, -1, np.int32) for k in ("cpu_s", "cpu_e", "gpu_s", "gpu_e")}
+        if self._offload:
+            self.cpu_restore_k = torch.cat([o[4] for o in self._offload])
+            self.cpu_restore_v = torch.cat([o[5] for o in self._offload])
+            try:
+                self.cpu_restore_k = self.cpu_restore_k.pin_memory()
+                self.cpu_restore_v = self.cpu_restore_v.pin_memory()
+            except RuntimeError:
+                pass
+            off = 0
+            for l, b, h, si, rk, _ in self._offload:
+                i = self._meta_base[l, b * H + h] + si
+                self._meta["cpu_s"][i], self._meta["cpu_e"][i] = off, off + rk.shape[0]
+                off += rk.shape[0]
+        else:
+            self.cpu_restore_k = torch.empty(0, D, dtype=dt)
+            self.cpu_restore_v = torch.empty(0, D, dtype=dt)
+        self._offload = []
+        # --- scoring geometry (needed by the initial selection)
+        self._setup_scoring()
+        # --- initial chunk selection from the summed prefill class-A scores
+        sel = torch.zeros(self._score_offsets_list[-1], dtype=torch.float32, device=self.device)
+        for b in range(B):
+            o0, o1 = self._score_offsets_list[b], self._score_offsets_list[b + 1]
+            if self._prefill_scores[b]:
+                sel[o0:o1] = torch.stack(self._prefill_scores[b]).sum(dim=0)
+            else:
+                sel[o0:o1] = 1.0
+            self._prefill_scores[b] = []
+        top = self._select_topk(sel)
+        for b in range(B):
+            needed = sorted({s for c in top[b] for s in self.chunk_to_segs[b][c]})
+            if needed:
+                self._initial_load(b, needed)
+            self.loaded_segments[b] = set(needed)
+        # --- slot layout, planner, per-step buffers
+        self._build_slots()
+        self._init_planner()
+        self.prefilled = True
+        self.stats.record_prefill(self._snapshot_cache_stats)
+
+    def _initial_load(self, b, segs):
+        """cache.py:651-714: append the selected host rows to sample b's
+        class-B segments, in ascending segment order."""
+        H = self.num_kv_heads
+        dev = self.device
+        for l in range(self.num_layers):
+            cu = [0] + list(accumulate(self.seq_lens[l]))
+            kp, vp = [], []
+            lens = list(self.seq_lens[l])
+            for fi in range(self.batch_size * H):
+                bb, h = divmod(fi, H)
+                kp.append(self._pk[l][cu[fi]:cu[fi + 1]])
+                vp.append(self._pv[l][cu[fi]:cu[fi + 1]])
+                if bb != b or not self.config.is_class_b(l, h):
+                    continue
+                rel = lens[fi]
+                for si in segs:
+                    i = self._meta_base[l, fi] + si
+                    cs, ce = int(self._meta["cpu_s"][i]), int(self._meta["cpu_e"][i])
+                    if cs < 0:
+                        continue
+                    kp.append(self.cpu_restore_k[cs:ce].to(dev))
+                    vp.append(self.cpu_restore_v[cs:ce].to(dev))
+                    self._meta["gpu_s"][i], self._meta["gpu_e"][i] = rel, rel + ce - cs
+                    rel += ce - cs
+                    self.stats.record_cpu_gpu_transfer(b, c2g_tokens=ce - cs,
+                                                       c2g_bytes=(ce - cs) * self.head_dim * 2 *
+                                                       self.cpu_restore_k.element_size())
+                lens[fi] = rel
+            self._pk[l] = torch.cat(kp)
+            self._pv[l] = torch.cat(vp)
+            self.seq_lens[l] = lens
+
+    def _loaded_bound(self, l, fi):
+        """Most host rows segment (l, fi) can hold at once: a segment stays
+        loaded at most ``eviction_lag`` steps after it was last needed, so at
+        most max(1, lag) * top_k * segs_per_chunk segments are resident."""
+        b = fi // self.num_kv_heads
+        m0 = self._meta_base[l, fi]
+        n = self.seg_count[b]
+        sizes = self._meta["cpu_e"][m0:m0 + n] - self._meta["cpu_s"][m0:m0 + n]
+        sizes = np.sort(sizes[self._meta["cpu_s"][m0:m0 + n] >= 0])[::-1]
+        m = max(1, self.config.eviction_lag) * self.config.top_k_chunks * self.segs_per_chunk
+        return int(sizes[:m].sum())
+
+    def _build_slots(self):
+        L, S, D = self.num_layers, self.batch_size * self.num_kv_heads, self.head_dim
+        dev = self.device
+        self._split = Kx.split_rows(self.dtype, D)
+        self._len_host = np.zeros((L, S), np.int64)     # rows stored (device seg_len mirror)
+        self._cap_host = np.zeros((L, S), np.int64)
+        self._base_host = np.zeros((L, S), np.int64)
+        self.k_store, self.v_store = [None] * L, [None] * L
+        for l in range(L):
+            lens = np.asarray(self.seq_lens[l], np.int64)
+            loaded_now = np.zeros(S, np.int64)
+            extra = np.zeros(S, np.int64)
+            for fi in range(S):
+                if self.config.is_class_b(l, fi % self.num_kv_heads):
+                    m0 = self._meta_base[l, fi]
+                    n = self.seg_count[fi // self.num_kv_heads]
+                    gs, ge = self._meta["gpu_s"][m0:m0 + n], self._meta["gpu_e"][m0:m0 + n]
+                    loaded_now[fi] = int((ge - gs)[gs >= 0].sum())
+                    extra[fi] = self._loaded_bound(l, fi)
+            cap = lens - loaded_now + extra + self.max_decode_tokens
+            self._len_host[l], self._cap_host[l] = lens, cap
+        self._alloc_stores(range(L), copy_from_packed=True)
+        self._pk = self._pv = None
+        self._seg_len = torch.from_numpy(self._len_host.astype(np.int32)).to(dev)
+        self._refresh_layout_tensors()
+
+    def _alloc_stores(self, layers, copy_from_packed=False):
+        D, dev = self.head_dim, self.device
+        for l in layers:
+            cap = self._cap_host[l]
+            # 16-row alignment keeps every slot start 16-byte aligned for any dtype
+            cap_al = (cap + 15) // 16 * 16
+            base = np.concatenate([[0], np.cumsum(cap_al)[:-1]]).astype(np.int64)
+            rows = int(cap_al.sum())
+            ks = torch.empty(rows, D, dtype=self.dtype, device=dev)
+            vs = torch.empty(rows, D, dtype=self.dtype, device=dev)
+            lens = torch.from_numpy(self._len_host[l].astype(np.int32)).to(dev)
+            dst_base = torch.from_numpy(base).to(dev)
+            if copy_from_packed:
+                src_base = torch.from_numpy(np.concatenate([[0], np.cumsum(self._len_host[l])[:-1]]).astype(np.int64)).to(dev)
+                Kx.copy_segments(self._pk[l], self._pv[l], src_base, ks, vs, dst_base, lens)
+            else:
+                src_base = torch.from_numpy(self._base_host[l]).to(dev)
+                Kx.copy_segments(self.k_store[l], self.v_store[l], src_base, ks, vs, dst_base, lens)
+            self.k_store[l], self.v_store[l] = ks, vs
+            self._base_host[l] = base
+
+    def _refresh_layout_tensors(self):
+        L, S, D, G = self.num_layers, self.batch_size * self.num_kv_heads, self.head_dim, self.num_kv_groups
+        dev = self.device
+        self._seg_base = torch.from_numpy(self._base_host).to(dev)
+        self._seg_cap = torch.from_numpy(self._cap_host.astype(np.int32)).to(dev)
+        max_rows = int((self._len_host + self.max_decode_tokens).max()) if S else 0
+        self._cluster = Kx.choose_cluster_size(int(self._cap_host.max()) if S else 0, self._split)
+        self._work = []
+        n_max = 0
+        for l in range(L):
+            w = Kx.build_work_table(self._cap_host[l], self._split, self._cluster)
+            self._work.append(torch.from_numpy(w).to(dev))
+            n_max = max(n_max, w.shape[0])
+        if getattr(self, "_scratch", None) is None or not self._scratch.fits(n_max, G, D, S):
+            self._scratch = Kx.AttnScratch(dev, n_max, G, D, S)
+        del max_rows
+
+    def _grow(self, l):
+        """Give layer l another ``max_decode_tokens`` rows per slot."""
+        self._cap_host[l] = self._cap_host[l] + self.max_decode_tokens
+        self._alloc_stores([l])
+        self._refresh_layout_tensors()
+
+    def _setup_scoring(self):
+        """Slots for the class-A logits of every (layer, class-A kv head,
+        sample) and the per-sample term table (layer-major, ascending kv)."""
+        L, H, B, G = self.num_layers, self.num_kv_heads, self.batch_size, self.num_kv_groups
+        S = B * H
+        dev = self.device
+        audio = [self._audio_ends_list[b] - self._audio_starts_list[b] for b in range(B)]
+        self._score_groups = []
+        for l in range(L):
+            by_kv = {}
+            for qh in self.config.get_layer_class_a(l):
+                by_kv.setdefault(qh // G, []).append(qh % G)
+            self._score_groups.append(sorted(by_kv.items()))
+        self._has_scoring = any(self._score_groups)
+        slot = np.full((L, S), -1, np.int32)
+        logit_off = []
+        terms = [[] for _ in range(B)]
+        total = 0
+        for l in range(L):
+            for kv, qs in self._score_groups[l]:
+                mask = sum(1 << g for g in qs)
+                for b in range(B):
+                    fi = b * H + kv
+                    slot[l, fi] = len(logit_off)
+                    terms[b].append((l, kv, total, mask))
+                    logit_off.append(total)
+                    total += audio[b] * G
+        self._slot_host = slot
+        self._score_slot = torch.from_numpy(slot).to(dev)
+        self._logits = torch.zeros(max(1, total), dtype=torch.float32, device=dev)
+        self._logits_off = torch.tensor(logit_off or [0], dtype=torch.int64, device=dev)
+        self._stats = torch.zeros(L * S * 2 * G, dtype=torch.float32, device=dev)
+        t_logit, t_stat, t_mask, t_off = [], [], [], [0]
+        for b in range(B):
+            for l, kv, off, mask in sorted(terms[b]):
+                t_logit.append(off)
+                t_stat.append((l * S + b * H + kv) * 2 * G)
+                t_mask.append(mask)
+            t_off.append(len(t_logit))
+        self._t_logit = torch.tensor(t_logit or [0], dtype=torch.int64, device=dev)
+        self._t_stat = torch.tensor(t_stat or [0], dtype=torch.int64, device=dev)
+        self._t_mask = torch.tensor(t_mask or [0], dtype=torch.int64, device=dev).to(torch.int32)
+        self._t_off = torch.tensor(t_off, dtype=torch.int32, device=dev)
+        self._audio_start_dev = torch.tensor(self._audio_starts_list, dtype=torch.int32, device=dev)
+        self._audio_end_dev = torch.tensor(self._audio_ends_list, dtype=torch.int32, device=dev)
+        self._topk_dev = torch.full((max(1, B), max(1, self.config.top_k_chunks)), -1, dtype=torch.int32,
+                                    device=dev)
+        self._topk_host = torch.empty_like(self._topk_dev, device="cpu").pin_memory()
+        self._err_host = torch.zeros(1, dtype=torch.int32).pin_memory()
+        self._ready = torch.cuda.Event()
+
+    def _select_topk(self, scores):
+        """Chunk means + top-k of a class-A score vector (device kernel), to
+        host lists per sample (a sync point)."""
+        if self.config.top_k_chunks <= 0 or self.max_audio <= 0:
+            return [[] for _ in range(self.batch_size)]
+        Kx.chunk_topk(scores, self.score_offsets, self.max_audio, self.config.stride_tokens,
+                      self.segs_per_chunk, self.config.top_k_chunks, self._topk_dev)
+        rows = self._topk_dev.cpu().tolist()
+        return [[c for c in r if c >= 0] for r in rows[:self.batch_size]]
+
+    def _init_planner(self):
+        """Hand the prefill state to the native planner (wnw_cpp/code/cache.py:40-116)."""
+        L, H, B = self.num_layers, self.num_kv_heads, self.batch_size
+        P = self._planner = Planner(L, H, B, self.num_kv_groups)
+        P.set_config(self.config.top_k_chunks, self.config.eviction_lag)
+        P.set_seg_count(self.seg_count)
+        for b in range(B):
+            flat = [s for c in self.chunk_to_segs[b] for s in c]
+            off = [0] + list(accumulate(len(c) for c in self.chunk_to_segs[b]))
+            P.set_chunk_to_segs(b, flat, off)
+        for l in range(L):
+            P.set_class_b(l, self._class_b_heads_by_layer[l])
+        P.set_restore_meta(self._meta["cpu_s"], self._meta["cpu_e"], self._meta["gpu_s"], self._meta["gpu_e"])
+        for b in range(B):
+            P.set_loaded(b, sorted(self.loaded_segments[b]))
+        P.set_seq_lens(self._len_host.reshape(-1))
+        S = B * H
+        self._plan_bufs = [np.zeros((L, S), np.int32), np.zeros((L, S), np.int32), np.zeros((L, S + 1), np.int32),
+                           np.zeros((L, S), np.int32), np.zeros((L, S + 1), np.int32), np.zeros(L, np.int32),
+                           np.zeros(L + 1, np.int32)]
+        self._plan_host = torch.zeros(1024, dtype=torch.int32).pin_memory()
+        self._plan_dev = torch.zeros(1024, dtype=torch.int32, device=self.device)
+        self._land_k = self._land_v = None
+        self._stage_k = self._stage_v = None
+        self._events = [torch.cuda.Event() for _ in range(L)]
+        self._layer_chg = [0] * L
+        self._layer_rows = np.zeros(L + 1, np.int64)
+        self._new_kv = [None] * L
+
+    # ------------------------------------------------------------- decode
+    def decode_before_attn(self, layer_idx, new_k, new_v):
+        """Rebuild the layer's changed slots if a plan is pending, check slot
+        capacity, and stash the step's new K/V rows for the fused append.
+        Returns (k_store, v_store, seg_len, max_seqlen_k); seg_len counts the
+        rows stored before this step's token (cache.py:487-515 contract)."""
+        l = layer_idx
+        if self._pending and self._layer_chg[l]:
+            recs = list(self._plan_records(l))
+            if any(nl + 1 > self._cap_host[l, seg] for seg, nl in recs):
+                self._grow(l)
+            torch.cuda.current_stream(self.device).wait_event(self._events[l])
+            Kx.rebuild_layer(self.k_store[l], self.v_store[l], self._seg_base[l], self._seg_len[l],
+                             self._seg_cap[l], self._land_k, self._land_v, self._plan_dev, l,
+                             self._layer_chg[l], self._scratch.err)
+            for seg, new_len in recs:
+                self._len_host[l, seg] = new_len
+        if (self._len_host[l] + 1 > self._cap_host[l]).any():
+            self._grow(l)
+        if l == self.num_layers - 1:
+            self._pending = False
+        S = self.batch_size * self.num_kv_heads
+        nk = new_k.reshape(S, self.head_dim)
+        nv = new_v.reshape(S, self.head_dim)
+        self._new_kv[l] = (nk if nk.is_contiguous() else nk.contiguous(),
+                           nv if nv.is_contiguous() else nv.contiguous())
+        self.seq_lens[l] = (self._len_host[l] + 1).tolist()
+        return self.k_store[l], self.v_store[l], self._seg_len[l], int(self._len_host[l].max()) + 1
+
+    def _plan_records(self, l):
+        blob = self._plan_np
+        o = int(blob[l])
+        n = int(blob[o])
+        return zip(blob[o + 1:o + 1 + n].tolist(), blob[o + 1 + 2 * n:o + 1 + 3 * n].tolist())
+
+    def _score_args(self, l):
+        if not self._score_groups[l]:
+            return None
+        S, G = self.batch_size * self.num_kv_heads, self.num_kv_groups
+        return dict(slot=self._score_slot[l], audio_start=self._audio_start_dev, audio_end=self._audio_end_dev,
+                    logits=self._logits, logits_off=self._logits_off,
+                    stats=self._stats[l * S * 2 * G:(l + 1) * S * 2 * G])
+
+    def fused_decode_attention(self, layer_idx, q_flat, q=None, k_flat=None, v_flat=None, cu_k=None,
+                               scale=None):
+        """cache.py:546-566: attention + append + class-A logits in one launch.
+        Class-A probabilities use the attention scale, which is what the
+        reference's fused kernel does; layers whose class-A set is not a
+        whole kv group use 1/sqrt(d) in the reference (kernels.py:149), so a
+        different attention scale triggers a separate scoring launch."""
+        l = layer_idx
+        G, D = self.num_kv_groups, self.head_dim
+        qf = q_flat if q_flat.is_contiguous() else q_flat.contiguous()
+        nk, nv = self._new_kv[l]
+        score = self._score_args(l)
+        foldable = all(len(qs) == G for _, qs in self._score_groups[l])
+        sep = score is not None and not foldable and not math.isclose(scale, D ** -0.5, rel_tol=0, abs_tol=1e-12)
+        out = Kx.decode_attention(qf, self.k_store[l], self.v_store[l], self._seg_base[l], self._seg_len[l],
+                                  self._work[l], self._cluster, scale, self._scratch, new_k=nk, new_v=nv,
+                                  seg_cap=self._seg_cap[l], num_kv_heads=self.num_kv_heads,
+                                  score=None if sep else score)
+        if sep:  # rescore with the reference's 1/sqrt(d) (the append is idempotent)
+            Kx.decode_attention(qf, self.k_store[l], self.v_store[l], self._seg_base[l], self._seg_len[l],
+                                self._work[l], self._cluster, D ** -0.5, self._scratch, new_k=nk, new_v=nv,
+                                seg_cap=self._seg_cap[l], num_kv_heads=self.num_kv_heads, score=score,
+                                out=torch.empty_like(qf))
+        return out
+
+    def decode_all_layers_done(self):
+        """cache.py:568-600: advance lengths, score, select, plan, prefetch."""
+        self._decode_step += 1
+        self.stats.flush_decode_step(self._decode_step)
+        if self.stats.enabled and self._decode_step % self.stats.interval == 0:
+            self.stats.record_decode(self._decode_step, self._snapshot_cache_stats)
+        Kx.advance_lengths(self._seg_len)
+        self._len_host += 1
+        B = self.batch_size
+        if self._has_scoring:
+            Kx.score_finalize(self._logits, self._stats, self._t_logit, self._t_stat, self._t_mask, self._t_off,
+                              self.num_kv_groups, self.score_offsets, self.max_audio, self.score_accumulator)
+        else:
+            self.score_accumulator.zero_()
+        if self.config.top_k_chunks > 0 and self.max_audio > 0:
+            Kx.chunk_topk(self.score_accumulator, self.score_offsets, self.max_audio, self.config.stride_tokens,
+                          self.segs_per_chunk, self.config.top_k_chunks, self._topk_dev)
+        self._topk_host.copy_(self._topk_dev, non_blocking=True)
+        self._err_host.copy_(self._scratch.err, non_blocking=True)
+        self._ready.record()
+        self._ready.synchronize()
+        if int(self._err_host[0]):
+            Kx.check_device_error(self._scratch.err)
+        rows = self._topk_host.tolist()
+        flat, off = [], [0]
+        for b in range(B):
+            if self.config.top_k_chunks > 0 and self.max_audio > 0:
+                flat.extend(c for c in rows[b] if c >= 0)
+            off.append(len(flat))
+        self.last_topk = [sorted(flat[off[b]:off[b + 1]]) for b in range(B)]
+        ch, total, _, _, ranges = self._planner.compute_and_prepare(flat, off, *self._plan_bufs)
+        for b in range(B):
+            self.loaded_segments[b] = set(self._planner.get_loaded_segments(b))
+        if ch:
+            self._prepare_fetch(total, ranges)
+
+    def _prepare_fetch(self, total, ranges):
+        """Device plan + host gather + per-layer async H2D on the copy stream
+        (the reference's staging cat + side-stream copy, cache.py:868-889)."""
+        L, D = self.num_layers, self.head_dim
+        plan = self._planner.device_plan()
+        if plan.size > self._plan_host.numel():
+            n = 1 << (plan.size - 1).bit_length()
+            self._plan_host = torch.zeros(n, dtype=torch.int32).pin_memory()
+            self._plan_dev = torch.zeros(n, dtype=torch.int32, device=self.device)
+        self._plan_host[:plan.size].copy_(torch.from_numpy(plan))
+        self._plan_np = plan.copy()
+        self._plan_dev[:plan.size].copy_(self._plan_host[:plan.size], non_blocking=True)
+        for l in range(L):
+            o = int(plan[l])
+            self._layer_chg[l] = int(plan[o])
+        self._layer_rows = self._planner.layer_transfer_rows().astype(np.int64)
+        if total > 0:
+            self._ensure_fetch_capacity(total)
+            gather_rows(self.cpu_restore_k, self.cpu_restore_v, ranges, self._stage_k, self._stage_v,
+                        self.fetch_threads)
+            if self._copy_stream is None:
+                self._copy_stream = torch.cuda.Stream(device=self.device)
+            row_bytes = D * self.cpu_restore_k.element_size()
+            sp = self._copy_stream.cuda_stream
+            for l in range(L):
+                r0, r1 = int(self._layer_rows[l]), int(self._layer_rows[l + 1])
+                N.call("wnw_h2d_async", self._land_k[r0:].data_ptr(), self._land_v[r0:].data_ptr(),
+                       self._stage_k[r0:].data_ptr(), self._stage_v[r0:].data_ptr(), (r1 - r0) * row_bytes,
+                       sp, None)
+                self._events[l].record(self._copy_stream)
+            if self.stats.enabled:
+                n = int((ranges[:, 1] - ranges[:, 0]).sum())
+                self.stats.record_cpu_gpu_transfer(0, c2g_tokens=n, c2g_bytes=n * row_bytes * 2)
+        else:
+            for l in range(L):
+                self._events[l].record(torch.cuda.current_stream(self.device))
+        self._pending = True
+
+    def _ensure_fetch_capacity(self, rows):
+        if self._land_k is not None and self._land_k.shape[0] >= rows:
+            return
+        n = 1 << max(0, rows - 1).bit_length()
+        D, dt = self.head_dim, self.dtype
+        self._land_k = torch.empty(n, D, dtype=dt, device=self.device)
+        self._land_v = torch.empty(n, D, dtype=dt, device=self.device)
+        self._stage_k = torch.empty(n, D, dtype=dt).pin_memory()
+        self._stage_v = torch.empty(n, D, dtype=dt).pin_memory()
+
+    # ---------------------------------------------------------- inspection
+    def packed_layer(self, layer_idx):
+        """The reference's flat view of a layer: (K [T, D], V [T, D], cu int32)
+        built by copying the slots (for checks and compatibility)."""
+        l = layer_idx
+        lens = self._seg_len[l]
+        lens_host = self._len_host[l]
+        cu = np.concatenate([[0], np.cumsum(lens_host)]).astype(np.int64)
+        T = int(cu[-1])
+        k = torch.empty(T, self.head_dim, dtype=self.dtype, device=self.device)
+        v = torch.empty_like(k)
+        Kx.copy_segments(self.k_store[l], self.v_store[l], self._seg_base[l], k, v,
+                         torch.from_numpy(cu[:-1]).to(self.device), lens)
+        return k, v, torch.from_numpy(cu.astype(np.int32)).to(self.device)
+
+    def get_loaded_segments(self, b):
+        return sorted(self._planner.get_loaded_segments(b)) if getattr(self, "_planner", None) else \
+            sorted(self.loaded_segments[b])
+
+    def _snapshot_cache_stats(self, step=-1):
+        """Cache occupancy snapshot with the reference's keys (cache.py:1013-1080)."""
+        out = []
+        L, H = self.num_layers, self.num_kv_heads
+        for b in range(self.batch_size):
+            n_audio = self._audio_ends_list[b] - self._audio_starts_list[b]
+            tot = 0
+            if getattr(self, "_len_host", None) is not None:
+                tot = int(self._len_host[:, b * H:(b + 1) * H].sum())
+            elif self.seq_lens and self.seq_lens[0] is not None:
+                tot = sum(sum(x[b * H:(b + 1) * H]) for x in self.seq_lens if x is not None)
+            out.append({"step": step, "num_audio": n_audio, "gpu_total_tokens": tot,
+                        "full_audio_tokens": L * H * n_audio})
+        return out

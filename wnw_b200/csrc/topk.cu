@@ -1,0 +1,218 @@
+// Class-A score finalisation and fused chunk scoring + top-k (sm_100a).
+//
+// The decode-attention kernel leaves, per class-A (layer, segment), the base-2
+// logits of the audio rows and the merged softmax statistics.  Here:
+//  * wnw_score_finalize forms acc[t] = sum over the step's class-A terms, in
+//    layer-major / ascending-kv order, of sum_g 2^(x - m_g) / l_g -- the
+//    probabilities the reference accumulates in fused_attn.py:107-121 and
+//    kernels.py:302-370 -- one thread per audio token, no atomics, a fixed
+//    summation order;
+//  * wnw_chunk_topk computes the chunk means of cache.py:632-640 and the top-k
+//    of cache.py:648 (ties -> lower index) in one CTA per sample.  The prefix
+//    sums are taken at segment boundaries only, accumulated in fp64 and rounded
+//    to fp32, which is what torch's CPU cumsum produces for an fp32 input.
+#include <algorithm>
+
+#include "common.cuh"
+
+namespace wnw {
+
+__global__ void score_finalize_kernel(const float* logits, const float* stats, const int64_t* logit_off,
+                                      const int64_t* stat_off, const uint32_t* qmask, const int32_t* term_off,
+                                      int group, const int32_t* score_off, float* acc) {
+  const int b = blockIdx.y;
+  const int n = score_off[b + 1] - score_off[b];
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= n) return;
+  float sum = 0.f;
+  const int i0 = term_off[b], i1 = term_off[b + 1];
+  for (int i = i0; i < i1; ++i) {
+    const float* st = stats + stat_off[i];
+    const float* lg = logits + logit_off[i] + int64_t(t) * group;
+    const uint32_t mask = qmask[i];
+    float p = 0.f;
+    for (int g = 0; g < group; ++g) {
+      if (mask & (1u << g)) p += ex2(lg[g] - __ldg(st + g)) / __ldg(st + group + g);
+    }
+    sum += p;
+  }
+  acc[score_off[b] + t] = sum;
+}
+
+constexpr int kTopkThreads = 512;
+
+// (value, index) ordering: larger value first, then lower index.
+__device__ inline bool better(float v, int i, float bv, int bi) {
+  return v > bv || (v == bv && i < bi);
+}
+
+__global__ void __launch_bounds__(kTopkThreads)
+    chunk_topk_kernel(const float* acc, const int32_t* score_off, int max_audio, int stride, int spc,
+                      int top_k, int32_t* topk, float* chunk_scores, const int32_t* chunk_off) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  const int b = blockIdx.x;
+  const int n = score_off[b + 1] - score_off[b];
+  if (n > max_audio || n < 0) {  // shared memory was sized for max_audio tokens
+    for (int j = threadIdx.x; j < top_k; j += blockDim.x) topk[b * top_k + j] = -1;
+    return;
+  }
+  const int nseg = (n + stride - 1) / stride;
+  double* segsum = reinterpret_cast<double*>(smem);        // [nseg + 1], becomes the prefix
+  float* cs = reinterpret_cast<float*>(segsum + nseg + 1);  // [nseg] chunk scores
+  uint8_t* taken = reinterpret_cast<uint8_t*>(cs + nseg);    // [nseg] selected flags
+  __shared__ float red_v[kTopkThreads / 32];
+  __shared__ int red_i[kTopkThreads / 32];
+  __shared__ double carry;
+  const float* a = acc + score_off[b];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int nwarps = kTopkThreads / 32;
+
+  // 1. per-segment sums in fp64 (fixed per-lane order, fixed shuffle tree)
+  for (int s = warp; s < nseg; s += nwarps) {
+    const int lo = s * stride, hi = min(n, lo + stride);
+    double x = 0.0;
+    for (int t = lo + lane; t < hi; t += 32) x += double(a[t]);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) x += __shfl_xor_sync(0xffffffffu, x, off);
+    if (lane == 0) segsum[s] = x;
+  }
+  __syncthreads();
+  // 2. exclusive prefix over segments (warp 0, 32 at a time) -> P at boundaries
+  if (warp == 0) {
+    if (lane == 0) carry = 0.0;
+    __syncwarp();
+    for (int s0 = 0; s0 <= nseg; s0 += 32) {
+      const int s = s0 + lane;
+      const double v = (s < nseg) ? segsum[s] : 0.0;
+      double inc = v;
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const double y = __shfl_up_sync(0xffffffffu, inc, off);
+        if (lane >= off) inc += y;
+      }
+      const double c = carry;
+      __syncwarp();
+      if (s <= nseg) segsum[s] = c + inc - v;  // exclusive prefix
+      const double tot = __shfl_sync(0xffffffffu, inc, 31);
+      if (lane == 0) carry = c + tot;
+      __syncwarp();
+    }
+  }
+  __syncthreads();
+  // 3. chunk means in fp32: (P[end] - P[start]) / max(1, end - start)
+  for (int c = tid; c < nseg; c += kTopkThreads) {
+    const int e = min(c + spc, nseg);
+    const int start = c * stride;
+    const int end = (e == nseg) ? n : e * stride;
+    const float pe = float(segsum[e]);
+    const float ps = float(segsum[c]);
+    const float len = float(max(1, end - start));
+    const float v = __fdiv_rn(__fsub_rn(pe, ps), len);
+    cs[c] = v;
+    if (chunk_scores != nullptr) chunk_scores[chunk_off[b] + c] = v;
+  }
+  __syncthreads();
+  // 4. top-k by repeated block argmax over the untaken chunks; NaN ranks as -inf
+  for (int c = tid; c < nseg; c += kTopkThreads) taken[c] = 0;
+  __syncthreads();
+  const int k = min(top_k, nseg);
+  for (int j = 0; j < top_k; ++j) {
+    if (j >= k) {
+      if (tid == 0) topk[b * top_k + j] = -1;
+      continue;
+    }
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int c = tid; c < nseg; c += kTopkThreads) {
+      if (taken[c]) continue;
+      float v = cs[c];
+      if (isnan(v)) v = -INFINITY;
+      if (better(v, c, bv, bi)) {
+        bv = v;
+        bi = c;
+      }
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+      if (better(ov, oi, bv, bi)) {
+        bv = ov;
+        bi = oi;
+      }
+    }
+    if (lane == 0) {
+      red_v[warp] = bv;
+      red_i[warp] = bi;
+    }
+    __syncthreads();
+    if (warp == 0) {
+      bv = (lane < nwarps) ? red_v[lane] : -INFINITY;
+      bi = (lane < nwarps) ? red_i[lane] : 0x7fffffff;
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+        if (better(ov, oi, bv, bi)) {
+          bv = ov;
+          bi = oi;
+        }
+      }
+      if (lane == 0) {
+        topk[b * top_k + j] = bi;
+        taken[bi] = 1;
+      }
+    }
+    __syncthreads();
+  }
+}
+
+}  // namespace wnw
+
+extern "C" wnw_status wnw_score_finalize(const float* logits, const float* stats, const int64_t* logit_off,
+                                         const int64_t* stat_off, const uint32_t* qmask, const int32_t* term_off,
+                                         int group, int batch, const int32_t* score_off, int max_audio,
+                                         float* acc, void* stream) {
+  using namespace wnw;
+  WNW_CHECK_ARG(logits && stats && logit_off && stat_off && qmask && term_off && score_off && acc,
+                "null pointer argument");
+  WNW_CHECK_ARG(group >= 1 && group <= 32, "group must be in 1..32");
+  WNW_CHECK_ARG(batch >= 0 && batch <= 65535, "batch must be in 0..65535");
+  if (batch == 0 || max_audio <= 0) return WNW_OK;
+  dim3 grid((max_audio + 255) / 256, batch);
+  score_finalize_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      logits, stats, logit_off, stat_off, qmask, term_off, group, score_off, acc);
+  WNW_CUDA_TRY(cudaGetLastError());
+  return WNW_OK;
+}
+
+namespace wnw {
+// shared memory needed for a sample with `max_audio` tokens
+inline size_t topk_smem(int max_audio, int stride) {
+  const int nseg = (max_audio + stride - 1) / stride;
+  return size_t(nseg + 1) * sizeof(double) + size_t(nseg) * (sizeof(float) + 1) + 16;
+}
+}  // namespace wnw
+
+extern "C" wnw_status wnw_chunk_topk(const float* acc, const int32_t* score_off, int batch, int max_audio,
+                                     int stride, int segs_per_chunk, int top_k, int32_t* topk,
+                                     float* chunk_scores, const int32_t* chunk_off, void* stream) {
+  using namespace wnw;
+  WNW_CHECK_ARG(acc && score_off && topk, "null pointer argument");
+  WNW_CHECK_ARG(stride > 0 && segs_per_chunk > 0 && top_k >= 0 && max_audio >= 0, "bad chunk geometry");
+  WNW_CHECK_ARG(chunk_scores == nullptr || chunk_off != nullptr, "chunk_scores needs chunk_off");
+  if (batch <= 0 || top_k == 0) return WNW_OK;
+  const size_t smem = topk_smem(max_audio, stride);
+  WNW_CHECK_ARG(smem <= 200 * 1024, "too many segments per sample for one CTA (%d tokens / stride %d)",
+                max_audio, stride);
+  static size_t configured = 48 * 1024;
+  if (smem > configured) {
+    WNW_CUDA_TRY(cudaFuncSetAttribute(chunk_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      static_cast<int>(smem)));
+    configured = smem;
+  }
+  chunk_topk_kernel<<<batch, kTopkThreads, smem, static_cast<cudaStream_t>(stream)>>>(
+      acc, score_off, max_audio, stride, segs_per_chunk, top_k, topk, chunk_scores, chunk_off);
+  WNW_CUDA_TRY(cudaGetLastError());
+  return WNW_OK;
+}

@@ -1,0 +1,169 @@
+"""Torch-tensor wrappers over the C ABI kernels (all launches go through
+``libwnw_b200.so``; nothing here computes on its own)."""
+from __future__ import annotations
+
+import ctypes as C
+import math
+
+import numpy as np
+import torch
+
+from wnw_b200 import native as N
+
+
+def split_rows(dtype, head_dim):
+    return N.lib.wnw_split_rows(N.dtype_code(dtype), int(head_dim))
+
+
+def choose_cluster_size(max_rows, split):
+    """Clusters of up to 8 CTAs; smaller when even the longest segment needs
+    fewer splits (idle cluster members only cost a barrier)."""
+    nsplit = max(1, math.ceil((int(max_rows) + 1) / split))
+    cs = 1
+    while cs < nsplit and cs < 8:
+        cs *= 2
+    return cs
+
+
+def build_work_table(seg_cap, split, cluster_size):
+    """numpy int32 [n_clusters, 2] (segment, cluster index) from capacities."""
+    cap = np.ascontiguousarray(np.asarray(seg_cap, dtype=np.int32))
+    n = C.c_int()
+    N.lib.wnw_build_work_table(N.ptr(cap), cap.size, split, cluster_size, None, 0, C.byref(n))
+    work = np.zeros((max(1, n.value), 2), np.int32)
+    N.call("wnw_build_work_table", N.ptr(cap), cap.size, split, cluster_size, N.ptr(work), n.value, C.byref(n))
+    return work[:n.value]
+
+
+class AttnScratch:
+    """Scratch of the decode-attention kernel: per-cluster partial states and
+    per-segment arrival counters (zeroed once; the kernel leaves them zero),
+    plus the device error word."""
+
+    def __init__(self, device, n_clusters, group, head_dim, num_segs):
+        self.partials = torch.empty(max(1, n_clusters) * group * (head_dim + 2), dtype=torch.float32,
+                                    device=device)
+        self.counters = torch.zeros(max(1, num_segs), dtype=torch.int32, device=device)
+        self.err = torch.zeros(1, dtype=torch.int32, device=device)
+        self.n_clusters, self.group, self.head_dim, self.num_segs = n_clusters, group, head_dim, num_segs
+
+    def fits(self, n_clusters, group, head_dim, num_segs):
+        return (n_clusters * group * (head_dim + 2) <= self.partials.numel() and num_segs <= self.counters.numel())
+
+
+def decode_attention(q, k_store, v_store, seg_base, seg_len, work, cluster_size, scale, scratch,
+                     new_k=None, new_v=None, seg_cap=None, out=None, num_kv_heads=None, score=None,
+                     stream=None):
+    """Launch ``wnw_decode_attn``.  q: [S, G, D]; work: device int32 [n, 2].
+    ``score`` (optional) = dict(slot=int32[S], audio_start=int32[B], audio_end=int32[B],
+    logits=fp32 buffer, logits_off=int64[n_slots], stats=fp32 [S, 2, G])."""
+    S, G, D = q.shape
+    if out is None:
+        out = torch.empty_like(q)
+    a = N.DecodeAttnArgs()
+    a.dtype = N.dtype_code(q.dtype)
+    a.head_dim, a.group, a.num_segs = D, G, S
+    a.num_kv_heads = num_kv_heads if num_kv_heads is not None else S
+    a.q = q.data_ptr()
+    a.new_k = new_k.data_ptr() if new_k is not None else None
+    a.new_v = new_v.data_ptr() if new_v is not None else None
+    a.k_store, a.v_store = k_store.data_ptr(), v_store.data_ptr()
+    a.seg_base, a.seg_len = seg_base.data_ptr(), seg_len.data_ptr()
+    a.seg_cap = seg_cap.data_ptr() if seg_cap is not None else None
+    a.work = work.data_ptr()
+    a.n_clusters = work.shape[0]
+    a.cluster_size = cluster_size
+    a.split_rows = split_rows(q.dtype, D)
+    a.out = out.data_ptr()
+    a.scale = float(scale)
+    if score is not None:
+        a.score_slot = score["slot"].data_ptr()
+        a.audio_start = score["audio_start"].data_ptr()
+        a.audio_end = score["audio_end"].data_ptr()
+        a.logits = score["logits"].data_ptr()
+        a.logits_off = score["logits_off"].data_ptr()
+        a.stats = score["stats"].data_ptr() if score.get("stats") is not None else None
+    elif isinstance(score, type(None)):
+        pass
+    a.partials = scratch.partials.data_ptr()
+    a.counters = scratch.counters.data_ptr()
+    a.err = scratch.err.data_ptr()
+    N.check(N.lib.wnw_decode_attn(C.byref(a), N.stream_ptr(stream)), "wnw_decode_attn")
+    return out
+
+
+def advance_lengths(seg_len, stream=None):
+    N.call("wnw_advance_lengths", seg_len.data_ptr(), seg_len.numel(), N.stream_ptr(stream))
+
+
+def score_finalize(logits, stats, logit_off, stat_off, qmask, term_off, group, score_off, max_audio, acc,
+                   stream=None):
+    batch = score_off.numel() - 1
+    N.call("wnw_score_finalize", logits.data_ptr(), stats.data_ptr(), logit_off.data_ptr(),
+           stat_off.data_ptr(), qmask.data_ptr(), term_off.data_ptr(), int(group), int(batch),
+           score_off.data_ptr(), int(max_audio), acc.data_ptr(), N.stream_ptr(stream))
+
+
+def chunk_topk(acc, score_off, max_audio, stride, segs_per_chunk, top_k, topk_out, chunk_scores=None,
+               chunk_off=None, stream=None):
+    batch = score_off.numel() - 1
+    N.call("wnw_chunk_topk", acc.data_ptr(), score_off.data_ptr(), int(batch), int(max_audio), int(stride),
+           int(segs_per_chunk), int(top_k), topk_out.data_ptr(),
+           chunk_scores.data_ptr() if chunk_scores is not None else None,
+           chunk_off.data_ptr() if chunk_off is not None else None, N.stream_ptr(stream))
+
+
+def rebuild_layer(k_store, v_store, seg_base, seg_len, seg_cap, k_landing, v_landing, plan_blob, layer,
+                  max_changed, err, stream=None):
+    N.call("wnw_rebuild_segments", N.dtype_code(k_store.dtype), k_store.shape[1], k_store.data_ptr(),
+           v_store.data_ptr(), seg_base.data_ptr(), seg_len.data_ptr(),
+           seg_cap.data_ptr() if seg_cap is not None else None,
+           k_landing.data_ptr() if k_landing is not None else None,
+           v_landing.data_ptr() if v_landing is not None else None, plan_blob.data_ptr(), int(layer),
+           int(max_changed), err.data_ptr(), N.stream_ptr(stream))
+
+
+def copy_segments(src_k, src_v, src_base, dst_k, dst_v, dst_base, lens, stream=None):
+    n = lens.numel()
+    for lo in range(0, n, 65535):
+        hi = min(n, lo + 65535)
+        N.call("wnw_copy_segments", N.dtype_code(src_k.dtype), src_k.shape[1], src_k.data_ptr(),
+               src_v.data_ptr(), src_base[lo:hi].data_ptr(), dst_k.data_ptr(), dst_v.data_ptr(),
+               dst_base[lo:hi].data_ptr(), lens[lo:hi].data_ptr(), hi - lo, N.stream_ptr(stream))
+
+
+def interleave_append(old, new_tokens, cu_old, stream=None):
+    """Reference-layout append (src/common/kv/kernels.py:76-97): returns
+    (out [T + S, D], cu_new)."""
+    S = new_tokens.shape[0]
+    out = torch.empty(old.shape[0] + S, old.shape[1], dtype=old.dtype, device=old.device)
+    N.call("wnw_interleave_append", N.dtype_code(old.dtype), old.shape[1],
+           old.data_ptr() if old.numel() else None, new_tokens.data_ptr(), cu_old.data_ptr(), S,
+           out.data_ptr(), N.stream_ptr(stream))
+    return out, cu_old + torch.arange(S + 1, dtype=cu_old.dtype, device=cu_old.device)
+
+
+def check_device_error(err_tensor):
+    """Raise on a non-zero device error word (reads it back: a sync point)."""
+    v = int(err_tensor.item())
+    if v:
+        names = [n for bit, n in ((N.DEVERR_MBAR_TIMEOUT, "mbarrier wait timed out"),
+                                  (N.DEVERR_LEN_MISMATCH, "segment length disagrees with the plan"),
+                                  (N.DEVERR_CAPACITY, "segment exceeds its slot capacity")) if v & bit]
+        raise N.WnwError(5 if v & N.DEVERR_MBAR_TIMEOUT else 4, "device", ", ".join(names))
+
+
+def packed_attention(q, k, v, cu, scale, scratch=None, cluster_size=None):
+    """Attention over a reference-layout packed buffer ([T, D] + cu): the slot
+    kernel with seg_base = cu[:-1], seg_len = diff(cu) and no append."""
+    S, G, D = q.shape
+    cu64 = cu.to(torch.int64)
+    lens = (cu64[1:] - cu64[:-1]).to(torch.int32)
+    lens_host = lens.cpu().numpy()
+    split = split_rows(q.dtype, D)
+    cs = cluster_size or choose_cluster_size(int(lens_host.max()) if S else 0, split)
+    # capacity = length - 1 so that ceil((cap+1)/split) covers exactly len rows
+    work = torch.from_numpy(build_work_table(np.maximum(lens_host - 1, 0), split, cs)).to(q.device)
+    if scratch is None or not scratch.fits(work.shape[0], G, D, S):
+        scratch = AttnScratch(q.device, work.shape[0], G, D, S)
+    return decode_attention(q.contiguous(), k, v, cu64[:-1].contiguous(), lens, work, cs, scale, scratch)
