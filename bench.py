@@ -1,0 +1,460 @@
+#!/usr/bin/env python
+"""Benchmark of the WnW decode hot path on B200 (one JSON line on rank 0).
+
+Workload: Voxtral-Mini-3B-shaped decoder, random
+init, bf16, batch 1 -- 30 layers, hidden 3072, 32 q / 8 kv heads, head_dim
+128, RoPE theta 1e8 (MLP 8192 and vocab 131072: the installed transformers
+Voxtral text-config defaults).  Prompt = 4 text tokens + 15,000 audio
+embeddings ~ N(0, 0.02) + 60 text tokens; 30 % of the kv heads are class A
+(seeded choice), the rest class B with chunk = segment = 128 tokens, top-16,
+eviction lag 1; class B keeps the 64 non-audio tokens, one audio token per
+segment (retention 0) and every decoded token.
+
+A step is one decode step of the hot path over all 30 layers: per layer the
+pending chunk rebuild and one fused decode-attention launch (attention +
+append + class-A logits), then length advance, class-A score finalisation,
+chunk top-k, the host planner and the per-layer H2D fetch of the chosen
+chunks.  Its per-layer q/k/v inputs come from the random-init decoder itself:
+the model is run once (untimed) through the session and every decode step's
+q/k/v is recorded; the timed legs replay them into a freshly prefilled cache,
+so they do exactly the work the model run did.
+
+* value -- decode tokens/s with the inputs resident in HBM;
+* e2e   -- the same through the Python hook API with each step's q/k/v copied
+           from pinned host memory and each step's attention outputs copied
+           back (bytes per step reported);
+* roofline -- the decode-attention kernel: algorithmic bytes (K+V rows
+           attended + q in + o out + class-A logits) / CUDA-event time;
+* cpu_baseline -- the CPU oracle (numpy/torch restatement of the reference's
+           path) replaying a bounded sample of the same steps.
+
+``--impl reference`` times that CPU path alone (rank 0; other ranks exit).
+With torchrun, every rank runs its own replica (request sharding, weak
+scaling); value = all ranks' tokens / max-over-ranks time.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+MODEL = dict(L=30, hidden=3072, Hq=32, Hkv=8, D=128, inter=8192, vocab=131072, theta=1e8)
+PROMPT = dict(sink=4, audio=15000, tail=60)
+WNW = dict(frac_a=0.30, chunk=128, top_k=16, lag=1, retention=0.0, seed=1234)
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=24)
+    ap.add_argument("--warmup", type=int, default=4)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--cpu-steps", type=int, default=3, help="oracle steps in the bounded CPU sample")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--profile", action="store_true", help="short run for ncu (no clocks, no CPU leg)")
+    return ap.parse_args()
+
+
+# ------------------------------------------------------------------ set-up
+def wnw_config():
+    from wnw_b200.config import WnWConfig
+    L, H, Hq = MODEL["L"], MODEL["Hkv"], MODEL["Hq"]
+    G = Hq // H
+    rng = np.random.default_rng(WNW["seed"])
+    n_a = round(WNW["frac_a"] * L * H)
+    a_kv = sorted(rng.choice(L * H, size=n_a, replace=False).tolist())
+    class_a = [(g // H) * Hq + (g % H) * G + j for g in a_kv for j in range(G)]
+    class_b = [g for g in range(L * H) if g not in set(a_kv)]
+    ret = [None if g in set(a_kv) else WNW["retention"] for g in range(L * H)]
+    return WnWConfig(chunk_size_s=float(WNW["chunk"]), overlap_s=0.0, token_rate=1.0, class_a=class_a,
+                     class_b=class_b, retention_ratios=ret, top_k_chunks=WNW["top_k"], eviction_lag=WNW["lag"],
+                     prefill_score_mode="last", num_layers=L, num_kv_heads=H, num_q_heads=Hq)
+
+
+def make_model(dev, seed):
+    from transformers import LlamaConfig, LlamaForCausalLM
+    cfg = LlamaConfig(vocab_size=MODEL["vocab"], hidden_size=MODEL["hidden"], intermediate_size=MODEL["inter"],
+                      num_hidden_layers=MODEL["L"], num_attention_heads=MODEL["Hq"],
+                      num_key_value_heads=MODEL["Hkv"], head_dim=MODEL["D"], max_position_embeddings=131072,
+                      rope_parameters={"rope_theta": MODEL["theta"], "rope_type": "default"}, rms_norm_eps=1e-5)
+    torch.manual_seed(seed)
+    prev = torch.get_default_dtype()
+    torch.set_default_dtype(torch.bfloat16)
+    try:
+        with torch.device(dev):
+            model = LlamaForCausalLM(cfg).eval()
+    finally:
+        torch.set_default_dtype(prev)
+    return model
+
+
+class Recorder:
+    """Cache mix-in that keeps the hook inputs of a model run."""
+
+    def prefill_after_attn(self, l, ca, ph, k, v):
+        self.rec_prefill.append((l, [x.clone() if x is not None else None for x in ca],
+                                 [[x.clone() if x is not None else None for x in r] for r in ph], k.clone(),
+                                 v.clone()))
+        return super().prefill_after_attn(l, ca, ph, k, v)
+
+    def decode_before_attn(self, l, k, v):
+        if l == 0:
+            self.rec_steps.append([None] * self.num_layers)
+        self.rec_steps[-1][l] = [None, k.clone(), v.clone()]
+        return super().decode_before_attn(l, k, v)
+
+    def fused_decode_attention(self, l, q_flat, q, k_flat, v_flat, cu_k, scale):
+        self.rec_steps[-1][l][0] = q_flat.clone()
+        self.rec_scale = scale
+        return super().fused_decode_attention(l, q_flat, q, k_flat, v_flat, cu_k, scale)
+
+
+def record(dev, n_steps, seed):
+    """Run the random-init decoder through the session: prefill + n_steps
+    greedy decode steps; return the recorded hook inputs and model timing."""
+    from wnw_b200.adapters import LlamaFamilyAdapter
+    from wnw_b200.cache import B200WnWCache
+    from wnw_b200.session import WnWSession
+
+    class RecCache(Recorder, B200WnWCache):
+        pass
+
+    cfg = wnw_config()
+    model = make_model(dev, seed)
+    S0 = PROMPT["sink"] + PROMPT["audio"] + PROMPT["tail"]
+    a0, a1 = PROMPT["sink"], PROMPT["sink"] + PROMPT["audio"]
+    cache = RecCache(cfg, MODEL["L"], MODEL["Hkv"], MODEL["Hq"], MODEL["D"], dev, max_decode_tokens=n_steps + 8)
+    cache.rec_prefill, cache.rec_steps = [], []
+    g = torch.Generator(device=dev).manual_seed(seed)
+    ids = torch.randint(1, MODEL["vocab"], (1, S0), device=dev, generator=g)
+    with torch.no_grad():
+        emb = model.get_input_embeddings()(ids)
+        emb[:, a0:a1] = (torch.randn(1, a1 - a0, MODEL["hidden"], device=dev, generator=g) * 0.02).to(emb.dtype)
+    adapter = LlamaFamilyAdapter(a0, a1)
+    times = []
+    with WnWSession(model, adapter, cache) as sess, torch.no_grad():
+        sess.setup_audio(ids)
+        out = model(inputs_embeds=emb, past_key_values=cache, use_cache=True, logits_to_keep=1)
+        tok = out.logits[:, -1:].argmax(-1)
+        for i in range(n_steps):
+            t0 = torch.cuda.Event(enable_timing=True)
+            t1 = torch.cuda.Event(enable_timing=True)
+            t0.record()
+            out = model(input_ids=tok, past_key_values=cache, use_cache=True)
+            tok = out.logits[:, -1:].argmax(-1)
+            t1.record()
+            times.append((t0, t1))
+    torch.cuda.synchronize()
+    ms = [a.elapsed_time(b) for a, b in times[2:]] or [float("nan")]
+    rec = dict(cfg=cfg, prefill=cache.rec_prefill, steps=cache.rec_steps, scale=cache.rec_scale,
+               audio=(a0, a1), S0=S0, model_ms=statistics.median(ms))
+    del model, cache, out
+    torch.cuda.empty_cache()
+    return rec
+
+
+def fresh_cache(rec, dev, n_steps):
+    from wnw_b200.cache import B200WnWCache
+    c = B200WnWCache(rec["cfg"], MODEL["L"], MODEL["Hkv"], MODEL["Hq"], MODEL["D"], dev,
+                     max_decode_tokens=n_steps + 8)
+    a0, a1 = rec["audio"]
+    c.setup_audio(torch.tensor([a0]), torch.tensor([a1]), None)
+    for l, ca, ph, k, v in rec["prefill"]:
+        c.prefill_after_attn(l, ca, ph, k, v)
+    c.prefill_all_layers_done()
+    return c
+
+
+def algorithmic_bytes(cache, l):
+    """Per decode-attention launch: K+V rows attended (incl. the new token),
+    q in + o out, and the class-A logit traffic (8 B per audio token per
+    class-A segment: fp32 written here and read by the score kernel)."""
+    S = cache.batch_size * cache.num_kv_heads
+    G, D, es = cache.num_kv_groups, cache.head_dim, 2
+    rows = int((cache._len_host[l] + 1).sum())
+    n_a = sum(1 for s in cache._slot_host[l] if s >= 0)
+    audio = cache._audio_ends_list[0] - cache._audio_starts_list[0]
+    return rows * D * es * 2 + S * G * D * es * 2 + 8 * n_a * audio
+
+
+def run_value(rec, dev, K, W):
+    """Timed replay with inputs resident in HBM; also times every attention
+    launch with CUDA events on the launching stream."""
+    from wnw_b200 import kernels as Kx
+    cache = fresh_cache(rec, dev, K + W)
+    steps, scale, L = rec["steps"], rec["scale"], MODEL["L"]
+
+    def one(i, ev=None, nbytes=None):
+        for l in range(L):
+            q, k, v = steps[i][l]
+            kk, vv, cu, _ = cache.decode_before_attn(l, k, v)
+            if ev is not None:
+                nbytes[0] += algorithmic_bytes(cache, l)
+                e0 = torch.cuda.Event(enable_timing=True)
+                e1 = torch.cuda.Event(enable_timing=True)
+                e0.record()
+            cache.fused_decode_attention(l, q, None, kk, vv, cu, scale)
+            if ev is not None:
+                e1.record()
+                ev.append((e0, e1))
+        cache.decode_all_layers_done()
+
+    for i in range(W):
+        one(i)
+    ev, nbytes = [], [0]
+    fetched = 0
+    launches0 = Kx.LAUNCHES[0]
+    torch.cuda.synchronize()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for i in range(W, W + K):
+        one(i, ev, nbytes)
+        fetched += int(cache._layer_rows[-1]) if cache._pending else 0
+    t1.record()
+    torch.cuda.synchronize()
+    launches = Kx.LAUNCHES[0] - launches0
+    total_ms = t0.elapsed_time(t1)
+    attn_ms = [a.elapsed_time(b) for a, b in ev]
+    return dict(ms=total_ms, attn_ms=attn_ms, attn_bytes=nbytes[0], launches=launches, fetched_rows=fetched,
+                cache=cache)
+
+
+def run_e2e(rec, dev, K, W):
+    """Hook API with host buffers: per step H2D of all layers' q/k/v from
+    pinned memory and D2H of all layers' attention outputs."""
+    cache = fresh_cache(rec, dev, K + W)
+    steps, scale, L = rec["steps"], rec["scale"], MODEL["L"]
+    q0, k0, _ = steps[0][0]
+    host_in = [[torch.empty(x.shape, dtype=x.dtype).pin_memory() for x in steps[i][l]]
+               for i in range(W + K) for l in range(L)]
+    for i in range(W + K):
+        for l in range(L):
+            for j in range(3):
+                host_in[i * L + l][j].copy_(steps[i][l][j])
+    dev_in = [torch.empty_like(x, device=dev) for x in steps[0][0]]
+    host_out = torch.empty((L,) + tuple(q0.shape), dtype=q0.dtype).pin_memory()
+    in_bytes = sum(x.numel() * x.element_size() for x in steps[0][0]) * L
+    out_bytes = host_out.numel() * host_out.element_size()
+    outs = [None] * L
+
+    def one(i):
+        for l in range(L):
+            q, k, v = (d.copy_(h, non_blocking=True) for d, h in zip(dev_in, host_in[i * L + l]))
+            kk, vv, cu, _ = cache.decode_before_attn(l, k, v)
+            outs[l] = cache.fused_decode_attention(l, q, None, kk, vv, cu, scale)
+        cache.decode_all_layers_done()
+        for l in range(L):
+            host_out[l].copy_(outs[l], non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+
+    for i in range(W):
+        one(i)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(W, W + K):
+        one(i)
+    e1.record()
+    torch.cuda.synchronize()
+    del t0
+    return dict(ms=e0.elapsed_time(e1), in_bytes=in_bytes, out_bytes=out_bytes)
+
+
+def cpu_replay(rec, n_steps, start=0):
+    """The CPU oracle replaying steps [start, start+n_steps) after its own
+    prefill from the same recorded inputs; returns seconds per step."""
+    from oracle.cache import OracleWnWCache
+    cfg = rec["cfg"]
+    c = OracleWnWCache(cfg, MODEL["L"], MODEL["Hkv"], MODEL["Hq"], MODEL["D"])
+    a0, a1 = rec["audio"]
+    c.setup_audio([a0], [a1], [0])
+    for l, ca, ph, k, v in rec["prefill"]:
+        c.prefill_after_attn(l, [x.cpu() if x is not None else None for x in ca],
+                             [[x.cpu() if x is not None else None for x in r] for r in ph], k.cpu(), v.cpu())
+    c.prefill_all_layers_done()
+    steps, scale = rec["steps"], rec["scale"]
+    for i in range(start):
+        _cpu_step(c, steps[i], scale)
+    t = time.perf_counter()
+    for i in range(start, start + n_steps):
+        _cpu_step(c, steps[i], scale)
+    return (time.perf_counter() - t) / n_steps
+
+
+def _cpu_step(c, step, scale):
+    for l, (q, k, v) in enumerate(step):
+        c.decode_before_attn(l, k.cpu(), v.cpu())
+        c.fused_decode_attention(l, q.cpu(), scale=scale)
+    c.decode_all_layers_done()
+
+
+# ------------------------------------------------------------------ clocks
+class Clocks:
+    """nvidia-smi sampling during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [x for x in out.splitlines() if x.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            p = [x.strip() for x in ln.split(",")]
+            try:
+                sm.append(float(p[1]))
+                mx.append(float(p[2]))
+            except (ValueError, IndexError):
+                continue
+            for n, v in zip(names, p[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback"
+
+
+def traffic_per_launch():
+    """DRAM bytes per decode-attention launch from the committed ncu capture
+    summary (profiles/), or None."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "decode_attn_traffic.json")) as f:
+            return json.load(f).get("dram_bytes_per_launch")
+    except (OSError, ValueError):
+        return None
+
+
+# ------------------------------------------------------------------ main
+def main():
+    a = parse()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dist = world > 1
+    if a.impl == "reference" and rank != 0:
+        return
+    dev = torch.device(f"cuda:{local}")
+    torch.cuda.set_device(dev)
+    if dist and a.impl == "b200":
+        import datetime
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                             device_id=dev)
+    K, W = a.steps, a.warmup
+    workload = "voxtral-mini-3b wnw decode hot path, B=1, 15064-token prompt (15000 audio), 30 layers"
+    cfg_json = {"workload": workload, "batch": 1, "prompt_tokens": 15064, "audio_tokens": 15000,
+                "layers": 30, "q_heads": 32, "kv_heads": 8, "head_dim": 128, "class_a_frac": WNW["frac_a"],
+                "chunk_tokens": WNW["chunk"], "top_k": WNW["top_k"], "eviction_lag": WNW["lag"],
+                "inputs": "q/k/v recorded from the random-init decoder, replayed",
+                "l2": "per-step K/V working set > L2 (30 layers x ~25 MB)",
+                "parallelism": f"request-sharded replicas x{world}"}
+    rec = record(dev, W + K, seed=1000 + rank)
+
+    if a.impl == "reference":
+        n = max(1, min(a.cpu_steps, K))
+        sec = cpu_replay(rec, n, start=W)
+        v = 1.0 / sec
+        line = {"impl": "reference", "metric": "decode tokens/s (WnW hot path)", "value": v, "unit": "tokens/s",
+                "n_gpus": a.gpus, "steps": n, "warmup": W, "ms_per_step": sec * 1e3, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+                "config": cfg_json,
+                "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
+                                 "sample": f"{n} decode steps (all 30 layers) replayed by the CPU oracle"},
+                "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return
+
+    with Clocks(local) as clk:
+        val = run_value(rec, dev, K, W)
+    e2e = run_e2e(rec, dev, K, W)
+    ms = val["ms"]
+    if dist:
+        t = torch.tensor([ms, e2e["ms"]], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms, e2e_ms = float(t[0]), float(t[1])
+        torch.distributed.barrier()
+    else:
+        e2e_ms = e2e["ms"]
+    tokens = world * 1 * K
+    peak, peak_kind = peaks()
+    attn_ms = sum(val["attn_ms"])
+    achieved = val["attn_bytes"] / (attn_ms * 1e-3) / 1e9 if attn_ms > 0 else None
+    n_launch = len(val["attn_ms"])
+    line = {
+        "metric": "decode tokens/s (WnW hot path) and decode-attention HBM GB/s", "value": tokens / (ms * 1e-3),
+        "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": ms / K,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (random-init decoder, N(0,0.02) audio embeddings)", "config": cfg_json,
+        "e2e": {"value": tokens / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": e2e["in_bytes"],
+                "d2h_bytes_per_step": e2e["out_bytes"]},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": (achieved / peak) if achieved else None, "peak_source": peak_kind,
+                     "traffic": traffic_per_launch(), "kernel": "wnw::decode_attn_kernel<bf16,128,4>",
+                     "bytes_per_launch": val["attn_bytes"] / max(1, n_launch),
+                     "us_per_launch": attn_ms * 1e3 / max(1, n_launch)},
+        "gpu_launches": val["launches"],
+        "clocks": clk.summary(),
+        "fetched_rows_per_step": val["fetched_rows"] / K,
+        "model_decode_ms_per_token": rec["model_ms"],
+    }
+    if rank == 0 and not a.no_cpu and not a.profile:
+        n = max(1, min(a.cpu_steps, K))
+        sec = cpu_replay(rec, n, start=W)
+        line["cpu_baseline"] = {"value": 1.0 / sec, "unit": "tokens/s", "cores": torch.get_num_threads(),
+                                "kind": "port",
+                                "sample": f"{n} decode steps (all 30 layers) replayed by the CPU oracle"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if dist:
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -134,10 +134,9 @@ def test_cache_matches_oracle_in_bf16(dev):
             assert np.array_equal(pcu, orc.cu(l))
             assert torch.equal(pk.cpu(), orc.layer_k[l])
             del ref
-        gpu_scores = cache.score_accumulator.clone()
-        cache.decode_all_layers_done()
-        np.testing.assert_allclose(gpu_scores.cpu().numpy(), orc.score_accumulator, atol=1e-4, rtol=1e-3)
+        cache.decode_all_layers_done()  # scores are formed here
         orc.decode_all_layers_done()
+        np.testing.assert_allclose(cache.score_accumulator.cpu().numpy(), orc.last_scores, atol=1e-4, rtol=1e-3)
         for b in range(sc["B"]):
             if cache.last_topk[b] != orc.last_topk[b]:
                 o0, o1 = orc.score_offsets[b], orc.score_offsets[b + 1]

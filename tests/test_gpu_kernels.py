@@ -117,7 +117,7 @@ def test_scoring_logits_and_finalize_match_oracle(dev):
     from wnw_b200 import kernels as Kx
     B, H, G, D = 2, 4, 4, 128
     dtype = torch.float32
-    lens = [3000, 2900, 700, 4100, 3500, 3300, 1200, 900]
+    lens = [3000, 2900, 2700, 4100, 3500, 3300, 2900, 900]  # class-A kv 0, 2 cover the audio
     a_s, a_e = [10, 40], [2600, 2800]
     ks, vs, base, cap = _slots(lens, 16, D, dtype, dev, seed=3)
     g = torch.Generator(device="cpu").manual_seed(11)

@@ -10,6 +10,13 @@ import torch
 
 from wnw_b200 import native as N
 
+#: kernel launches issued through these wrappers (bench.py reports it)
+LAUNCHES = [0]
+
+
+def _count(n=1):
+    LAUNCHES[0] += n
+
 
 def split_rows(dtype, head_dim):
     return N.lib.wnw_split_rows(N.dtype_code(dtype), int(head_dim))
@@ -83,17 +90,17 @@ def decode_attention(q, k_store, v_store, seg_base, seg_len, work, cluster_size,
         a.logits = score["logits"].data_ptr()
         a.logits_off = score["logits_off"].data_ptr()
         a.stats = score["stats"].data_ptr() if score.get("stats") is not None else None
-    elif isinstance(score, type(None)):
-        pass
     a.partials = scratch.partials.data_ptr()
     a.counters = scratch.counters.data_ptr()
     a.err = scratch.err.data_ptr()
     N.check(N.lib.wnw_decode_attn(C.byref(a), N.stream_ptr(stream)), "wnw_decode_attn")
+    _count()
     return out
 
 
 def advance_lengths(seg_len, stream=None):
     N.call("wnw_advance_lengths", seg_len.data_ptr(), seg_len.numel(), N.stream_ptr(stream))
+    _count()
 
 
 def score_finalize(logits, stats, logit_off, stat_off, qmask, term_off, group, score_off, max_audio, acc,
@@ -102,6 +109,7 @@ def score_finalize(logits, stats, logit_off, stat_off, qmask, term_off, group, s
     N.call("wnw_score_finalize", logits.data_ptr(), stats.data_ptr(), logit_off.data_ptr(),
            stat_off.data_ptr(), qmask.data_ptr(), term_off.data_ptr(), int(group), int(batch),
            score_off.data_ptr(), int(max_audio), acc.data_ptr(), N.stream_ptr(stream))
+    _count()
 
 
 def chunk_topk(acc, score_off, max_audio, stride, segs_per_chunk, top_k, topk_out, chunk_scores=None,
@@ -111,6 +119,7 @@ def chunk_topk(acc, score_off, max_audio, stride, segs_per_chunk, top_k, topk_ou
            int(segs_per_chunk), int(top_k), topk_out.data_ptr(),
            chunk_scores.data_ptr() if chunk_scores is not None else None,
            chunk_off.data_ptr() if chunk_off is not None else None, N.stream_ptr(stream))
+    _count()
 
 
 def rebuild_layer(k_store, v_store, seg_base, seg_len, seg_cap, k_landing, v_landing, plan_blob, layer,
@@ -121,6 +130,7 @@ def rebuild_layer(k_store, v_store, seg_base, seg_len, seg_cap, k_landing, v_lan
            k_landing.data_ptr() if k_landing is not None else None,
            v_landing.data_ptr() if v_landing is not None else None, plan_blob.data_ptr(), int(layer),
            int(max_changed), err.data_ptr(), N.stream_ptr(stream))
+    _count()
 
 
 def copy_segments(src_k, src_v, src_base, dst_k, dst_v, dst_base, lens, stream=None):
@@ -130,6 +140,7 @@ def copy_segments(src_k, src_v, src_base, dst_k, dst_v, dst_base, lens, stream=N
         N.call("wnw_copy_segments", N.dtype_code(src_k.dtype), src_k.shape[1], src_k.data_ptr(),
                src_v.data_ptr(), src_base[lo:hi].data_ptr(), dst_k.data_ptr(), dst_v.data_ptr(),
                dst_base[lo:hi].data_ptr(), lens[lo:hi].data_ptr(), hi - lo, N.stream_ptr(stream))
+        _count()
 
 
 def interleave_append(old, new_tokens, cu_old, stream=None):
@@ -140,6 +151,7 @@ def interleave_append(old, new_tokens, cu_old, stream=None):
     N.call("wnw_interleave_append", N.dtype_code(old.dtype), old.shape[1],
            old.data_ptr() if old.numel() else None, new_tokens.data_ptr(), cu_old.data_ptr(), S,
            out.data_ptr(), N.stream_ptr(stream))
+    _count()
     return out, cu_old + torch.arange(S + 1, dtype=cu_old.dtype, device=cu_old.device)
 
 
