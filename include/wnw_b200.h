@@ -207,8 +207,10 @@ wnw_status wnw_planner_get_evictions(const wnw_planner* p, int32_t* starts, int3
                                      int* n);
 wnw_status wnw_planner_get_cpu_ranges(const wnw_planner* p, int32_t* ranges, int cap_pairs,
                                       int* n_pairs);
-/* Transfer-row offset of each layer's loads in the gathered order ([L+1]). */
-wnw_status wnw_planner_get_layer_transfer(const wnw_planner* p, int32_t* layer_rows);
+/* Transfer-row offset ([L+1]) and cpu-range offset ([L+1], may be NULL) of
+ * each layer's loads in the gathered order. */
+wnw_status wnw_planner_get_layer_transfer(const wnw_planner* p, int32_t* layer_rows,
+                                          int32_t* layer_ranges);
 /* Per-sample to_load / to_evict of the last call (sorted segment ids). */
 wnw_status wnw_planner_get_changes(const wnw_planner* p, int b, int32_t* to_load, int cap_load,
                                    int* n_load, int32_t* to_evict, int cap_evict, int* n_evict);
@@ -223,6 +225,19 @@ wnw_status wnw_planner_device_plan(const wnw_planner* p, int32_t* blob, int64_t 
 wnw_status wnw_gather_rows(const void* src_k, const void* src_v, int64_t row_bytes,
                            const int32_t* ranges, int n_pairs, void* dst_k, void* dst_v,
                            int n_threads);
+
+/* Device address of pinned (page-locked, mapped) host memory, for
+ * wnw_fetch_rows; WNW_ERR_CUDA when the memory is not mapped. */
+wnw_status wnw_host_device_pointer(const void* host_ptr, void** dev_ptr);
+
+/* Zero-copy fetch (replaces the staging gather + H2D copy of
+ * src/algorithms/wnw/code/cache.py:868-889 / planner.cpp:113-122): the GPU
+ * reads rows [ranges[i][0], ranges[i][1]) of src_k/src_v (device addresses of
+ * pinned host memory, row_bytes per row) and writes them to dst_k/dst_v at row
+ * dst_row[i].  ranges and dst_row are device arrays; at most max_ctas CTAs. */
+wnw_status wnw_fetch_rows(const void* src_k, const void* src_v, int64_t row_bytes,
+                          const int32_t* ranges, const int64_t* dst_row, int n_ranges,
+                          void* dst_k, void* dst_v, int max_ctas, void* stream);
 
 /* Async H2D copy of n bytes for K and V on `stream`, then record `event`
  * (cudaEvent_t as void*, may be NULL) -- one per layer. */

@@ -83,11 +83,15 @@ class B200WnWCache(FlatVarlenCache):
 
     Extra keyword arguments (all optional):
       max_decode_tokens -- decode rows reserved per slot (grown on demand);
-      fetch_threads     -- host threads for gathering offloaded rows.
+      fetch_mode        -- "zerocopy" (default): a kernel on the copy stream
+                           reads the offloaded rows straight from pinned host
+                           memory; "dma": host threads gather them into pinned
+                           staging and cudaMemcpyAsync copies each layer;
+      fetch_threads     -- host threads of the "dma" gather.
     """
 
     def __init__(self, config, num_layers, num_kv_heads, num_q_heads, head_dim, device, adapter=None, *,
-                 max_decode_tokens=256, fetch_threads=8):
+                 max_decode_tokens=256, fetch_mode="zerocopy", fetch_threads=8):
         super().__init__(num_layers, num_kv_heads, num_q_heads, head_dim, device, adapter)
         if self.device.type != "cuda":
             raise RuntimeError("B200WnWCache needs a CUDA device; the CPU oracle lives in the test suite")
@@ -97,6 +101,9 @@ class B200WnWCache(FlatVarlenCache):
             raise ValueError(f"GQA group {self.num_kv_groups} not supported (1..8)")
         self.config = config
         self.max_decode_tokens = int(max_decode_tokens)
+        if fetch_mode not in ("zerocopy", "dma"):
+            raise ValueError(f"fetch_mode must be 'zerocopy' or 'dma', not {fetch_mode!r}")
+        self.fetch_mode = fetch_mode
         self.fetch_threads = int(fetch_threads)
         self._class_b_heads_by_layer = [config.get_layer_class_b(l) for l in range(num_layers)]
         self.batch_size = 0
@@ -349,6 +356,7 @@ class B200WnWCache(FlatVarlenCache):
         if getattr(self, "_scratch", None) is None or not self._scratch.fits(n_max, G, D, S):
             self._scratch = Kx.AttnScratch(dev, n_max, G, D, S)
         del max_rows
+        self._attn_args = [None] * L  # launch arguments, built lazily per (layer, scale)
 
     def _grow(self, l):
         """Give layer l another ``max_decode_tokens`` rows per slot."""
@@ -442,6 +450,8 @@ class B200WnWCache(FlatVarlenCache):
         self._land_k = self._land_v = None
         self._stage_k = self._stage_v = None
         self._events = [torch.cuda.Event() for _ in range(L)]
+        self._restore_ptrs = None
+        self._fetched_rows = 0
         self._layer_chg = [0] * L
         self._layer_rows = np.zeros(L + 1, np.int64)
         self._new_kv = [None] * L
@@ -500,14 +510,23 @@ class B200WnWCache(FlatVarlenCache):
         G, D = self.num_kv_groups, self.head_dim
         qf = q_flat if q_flat.is_contiguous() else q_flat.contiguous()
         nk, nv = self._new_kv[l]
-        score = self._score_args(l)
-        foldable = all(len(qs) == G for _, qs in self._score_groups[l])
-        sep = score is not None and not foldable and not math.isclose(scale, D ** -0.5, rel_tol=0, abs_tol=1e-12)
-        out = Kx.decode_attention(qf, self.k_store[l], self.v_store[l], self._seg_base[l], self._seg_len[l],
-                                  self._work[l], self._cluster, scale, self._scratch, new_k=nk, new_v=nv,
-                                  seg_cap=self._seg_cap[l], num_kv_heads=self.num_kv_heads,
-                                  score=None if sep else score)
-        if sep:  # rescore with the reference's 1/sqrt(d) (the append is idempotent)
+        cached = self._attn_args[l]
+        if cached is None or cached[0] != scale:
+            score = self._score_args(l)
+            foldable = all(len(qs) == G for _, qs in self._score_groups[l])
+            sep = score is not None and not foldable and not math.isclose(scale, D ** -0.5, rel_tol=0,
+                                                                          abs_tol=1e-12)
+            S = self.batch_size * self.num_kv_heads
+            args = Kx.make_attn_args(self.dtype, S, G, D, self.k_store[l], self.v_store[l], self._seg_base[l],
+                                     self._seg_len[l], self._work[l], self._cluster, scale, self._scratch,
+                                     seg_cap=self._seg_cap[l], num_kv_heads=self.num_kv_heads,
+                                     score=None if sep else score)
+            cached = self._attn_args[l] = (scale, sep, args)
+        _, sep, args = cached
+        out = torch.empty_like(qf)
+        Kx.launch_attn(args, qf, nk, nv, out, torch.cuda.current_stream(self.device).cuda_stream)
+        if sep:
+            score = self._score_args(l)  # rescore with the reference's 1/sqrt(d) (the append is idempotent)
             Kx.decode_attention(qf, self.k_store[l], self.v_store[l], self._seg_base[l], self._seg_len[l],
                                 self._work[l], self._cluster, D ** -0.5, self._scratch, new_k=nk, new_v=nv,
                                 seg_cap=self._seg_cap[l], num_kv_heads=self.num_kv_heads, score=score,
@@ -551,9 +570,14 @@ class B200WnWCache(FlatVarlenCache):
             self._prepare_fetch(total, ranges)
 
     def _prepare_fetch(self, total, ranges):
-        """Device plan + host gather + per-layer async H2D on the copy stream
-        (the reference's staging cat + side-stream copy, cache.py:868-889)."""
+        """Device plan + fetch of the newly needed host rows, per layer on the
+        copy stream, each layer followed by its own event (the reference's
+        staging cat + side-stream copy, cache.py:868-889)."""
         L, D = self.num_layers, self.head_dim
+        if self._copy_stream is None:
+            self._copy_stream = torch.cuda.Stream(device=self.device)
+        cs = self._copy_stream
+        cs.synchronize()  # the previous plan's copies no longer read the pinned buffers
         plan = self._planner.device_plan()
         if plan.size > self._plan_host.numel():
             n = 1 << (plan.size - 1).bit_length()
@@ -561,42 +585,74 @@ class B200WnWCache(FlatVarlenCache):
             self._plan_dev = torch.zeros(n, dtype=torch.int32, device=self.device)
         self._plan_host[:plan.size].copy_(torch.from_numpy(plan))
         self._plan_np = plan.copy()
-        self._plan_dev[:plan.size].copy_(self._plan_host[:plan.size], non_blocking=True)
         for l in range(L):
-            o = int(plan[l])
-            self._layer_chg[l] = int(plan[o])
-        self._layer_rows = self._planner.layer_transfer_rows().astype(np.int64)
-        if total > 0:
-            self._ensure_fetch_capacity(total)
-            gather_rows(self.cpu_restore_k, self.cpu_restore_v, ranges, self._stage_k, self._stage_v,
-                        self.fetch_threads)
-            if self._copy_stream is None:
-                self._copy_stream = torch.cuda.Stream(device=self.device)
-            row_bytes = D * self.cpu_restore_k.element_size()
-            sp = self._copy_stream.cuda_stream
-            for l in range(L):
-                r0, r1 = int(self._layer_rows[l]), int(self._layer_rows[l + 1])
-                N.call("wnw_h2d_async", self._land_k[r0:].data_ptr(), self._land_v[r0:].data_ptr(),
-                       self._stage_k[r0:].data_ptr(), self._stage_v[r0:].data_ptr(), (r1 - r0) * row_bytes,
-                       sp, None)
-                self._events[l].record(self._copy_stream)
-            if self.stats.enabled:
-                n = int((ranges[:, 1] - ranges[:, 0]).sum())
-                self.stats.record_cpu_gpu_transfer(0, c2g_tokens=n, c2g_bytes=n * row_bytes * 2)
-        else:
-            for l in range(L):
-                self._events[l].record(torch.cuda.current_stream(self.device))
+            self._layer_chg[l] = int(plan[int(plan[l])])
+        rows, rng = self._planner.layer_transfer()
+        self._layer_rows = rows.astype(np.int64)
+        row_bytes = D * self.cpu_restore_k.element_size()
+        with torch.cuda.stream(cs):
+            self._plan_dev[:plan.size].copy_(self._plan_host[:plan.size], non_blocking=True)
+            if total > 0:
+                self._ensure_fetch_capacity(total, len(ranges))
+                if self.fetch_mode == "zerocopy":
+                    nr = len(ranges)
+                    lens = (ranges[:, 1] - ranges[:, 0]).astype(np.int64)
+                    self._rng_host[:nr].copy_(torch.from_numpy(np.ascontiguousarray(ranges, np.int32)))
+                    self._dst_host[0] = 0
+                    if nr > 1:
+                        self._dst_host[1:nr].copy_(torch.from_numpy(np.cumsum(lens)[:-1]))
+                    self._rng_dev[:nr].copy_(self._rng_host[:nr], non_blocking=True)
+                    self._dst_dev[:nr].copy_(self._dst_host[:nr], non_blocking=True)
+                    src_k, src_v = self._restore_dev_ptrs()
+                    for l in range(L):
+                        r0, r1 = int(rng[l]), int(rng[l + 1])
+                        if r1 > r0:
+                            Kx.fetch_rows(src_k, src_v, row_bytes, self._rng_dev[r0:r1], self._dst_dev[r0:r1],
+                                          self._land_k, self._land_v, stream=cs)
+                        self._events[l].record(cs)
+                else:
+                    gather_rows(self.cpu_restore_k, self.cpu_restore_v, ranges, self._stage_k, self._stage_v,
+                                self.fetch_threads)
+                    for l in range(L):
+                        r0, r1 = int(self._layer_rows[l]), int(self._layer_rows[l + 1])
+                        N.call("wnw_h2d_async", self._land_k[r0:].data_ptr(), self._land_v[r0:].data_ptr(),
+                               self._stage_k[r0:].data_ptr(), self._stage_v[r0:].data_ptr(),
+                               (r1 - r0) * row_bytes, cs.cuda_stream, None)
+                        self._events[l].record(cs)
+                if self.stats.enabled:
+                    n = int((ranges[:, 1] - ranges[:, 0]).sum())
+                    self.stats.record_cpu_gpu_transfer(0, c2g_tokens=n, c2g_bytes=n * row_bytes * 2)
+            else:
+                for l in range(L):
+                    self._events[l].record(cs)
+        self._fetched_rows = int(total)
         self._pending = True
 
-    def _ensure_fetch_capacity(self, rows):
-        if self._land_k is not None and self._land_k.shape[0] >= rows:
-            return
-        n = 1 << max(0, rows - 1).bit_length()
+    def _restore_dev_ptrs(self):
+        if getattr(self, "_restore_ptrs", None) is None:
+            if not self.cpu_restore_k.is_pinned():
+                raise RuntimeError("zero-copy fetch needs the host restore store in pinned memory "
+                                   "(use fetch_mode='dma')")
+            self._restore_ptrs = (Kx.host_device_pointer(self.cpu_restore_k),
+                                  Kx.host_device_pointer(self.cpu_restore_v))
+        return self._restore_ptrs
+
+    def _ensure_fetch_capacity(self, rows, n_ranges):
         D, dt = self.head_dim, self.dtype
-        self._land_k = torch.empty(n, D, dtype=dt, device=self.device)
-        self._land_v = torch.empty(n, D, dtype=dt, device=self.device)
-        self._stage_k = torch.empty(n, D, dtype=dt).pin_memory()
-        self._stage_v = torch.empty(n, D, dtype=dt).pin_memory()
+        if self._land_k is None or self._land_k.shape[0] < rows:
+            n = 1 << max(0, rows - 1).bit_length()
+            self._land_k = torch.empty(n, D, dtype=dt, device=self.device)
+            self._land_v = torch.empty(n, D, dtype=dt, device=self.device)
+            if self.fetch_mode == "dma":
+                self._stage_k = torch.empty(n, D, dtype=dt).pin_memory()
+                self._stage_v = torch.empty(n, D, dtype=dt).pin_memory()
+        if self.fetch_mode == "zerocopy" and (getattr(self, "_rng_host", None) is None
+                                              or self._rng_host.shape[0] < n_ranges):
+            n = 1 << max(0, n_ranges - 1).bit_length()
+            self._rng_host = torch.zeros(n, 2, dtype=torch.int32).pin_memory()
+            self._dst_host = torch.zeros(n, dtype=torch.int64).pin_memory()
+            self._rng_dev = torch.zeros(n, 2, dtype=torch.int32, device=self.device)
+            self._dst_dev = torch.zeros(n, dtype=torch.int64, device=self.device)
 
     # ---------------------------------------------------------- inspection
     def packed_layer(self, layer_idx):

@@ -45,6 +45,7 @@ struct wnw_planner {
   // results of the last compute_and_prepare
   std::vector<int32_t> ev_starts, ev_ends, cpu_ranges;
   std::vector<int32_t> layer_rows;                // [L+1] transfer-row offsets
+  std::vector<int32_t> layer_ranges;              // [L+1] cpu-range offsets
   std::vector<std::vector<int>> to_load, to_evict;  // [B] sorted
   std::vector<int> changed;                       // changed samples
   // per layer: changed segments and their records (for the device plan)
@@ -91,6 +92,7 @@ wnw_status wnw_planner_create(int num_layers, int num_kv_heads, int batch_size, 
   p->to_evict.resize(p->B);
   p->chg.resize(p->L);
   p->layer_rows.assign(p->L + 1, 0);
+  p->layer_ranges.assign(p->L + 1, 0);
   *out = p;
   return WNW_OK;
 }
@@ -258,6 +260,7 @@ wnw_status wnw_planner_compute_and_prepare(wnw_planner* p, const int32_t* topk_i
   p->changed.clear();
   for (auto& v : p->chg) v.clear();
   std::fill(p->layer_rows.begin(), p->layer_rows.end(), 0);
+  std::fill(p->layer_ranges.begin(), p->layer_ranges.end(), 0);
   p->last_change = change;
   if (!change) {
     p->prev_changed = false;
@@ -277,6 +280,7 @@ wnw_status wnw_planner_compute_and_prepare(wnw_planner* p, const int32_t* topk_i
   int gts = 0;
   for (int l = 0; l < L; ++l) {
     p->layer_rows[l] = gts;
+    p->layer_ranges[l] = static_cast<int32_t>(p->cpu_ranges.size() / 2);
     int32_t* ls = load_starts_2d + size_t(l) * S;
     int32_t* ll = load_lens_2d + size_t(l) * S;
     int32_t* cun = cu_new_2d + size_t(l) * (S + 1);
@@ -392,6 +396,7 @@ wnw_status wnw_planner_compute_and_prepare(wnw_planner* p, const int32_t* topk_i
     p->ev_ends.swap(ee);
   }
   p->layer_rows[L] = gts;
+  p->layer_ranges[L] = static_cast<int32_t>(p->cpu_ranges.size() / 2);
   p->seq_lens.swap(new_lens);
   p->prev_changed = true;
   *any_change = 1;
@@ -430,9 +435,10 @@ wnw_status wnw_planner_get_cpu_ranges(const wnw_planner* p, int32_t* ranges, int
   return WNW_OK;
 }
 
-wnw_status wnw_planner_get_layer_transfer(const wnw_planner* p, int32_t* layer_rows) {
+wnw_status wnw_planner_get_layer_transfer(const wnw_planner* p, int32_t* layer_rows, int32_t* layer_ranges) {
   if (!p || !layer_rows) return bad("null argument");
   std::memcpy(layer_rows, p->layer_rows.data(), sizeof(int32_t) * (p->L + 1));
+  if (layer_ranges) std::memcpy(layer_ranges, p->layer_ranges.data(), sizeof(int32_t) * (p->L + 1));
   return WNW_OK;
 }
 

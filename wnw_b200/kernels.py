@@ -58,6 +58,65 @@ class AttnScratch:
         return (n_clusters * group * (head_dim + 2) <= self.partials.numel() and num_segs <= self.counters.numel())
 
 
+def make_attn_args(dtype, S, G, D, k_store, v_store, seg_base, seg_len, work, cluster_size, scale, scratch,
+                   seg_cap=None, num_kv_heads=None, score=None):
+    """A reusable ``wnw_decode_attn_args`` with everything but q / new rows /
+    out filled in (the per-layer constant part of a decode step)."""
+    a = N.DecodeAttnArgs()
+    a.dtype = N.dtype_code(dtype)
+    a.head_dim, a.group, a.num_segs = D, G, S
+    a.num_kv_heads = num_kv_heads if num_kv_heads is not None else S
+    a.k_store, a.v_store = k_store.data_ptr(), v_store.data_ptr()
+    a.seg_base, a.seg_len = seg_base.data_ptr(), seg_len.data_ptr()
+    a.seg_cap = seg_cap.data_ptr() if seg_cap is not None else None
+    a.work = work.data_ptr()
+    a.n_clusters = work.shape[0]
+    a.cluster_size = cluster_size
+    a.split_rows = split_rows(dtype, D)
+    a.scale = float(scale)
+    if score is not None:
+        a.score_slot = score["slot"].data_ptr()
+        a.audio_start = score["audio_start"].data_ptr()
+        a.audio_end = score["audio_end"].data_ptr()
+        a.logits = score["logits"].data_ptr()
+        a.logits_off = score["logits_off"].data_ptr()
+        a.stats = score["stats"].data_ptr() if score.get("stats") is not None else None
+    a.partials = scratch.partials.data_ptr()
+    a.counters = scratch.counters.data_ptr()
+    a.err = scratch.err.data_ptr()
+    return a
+
+
+def launch_attn(args, q, new_k, new_v, out, stream_handle):
+    """Fill the per-step pointers of a prepared args struct and launch."""
+    args.q = q.data_ptr()
+    args.new_k = new_k.data_ptr() if new_k is not None else None
+    args.new_v = new_v.data_ptr() if new_v is not None else None
+    args.out = out.data_ptr()
+    st = N.lib.wnw_decode_attn(C.byref(args), stream_handle)
+    if st:
+        N.check(st, "wnw_decode_attn")
+    LAUNCHES[0] += 1
+    return out
+
+
+def fetch_rows(src_k_dev, src_v_dev, row_bytes, ranges, dst_row, dst_k, dst_v, max_ctas=256, stream=None):
+    """Zero-copy gather of host rows (device addresses of pinned memory)."""
+    n = ranges.shape[0]
+    if n == 0:
+        return
+    N.call("wnw_fetch_rows", src_k_dev, src_v_dev, int(row_bytes), ranges.data_ptr(), dst_row.data_ptr(), int(n),
+           dst_k.data_ptr(), dst_v.data_ptr(), int(max_ctas), N.stream_ptr(stream))
+    _count()
+
+
+def host_device_pointer(t):
+    """Device address of a pinned host tensor (raises if it is not mapped)."""
+    out = C.c_void_p()
+    N.call("wnw_host_device_pointer", t.data_ptr(), C.byref(out))
+    return out.value
+
+
 def decode_attention(q, k_store, v_store, seg_base, seg_len, work, cluster_size, scale, scratch,
                      new_k=None, new_v=None, seg_cap=None, out=None, num_kv_heads=None, score=None,
                      stream=None):

@@ -107,9 +107,14 @@ class Planner:
         return r
 
     def layer_transfer_rows(self):
-        out = np.zeros(self.L + 1, np.int32)
-        N.call("wnw_planner_get_layer_transfer", self._h, N.ptr(out))
-        return out
+        return self.layer_transfer()[0]
+
+    def layer_transfer(self):
+        """(transfer-row offsets [L+1], cpu-range offsets [L+1]) of the last plan."""
+        rows = np.zeros(self.L + 1, np.int32)
+        rng = np.zeros(self.L + 1, np.int32)
+        N.call("wnw_planner_get_layer_transfer", self._h, N.ptr(rows), N.ptr(rng))
+        return rows, rng
 
     def changes(self, b):
         nl, ne = C.c_int(), C.c_int()
