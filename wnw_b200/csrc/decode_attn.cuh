@@ -381,14 +381,30 @@ __global__ void __launch_bounds__(kAttnThreads)
   T* outp = reinterpret_cast<T*>(p.out) + int64_t(seg) * G * D;
   for (int i = i_lo + tid; i < i_hi; i += kAttnThreads) {
     const int g = i / D, d = i % D;
+    // pull every rank's (max, sum, o) first so the remote loads overlap
+    float pm[8], pl[8], po[8];
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+      if (r < cs) {
+        pm[r] = *cluster.map_shared_rank(Pm + g, r);
+        pl[r] = *cluster.map_shared_rank(Pl + g, r);
+        po[r] = *cluster.map_shared_rank(Po + i, r);
+      } else {
+        pm[r] = -INFINITY;
+        pl[r] = 0.f;
+        po[r] = 0.f;
+      }
+    }
     float mx = -INFINITY;
-    for (int r = 0; r < cs; ++r) mx = fmaxf(mx, *cluster.map_shared_rank(Pm + g, r));
+#pragma unroll
+    for (int r = 0; r < 8; ++r) mx = fmaxf(mx, pm[r]);
     const float bse = (mx == -INFINITY) ? 0.f : mx;
     float acc = 0.f, ls = 0.f;
-    for (int r = 0; r < cs; ++r) {
-      const float f = ex2(*cluster.map_shared_rank(Pm + g, r) - bse);
-      acc += *cluster.map_shared_rank(Po + i, r) * f;
-      ls += *cluster.map_shared_rank(Pl + g, r) * f;
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+      const float f = ex2(pm[r] - bse);
+      acc += po[r] * f;
+      ls += pl[r] * f;
     }
     if (ncl == 1) {
       outp[i] = DT<T>::from_f(ls > 0.f ? acc / ls : 0.f);
@@ -421,17 +437,40 @@ __global__ void __launch_bounds__(kAttnThreads)
   __threadfence();
   // final merge across the segment's clusters, sliced over the ranks
   const float* part0 = p.partials + int64_t(cid - j) * G * (D + 2);
+  constexpr int kBatch = 16;  // cluster partials loaded per round trip
   for (int i = i_lo + tid; i < i_hi; i += kAttnThreads) {
     const int g = i / D, d = i % D;
-    float mx = -INFINITY;
-    for (int c = 0; c < ncl; ++c) mx = fmaxf(mx, __ldcg(part0 + int64_t(c) * G * (D + 2) + G * D + g));
-    const float bse = (mx == -INFINITY) ? 0.f : mx;
-    float acc = 0.f, ls = 0.f;
-    for (int c = 0; c < ncl; ++c) {
-      const float* pc = part0 + int64_t(c) * G * (D + 2);
-      const float f = ex2(__ldcg(pc + G * D + g) - bse);
-      acc += __ldcg(pc + i) * f;
-      ls += __ldcg(pc + G * D + G + g) * f;
+    float mx = -INFINITY, acc = 0.f, ls = 0.f;
+    for (int c0 = 0; c0 < ncl; c0 += kBatch) {
+      float bm[kBatch], bl[kBatch], bo[kBatch];
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u) {
+        const int c = c0 + u;
+        if (c < ncl) {
+          const float* pc = part0 + int64_t(c) * G * (D + 2);
+          bm[u] = __ldcg(pc + G * D + g);
+          bl[u] = __ldcg(pc + G * D + G + g);
+          bo[u] = __ldcg(pc + i);
+        } else {
+          bm[u] = -INFINITY;
+          bl[u] = 0.f;
+          bo[u] = 0.f;
+        }
+      }
+      float mn = mx;
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u) mn = fmaxf(mn, bm[u]);
+      const float bse = (mn == -INFINITY) ? 0.f : mn;
+      const float a = ex2(mx - bse);
+      acc *= a;
+      ls *= a;
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u) {
+        const float f = ex2(bm[u] - bse);
+        acc += bo[u] * f;
+        ls += bl[u] * f;
+      }
+      mx = mn;
     }
     outp[i] = DT<T>::from_f(ls > 0.f ? acc / ls : 0.f);
     if (d == 0 && p.stats != nullptr) {

@@ -61,8 +61,11 @@ class AttnScratch:
 def make_attn_args(dtype, S, G, D, k_store, v_store, seg_base, seg_len, work, cluster_size, scale, scratch,
                    seg_cap=None, num_kv_heads=None, score=None):
     """A reusable ``wnw_decode_attn_args`` with everything but q / new rows /
-    out filled in (the per-layer constant part of a decode step)."""
+    out filled in (the per-layer constant part of a decode step).  The struct
+    keeps references to every tensor it points at, so temporaries passed in
+    stay alive as long as the arguments do."""
     a = N.DecodeAttnArgs()
+    a._keep = (k_store, v_store, seg_base, seg_len, work, scratch, seg_cap, score)
     a.dtype = N.dtype_code(dtype)
     a.head_dim, a.group, a.num_segs = D, G, S
     a.num_kv_heads = num_kv_heads if num_kv_heads is not None else S
