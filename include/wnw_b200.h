@@ -95,11 +95,13 @@ typedef struct wnw_decode_attn_args {
   float* partials;
   int32_t* counters;
   int32_t* err;                  /* device error word (WNW_DEVERR_* bits)    */
+  int64_t store_rows;            /* rows of k_store / v_store (the TMA extent) */
 } wnw_decode_attn_args;
 
 wnw_status wnw_decode_attn(const wnw_decode_attn_args* a, void* stream);
 
-/* Rows per CTA used by wnw_decode_attn for a dtype / head_dim. */
+/* Rows per CTA used by wnw_decode_attn for a dtype / head_dim (16-bit K/V
+ * with head_dim 64 or 128 take the tensor-core kernel: 128 rows per CTA). */
 int wnw_split_rows(int dtype, int head_dim);
 
 /* Build the cluster work table on the host from per-segment row capacities

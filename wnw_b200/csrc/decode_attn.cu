@@ -7,6 +7,7 @@ namespace wnw {
 int split_rows_for(int dtype, int head_dim) {
   const int esz = dtype == WNW_F32 ? 4 : 2;
   if (head_dim <= 0) return 0;
+  if (esz == 2 && (head_dim == 64 || head_dim == 128)) return 128;  // tensor-core kernel tile
   return kAttnTileBytes / (2 * head_dim * esz);
 }
 

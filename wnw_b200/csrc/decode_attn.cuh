@@ -85,13 +85,158 @@ struct AttnParams {
   int32_t* err;
 };
 
+// Merge the 4 warp partials (wm, wl, wo at the start of `smem`) into the
+// CTA partial, then the cluster's CTAs through distributed shared memory, then
+// -- for segments longer than one cluster -- the clusters through the global
+// partial buffer, the last-arriving cluster writing the output.
+template <typename T, int D, int G>
+__device__ __forceinline__ void attn_finish(const AttnParams& p, uint8_t* smem, int seg, int j, int cid, int ncl) {
+  cg::cluster_group cluster = cg::this_cluster();
+  const int cs = static_cast<int>(cluster.num_blocks());
+  const int rank = static_cast<int>(cluster.block_rank());
+  const int tid = threadIdx.x;
+  __shared__ int s_last;
+  float* wm = reinterpret_cast<float*>(smem);
+  float* wl = wm + kAttnWarps * G;
+  float* wo = wl + kAttnWarps * G;
+  float* Pm = wo + kAttnWarps * G * D;
+  float* Pl = Pm + G;
+  float* Po = Pl + G;
+  for (int i = tid; i < G * D; i += kAttnThreads) {
+    const int g = i / D, d = i % D;
+    float mx = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kAttnWarps; ++w) mx = fmaxf(mx, wm[w * G + g]);
+    const float bse = (mx == -INFINITY) ? 0.f : mx;
+    float acc = 0.f, ls = 0.f;
+#pragma unroll
+    for (int w = 0; w < kAttnWarps; ++w) {
+      const float f = ex2(wm[w * G + g] - bse);
+      acc += wo[(w * G + g) * D + d] * f;
+      ls += wl[w * G + g] * f;
+    }
+    Po[i] = acc;
+    if (d == 0) {
+      Pm[g] = mx;
+      Pl[g] = ls;
+    }
+  }
+
+  // ---- merge the CTAs of the cluster through distributed shared memory;
+  // each rank merges a slice of the G*D outputs
+  cluster.sync();
+  const int per = (G * D + cs - 1) / cs;
+  const int i_lo = rank * per;
+  const int i_hi = min(G * D, i_lo + per);
+  float* part = p.partials + int64_t(cid) * G * (D + 2);
+  T* outp = reinterpret_cast<T*>(p.out) + int64_t(seg) * G * D;
+  for (int i = i_lo + tid; i < i_hi; i += kAttnThreads) {
+    const int g = i / D, d = i % D;
+    // pull every rank's (max, sum, o) first so the remote loads overlap
+    float pm[8], pl[8], po[8];
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+      if (r < cs) {
+        pm[r] = *cluster.map_shared_rank(Pm + g, r);
+        pl[r] = *cluster.map_shared_rank(Pl + g, r);
+        po[r] = *cluster.map_shared_rank(Po + i, r);
+      } else {
+        pm[r] = -INFINITY;
+        pl[r] = 0.f;
+        po[r] = 0.f;
+      }
+    }
+    float mx = -INFINITY;
+#pragma unroll
+    for (int r = 0; r < 8; ++r) mx = fmaxf(mx, pm[r]);
+    const float bse = (mx == -INFINITY) ? 0.f : mx;
+    float acc = 0.f, ls = 0.f;
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+      const float f = ex2(pm[r] - bse);
+      acc += po[r] * f;
+      ls += pl[r] * f;
+    }
+    if (ncl == 1) {
+      outp[i] = DT<T>::from_f(ls > 0.f ? acc / ls : 0.f);
+      if (d == 0 && p.stats != nullptr) {
+        p.stats[int64_t(seg) * 2 * G + g] = mx;
+        p.stats[int64_t(seg) * 2 * G + G + g] = ls;
+      }
+    } else {
+      part[i] = acc;
+      if (d == 0) {
+        part[G * D + g] = mx;
+        part[G * D + G + g] = ls;
+      }
+    }
+  }
+  if (ncl == 1) {
+    cluster.sync();  // keep this CTA's shared memory alive for the remote reads
+    return;
+  }
+  __threadfence();
+  cluster.sync();
+  if (rank == 0 && tid == 0) {
+    const int old = atomicAdd(p.counters + seg, 1);
+    const int last = (old == ncl - 1) ? 1 : 0;
+    if (last) p.counters[seg] = 0;  // every cluster of this launch has arrived
+    for (int r = 0; r < cs; ++r) *cluster.map_shared_rank(&s_last, r) = last;
+  }
+  cluster.sync();
+  if (!s_last) return;
+  __threadfence();
+  // final merge across the segment's clusters, sliced over the ranks
+  const float* part0 = p.partials + int64_t(cid - j) * G * (D + 2);
+  constexpr int kBatch = 16;  // cluster partials loaded per round trip
+  for (int i = i_lo + tid; i < i_hi; i += kAttnThreads) {
+    const int g = i / D, d = i % D;
+    float mx = -INFINITY, acc = 0.f, ls = 0.f;
+    for (int c0 = 0; c0 < ncl; c0 += kBatch) {
+      float bm[kBatch], bl[kBatch], bo[kBatch];
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u) {
+        const int c = c0 + u;
+        if (c < ncl) {
+          const float* pc = part0 + int64_t(c) * G * (D + 2);
+          bm[u] = __ldcg(pc + G * D + g);
+          bl[u] = __ldcg(pc + G * D + G + g);
+          bo[u] = __ldcg(pc + i);
+        } else {
+          bm[u] = -INFINITY;
+          bl[u] = 0.f;
+          bo[u] = 0.f;
+        }
+      }
+      float mn = mx;
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u) mn = fmaxf(mn, bm[u]);
+      const float bse = (mn == -INFINITY) ? 0.f : mn;
+      const float a = ex2(mx - bse);
+      acc *= a;
+      ls *= a;
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u) {
+        const float f = ex2(bm[u] - bse);
+        acc += bo[u] * f;
+        ls += bl[u] * f;
+      }
+      mx = mn;
+    }
+    outp[i] = DT<T>::from_f(ls > 0.f ? acc / ls : 0.f);
+    if (d == 0 && p.stats != nullptr) {
+      p.stats[int64_t(seg) * 2 * G + g] = mx;
+      p.stats[int64_t(seg) * 2 * G + G + g] = ls;
+    }
+  }
+}
+
 template <typename T, int D, int G>
 __global__ void __launch_bounds__(kAttnThreads)
     decode_attn_kernel(const AttnParams p) {
   using C = AttnCfg<T, D, G>;
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ __align__(8) uint64_t bars[kAttnWarps];
-  __shared__ int s_last;
 
   cg::cluster_group cluster = cg::this_cluster();
   const int cs = static_cast<int>(cluster.num_blocks());
@@ -330,9 +475,6 @@ __global__ void __launch_bounds__(kAttnThreads)
   float* wm = reinterpret_cast<float*>(smem);
   float* wl = wm + kAttnWarps * G;
   float* wo = wl + kAttnWarps * G;
-  float* Pm = wo + kAttnWarps * G * D;
-  float* Pl = Pm + G;
-  float* Po = Pl + G;
   if (lane < C::LPR) {
 #pragma unroll
     for (int g = 0; g < G; ++g) {
@@ -351,146 +493,10 @@ __global__ void __launch_bounds__(kAttnThreads)
     }
   }
   __syncthreads();
-  for (int i = tid; i < G * D; i += kAttnThreads) {
-    const int g = i / D, d = i % D;
-    float mx = -INFINITY;
-#pragma unroll
-    for (int w = 0; w < kAttnWarps; ++w) mx = fmaxf(mx, wm[w * G + g]);
-    const float bse = (mx == -INFINITY) ? 0.f : mx;
-    float acc = 0.f, ls = 0.f;
-#pragma unroll
-    for (int w = 0; w < kAttnWarps; ++w) {
-      const float f = ex2(wm[w * G + g] - bse);
-      acc += wo[(w * G + g) * D + d] * f;
-      ls += wl[w * G + g] * f;
-    }
-    Po[i] = acc;
-    if (d == 0) {
-      Pm[g] = mx;
-      Pl[g] = ls;
-    }
-  }
-
-  // ---- merge the CTAs of the cluster through distributed shared memory;
-  // each rank merges a slice of the G*D outputs
-  cluster.sync();
-  const int per = (G * D + cs - 1) / cs;
-  const int i_lo = rank * per;
-  const int i_hi = min(G * D, i_lo + per);
-  float* part = p.partials + int64_t(cid) * G * (D + 2);
-  T* outp = reinterpret_cast<T*>(p.out) + int64_t(seg) * G * D;
-  for (int i = i_lo + tid; i < i_hi; i += kAttnThreads) {
-    const int g = i / D, d = i % D;
-    // pull every rank's (max, sum, o) first so the remote loads overlap
-    float pm[8], pl[8], po[8];
-#pragma unroll
-    for (int r = 0; r < 8; ++r) {
-      if (r < cs) {
-        pm[r] = *cluster.map_shared_rank(Pm + g, r);
-        pl[r] = *cluster.map_shared_rank(Pl + g, r);
-        po[r] = *cluster.map_shared_rank(Po + i, r);
-      } else {
-        pm[r] = -INFINITY;
-        pl[r] = 0.f;
-        po[r] = 0.f;
-      }
-    }
-    float mx = -INFINITY;
-#pragma unroll
-    for (int r = 0; r < 8; ++r) mx = fmaxf(mx, pm[r]);
-    const float bse = (mx == -INFINITY) ? 0.f : mx;
-    float acc = 0.f, ls = 0.f;
-#pragma unroll
-    for (int r = 0; r < 8; ++r) {
-      const float f = ex2(pm[r] - bse);
-      acc += po[r] * f;
-      ls += pl[r] * f;
-    }
-    if (ncl == 1) {
-      outp[i] = DT<T>::from_f(ls > 0.f ? acc / ls : 0.f);
-      if (d == 0 && p.stats != nullptr) {
-        p.stats[int64_t(seg) * 2 * G + g] = mx;
-        p.stats[int64_t(seg) * 2 * G + G + g] = ls;
-      }
-    } else {
-      part[i] = acc;
-      if (d == 0) {
-        part[G * D + g] = mx;
-        part[G * D + G + g] = ls;
-      }
-    }
-  }
-  if (ncl == 1) {
-    cluster.sync();  // keep this CTA's shared memory alive for the remote reads
-    return;
-  }
-  __threadfence();
-  cluster.sync();
-  if (rank == 0 && tid == 0) {
-    const int old = atomicAdd(p.counters + seg, 1);
-    const int last = (old == ncl - 1) ? 1 : 0;
-    if (last) p.counters[seg] = 0;  // every cluster of this launch has arrived
-    for (int r = 0; r < cs; ++r) *cluster.map_shared_rank(&s_last, r) = last;
-  }
-  cluster.sync();
-  if (!s_last) return;
-  __threadfence();
-  // final merge across the segment's clusters, sliced over the ranks
-  const float* part0 = p.partials + int64_t(cid - j) * G * (D + 2);
-  constexpr int kBatch = 16;  // cluster partials loaded per round trip
-  for (int i = i_lo + tid; i < i_hi; i += kAttnThreads) {
-    const int g = i / D, d = i % D;
-    float mx = -INFINITY, acc = 0.f, ls = 0.f;
-    for (int c0 = 0; c0 < ncl; c0 += kBatch) {
-      float bm[kBatch], bl[kBatch], bo[kBatch];
-#pragma unroll
-      for (int u = 0; u < kBatch; ++u) {
-        const int c = c0 + u;
-        if (c < ncl) {
-          const float* pc = part0 + int64_t(c) * G * (D + 2);
-          bm[u] = __ldcg(pc + G * D + g);
-          bl[u] = __ldcg(pc + G * D + G + g);
-          bo[u] = __ldcg(pc + i);
-        } else {
-          bm[u] = -INFINITY;
-          bl[u] = 0.f;
-          bo[u] = 0.f;
-        }
-      }
-      float mn = mx;
-#pragma unroll
-      for (int u = 0; u < kBatch; ++u) mn = fmaxf(mn, bm[u]);
-      const float bse = (mn == -INFINITY) ? 0.f : mn;
-      const float a = ex2(mx - bse);
-      acc *= a;
-      ls *= a;
-#pragma unroll
-      for (int u = 0; u < kBatch; ++u) {
-        const float f = ex2(bm[u] - bse);
-        acc += bo[u] * f;
-        ls += bl[u] * f;
-      }
-      mx = mn;
-    }
-    outp[i] = DT<T>::from_f(ls > 0.f ? acc / ls : 0.f);
-    if (d == 0 && p.stats != nullptr) {
-      p.stats[int64_t(seg) * 2 * G + g] = mx;
-      p.stats[int64_t(seg) * 2 * G + G + g] = ls;
-    }
-  }
+  attn_finish<T, D, G>(p, smem, seg, j, cid, ncl);
 }
 
-template <typename T, int D, int G>
-wnw_status launch_attn(const wnw_decode_attn_args* a, cudaStream_t stream) {
-  using C = AttnCfg<T, D, G>;
-  static bool configured = false;  // attribute setting is idempotent; a race only repeats it
-  auto kern = decode_attn_kernel<T, D, G>;
-  if (!configured) {
-    WNW_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnTileBytes));
-    configured = true;
-  }
-  WNW_CHECK_ARG(a->split_rows == C::SPLIT, "split_rows %d does not match kernel split %d", a->split_rows,
-                C::SPLIT);
+inline AttnParams make_params(const wnw_decode_attn_args* a) {
   AttnParams p;
   p.q = a->q;
   p.new_k = a->new_k;
@@ -513,6 +519,21 @@ wnw_status launch_attn(const wnw_decode_attn_args* a, cudaStream_t stream) {
   p.partials = a->partials;
   p.counters = a->counters;
   p.err = a->err;
+  return p;
+}
+
+template <typename T, int D, int G>
+wnw_status launch_attn(const wnw_decode_attn_args* a, cudaStream_t stream) {
+  using C = AttnCfg<T, D, G>;
+  static bool configured = false;  // attribute setting is idempotent; a race only repeats it
+  auto kern = decode_attn_kernel<T, D, G>;
+  if (!configured) {
+    WNW_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnTileBytes));
+    configured = true;
+  }
+  WNW_CHECK_ARG(a->split_rows == C::SPLIT, "split_rows %d does not match kernel split %d", a->split_rows,
+                C::SPLIT);
+  AttnParams p = make_params(a);
 
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a->n_clusters * a->cluster_size, 1, 1);

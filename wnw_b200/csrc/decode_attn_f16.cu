@@ -1,6 +1,6 @@
 // Instantiations of the decode-attention kernel for one dtype (split per
 // dtype so the three translation units compile in parallel).
-#include "decode_attn.cuh"
+#include "decode_attn_mma.cuh"
 
 namespace wnw {
 
@@ -19,13 +19,28 @@ static wnw_status dispatch_g(const wnw_decode_attn_args* a, cudaStream_t s) {
   }
 }
 
+template <typename T, int D>
+static wnw_status dispatch_mma(const wnw_decode_attn_args* a, cudaStream_t s) {
+  switch (a->group) {
+    case 1: return launch_attn_mma<T, D, 1>(a, s);
+    case 2: return launch_attn_mma<T, D, 2>(a, s);
+    case 3: return launch_attn_mma<T, D, 3>(a, s);
+    case 4: return launch_attn_mma<T, D, 4>(a, s);
+    case 5: return launch_attn_mma<T, D, 5>(a, s);
+    case 6: return launch_attn_mma<T, D, 6>(a, s);
+    case 7: return launch_attn_mma<T, D, 7>(a, s);
+    case 8: return launch_attn_mma<T, D, 8>(a, s);
+    default: set_error("group %d not compiled (1..8)", a->group); return WNW_ERR_UNSUPPORTED;
+  }
+}
+
 template <>
 wnw_status dispatch_dtype<__half>(const wnw_decode_attn_args* a, cudaStream_t s) {
   switch (a->head_dim) {
     case 16: return dispatch_g<__half, 16>(a, s);
     case 32: return dispatch_g<__half, 32>(a, s);
-    case 64: return dispatch_g<__half, 64>(a, s);
-    case 128: return dispatch_g<__half, 128>(a, s);
+    case 64: return dispatch_mma<__half, 64>(a, s);
+    case 128: return dispatch_mma<__half, 128>(a, s);
     default: set_error("head_dim %d not compiled (16, 32, 64, 128)", a->head_dim); return WNW_ERR_UNSUPPORTED;
   }
 }

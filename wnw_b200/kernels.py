@@ -87,6 +87,7 @@ def make_attn_args(dtype, S, G, D, k_store, v_store, seg_base, seg_len, work, cl
     a.partials = scratch.partials.data_ptr()
     a.counters = scratch.counters.data_ptr()
     a.err = scratch.err.data_ptr()
+    a.store_rows = k_store.shape[0]
     return a
 
 
@@ -155,6 +156,7 @@ def decode_attention(q, k_store, v_store, seg_base, seg_len, work, cluster_size,
     a.partials = scratch.partials.data_ptr()
     a.counters = scratch.counters.data_ptr()
     a.err = scratch.err.data_ptr()
+    a.store_rows = k_store.shape[0]
     N.check(N.lib.wnw_decode_attn(C.byref(a), N.stream_ptr(stream)), "wnw_decode_attn")
     _count()
     return out

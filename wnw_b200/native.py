@@ -47,7 +47,7 @@ class DecodeAttnArgs(C.Structure):
         ("n_clusters", C.c_int), ("cluster_size", C.c_int), ("split_rows", C.c_int),
         ("out", P), ("scale", C.c_float),
         ("score_slot", P), ("audio_start", P), ("audio_end", P), ("logits", P), ("logits_off", P),
-        ("stats", P), ("partials", P), ("counters", P), ("err", P),
+        ("stats", P), ("partials", P), ("counters", P), ("err", P), ("store_rows", C.c_int64),
     ]
 
 
