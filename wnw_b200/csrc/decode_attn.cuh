@@ -175,17 +175,19 @@ __device__ __forceinline__ void attn_finish(const AttnParams& p, uint8_t* smem, 
     cluster.sync();  // keep this CTA's shared memory alive for the remote reads
     return;
   }
-  __threadfence();
+  fence_acq_rel_gpu();  // release this thread's partial slice at gpu scope
   cluster.sync();
   if (rank == 0 && tid == 0) {
     const int old = atomicAdd(p.counters + seg, 1);
     const int last = (old == ncl - 1) ? 1 : 0;
-    if (last) p.counters[seg] = 0;  // every cluster of this launch has arrived
+    if (last) {
+      p.counters[seg] = 0;  // every cluster of this launch has arrived
+      fence_acq_rel_gpu();  // acquire the other clusters' partials
+    }
     for (int r = 0; r < cs; ++r) *cluster.map_shared_rank(&s_last, r) = last;
   }
   cluster.sync();
   if (!s_last) return;
-  __threadfence();
   // final merge across the segment's clusters, sliced over the ranks
   const float* part0 = p.partials + int64_t(cid - j) * G * (D + 2);
   constexpr int kBatch = 16;  // cluster partials loaded per round trip
