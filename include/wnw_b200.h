@@ -100,6 +100,23 @@ typedef struct wnw_decode_attn_args {
 
 wnw_status wnw_decode_attn(const wnw_decode_attn_args* a, void* stream);
 
+/* Allocation-free variant of wnw_decode_attn.  It has no counterpart in the
+ * reference.  It is for callers that cannot allocate device memory because
+ * their host owns every byte of it (a serving engine with a fixed, pre-split
+ * memory budget; a plugin host that only hands in its own buffers), where a
+ * cudaMalloc would fail or escape the host's accounting.  The partial-state
+ * and counter scratch come from a file-scope device array of
+ * WNW_NOALLOC_MAX_PARTIAL_FLOATS floats + WNW_NOALLOC_MAX_SEGS counters (about
+ * 4.3 MB, held by every device that loads the library until exit); a->partials
+ * and a->counters are ignored, every other field means what it means for
+ * wnw_decode_attn, and a->err is required.  Larger requests return
+ * WNW_ERR_CAPACITY.  Calls share the array: calls that overlap on the GPU race.
+ * The first call on a device looks up the array's address (make it before any
+ * stream capture); each call clears the counters it uses. */
+#define WNW_NOALLOC_MAX_PARTIAL_FLOATS (1 << 20)
+#define WNW_NOALLOC_MAX_SEGS (1 << 16)
+wnw_status wnw_decode_attn_noalloc(const wnw_decode_attn_args* a, void* stream);
+
 /* Rows per CTA used by wnw_decode_attn for a dtype / head_dim (16-bit K/V
  * with head_dim 64 or 128 take the tensor-core kernel: 128 rows per CTA). */
 int wnw_split_rows(int dtype, int head_dim);
