@@ -379,13 +379,15 @@ def peaks():
         return 6650.0, "fallback"
 
 
-def traffic_per_launch():
-    """DRAM bytes per decode-attention launch from the committed ncu capture
-    summary (profiles/), or None."""
+def traffic_per_launch(algorithmic_bytes):
+    """DRAM bytes per decode-attention launch: the committed ncu capture's
+    DRAM/algorithmic ratio (profiles/decode_attn_traffic.json, a config-2
+    layer geometry case) scaled to this launch's algorithmic bytes; None when
+    no capture is committed."""
     try:
         with open(os.path.join(ROOT, "profiles", "decode_attn_traffic.json")) as f:
-            return json.load(f).get("dram_bytes_per_launch")
-    except (OSError, ValueError):
+            return float(json.load(f)["ratio"]) * algorithmic_bytes
+    except (OSError, ValueError, KeyError):
         return None
 
 
@@ -451,7 +453,7 @@ def main():
                 "d2h_bytes_per_step": e2e["out_bytes"]},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": (achieved / peak) if achieved else None, "peak_source": peak_kind,
-                     "traffic": traffic_per_launch(), "kernel": "wnw::decode_attn_kernel<bf16,128,4>",
+                     "traffic": traffic_per_launch(val["attn_bytes"]), "kernel": "wnw::decode_attn_kernel<bf16,128,4>",
                      "bytes_per_launch": val["attn_bytes"], "us_per_launch": val["attn_us"],
                      "launches_timed": val["attn_n"],
                      "how": "all 30 layers' launches back to back on the timed run's final state, CUDA events"},

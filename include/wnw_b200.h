@@ -167,15 +167,18 @@ wnw_status wnw_chunk_topk(const float* acc, const int32_t* score_off, int batch,
 /* Compaction + splice of the changed segments of one layer (replaces
  * rebuild_append_kv, src/algorithms/wnw/code/kernels.py:375-473, and
  * WnWCache._apply_chunk_update_to_layer, cache.py:891-1010).  `plan_blob` is
- * the blob written by wnw_planner_device_plan and `layer` selects its record;
- * one CTA per changed segment (max_changed >= the record's count); rows are moved inside each
- * segment's slot (evicted ranges removed, later rows shifted down), then
- * `landing` rows are spliced after the kept rows and seg_len is set. */
+ * the blob written by wnw_planner_device_plan and `layer` selects its record.
+ * Two grid-stride launches: the kept rows that move are gathered into
+ * k_move/v_move (>= the record's moved_total rows) while every plan record is
+ * validated against seg_len / seg_cap (status[n_chg] scratch); then moved and
+ * fetched (`landing`) rows are written to their final slot rows and seg_len
+ * is set.  A record that fails validation moves nothing and sets
+ * WNW_DEVERR_LEN_MISMATCH (or _CAPACITY) in *err. */
 wnw_status wnw_rebuild_segments(int dtype, int head_dim, void* k_store, void* v_store,
                                 const int64_t* seg_base, int32_t* seg_len, const int32_t* seg_cap,
                                 const void* k_landing, const void* v_landing,
-                                const int32_t* plan_blob, int layer, int max_changed,
-                                int32_t* err, void* stream);
+                                const int32_t* plan_blob, int layer, void* k_move, void* v_move,
+                                int64_t move_rows, int32_t* status, int32_t* err, void* stream);
 
 /* Copy rows [0, len[s]) of every segment from src (+src_base[s]) to dst
  * (+dst_base[s]); src and dst must not overlap.  Used to pack a slot layout
@@ -234,8 +237,11 @@ wnw_status wnw_planner_get_layer_transfer(const wnw_planner* p, int32_t* layer_r
 wnw_status wnw_planner_get_changes(const wnw_planner* p, int b, int32_t* to_load, int cap_load,
                                    int* n_load, int32_t* to_evict, int cap_evict, int* n_evict);
 /* Device-plan blob for wnw_rebuild_segments: int32 [L+1] layer offsets, then
- * per layer {n_chg, seg[n], old_len[n], new_len[n], load_src[n], load_len[n],
- * ev_off[n+1], ev_s[m], ev_e[m]} with lengths EXCLUDING the step's new token. */
+ * per layer {n_chg, moved_total, out_total, seg[n], old_len[n], new_len[n],
+ * load_src[n], load_len[n], mov_off[n+1], out_off[n+1], ev_off[n+1],
+ * ev_s[m], ev_e[m]} with lengths EXCLUDING the step's new token; moved rows
+ * of a segment = its kept rows after the first evicted range, output rows =
+ * moved + loaded. */
 wnw_status wnw_planner_device_plan(const wnw_planner* p, int32_t* blob, int64_t cap, int64_t* used);
 
 /* Gather the planned CPU ranges (cpu_ranges order) of row_bytes-wide rows from

@@ -220,28 +220,26 @@ def test_rebuild_matches_oracle(dev):
     land_k = torch.randn(land_rows, D, generator=g).to(dtype).to(dev)
     land_v = torch.randn(land_rows, D, generator=g).to(dtype).to(dev)
     n = len(recs)
-    seg, old, new, lsrc, llen, eoff, es, ee = [], [], [], [], [], [0], [], []
+    new, lsrc = [], []
     cur = 0
-    for s, ev, nl in recs:
-        seg.append(s)
-        old.append(lens[s])
-        new.append(lens[s] - sum(b - a for a, b in ev) + nl)
+    plan_recs = []
+    for s_, ev, nl in recs:
+        new.append(lens[s_] - sum(b - a for a, b in ev) + nl)
         lsrc.append(cur)
-        llen.append(nl)
+        plan_recs.append((s_, lens[s_], new[-1], cur, nl, ev))
         cur += nl
-        for a, b in ev:
-            es.append(a)
-            ee.append(b)
-        eoff.append(len(es))
-    blob = np.array([2] + [0] + [n] + seg + old + new + lsrc + llen + eoff + es + ee, np.int32)
-    blob[1] = len(blob)  # layer 1 record: empty, at the end
-    blob = np.concatenate([blob, [0]]).astype(np.int32)
+    blob = Kx.pack_plan([plan_recs, []])  # layer 1: no changes
     blob_d = torch.from_numpy(blob).to(dev)
+    move_k = torch.empty(4096, D, dtype=dtype, device=dev)
+    move_v = torch.empty_like(move_k)
+    status = torch.zeros(8, dtype=torch.int32, device=dev)
     seg_len = torch.tensor(lens, dtype=torch.int32, device=dev)
     err = torch.zeros(1, dtype=torch.int32, device=dev)
-    Kx.rebuild_layer(ks, vs, torch.from_numpy(base).to(dev), seg_len, torch.from_numpy(cap.astype(np.int32)).to(dev),
-                     land_k, land_v, blob_d, 0, n, err)
-    Kx.rebuild_layer(ks, vs, torch.from_numpy(base).to(dev), seg_len, None, land_k, land_v, blob_d, 1, n, err)
+    cap_d = torch.from_numpy(cap.astype(np.int32)).to(dev)
+    Kx.rebuild_layer(ks, vs, torch.from_numpy(base).to(dev), seg_len, cap_d, land_k, land_v, blob_d, 0,
+                     move_k, move_v, status, err)
+    Kx.rebuild_layer(ks, vs, torch.from_numpy(base).to(dev), seg_len, cap_d, land_k, land_v, blob_d, 1,
+                     move_k, move_v, status, err)
     torch.cuda.synchronize()
     assert int(err.item()) == 0
     new_lens = list(lens)
@@ -263,9 +261,12 @@ def test_rebuild_matches_oracle(dev):
     for s in (1, 4):  # untouched segments
         assert torch.equal(ks[base[s]:base[s] + cap[s]], before_k[base[s]:base[s] + cap[s]])
     # a stale plan (length mismatch) is refused on the device, not applied
-    Kx.rebuild_layer(ks, vs, torch.from_numpy(base).to(dev), seg_len, None, land_k, land_v, blob_d, 0, n, err)
+    snap = ks.clone()
+    Kx.rebuild_layer(ks, vs, torch.from_numpy(base).to(dev), seg_len, cap_d, land_k, land_v, blob_d, 0,
+                     move_k, move_v, status, err)
     torch.cuda.synchronize()
     assert int(err.item()) & N.DEVERR_LEN_MISMATCH
+    assert torch.equal(ks, snap)
 
 
 def test_copy_segments_and_interleave_append_exact(dev):

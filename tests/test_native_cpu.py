@@ -72,28 +72,25 @@ def test_native_planner_matches_reference_planner(golden_dir, i):
 
 def _check_device_plan(P, bufs, evs, eve, L, S):
     """The rebuild blob restates the reference outputs per changed segment."""
+    from wnw_b200.kernels import plan_record
     blob = P.device_plan()
     ls, ll, _, nl, eo, _, elp = bufs
     for l in range(L):
-        o = int(blob[l])
-        n = int(blob[o])
-        segs = blob[o + 1:o + 1 + n]
-        new_len = blob[o + 1 + 2 * n:o + 1 + 3 * n]
-        lsrc = blob[o + 1 + 3 * n:o + 1 + 4 * n]
-        llen = blob[o + 1 + 4 * n:o + 1 + 5 * n]
-        ev_off = blob[o + 1 + 5 * n:o + 2 + 6 * n]
-        ne = int(ev_off[-1])
-        es = blob[o + 2 + 6 * n:o + 2 + 6 * n + ne]
-        ee = blob[o + 2 + 6 * n + ne:o + 2 + 6 * n + 2 * ne]
-        for i, fi in enumerate(segs):
-            assert new_len[i] == nl[l, fi] - 1
-            assert llen[i] == ll[l, fi]
-            if llen[i]:
-                assert lsrc[i] == ls[l, fi]
-            r0 = elp[l] + eo[l, fi]
-            r1 = elp[l] + eo[l, fi + 1]
-            assert list(es[ev_off[i]:ev_off[i + 1]]) == list(evs[r0:r1])
-            assert list(ee[ev_off[i]:ev_off[i + 1]]) == list(eve[r0:r1])
+        r = plan_record(blob, l)
+        for i, fi in enumerate(r["seg"]):
+            assert r["new_len"][i] == nl[l, fi] - 1
+            assert r["load_len"][i] == ll[l, fi]
+            if r["load_len"][i]:
+                assert r["load_src"][i] == ls[l, fi]
+            r0, r1 = elp[l] + eo[l, fi], elp[l] + eo[l, fi + 1]
+            e0, e1 = r["ev_off"][i], r["ev_off"][i + 1]
+            assert list(r["ev_s"][e0:e1]) == list(evs[r0:r1])
+            assert list(r["ev_e"][e0:e1]) == list(eve[r0:r1])
+            kept = r["new_len"][i] - r["load_len"][i]
+            moved = kept - r["ev_s"][e0] if e1 > e0 else 0
+            assert r["mov_off"][i + 1] - r["mov_off"][i] == moved
+            assert r["out_off"][i + 1] - r["out_off"][i] == moved + r["load_len"][i]
+        assert r["moved_total"] == r["mov_off"][-1] and r["out_total"] == r["out_off"][-1]
 
 
 def test_gather_rows_matches_oracle():

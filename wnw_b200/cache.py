@@ -452,6 +452,8 @@ class B200WnWCache(FlatVarlenCache):
         self._events = [torch.cuda.Event() for _ in range(L)]
         self._restore_ptrs = None
         self._fetched_rows = 0
+        self._move_k = self._move_v = None
+        self._rb_status = torch.zeros(max(1, S), dtype=torch.int32, device=self.device)
         self._layer_chg = [0] * L
         self._layer_rows = np.zeros(L + 1, np.int64)
         self._new_kv = [None] * L
@@ -470,7 +472,7 @@ class B200WnWCache(FlatVarlenCache):
             torch.cuda.current_stream(self.device).wait_event(self._events[l])
             Kx.rebuild_layer(self.k_store[l], self.v_store[l], self._seg_base[l], self._seg_len[l],
                              self._seg_cap[l], self._land_k, self._land_v, self._plan_dev, l,
-                             self._layer_chg[l], self._scratch.err)
+                             self._move_k, self._move_v, self._rb_status, self._scratch.err)
             for seg, new_len in recs:
                 self._len_host[l, seg] = new_len
         if (self._len_host[l] + 1 > self._cap_host[l]).any():
@@ -486,10 +488,8 @@ class B200WnWCache(FlatVarlenCache):
         return self.k_store[l], self.v_store[l], self._seg_len[l], int(self._len_host[l].max()) + 1
 
     def _plan_records(self, l):
-        blob = self._plan_np
-        o = int(blob[l])
-        n = int(blob[o])
-        return zip(blob[o + 1:o + 1 + n].tolist(), blob[o + 1 + 2 * n:o + 1 + 3 * n].tolist())
+        r = Kx.plan_record(self._plan_np, l)
+        return zip(r["seg"].tolist(), r["new_len"].tolist())
 
     def _score_args(self, l):
         if not self._score_groups[l]:
@@ -585,8 +585,11 @@ class B200WnWCache(FlatVarlenCache):
             self._plan_dev = torch.zeros(n, dtype=torch.int32, device=self.device)
         self._plan_host[:plan.size].copy_(torch.from_numpy(plan))
         self._plan_np = plan.copy()
+        moved = 0
         for l in range(L):
             self._layer_chg[l] = int(plan[int(plan[l])])
+            moved = max(moved, int(plan[int(plan[l]) + 1]))
+        self._ensure_move_capacity(moved)
         rows, rng = self._planner.layer_transfer()
         self._layer_rows = rows.astype(np.int64)
         row_bytes = D * self.cpu_restore_k.element_size()
@@ -627,6 +630,12 @@ class B200WnWCache(FlatVarlenCache):
                     self._events[l].record(cs)
         self._fetched_rows = int(total)
         self._pending = True
+
+    def _ensure_move_capacity(self, rows):
+        if self._move_k is None or self._move_k.shape[0] < max(1, rows):
+            n = 1 << max(0, rows - 1).bit_length()
+            self._move_k = torch.empty(n, self.head_dim, dtype=self.dtype, device=self.device)
+            self._move_v = torch.empty(n, self.head_dim, dtype=self.dtype, device=self.device)
 
     def _restore_dev_ptrs(self):
         if getattr(self, "_restore_ptrs", None) is None:

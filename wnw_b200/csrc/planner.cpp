@@ -467,7 +467,7 @@ wnw_status wnw_planner_device_plan(const wnw_planner* p, int32_t* blob, int64_t 
     const int64_t n = static_cast<int64_t>(p->chg[l].size());
     int64_t ne = 0;
     for (auto& c : p->chg[l]) ne += c.ev_hi - c.ev_lo;
-    need += 1 + 5 * n + (n + 1) + 2 * ne;
+    need += 3 + 5 * n + 3 * (n + 1) + 2 * ne;
   }
   *used = need;
   if (!blob) return WNW_OK;
@@ -480,17 +480,32 @@ wnw_status wnw_planner_device_plan(const wnw_planner* p, int32_t* blob, int64_t 
     blob[l] = static_cast<int32_t>(o);
     const auto& cl = p->chg[l];
     const int n = static_cast<int>(cl.size());
-    blob[o++] = n;
-    for (int i = 0; i < n; ++i) blob[o + i] = cl[i].seg;
-    for (int i = 0; i < n; ++i) blob[o + n + i] = cl[i].old_len;
-    for (int i = 0; i < n; ++i) blob[o + 2 * n + i] = cl[i].new_len;
-    for (int i = 0; i < n; ++i) blob[o + 3 * n + i] = cl[i].load_src;
-    for (int i = 0; i < n; ++i) blob[o + 4 * n + i] = cl[i].load_len;
-    int32_t* eo = blob + o + 5 * n;
-    eo[0] = 0;
-    for (int i = 0; i < n; ++i) eo[i + 1] = eo[i] + (cl[i].ev_hi - cl[i].ev_lo);
-    const int ne = eo[n];
-    int32_t* es = eo + n + 1;
+    int32_t* h = blob + o;  // n, moved rows, output rows
+    int32_t* seg = h + 3;
+    int32_t* old_len = seg + n;
+    int32_t* new_len = old_len + n;
+    int32_t* lsrc = new_len + n;
+    int32_t* llen = lsrc + n;
+    int32_t* mov_off = llen + n;
+    int32_t* out_off = mov_off + n + 1;
+    int32_t* ev_off = out_off + n + 1;
+    int32_t* es = ev_off + n + 1;
+    mov_off[0] = out_off[0] = ev_off[0] = 0;
+    for (int i = 0; i < n; ++i) {
+      const auto& c = cl[i];
+      seg[i] = c.seg;
+      old_len[i] = c.old_len;
+      new_len[i] = c.new_len;
+      lsrc[i] = c.load_src;
+      llen[i] = c.load_len;
+      const int n_ev = c.ev_hi - c.ev_lo;
+      // rows that move: the kept rows after the first evicted range
+      const int moved = n_ev > 0 ? (c.new_len - c.load_len) - p->ev_starts[c.ev_lo] : 0;
+      mov_off[i + 1] = mov_off[i] + moved;
+      out_off[i + 1] = out_off[i] + moved + c.load_len;
+      ev_off[i + 1] = ev_off[i] + n_ev;
+    }
+    const int ne = ev_off[n];
     int32_t* ee = es + ne;
     int k = 0;
     for (int i = 0; i < n; ++i)
@@ -498,7 +513,10 @@ wnw_status wnw_planner_device_plan(const wnw_planner* p, int32_t* blob, int64_t 
         es[k] = p->ev_starts[e];
         ee[k] = p->ev_ends[e];
       }
-    o += 5 * n + (n + 1) + 2 * ne;
+    h[0] = n;
+    h[1] = mov_off[n];
+    h[2] = out_off[n];
+    o += 3 + 5 * n + 3 * (n + 1) + 2 * ne;
   }
   blob[L] = static_cast<int32_t>(o);
   return WNW_OK;

@@ -4,8 +4,11 @@
 // of its layer's K / V store.  A chunk update of the reference rewrites the
 // whole flat buffer (rebuild_append_kv, src/algorithms/wnw/code/kernels.py:
 // 375-473); here only the changed segments move rows inside their own slot:
-// evicted ranges are squeezed out (later rows shift down) and the rows fetched
-// from host memory are spliced after the kept rows.  The step's new token is
+// evicted ranges are squeezed out (later kept rows shift down) and the rows
+// fetched from host memory are spliced after the kept rows.  Moving rows down
+// inside one buffer in parallel would let a write clobber a source another
+// thread has not read yet, so the moving rows go through a scratch buffer in
+// two grid-wide launches (gather, then scatter).  The step's new token is
 // appended afterwards by the decode-attention kernel.
 #include <algorithm>
 
@@ -13,198 +16,133 @@
 
 namespace wnw {
 
-constexpr int kRbThreads = 128;
-constexpr int kRbStages = 8;
-constexpr int kRbStageBytes = 8 * 1024;  // per tensor per stage
+constexpr int kRbThreads = 256;
+constexpr int kRbMaxBlocks = 148 * 4;
 
-// One tile of a row move: `n` rows from src (slot-relative row or landing
-// row) to dst (slot-relative row).
-struct RbTile {
-  int src;
-  int dst;
-  int n;
-  int landing;
-};
-
-// Walks the moves of one segment in ascending source order: the kept runs
-// after the first evicted range (each shifted down by the rows evicted before
-// it), then the spliced landing rows.
-struct RbWalker {
-  const int32_t* ev_s;
-  const int32_t* ev_e;
-  int n_ev;
-  int old_len;
-  int kept_len;
-  int load_src;
-  int load_len;
-  int tile_rows;
-  // state
-  int k;      // current run (0..n_ev-1), n_ev = splice phase, n_ev+1 = done
-  int off;    // rows of the current piece already emitted
-  int shift;  // rows evicted up to and including run k's range
-
-  __device__ void init() {
-    k = 0;
-    off = 0;
-    shift = n_ev > 0 ? (ev_e[0] - ev_s[0]) : 0;
-    if (n_ev == 0) k = 0;  // no runs: go straight to the splice phase
+// One layer record of the device plan (see wnw_planner_device_plan).
+struct RbRec {
+  int n, moved_total, out_total;
+  const int32_t *seg, *old_len, *new_len, *lsrc, *llen, *mov_off, *out_off, *ev_off, *ev_s, *ev_e;
+  __device__ explicit RbRec(const int32_t* blob, int layer) {
+    const int32_t* h = blob + blob[layer];
+    n = h[0];
+    moved_total = h[1];
+    out_total = h[2];
+    seg = h + 3;
+    old_len = seg + n;
+    new_len = old_len + n;
+    lsrc = new_len + n;
+    llen = lsrc + n;
+    mov_off = llen + n;
+    out_off = mov_off + n + 1;
+    ev_off = out_off + n + 1;
+    ev_s = ev_off + n + 1;
+    ev_e = ev_s + ev_off[n];
   }
-  __device__ bool next(RbTile& t) {
-    while (k < n_ev) {
-      const int run_lo = ev_e[k];
-      const int run_hi = (k + 1 < n_ev) ? ev_s[k + 1] : old_len;
-      const int left = run_hi - run_lo - off;
-      if (left > 0) {
-        const int n = min(left, tile_rows);
-        t.src = run_lo + off;
-        t.dst = run_lo + off - shift;
-        t.n = n;
-        t.landing = 0;
-        off += n;
-        return true;
-      }
-      ++k;
-      off = 0;
-      if (k < n_ev) shift += ev_e[k] - ev_s[k];
+  // record index i with off[i] <= x < off[i+1] (off non-decreasing, off[0] = 0)
+  __device__ int find(const int32_t* off, int x) const {
+    int lo = 0, hi = n;
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if (off[mid] <= x) lo = mid; else hi = mid;
     }
-    if (k == n_ev) {
-      const int left = load_len - off;
-      if (left > 0) {
-        const int n = min(left, tile_rows);
-        t.src = load_src + off;
-        t.dst = kept_len + off;
-        t.n = n;
-        t.landing = 1;
-        off += n;
-        return true;
-      }
-      k = n_ev + 1;
-    }
-    return false;
+    return lo;
   }
 };
 
-template <int ROW_BYTES>
-__global__ void __launch_bounds__(kRbThreads)
-    rebuild_kernel(uint8_t* k_store, uint8_t* v_store, const int64_t* seg_base, int32_t* seg_len,
-                   const int32_t* seg_cap, const uint8_t* k_land, const uint8_t* v_land,
-                   const int32_t* blob, int layer, int32_t* err) {
-  constexpr int TR = kRbStageBytes / ROW_BYTES;  // rows per tile
-  extern __shared__ __align__(128) uint8_t smem[];
-  __shared__ __align__(8) uint64_t bars[kRbStages];
-  __shared__ RbTile tiles[kRbStages];
-
-  const int32_t* rec = blob + blob[layer];
-  const int n = rec[0];
-  const int i = blockIdx.x;
-  if (i >= n) return;
-  const int seg = rec[1 + i];
-  const int old_len = rec[1 + n + i];
-  const int new_len = rec[1 + 2 * n + i];
-  const int load_src = rec[1 + 3 * n + i];
-  const int load_len = rec[1 + 4 * n + i];
-  const int32_t* ev_off = rec + 1 + 5 * n;
-  const int n_ev_total = ev_off[n];
-  const int32_t* ev_s = ev_off + n + 1 + ev_off[i];
-  const int32_t* ev_e = ev_off + n + 1 + n_ev_total + ev_off[i];
-  const int n_ev = ev_off[i + 1] - ev_off[i];
-
-  if (threadIdx.x != 0) return;  // a single thread drives the bulk-copy pipeline
-  if (seg_len[seg] != old_len) {
-    atomicOr(err, WNW_DEVERR_LEN_MISMATCH);
-    return;
+// Kept-row index k (0-based among the kept rows after the first evicted
+// range) -> slot-relative source row.
+__device__ inline int kept_source_row(const RbRec& r, int i, int k) {
+  const int e0 = r.ev_off[i], e1 = r.ev_off[i + 1];
+  int run_lo = r.ev_e[e0];
+  for (int e = e0; e < e1; ++e) {
+    const int run_hi = (e + 1 < e1) ? r.ev_s[e + 1] : r.old_len[i];
+    const int n = run_hi - run_lo;
+    if (k < n) return run_lo + k;
+    k -= n;
+    if (e + 1 < e1) run_lo = r.ev_e[e + 1];
   }
-  // ranges must be sorted, disjoint and inside the segment: a malformed plan
-  // is refused rather than allowed to move rows outside the slot
-  int evicted = 0, prev_end = 0;
-  for (int e = 0; e < n_ev; ++e) {
-    if (ev_s[e] < prev_end || ev_e[e] < ev_s[e] || ev_e[e] > old_len) {
-      atomicOr(err, WNW_DEVERR_LEN_MISMATCH);
-      return;
-    }
-    prev_end = ev_e[e];
-    evicted += ev_e[e] - ev_s[e];
-  }
-  if (load_len < 0 || load_src < 0) {
-    atomicOr(err, WNW_DEVERR_LEN_MISMATCH);
-    return;
-  }
-  const int kept_len = old_len - evicted;
-  if (kept_len + load_len != new_len) {
-    atomicOr(err, WNW_DEVERR_LEN_MISMATCH);
-    return;
-  }
-  if (seg_cap != nullptr && new_len + 1 > seg_cap[seg]) {
-    atomicOr(err, WNW_DEVERR_CAPACITY);
-    return;
-  }
-  for (int s = 0; s < kRbStages; ++s) mbar_init(&bars[s], 1);
-  fence_mbar_init();
-  fence_proxy_async();
-
-  uint8_t* kbase = k_store + seg_base[seg] * ROW_BYTES;
-  uint8_t* vbase = v_store + seg_base[seg] * ROW_BYTES;
-  RbWalker walk{ev_s, ev_e, n_ev, old_len, kept_len, load_src, load_len, TR, 0, 0, 0};
-  walk.init();
-
-  // Loads run up to kRbStages tiles ahead of the stores.  Sources of later
-  // tiles lie at or above the end of every earlier tile's source, and a tile's
-  // destination never extends past its own source's end, so no store can
-  // clobber a source that is still to be read; stores are issued in tile
-  // order after the tile's own load (and hence all earlier loads) completed.
-  int issued = 0, done = 0;
-  bool more = true;
-  for (;;) {
-    while (more && issued - done < kRbStages) {
-      RbTile t;
-      if (!walk.next(t)) {
-        more = false;
-        break;
-      }
-      const int s = issued % kRbStages;
-      if (issued >= kRbStages) bulk_wait_read<0>();  // the stage's previous store has read smem
-      tiles[s] = t;
-      const uint32_t bytes = uint32_t(t.n) * ROW_BYTES;
-      uint8_t* ks = smem + s * 2 * kRbStageBytes;
-      uint8_t* vs = ks + kRbStageBytes;
-      mbar_arrive_expect_tx(&bars[s], 2 * bytes);
-      const uint8_t* ksrc = t.landing ? (k_land + int64_t(t.src) * ROW_BYTES) : (kbase + int64_t(t.src) * ROW_BYTES);
-      const uint8_t* vsrc = t.landing ? (v_land + int64_t(t.src) * ROW_BYTES) : (vbase + int64_t(t.src) * ROW_BYTES);
-      bulk_g2s(ks, ksrc, bytes, &bars[s]);
-      bulk_g2s(vs, vsrc, bytes, &bars[s]);
-      ++issued;
-    }
-    if (done == issued) break;
-    const int s = done % kRbStages;
-    if (!mbar_wait(&bars[s], (done / kRbStages) & 1, err)) break;
-    const RbTile t = tiles[s];
-    uint8_t* ks = smem + s * 2 * kRbStageBytes;
-    uint8_t* vs = ks + kRbStageBytes;
-    bulk_s2g(kbase + int64_t(t.dst) * ROW_BYTES, ks, uint32_t(t.n) * ROW_BYTES);
-    bulk_s2g(vbase + int64_t(t.dst) * ROW_BYTES, vs, uint32_t(t.n) * ROW_BYTES);
-    bulk_commit();
-    ++done;
-  }
-  bulk_wait_all();
-  seg_len[seg] = new_len;
+  return -1;
 }
 
-template <int ROW_BYTES>
-wnw_status launch_rebuild(void* k_store, void* v_store, const int64_t* seg_base, int32_t* seg_len,
-                          const int32_t* seg_cap, const void* kl, const void* vl, const int32_t* plan,
-                          int layer, int max_changed, int32_t* err, cudaStream_t s) {
-  auto kern = rebuild_kernel<ROW_BYTES>;
-  constexpr int smem = kRbStages * 2 * kRbStageBytes;
-  static bool configured = false;
-  if (!configured) {
-    WNW_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    configured = true;
+// Phase 1: validate every record, gather the moving kept rows into scratch.
+__global__ void __launch_bounds__(kRbThreads)
+    rebuild_gather_kernel(const uint4* k_store, const uint4* v_store, const int64_t* seg_base, const int32_t* seg_len,
+                          const int32_t* seg_cap, const int32_t* blob, int layer, uint4* k_move, uint4* v_move,
+                          int64_t move_rows, int32_t* status, int32_t* err, int cpr) {
+  const RbRec r(blob, layer);
+  const int64_t gtid = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t nthreads = int64_t(gridDim.x) * blockDim.x;
+  for (int i = static_cast<int>(gtid); i < r.n; i += static_cast<int>(nthreads)) {
+    const int seg = r.seg[i];
+    const int e0 = r.ev_off[i], e1 = r.ev_off[i + 1];
+    int ok = seg_len[seg] == r.old_len[i] ? 1 : 0;
+    int prev = 0, evicted = 0;
+    for (int e = e0; e < e1 && ok; ++e) {
+      if (r.ev_s[e] < prev || r.ev_e[e] < r.ev_s[e] || r.ev_e[e] > r.old_len[i]) ok = 0;
+      prev = r.ev_e[e];
+      evicted += r.ev_e[e] - r.ev_s[e];
+    }
+    const int moved = r.mov_off[i + 1] - r.mov_off[i];
+    if (ok && (r.old_len[i] - evicted + r.llen[i] != r.new_len[i] || r.llen[i] < 0 || r.lsrc[i] < 0 ||
+               moved != (e1 > e0 ? r.old_len[i] - evicted - r.ev_s[e0] : 0)))
+      ok = 0;
+    if (!ok) atomicOr(err, WNW_DEVERR_LEN_MISMATCH);
+    if (ok && r.new_len[i] + 1 > seg_cap[seg]) {
+      ok = 0;
+      atomicOr(err, WNW_DEVERR_CAPACITY);
+    }
+    status[i] = ok;
   }
-  kern<<<max_changed, kRbThreads, smem, s>>>(static_cast<uint8_t*>(k_store), static_cast<uint8_t*>(v_store),
-                                             seg_base, seg_len, seg_cap, static_cast<const uint8_t*>(kl),
-                                             static_cast<const uint8_t*>(vl), plan, layer, err);
-  WNW_CUDA_TRY(cudaGetLastError());
-  return WNW_OK;
+  if (r.moved_total > move_rows) {
+    if (gtid == 0) atomicOr(err, WNW_DEVERR_CAPACITY);
+    return;
+  }
+  const int64_t total = int64_t(r.moved_total) * cpr;
+  for (int64_t x = gtid; x < total; x += nthreads) {
+    const int row = static_cast<int>(x / cpr);
+    const int c = static_cast<int>(x % cpr);
+    const int i = r.find(r.mov_off, row);
+    const int src = kept_source_row(r, i, row - r.mov_off[i]);
+    const int seg = r.seg[i];
+    if (src < 0 || src >= seg_cap[seg]) continue;  // malformed record: refused by status[i]
+    const int64_t s = (seg_base[seg] + src) * cpr + c;
+    k_move[int64_t(row) * cpr + c] = k_store[s];
+    v_move[int64_t(row) * cpr + c] = v_store[s];
+  }
+}
+
+// Phase 2: write moved and fetched rows to their final slot rows; set seg_len.
+__global__ void __launch_bounds__(kRbThreads)
+    rebuild_scatter_kernel(uint4* k_store, uint4* v_store, const int64_t* seg_base, int32_t* seg_len,
+                           const int32_t* seg_cap, const uint4* k_land, const uint4* v_land, const int32_t* blob,
+                           int layer, const uint4* k_move, const uint4* v_move, const int32_t* status, int cpr) {
+  const RbRec r(blob, layer);
+  const int64_t gtid = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t nthreads = int64_t(gridDim.x) * blockDim.x;
+  const int64_t total = int64_t(r.out_total) * cpr;
+  for (int64_t x = gtid; x < total; x += nthreads) {
+    const int row = static_cast<int>(x / cpr);
+    const int c = static_cast<int>(x % cpr);
+    const int i = r.find(r.out_off, row);
+    if (!status[i]) continue;
+    const int seg = r.seg[i];
+    const int k = row - r.out_off[i];
+    const int moved = r.mov_off[i + 1] - r.mov_off[i];
+    const int64_t dst = (seg_base[seg] + (k < moved ? r.ev_s[r.ev_off[i]] + k
+                                                    : r.new_len[i] - r.llen[i] + (k - moved))) * cpr + c;
+    if (k < moved) {
+      const int64_t s = int64_t(r.mov_off[i] + k) * cpr + c;
+      k_store[dst] = k_move[s];
+      v_store[dst] = v_move[s];
+    } else {
+      const int64_t s = int64_t(r.lsrc[i] + (k - moved)) * cpr + c;
+      k_store[dst] = k_land[s];
+      v_store[dst] = v_land[s];
+    }
+  }
+  for (int i = static_cast<int>(gtid); i < r.n; i += static_cast<int>(nthreads))
+    if (status[i]) seg_len[r.seg[i]] = r.new_len[i];
 }
 
 // ------------------------------------------------------------ segment copy
@@ -247,23 +185,30 @@ inline int row_bytes_of(int dtype, int head_dim) { return head_dim * (dtype == W
 extern "C" wnw_status wnw_rebuild_segments(int dtype, int head_dim, void* k_store, void* v_store,
                                            const int64_t* seg_base, int32_t* seg_len, const int32_t* seg_cap,
                                            const void* k_landing, const void* v_landing, const int32_t* plan_blob,
-                                           int layer, int max_changed, int32_t* err, void* stream) {
+                                           int layer, void* k_move, void* v_move, int64_t move_rows,
+                                           int32_t* status, int32_t* err, void* stream) {
   using namespace wnw;
-  WNW_CHECK_ARG(k_store && v_store && seg_base && seg_len && plan_blob && err, "null pointer argument");
+  WNW_CHECK_ARG(k_store && v_store && seg_base && seg_len && seg_cap && plan_blob && status && err,
+                "null pointer argument");
   WNW_CHECK_ARG(layer >= 0, "negative layer");
   WNW_CHECK_ARG(aligned16(k_store) && aligned16(v_store), "stores must be 16-byte aligned");
   WNW_CHECK_ARG(k_landing == nullptr || (aligned16(k_landing) && aligned16(v_landing)),
                 "landing buffers must be 16-byte aligned");
-  if (max_changed <= 0) return WNW_OK;
+  WNW_CHECK_ARG(move_rows == 0 || (k_move && v_move && aligned16(k_move) && aligned16(v_move)),
+                "move buffers must be given and 16-byte aligned when move_rows > 0");
+  const int rb = row_bytes_of(dtype, head_dim);
+  WNW_CHECK_ARG(rb > 0 && rb % 16 == 0, "row size must be a positive multiple of 16 bytes");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  switch (row_bytes_of(dtype, head_dim)) {
-    case 32: return launch_rebuild<32>(k_store, v_store, seg_base, seg_len, seg_cap, k_landing, v_landing, plan_blob, layer, max_changed, err, s);
-    case 64: return launch_rebuild<64>(k_store, v_store, seg_base, seg_len, seg_cap, k_landing, v_landing, plan_blob, layer, max_changed, err, s);
-    case 128: return launch_rebuild<128>(k_store, v_store, seg_base, seg_len, seg_cap, k_landing, v_landing, plan_blob, layer, max_changed, err, s);
-    case 256: return launch_rebuild<256>(k_store, v_store, seg_base, seg_len, seg_cap, k_landing, v_landing, plan_blob, layer, max_changed, err, s);
-    case 512: return launch_rebuild<512>(k_store, v_store, seg_base, seg_len, seg_cap, k_landing, v_landing, plan_blob, layer, max_changed, err, s);
-    default: set_error("row size %d bytes not compiled", row_bytes_of(dtype, head_dim)); return WNW_ERR_UNSUPPORTED;
-  }
+  rebuild_gather_kernel<<<kRbMaxBlocks, kRbThreads, 0, s>>>(
+      static_cast<const uint4*>(k_store), static_cast<const uint4*>(v_store), seg_base, seg_len, seg_cap, plan_blob,
+      layer, static_cast<uint4*>(k_move), static_cast<uint4*>(v_move), move_rows, status, err, rb / 16);
+  WNW_CUDA_TRY(cudaGetLastError());
+  rebuild_scatter_kernel<<<kRbMaxBlocks, kRbThreads, 0, s>>>(
+      static_cast<uint4*>(k_store), static_cast<uint4*>(v_store), seg_base, seg_len, seg_cap,
+      static_cast<const uint4*>(k_landing), static_cast<const uint4*>(v_landing), plan_blob, layer,
+      static_cast<const uint4*>(k_move), static_cast<const uint4*>(v_move), status, rb / 16);
+  WNW_CUDA_TRY(cudaGetLastError());
+  return WNW_OK;
 }
 
 extern "C" wnw_status wnw_copy_segments(int dtype, int head_dim, const void* src_k, const void* src_v,

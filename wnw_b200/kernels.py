@@ -187,14 +187,60 @@ def chunk_topk(acc, score_off, max_audio, stride, segs_per_chunk, top_k, topk_ou
 
 
 def rebuild_layer(k_store, v_store, seg_base, seg_len, seg_cap, k_landing, v_landing, plan_blob, layer,
-                  max_changed, err, stream=None):
+                  k_move, v_move, status, err, stream=None):
+    """Compaction + splice of one layer's changed slots (two launches)."""
     N.call("wnw_rebuild_segments", N.dtype_code(k_store.dtype), k_store.shape[1], k_store.data_ptr(),
-           v_store.data_ptr(), seg_base.data_ptr(), seg_len.data_ptr(),
-           seg_cap.data_ptr() if seg_cap is not None else None,
+           v_store.data_ptr(), seg_base.data_ptr(), seg_len.data_ptr(), seg_cap.data_ptr(),
            k_landing.data_ptr() if k_landing is not None else None,
            v_landing.data_ptr() if v_landing is not None else None, plan_blob.data_ptr(), int(layer),
-           int(max_changed), err.data_ptr(), N.stream_ptr(stream))
-    _count()
+           k_move.data_ptr() if k_move is not None else None, v_move.data_ptr() if v_move is not None else None,
+           int(k_move.shape[0]) if k_move is not None else 0, status.data_ptr(), err.data_ptr(),
+           N.stream_ptr(stream))
+    _count(2)
+
+
+def plan_record(blob, layer):
+    """Host-side view of one layer record of a device-plan blob (numpy int32)."""
+    o = int(blob[layer])
+    n, moved, out = (int(x) for x in blob[o:o + 3])
+    f = o + 3
+    rec = {"n": n, "moved_total": moved, "out_total": out}
+    for name in ("seg", "old_len", "new_len", "load_src", "load_len"):
+        rec[name] = blob[f:f + n]
+        f += n
+    for name in ("mov_off", "out_off", "ev_off"):
+        rec[name] = blob[f:f + n + 1]
+        f += n + 1
+    ne = int(rec["ev_off"][-1]) if n else 0
+    rec["ev_s"] = blob[f:f + ne]
+    rec["ev_e"] = blob[f + ne:f + 2 * ne]
+    return rec
+
+
+def pack_plan(layers):
+    """Build a device-plan blob from per-layer lists of records
+    (seg, old_len, new_len, load_src, load_len, [(ev_s, ev_e), ...]); the same
+    format wnw_planner_device_plan writes (used by tests)."""
+    L = len(layers)
+    out = [0] * (L + 1)
+    for l, recs in enumerate(layers):
+        out[l] = len(out)
+        n = len(recs)
+        mov, outo, evo = [0], [0], [0]
+        es, ee = [], []
+        for seg, old, new, ls, ll, ev in recs:
+            moved = (new - ll) - ev[0][0] if ev else 0
+            mov.append(mov[-1] + moved)
+            outo.append(outo[-1] + moved + ll)
+            evo.append(evo[-1] + len(ev))
+            es += [a for a, _ in ev]
+            ee += [b for _, b in ev]
+        out += [n, mov[-1], outo[-1]]
+        for k in range(5):
+            out += [r[k] for r in recs]
+        out += mov + outo + evo + es + ee
+    out[L] = len(out)
+    return np.asarray(out, np.int32)
 
 
 def copy_segments(src_k, src_v, src_base, dst_k, dst_v, dst_base, lens, stream=None):
