@@ -264,6 +264,15 @@ wnw_status wnw_fetch_rows(const void* src_k, const void* src_v, int64_t row_byte
                           const int32_t* ranges, const int64_t* dst_row, int n_ranges,
                           void* dst_k, void* dst_v, int max_ctas, void* stream);
 
+/* All layers of a step's fetch: for layer l, wnw_fetch_rows over ranges
+ * [layer_ranges[l], layer_ranges[l+1]) (host array, [num_layers+1]) followed
+ * by cudaEventRecord(events[l]) on `stream` (events may be NULL), so the
+ * consumer of layer l waits for its rows only. */
+wnw_status wnw_fetch_layers(const void* src_k, const void* src_v, int64_t row_bytes,
+                            const int32_t* ranges, const int64_t* dst_row, const int32_t* layer_ranges,
+                            int num_layers, void* dst_k, void* dst_v, int max_ctas, void* stream,
+                            void* const* events);
+
 /* Async H2D copy of n bytes for K and V on `stream`, then record `event`
  * (cudaEvent_t as void*, may be NULL) -- one per layer. */
 wnw_status wnw_h2d_async(void* dst_k, void* dst_v, const void* src_k, const void* src_v,

@@ -91,7 +91,7 @@ class B200WnWCache(FlatVarlenCache):
     """
 
     def __init__(self, config, num_layers, num_kv_heads, num_q_heads, head_dim, device, adapter=None, *,
-                 max_decode_tokens=256, fetch_mode="zerocopy", fetch_threads=8):
+                 max_decode_tokens=256, fetch_mode="zerocopy", fetch_threads=8, fetch_ctas=512):
         super().__init__(num_layers, num_kv_heads, num_q_heads, head_dim, device, adapter)
         if self.device.type != "cuda":
             raise RuntimeError("B200WnWCache needs a CUDA device; the CPU oracle lives in the test suite")
@@ -105,6 +105,7 @@ class B200WnWCache(FlatVarlenCache):
             raise ValueError(f"fetch_mode must be 'zerocopy' or 'dma', not {fetch_mode!r}")
         self.fetch_mode = fetch_mode
         self.fetch_threads = int(fetch_threads)
+        self.fetch_ctas = int(fetch_ctas)
         self._class_b_heads_by_layer = [config.get_layer_class_b(l) for l in range(num_layers)]
         self.batch_size = 0
         self.prefilled = False
@@ -450,6 +451,12 @@ class B200WnWCache(FlatVarlenCache):
         self._land_k = self._land_v = None
         self._stage_k = self._stage_v = None
         self._events = [torch.cuda.Event() for _ in range(L)]
+        if self._copy_stream is None:
+            self._copy_stream = torch.cuda.Stream(device=self.device)
+        for e in self._events:  # create the CUDA events now so their handles can be passed down
+            e.record(self._copy_stream)
+        import ctypes as _C
+        self._event_handles = (_C.c_void_p * L)(*[e.cuda_event for e in self._events])
         self._restore_ptrs = None
         self._fetched_rows = 0
         self._move_k = self._move_v = None
@@ -607,12 +614,11 @@ class B200WnWCache(FlatVarlenCache):
                     self._rng_dev[:nr].copy_(self._rng_host[:nr], non_blocking=True)
                     self._dst_dev[:nr].copy_(self._dst_host[:nr], non_blocking=True)
                     src_k, src_v = self._restore_dev_ptrs()
-                    for l in range(L):
-                        r0, r1 = int(rng[l]), int(rng[l + 1])
-                        if r1 > r0:
-                            Kx.fetch_rows(src_k, src_v, row_bytes, self._rng_dev[r0:r1], self._dst_dev[r0:r1],
-                                          self._land_k, self._land_v, stream=cs)
-                        self._events[l].record(cs)
+                    lr = np.ascontiguousarray(rng, np.int32)
+                    N.call("wnw_fetch_layers", src_k, src_v, int(row_bytes), self._rng_dev.data_ptr(),
+                           self._dst_dev.data_ptr(), N.ptr(lr), L, self._land_k.data_ptr(), self._land_v.data_ptr(),
+                           self.fetch_ctas, cs.cuda_stream, self._event_handles)
+                    Kx.LAUNCHES[0] += int(np.count_nonzero(np.diff(lr)))
                 else:
                     gather_rows(self.cpu_restore_k, self.cpu_restore_v, ranges, self._stage_k, self._stage_v,
                                 self.fetch_threads)

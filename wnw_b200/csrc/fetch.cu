@@ -78,3 +78,23 @@ extern "C" wnw_status wnw_fetch_rows(const void* src_k, const void* src_v, int64
   WNW_CUDA_TRY(cudaGetLastError());
   return WNW_OK;
 }
+
+extern "C" wnw_status wnw_fetch_layers(const void* src_k, const void* src_v, int64_t row_bytes,
+                                       const int32_t* ranges, const int64_t* dst_row, const int32_t* layer_ranges,
+                                       int num_layers, void* dst_k, void* dst_v, int max_ctas, void* stream,
+                                       void* const* events) {
+  using namespace wnw;
+  WNW_CHECK_ARG(layer_ranges && num_layers >= 0, "null layer offsets");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  for (int l = 0; l < num_layers; ++l) {
+    const int r0 = layer_ranges[l], r1 = layer_ranges[l + 1];
+    WNW_CHECK_ARG(r1 >= r0 && r0 >= 0, "layer range offsets must be non-decreasing");
+    if (r1 > r0) {
+      const wnw_status st = wnw_fetch_rows(src_k, src_v, row_bytes, ranges + 2 * int64_t(r0), dst_row + r0,
+                                           r1 - r0, dst_k, dst_v, max_ctas, stream);
+      if (st != WNW_OK) return st;
+    }
+    if (events && events[l]) WNW_CUDA_TRY(cudaEventRecord(static_cast<cudaEvent_t>(events[l]), s));
+  }
+  return WNW_OK;
+}

@@ -2,11 +2,11 @@
 //
 // The decode-attention kernel leaves, per class-A (layer, segment), the base-2
 // logits of the audio rows and the merged softmax statistics.  Here:
-//  * wnw_score_finalize forms acc[t] = sum over the step's class-A terms, in
-//    layer-major / ascending-kv order, of sum_g 2^(x - m_g) / l_g -- the
-//    probabilities the reference accumulates in fused_attn.py:107-121 and
-//    kernels.py:302-370 -- one thread per audio token, no atomics, a fixed
-//    summation order;
+//  * wnw_score_finalize forms acc[t] = sum over the step's class-A terms of
+//    sum_g 2^(x - m_g) / l_g -- the probabilities the reference accumulates
+//    in fused_attn.py:107-121 and kernels.py:302-370 -- no atomics, a fixed
+//    summation order (8 interleaved partial sums over the layer-major /
+//    ascending-kv term list, combined in order);
 //  * wnw_chunk_topk computes the chunk means of cache.py:632-640 and the top-k
 //    of cache.py:648 (ties -> lower index) in one CTA per sample.  The prefix
 //    sums are taken at segment boundaries only, accumulated in fp64 and rounded
@@ -17,26 +17,40 @@
 
 namespace wnw {
 
-__global__ void score_finalize_kernel(const float* logits, const float* stats, const int64_t* logit_off,
-                                      const int64_t* stat_off, const uint32_t* qmask, const int32_t* term_off,
-                                      int group, const int32_t* score_off, float* acc) {
+// One CTA per (32 audio tokens, sample): the 8 warps split the sample's
+// class-A terms (warp w takes terms w, w+8, ...; lane = token) and the warp
+// sums are added in warp order -- a fixed order, so results repeat bit for bit.
+constexpr int kFinWarps = 8;
+__global__ void __launch_bounds__(kFinWarps * 32)
+    score_finalize_kernel(const float* logits, const float* stats, const int64_t* logit_off, const int64_t* stat_off,
+                          const uint32_t* qmask, const int32_t* term_off, int group, const int32_t* score_off,
+                          float* acc) {
+  __shared__ float part[kFinWarps][32];
   const int b = blockIdx.y;
   const int n = score_off[b + 1] - score_off[b];
-  const int t = blockIdx.x * blockDim.x + threadIdx.x;
-  if (t >= n) return;
-  float sum = 0.f;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t = blockIdx.x * 32 + lane;
   const int i0 = term_off[b], i1 = term_off[b + 1];
-  for (int i = i0; i < i1; ++i) {
-    const float* st = stats + stat_off[i];
-    const float* lg = logits + logit_off[i] + int64_t(t) * group;
-    const uint32_t mask = qmask[i];
-    float p = 0.f;
-    for (int g = 0; g < group; ++g) {
-      if (mask & (1u << g)) p += ex2(lg[g] - __ldg(st + g)) / __ldg(st + group + g);
+  float sum = 0.f;
+  if (t < n) {
+    for (int i = i0 + warp; i < i1; i += kFinWarps) {
+      const float* st = stats + stat_off[i];
+      const float* lg = logits + logit_off[i] + int64_t(t) * group;
+      const uint32_t mask = qmask[i];
+      float p = 0.f;
+      for (int g = 0; g < group; ++g)
+        if (mask & (1u << g)) p += ex2(lg[g] - __ldg(st + g)) / __ldg(st + group + g);
+      sum += p;
     }
-    sum += p;
   }
-  acc[score_off[b] + t] = sum;
+  part[warp][lane] = sum;
+  __syncthreads();
+  if (warp == 0 && t < n) {
+    float s = 0.f;
+#pragma unroll
+    for (int w = 0; w < kFinWarps; ++w) s += part[w][lane];
+    acc[score_off[b] + t] = s;
+  }
 }
 
 constexpr int kTopkThreads = 512;
@@ -179,8 +193,8 @@ extern "C" wnw_status wnw_score_finalize(const float* logits, const float* stats
   WNW_CHECK_ARG(group >= 1 && group <= 32, "group must be in 1..32");
   WNW_CHECK_ARG(batch >= 0 && batch <= 65535, "batch must be in 0..65535");
   if (batch == 0 || max_audio <= 0) return WNW_OK;
-  dim3 grid((max_audio + 255) / 256, batch);
-  score_finalize_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+  dim3 grid((max_audio + 31) / 32, batch);
+  score_finalize_kernel<<<grid, kFinWarps * 32, 0, static_cast<cudaStream_t>(stream)>>>(
       logits, stats, logit_off, stat_off, qmask, term_off, group, score_off, acc);
   WNW_CUDA_TRY(cudaGetLastError());
   return WNW_OK;

@@ -94,6 +94,7 @@ _sig("wnw_gather_rows", _S, P, P, C.c_int64, P, C.c_int, P, P, C.c_int)
 _sig("wnw_h2d_async", _S, P, P, P, P, C.c_int64, P, P)
 _sig("wnw_host_device_pointer", _S, P, C.POINTER(P))
 _sig("wnw_fetch_rows", _S, P, P, C.c_int64, P, P, C.c_int, P, P, C.c_int, P)
+_sig("wnw_fetch_layers", _S, P, P, C.c_int64, P, P, P, C.c_int, P, P, C.c_int, P, P)
 
 #: every symbol the header declares (checked by the CPU test suite)
 EXPORTS = [
@@ -107,6 +108,7 @@ EXPORTS = [
     "wnw_planner_compute_and_prepare", "wnw_planner_get_evictions", "wnw_planner_get_cpu_ranges",
     "wnw_planner_get_layer_transfer", "wnw_planner_get_changes", "wnw_planner_device_plan",
     "wnw_gather_rows", "wnw_h2d_async", "wnw_host_device_pointer", "wnw_fetch_rows",
+    "wnw_fetch_layers",
 ]
 
 
