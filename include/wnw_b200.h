@@ -79,7 +79,7 @@ typedef struct wnw_decode_attn_args {
   const int32_t* seg_cap;   /* [num_segs] slot capacity or NULL (unchecked)  */
   const int32_t* work;      /* [n_clusters][2] (segment, cluster-in-segment) */
   int n_clusters;
-  int cluster_size;         /* 1, 2, 4 or 8                                  */
+  int cluster_size;         /* 1, 2, 4, 8 or 16 (16: non-portable size)      */
   int split_rows;           /* rows per CTA; wnw_split_rows()                */
   void* out;                /* [num_segs, group, head_dim]                   */
   float scale;

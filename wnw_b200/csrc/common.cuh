@@ -105,6 +105,12 @@ __device__ inline void fence_mbar_init() {
 // consistent __threadfence)
 __device__ inline void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
 
+// Programmatic dependent launch: wait until the preceding kernel in the
+// stream has completed and its writes are visible / let the next kernel in
+// the stream start its prologue.
+__device__ inline void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ inline void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 __device__ inline void fence_proxy_async() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }

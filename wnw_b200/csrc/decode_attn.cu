@@ -23,8 +23,9 @@ extern "C" wnw_status wnw_decode_attn(const wnw_decode_attn_args* a, void* strea
                 "null pointer argument");
   WNW_CHECK_ARG((a->new_k == nullptr) == (a->new_v == nullptr), "new_k and new_v must both be given or both null");
   WNW_CHECK_ARG(a->num_segs > 0 && a->num_kv_heads > 0, "bad segment counts");
-  WNW_CHECK_ARG(a->cluster_size == 1 || a->cluster_size == 2 || a->cluster_size == 4 || a->cluster_size == 8,
-                "cluster_size must be 1, 2, 4 or 8");
+  WNW_CHECK_ARG(a->cluster_size == 1 || a->cluster_size == 2 || a->cluster_size == 4 || a->cluster_size == 8 ||
+                    a->cluster_size == 16,
+                "cluster_size must be 1, 2, 4, 8 or 16");
   WNW_CHECK_ARG(a->n_clusters >= 0, "n_clusters < 0");
   WNW_CHECK_ARG(aligned16(a->q) && aligned16(a->k_store) && aligned16(a->v_store) && aligned16(a->out) &&
                     (a->new_k == nullptr || (aligned16(a->new_k) && aligned16(a->new_v))),

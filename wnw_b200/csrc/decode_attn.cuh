@@ -37,6 +37,7 @@ namespace wnw {
 constexpr int kAttnThreads = 128;
 constexpr int kAttnWarps = 4;
 constexpr int kAttnTileBytes = 64 * 1024;  // K + V rows staged per CTA
+constexpr int kMaxCluster = 16;             // CTAs per cluster (16 needs the non-portable opt-in)
 constexpr float kLog2e = 1.4426950408889634f;
 
 template <typename T, int D, int G>
@@ -133,9 +134,9 @@ __device__ __forceinline__ void attn_finish(const AttnParams& p, uint8_t* smem, 
   for (int i = i_lo + tid; i < i_hi; i += kAttnThreads) {
     const int g = i / D, d = i % D;
     // pull every rank's (max, sum, o) first so the remote loads overlap
-    float pm[8], pl[8], po[8];
+    float pm[kMaxCluster], pl[kMaxCluster], po[kMaxCluster];
 #pragma unroll
-    for (int r = 0; r < 8; ++r) {
+    for (int r = 0; r < kMaxCluster; ++r) {
       if (r < cs) {
         pm[r] = *cluster.map_shared_rank(Pm + g, r);
         pl[r] = *cluster.map_shared_rank(Pl + g, r);
@@ -148,11 +149,11 @@ __device__ __forceinline__ void attn_finish(const AttnParams& p, uint8_t* smem, 
     }
     float mx = -INFINITY;
 #pragma unroll
-    for (int r = 0; r < 8; ++r) mx = fmaxf(mx, pm[r]);
+    for (int r = 0; r < kMaxCluster; ++r) mx = fmaxf(mx, pm[r]);
     const float bse = (mx == -INFINITY) ? 0.f : mx;
     float acc = 0.f, ls = 0.f;
 #pragma unroll
-    for (int r = 0; r < 8; ++r) {
+    for (int r = 0; r < kMaxCluster; ++r) {
       const float f = ex2(pm[r] - bse);
       acc += po[r] * f;
       ls += pl[r] * f;
@@ -531,6 +532,7 @@ wnw_status launch_attn(const wnw_decode_attn_args* a, cudaStream_t stream) {
   auto kern = decode_attn_kernel<T, D, G>;
   if (!configured) {
     WNW_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnTileBytes));
+    WNW_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
     configured = true;
   }
   WNW_CHECK_ARG(a->split_rows == C::SPLIT, "split_rows %d does not match kernel split %d", a->split_rows,

@@ -96,8 +96,17 @@ __global__ void __launch_bounds__(kAttnThreads)
   const int cs = static_cast<int>(cluster.num_blocks());
   const int rank = static_cast<int>(cluster.block_rank());
   const int cid = blockIdx.x / cs;
-  const int seg = p.work[2 * cid];
-  const int j = p.work[2 * cid + 1];
+  // prologue that does not depend on the preceding kernel (work table and
+  // slot bases are fixed per layout) overlaps its tail under PDL
+  const int seg = __ldg(p.work + 2 * cid);
+  const int j = __ldg(p.work + 2 * cid + 1);
+  const int64_t base = __ldg(p.seg_base + seg);
+  if (threadIdx.x == 0) {
+#pragma unroll
+    for (int w = 0; w < kAttnWarps; ++w) mbar_init(&bars[w], 1);
+    fence_mbar_init();
+  }
+  pdl_wait();  // seg_len, K/V rows and q may come from the preceding kernel
   const int len = p.seg_len[seg];
   const bool append = p.new_k != nullptr;
   const int total = len + (append ? 1 : 0);
@@ -108,18 +117,11 @@ __global__ void __launch_bounds__(kAttnThreads)
   const int split = j * cs + rank;
   const int row0 = split * kMmaTileRows;
   const int nvalid = max(0, min(kMmaTileRows, total - row0));
-  const int64_t base = p.seg_base[seg];
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
   const int gid = lane >> 2;
   const int tig = lane & 3;
-
-  if (tid == 0) {
-#pragma unroll
-    for (int w = 0; w < kAttnWarps; ++w) mbar_init(&bars[w], 1);
-    fence_mbar_init();
-  }
   __syncthreads();
 
   // ---- producer: one 2-D TMA box (32 rows x 64 columns) per half per tensor
@@ -137,6 +139,7 @@ __global__ void __launch_bounds__(kAttnThreads)
       }
     }
   }
+  pdl_launch_dependents();  // the next kernel may start its own prologue now
 
   // ---- q as the mma B operand: b[k = d][n = g], zero for padded heads
   const T* qs = reinterpret_cast<const T*>(p.q) + int64_t(seg) * G * D;
@@ -330,6 +333,7 @@ wnw_status launch_attn_mma(const wnw_decode_attn_args* a, cudaStream_t stream) {
   static bool configured = false;
   if (!configured) {
     WNW_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    WNW_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
     configured = true;
   }
   WNW_CHECK_ARG(a->split_rows == kMmaTileRows, "split_rows %d does not match the tensor-core tile %d",
@@ -345,13 +349,15 @@ wnw_status launch_attn_mma(const wnw_decode_attn_args* a, cudaStream_t stream) {
   cfg.blockDim = dim3(kAttnThreads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = a->cluster_size;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   WNW_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, p, tk, tv));
   return WNW_OK;
 }
