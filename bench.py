@@ -291,6 +291,34 @@ def run_e2e(rec, dev, K, W):
     return dict(ms=e0.elapsed_time(e1), in_bytes=in_bytes, out_bytes=out_bytes)
 
 
+def h2d_link_probe(dev, mb=128, reps=5):
+    """Zero-copy H2D bandwidth of this GPU's host link right now (the fetch
+    kernel reading 128-row ranges of a pinned buffer), GB/s.  The decode step
+    fetches its offloaded rows over this link, so it bounds the step."""
+    from wnw_b200 import kernels as Kx
+    D = MODEL["D"]
+    rows = mb * (1 << 20) // (2 * D * 2)
+    hk = torch.ones(rows, D, dtype=torch.bfloat16).pin_memory()
+    hv = torch.ones(rows, D, dtype=torch.bfloat16).pin_memory()
+    pk, pv = Kx.host_device_pointer(hk), Kx.host_device_pointer(hv)
+    n = rows // 128
+    perm = torch.randperm(n, generator=torch.Generator().manual_seed(0))
+    st = (perm * 128).to(torch.int32)
+    ranges = torch.stack([st, st + 128], 1).to(dev)
+    dst = torch.arange(0, n * 128, 128, dtype=torch.int64, device=dev)
+    dk = torch.empty(rows, D, dtype=torch.bfloat16, device=dev)
+    dv = torch.empty_like(dk)
+    Kx.fetch_rows(pk, pv, D * 2, ranges, dst, dk, dv, max_ctas=512)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        Kx.fetch_rows(pk, pv, D * 2, ranges, dst, dk, dv, max_ctas=512)
+    e1.record()
+    torch.cuda.synchronize()
+    return 2 * rows * D * 2 * reps / (e0.elapsed_time(e1) * 1e-3) / 1e9
+
+
 def cpu_replay(rec, n_steps, start=0):
     """The CPU oracle replaying steps [start, start+n_steps) after its own
     prefill from the same recorded inputs; returns seconds per step."""
@@ -443,6 +471,8 @@ def main():
         e2e_ms = e2e["ms"]
     tokens = world * 1 * K
     peak, peak_kind = peaks()
+    link = h2d_link_probe(dev)
+    fetch_bytes = val["fetched_rows"] / K * MODEL["D"] * 2 * 2
     achieved = val["attn_bytes"] / (val["attn_us"] * 1e-6) / 1e9
     line = {
         "metric": "decode tokens/s (WnW hot path) and decode-attention HBM GB/s", "value": tokens / (ms * 1e-3),
@@ -453,13 +483,18 @@ def main():
                 "d2h_bytes_per_step": e2e["out_bytes"]},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": (achieved / peak) if achieved else None, "peak_source": peak_kind,
-                     "traffic": traffic_per_launch(val["attn_bytes"]), "kernel": "wnw::decode_attn_kernel<bf16,128,4>",
+                     "traffic": traffic_per_launch(val["attn_bytes"]),
+                     "kernel": "wnw::decode_attn_mma_kernel<bf16,128,4>",
                      "bytes_per_launch": val["attn_bytes"], "us_per_launch": val["attn_us"],
                      "launches_timed": val["attn_n"],
                      "how": "all 30 layers' launches back to back on the timed run's final state, CUDA events"},
         "gpu_launches": val["launches"],
         "clocks": clk.summary(),
         "fetched_rows_per_step": val["fetched_rows"] / K,
+        "host_link": {"fetch_bytes_per_step": fetch_bytes, "link_gbs": link,
+                      "fetch_ms_at_link": fetch_bytes / (link * 1e9) * 1e3 if link else None,
+                      "how": "offloaded rows fetched per step over the host link (zero-copy kernel); link_gbs = "
+                             "that kernel on 128 MB of random 128-row ranges, measured in this run"},
         "model_decode_ms_per_token": rec["model_ms"],
     }
     if rank == 0 and not a.no_cpu and not a.profile:

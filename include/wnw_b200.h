@@ -117,14 +117,25 @@ wnw_status wnw_decode_attn(const wnw_decode_attn_args* a, void* stream);
 #define WNW_NOALLOC_MAX_SEGS (1 << 16)
 wnw_status wnw_decode_attn_noalloc(const wnw_decode_attn_args* a, void* stream);
 
-/* Rows per CTA used by wnw_decode_attn for a dtype / head_dim (16-bit K/V
- * with head_dim 64 or 128 take the tensor-core kernel: 128 rows per CTA). */
+/* Smallest rows per CTA of wnw_decode_attn for a dtype / head_dim (16-bit
+ * K/V with head_dim 64 or 128 take the tensor-core kernel, whose CTAs stream
+ * any positive multiple of its 128-row tile: split_rows = 128 * tiles). */
 int wnw_split_rows(int dtype, int head_dim);
+
+/* Launch shape for one layer (no reference counterpart: the reference's
+ * kernels take one CTA per segment).  From the per-segment row capacities,
+ * picks split_rows (a multiple of wnw_split_rows) and cluster_size so the
+ * layer's CTAs fit the device's resident clusters in as few waves and tiles
+ * per SM as possible (cudaOccupancyMaxActiveClusters on the current device;
+ * the CUDA-core kernel keeps its fixed split and needs no device). */
+wnw_status wnw_attn_launch_shape(int dtype, int head_dim, const int32_t* seg_cap, int num_segs,
+                                 int* split_rows, int* cluster_size);
 
 /* Build the cluster work table on the host from per-segment row capacities
  * (a segment needs ceil((cap+1)/split_rows) splits).  Writes up to max_clusters
  * pairs and the count (work == NULL with max_clusters == 0 only counts);
- * WNW_ERR_CAPACITY when max_clusters is too small. */
+ * WNW_ERR_CAPACITY when max_clusters is too small.  Segments that need
+ * several clusters come first; each segment's clusters are consecutive. */
 wnw_status wnw_build_work_table(const int32_t* seg_cap, int num_segs, int split_rows,
                                 int cluster_size, int32_t* work, int max_clusters,
                                 int* n_clusters);

@@ -65,6 +65,7 @@ CASES = [
     (torch.bfloat16, 128, 7, 8, [100, 6000, 1, 30000]),
     (torch.bfloat16, 128, 8, 2, [333, 256, 2]),
     (torch.bfloat16, 128, 1, 1, [10, 500, 129]),
+    (torch.bfloat16, 128, 4, 1, [15064, 3, 2000, 129]),
     (torch.float32, 64, 2, 8, [3, 900, 4097]),
     (torch.bfloat16, 64, 3, 4, [1, 2, 3, 1000]),
     (torch.float32, 32, 2, 8, [400, 12]),
@@ -74,10 +75,15 @@ CASES = [
 
 @pytest.mark.parametrize("dtype,D,G,cs,lens", CASES)
 @pytest.mark.parametrize("append", [True, False])
-def test_decode_attention_matches_oracle(dev, dtype, D, G, cs, lens, append):
+@pytest.mark.parametrize("tiles", [1, 3])
+def test_decode_attention_matches_oracle(dev, dtype, D, G, cs, lens, append, tiles):
+    """``tiles`` > 1: each CTA of the tensor-core kernel streams that many
+    128-row tiles of its segment (two-stage pipeline, online softmax)."""
     from wnw_b200 import kernels as Kx
     S = len(lens)
-    split = Kx.split_rows(dtype, D)
+    if tiles > 1 and (dtype == torch.float32 or D not in (64, 128)):
+        pytest.skip("multi-tile CTAs are a tensor-core kernel mode")
+    split = Kx.split_rows(dtype, D) * tiles
     ks, vs, base, cap = _slots(lens, 40, D, dtype, dev, seed=sum(lens) + G)
     g = torch.Generator(device="cpu").manual_seed(7)
     q = torch.randn(S, G, D, generator=g).to(dtype).to(dev)
@@ -89,7 +95,8 @@ def test_decode_attention_matches_oracle(dev, dtype, D, G, cs, lens, append):
     before_k = ks.clone()
     scale = D ** -0.5
     out = Kx.decode_attention(q, ks, vs, torch.from_numpy(base).to(dev), seg_len, work, cs, scale, scratch,
-                              new_k=nk, new_v=nv, seg_cap=torch.from_numpy(cap.astype(np.int32)).to(dev))
+                              new_k=nk, new_v=nv, seg_cap=torch.from_numpy(cap.astype(np.int32)).to(dev),
+                              split=split)
     torch.cuda.synchronize()
     assert int(scratch.err.item()) == 0
     assert int(scratch.counters.abs().sum()) == 0  # left zero for the next launch
@@ -111,18 +118,44 @@ def test_decode_attention_matches_oracle(dev, dtype, D, G, cs, lens, append):
     assert np.all(got[~nz] == 0)
 
 
-def test_scoring_logits_and_finalize_match_oracle(dev):
+@pytest.mark.parametrize("lens", [[15100, 15100, 2300, 2300, 2300, 2300, 2300, 2300], [120000, 4000, 3],
+                                  [1, 2, 3, 300], [5000] * 64])
+def test_library_launch_shape_matches_oracle(dev, lens):
+    """The shape wnw_attn_launch_shape picks (tiles per CTA, cluster size) is
+    valid and its output matches the oracle."""
+    from wnw_b200 import kernels as Kx
+    dtype, D, G = torch.bfloat16, 128, 4
+    S = len(lens)
+    ks, vs, base, cap = _slots(lens, 64, D, dtype, dev, seed=len(lens))
+    split, cs = Kx.attn_launch_shape(dtype, D, cap)
+    assert split % 128 == 0 and split >= 128 and cs in (1, 2, 4, 8)
+    g = torch.Generator(device="cpu").manual_seed(5)
+    q = torch.randn(S, G, D, generator=g).to(dtype).to(dev)
+    work = torch.from_numpy(Kx.build_work_table(cap, split, cs)).to(dev)
+    scratch = Kx.AttnScratch(dev, work.shape[0], G, D, S)
+    out = Kx.decode_attention(q, ks, vs, torch.from_numpy(base).to(dev),
+                              torch.tensor(lens, dtype=torch.int32, device=dev), work, cs, D ** -0.5, scratch,
+                              seg_cap=torch.from_numpy(cap.astype(np.int32)).to(dev), split=split)
+    torch.cuda.synchronize()
+    assert int(scratch.err.item()) == 0
+    pk, pv = _packed(ks, base, lens), _packed(vs, base, lens)
+    ref, _, _ = K.decode_attn(q.float().cpu().numpy(), pk, pv, np.concatenate([[0], np.cumsum(lens)]), D ** -0.5)
+    np.testing.assert_allclose(out.float().cpu().numpy(), ref, atol=TOL[dtype], rtol=TOL[dtype])
+
+
+@pytest.mark.parametrize("dtype,tiles", [(torch.float32, 1), (torch.bfloat16, 1), (torch.bfloat16, 4)])
+def test_scoring_logits_and_finalize_match_oracle(dev, dtype, tiles):
     """Fused class-A logits + stats, then wnw_score_finalize, equal the
-    reference's per-token probabilities summed over kv heads and q heads."""
+    reference's per-token probabilities summed over kv heads and q heads
+    (bf16: the same inputs as fp32 values, logits accumulated in fp32)."""
     from wnw_b200 import kernels as Kx
     B, H, G, D = 2, 4, 4, 128
-    dtype = torch.float32
     lens = [3000, 2900, 2700, 4100, 3500, 3300, 2900, 900]  # class-A kv 0, 2 cover the audio
     a_s, a_e = [10, 40], [2600, 2800]
     ks, vs, base, cap = _slots(lens, 16, D, dtype, dev, seed=3)
     g = torch.Generator(device="cpu").manual_seed(11)
-    q = torch.randn(B * H, G, D, generator=g).to(dev)
-    split = Kx.split_rows(dtype, D)
+    q = torch.randn(B * H, G, D, generator=g).to(dtype).to(dev)
+    split = Kx.split_rows(dtype, D) * tiles
     work = torch.from_numpy(Kx.build_work_table(cap, split, 8)).to(dev)
     scratch = Kx.AttnScratch(dev, work.shape[0], G, D, B * H)
     ca_kv = [0, 2]                       # class-A kv heads (all q heads of each)
@@ -144,7 +177,7 @@ def test_scoring_logits_and_finalize_match_oracle(dev):
                  audio_end=torch.tensor(a_e, dtype=torch.int32, device=dev), logits=logits,
                  logits_off=torch.tensor(offs, dtype=torch.int64, device=dev), stats=stats)
     Kx.decode_attention(q, ks, vs, torch.from_numpy(base).to(dev), torch.tensor(lens, dtype=torch.int32, device=dev),
-                        work, 8, D ** -0.5, scratch, num_kv_heads=H, score=score)
+                        work, 8, D ** -0.5, scratch, num_kv_heads=H, score=score, split=split)
     n_audio = [e - s for s, e in zip(a_s, a_e)]
     score_off = torch.tensor([0, n_audio[0], sum(n_audio)], dtype=torch.int32, device=dev)
     acc = torch.full((sum(n_audio),), -1.0, device=dev)
@@ -159,7 +192,7 @@ def test_scoring_logits_and_finalize_match_oracle(dev):
     ref_acc = np.zeros(sum(n_audio))
     ca_mask = np.zeros(H, np.int32)
     ca_mask[ca_kv] = 1
-    K.decode_attn_score(q.cpu().numpy(), pk, pv, cu, D ** -0.5, ca_mask, H, a_s, a_e, ref_acc,
+    K.decode_attn_score(q.float().cpu().numpy(), pk, pv, cu, D ** -0.5, ca_mask, H, a_s, a_e, ref_acc,
                         [0, n_audio[0], sum(n_audio)])
     np.testing.assert_allclose(acc.cpu().numpy(), ref_acc, atol=1e-6, rtol=1e-5)
 

@@ -120,3 +120,16 @@ def test_work_table_covers_capacity():
     out = np.zeros((2, 2), np.int32)
     st = N.lib.wnw_build_work_table(N.ptr(cap), cap.size, 128, 4, N.ptr(out), 2, ctypes.byref(n))
     assert st == 3 and n.value == w.shape[0]
+
+
+def test_launch_shape_cuda_core_kernel():
+    """fp32 keeps the CUDA-core kernel's fixed split; clusters grow to 8 with
+    the longest segment (no device query on this path)."""
+    from wnw_b200.kernels import attn_launch_shape, split_rows
+    import torch
+    base = split_rows(torch.float32, 128)
+    assert attn_launch_shape(torch.float32, 128, [10, 20]) == (base, 1)
+    assert attn_launch_shape(torch.float32, 128, [3 * base]) == (base, 4)
+    assert attn_launch_shape(torch.float32, 128, [100000, 5]) == (base, 8)
+    with pytest.raises(N.WnwError, match="negative capacity"):
+        attn_launch_shape(torch.float32, 128, [-1])

@@ -297,7 +297,6 @@ class B200WnWCache(FlatVarlenCache):
     def _build_slots(self):
         L, S, D = self.num_layers, self.batch_size * self.num_kv_heads, self.head_dim
         dev = self.device
-        self._split = Kx.split_rows(self.dtype, D)
         self._len_host = np.zeros((L, S), np.int64)     # rows stored (device seg_len mirror)
         self._cap_host = np.zeros((L, S), np.int64)
         self._base_host = np.zeros((L, S), np.int64)
@@ -347,11 +346,13 @@ class B200WnWCache(FlatVarlenCache):
         self._seg_base = torch.from_numpy(self._base_host).to(dev)
         self._seg_cap = torch.from_numpy(self._cap_host.astype(np.int32)).to(dev)
         max_rows = int((self._len_host + self.max_decode_tokens).max()) if S else 0
-        self._cluster = Kx.choose_cluster_size(int(self._cap_host.max()) if S else 0, self._split)
-        self._work = []
+        self._work, self._shape = [], []
         n_max = 0
         for l in range(L):
-            w = Kx.build_work_table(self._cap_host[l], self._split, self._cluster)
+            # rows per CTA and cluster size fitted to this layer's capacities
+            split, cs = Kx.attn_launch_shape(self.dtype, D, self._cap_host[l])
+            self._shape.append((split, cs))
+            w = Kx.build_work_table(self._cap_host[l], split, cs)
             self._work.append(torch.from_numpy(w).to(dev))
             n_max = max(n_max, w.shape[0])
         if getattr(self, "_scratch", None) is None or not self._scratch.fits(n_max, G, D, S):
@@ -525,9 +526,9 @@ class B200WnWCache(FlatVarlenCache):
                                                                           abs_tol=1e-12)
             S = self.batch_size * self.num_kv_heads
             args = Kx.make_attn_args(self.dtype, S, G, D, self.k_store[l], self.v_store[l], self._seg_base[l],
-                                     self._seg_len[l], self._work[l], self._cluster, scale, self._scratch,
+                                     self._seg_len[l], self._work[l], self._shape[l][1], scale, self._scratch,
                                      seg_cap=self._seg_cap[l], num_kv_heads=self.num_kv_heads,
-                                     score=None if sep else score)
+                                     score=None if sep else score, split=self._shape[l][0])
             cached = self._attn_args[l] = (scale, sep, args)
         _, sep, args = cached
         out = torch.empty_like(qf)
@@ -535,9 +536,9 @@ class B200WnWCache(FlatVarlenCache):
         if sep:
             score = self._score_args(l)  # rescore with the reference's 1/sqrt(d) (the append is idempotent)
             Kx.decode_attention(qf, self.k_store[l], self.v_store[l], self._seg_base[l], self._seg_len[l],
-                                self._work[l], self._cluster, D ** -0.5, self._scratch, new_k=nk, new_v=nv,
+                                self._work[l], self._shape[l][1], D ** -0.5, self._scratch, new_k=nk, new_v=nv,
                                 seg_cap=self._seg_cap[l], num_kv_heads=self.num_kv_heads, score=score,
-                                out=torch.empty_like(qf))
+                                out=torch.empty_like(qf), split=self._shape[l][0])
         return out
 
     def decode_all_layers_done(self):

@@ -104,6 +104,10 @@ __device__ inline void fence_mbar_init() {
 // acquire-release fence at gpu scope (cheaper than the sequentially
 // consistent __threadfence)
 __device__ inline void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+// split cluster barrier: arrive (release) now, wait (acquire) later; every
+// thread of every CTA of the cluster executes both, in this order
+__device__ inline void cluster_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
+__device__ inline void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
 
 // Programmatic dependent launch: wait until the preceding kernel in the
 // stream has completed and its writes are visible / let the next kernel in

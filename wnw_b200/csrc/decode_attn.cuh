@@ -38,6 +38,8 @@ constexpr int kAttnThreads = 128;
 constexpr int kAttnWarps = 4;
 constexpr int kAttnTileBytes = 64 * 1024;  // K + V rows staged per CTA
 constexpr int kMaxCluster = 16;             // CTAs per cluster (16 needs the non-portable opt-in)
+constexpr int kMmaMaxStages = 3;            // tensor-core kernel: shared-memory stages per CTA
+inline int mma_stages(int64_t tiles) { return static_cast<int>(tiles < kMmaMaxStages ? tiles : kMmaMaxStages); }
 constexpr float kLog2e = 1.4426950408889634f;
 
 template <typename T, int D, int G>
@@ -57,7 +59,7 @@ struct AttnCfg {
   static_assert(CPR % LPR == 0, "lanes must tile a row");
   static_assert(WROWS % (RPW * U) == 0, "warp chunk must tile into passes");
   // merge scratch (reuses the tile region): wm, wl [warps][G], wo [warps][G][D],
-  // then the CTA partial Pm, Pl [G], Po [G][D]
+  // then the CTA partial Po [G][D], Pm, Pl [G]
   static constexpr int MERGE_FLOATS = 2 * kAttnWarps * G + kAttnWarps * G * D + 2 * G + G * D;
   static_assert(MERGE_FLOATS * 4 <= kAttnTileBytes, "merge scratch fits the tile");
 };
@@ -86,129 +88,108 @@ struct AttnParams {
   int32_t* err;
 };
 
-// Merge the 4 warp partials (wm, wl, wo at the start of `smem`) into the
-// CTA partial, then the cluster's CTAs through distributed shared memory, then
-// -- for segments longer than one cluster -- the clusters through the global
-// partial buffer, the last-arriving cluster writing the output.
-template <typename T, int D, int G>
-__device__ __forceinline__ void attn_finish(const AttnParams& p, uint8_t* smem, int seg, int j, int cid, int ncl) {
-  cg::cluster_group cluster = cg::this_cluster();
-  const int cs = static_cast<int>(cluster.num_blocks());
-  const int rank = static_cast<int>(cluster.block_rank());
-  const int tid = threadIdx.x;
-  __shared__ int s_last;
-  float* wm = reinterpret_cast<float*>(smem);
-  float* wl = wm + kAttnWarps * G;
-  float* wo = wl + kAttnWarps * G;
-  float* Pm = wo + kAttnWarps * G * D;
-  float* Pl = Pm + G;
-  float* Po = Pl + G;
-  for (int i = tid; i < G * D; i += kAttnThreads) {
-    const int g = i / D, d = i % D;
-    float mx = -INFINITY;
-#pragma unroll
-    for (int w = 0; w < kAttnWarps; ++w) mx = fmaxf(mx, wm[w * G + g]);
-    const float bse = (mx == -INFINITY) ? 0.f : mx;
-    float acc = 0.f, ls = 0.f;
-#pragma unroll
-    for (int w = 0; w < kAttnWarps; ++w) {
-      const float f = ex2(wm[w * G + g] - bse);
-      acc += wo[(w * G + g) * D + d] * f;
-      ls += wl[w * G + g] * f;
-    }
-    Po[i] = acc;
-    if (d == 0) {
-      Pm[g] = mx;
-      Pl[g] = ls;
-    }
-  }
-
-  // ---- merge the CTAs of the cluster through distributed shared memory;
-  // each rank merges a slice of the G*D outputs
-  cluster.sync();
-  const int per = (G * D + cs - 1) / cs;
-  const int i_lo = rank * per;
-  const int i_hi = min(G * D, i_lo + per);
-  float* part = p.partials + int64_t(cid) * G * (D + 2);
-  T* outp = reinterpret_cast<T*>(p.out) + int64_t(seg) * G * D;
-  for (int i = i_lo + tid; i < i_hi; i += kAttnThreads) {
-    const int g = i / D, d = i % D;
-    // pull every rank's (max, sum, o) first so the remote loads overlap
-    float pm[kMaxCluster], pl[kMaxCluster], po[kMaxCluster];
-#pragma unroll
-    for (int r = 0; r < kMaxCluster; ++r) {
-      if (r < cs) {
-        pm[r] = *cluster.map_shared_rank(Pm + g, r);
-        pl[r] = *cluster.map_shared_rank(Pl + g, r);
-        po[r] = *cluster.map_shared_rank(Po + i, r);
-      } else {
-        pm[r] = -INFINITY;
-        pl[r] = 0.f;
-        po[r] = 0.f;
-      }
-    }
-    float mx = -INFINITY;
-#pragma unroll
-    for (int r = 0; r < kMaxCluster; ++r) mx = fmaxf(mx, pm[r]);
-    const float bse = (mx == -INFINITY) ? 0.f : mx;
-    float acc = 0.f, ls = 0.f;
-#pragma unroll
-    for (int r = 0; r < kMaxCluster; ++r) {
-      const float f = ex2(pm[r] - bse);
-      acc += po[r] * f;
-      ls += pl[r] * f;
-    }
-    if (ncl == 1) {
-      outp[i] = DT<T>::from_f(ls > 0.f ? acc / ls : 0.f);
-      if (d == 0 && p.stats != nullptr) {
-        p.stats[int64_t(seg) * 2 * G + g] = mx;
-        p.stats[int64_t(seg) * 2 * G + G + g] = ls;
-      }
+// A global partial is {o[G*D], max[G], sum[G]} (stride G * (D + 2) floats);
+// its o row is read / written as float4 when that stride keeps 16-byte
+// alignment (G even), else element-wise.
+template <int D, int G>
+struct PartIO {
+  static constexpr int kStride = G * (D + 2);
+  static constexpr bool kVec = (kStride % 4) == 0;
+  __device__ static float4 ld(const float* p) {
+    if constexpr (kVec) {
+      return __ldcg(reinterpret_cast<const float4*>(p));
     } else {
-      part[i] = acc;
-      if (d == 0) {
-        part[G * D + g] = mx;
-        part[G * D + G + g] = ls;
-      }
+      return make_float4(__ldcg(p), __ldcg(p + 1), __ldcg(p + 2), __ldcg(p + 3));
     }
   }
-  if (ncl == 1) {
-    cluster.sync();  // keep this CTA's shared memory alive for the remote reads
-    return;
-  }
-  fence_acq_rel_gpu();  // release this thread's partial slice at gpu scope
-  cluster.sync();
-  if (rank == 0 && tid == 0) {
-    const int old = atomicAdd(p.counters + seg, 1);
-    const int last = (old == ncl - 1) ? 1 : 0;
-    if (last) {
-      p.counters[seg] = 0;  // every cluster of this launch has arrived
-      fence_acq_rel_gpu();  // acquire the other clusters' partials
+  __device__ static void st(float* p, float4 v) {
+    if constexpr (kVec) {
+      *reinterpret_cast<float4*>(p) = v;
+    } else {
+      p[0] = v.x;
+      p[1] = v.y;
+      p[2] = v.z;
+      p[3] = v.w;
     }
-    for (int r = 0; r < cs; ++r) *cluster.map_shared_rank(&s_last, r) = last;
   }
-  cluster.sync();
-  if (!s_last) return;
-  // final merge across the segment's clusters, sliced over the ranks
-  const float* part0 = p.partials + int64_t(cid - j) * G * (D + 2);
-  constexpr int kBatch = 16;  // cluster partials loaded per round trip
-  for (int i = i_lo + tid; i < i_hi; i += kAttnThreads) {
-    const int g = i / D, d = i % D;
-    float mx = -INFINITY, acc = 0.f, ls = 0.f;
+};
+
+// Output (and class-A stats) of the 4 merged elements [i, i + 4) of one head.
+template <typename T, int D, int G>
+__device__ __forceinline__ void attn_store4(const AttnParams& p, int seg, int i, float mx, float ls, float4 acc) {
+  T* outp = reinterpret_cast<T*>(p.out) + int64_t(seg) * G * D + i;
+  const bool nz = ls > 0.f;
+  outp[0] = DT<T>::from_f(nz ? acc.x / ls : 0.f);
+  outp[1] = DT<T>::from_f(nz ? acc.y / ls : 0.f);
+  outp[2] = DT<T>::from_f(nz ? acc.z / ls : 0.f);
+  outp[3] = DT<T>::from_f(nz ? acc.w / ls : 0.f);
+  if (i % D == 0 && p.stats != nullptr) {
+    const int g = i / D;
+    p.stats[int64_t(seg) * 2 * G + g] = mx;
+    p.stats[int64_t(seg) * 2 * G + G + g] = ls;
+  }
+}
+
+__device__ __forceinline__ void fma4(float4& acc, float4 v, float f) {
+  acc.x += v.x * f;
+  acc.y += v.y * f;
+  acc.z += v.z * f;
+  acc.w += v.w * f;
+}
+__device__ __forceinline__ void scale4(float4& acc, float f) {
+  acc.x *= f;
+  acc.y *= f;
+  acc.z *= f;
+  acc.w *= f;
+}
+
+// Merge the 4 warp partials (wm, wl, wo at the start of `smem`) of elements
+// [i, i + 4) (one head g) into (max, sum, o).
+template <int D, int G>
+__device__ __forceinline__ void merge_warps4(const float* smem, int i, float& mx, float& ls, float4& acc) {
+  const float* wm = smem;
+  const float* wl = wm + kAttnWarps * G;
+  const float* wo = wl + kAttnWarps * G;
+  const int g = i / D, d = i % D;
+  mx = -INFINITY;
+#pragma unroll
+  for (int w = 0; w < kAttnWarps; ++w) mx = fmaxf(mx, wm[w * G + g]);
+  const float bse = (mx == -INFINITY) ? 0.f : mx;
+  ls = 0.f;
+  acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+  for (int w = 0; w < kAttnWarps; ++w) {
+    const float f = ex2(wm[w * G + g] - bse);
+    fma4(acc, *reinterpret_cast<const float4*>(wo + (w * G + g) * D + d), f);
+    ls += wl[w * G + g] * f;
+  }
+}
+
+// Final merge of a segment's `ncl` global partials (part0 = the first),
+// written as the output; this CTA's threads take 4 elements at a time.
+template <typename T, int D, int G>
+__device__ __forceinline__ void attn_merge_partials(const AttnParams& p, const float* part0, int seg, int ncl) {
+  using IO = PartIO<D, G>;
+  constexpr int kBatch = 16;  // partials loaded per round trip
+  for (int i = 4 * static_cast<int>(threadIdx.x); i < G * D; i += 4 * kAttnThreads) {
+    const int g = i / D;
+    float mx = -INFINITY, ls = 0.f;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int c0 = 0; c0 < ncl; c0 += kBatch) {
-      float bm[kBatch], bl[kBatch], bo[kBatch];
+      float bm[kBatch], bl[kBatch];
+      float4 bo[kBatch];
 #pragma unroll
       for (int u = 0; u < kBatch; ++u) {
         const int c = c0 + u;
         if (c < ncl) {
-          const float* pc = part0 + int64_t(c) * G * (D + 2);
+          const float* pc = part0 + int64_t(c) * IO::kStride;
           bm[u] = __ldcg(pc + G * D + g);
           bl[u] = __ldcg(pc + G * D + G + g);
-          bo[u] = __ldcg(pc + i);
+          bo[u] = IO::ld(pc + i);
         } else {
           bm[u] = -INFINITY;
           bl[u] = 0.f;
-          bo[u] = 0.f;
+          bo[u] = make_float4(0.f, 0.f, 0.f, 0.f);
         }
       }
       float mn = mx;
@@ -216,22 +197,137 @@ __device__ __forceinline__ void attn_finish(const AttnParams& p, uint8_t* smem, 
       for (int u = 0; u < kBatch; ++u) mn = fmaxf(mn, bm[u]);
       const float bse = (mn == -INFINITY) ? 0.f : mn;
       const float a = ex2(mx - bse);
-      acc *= a;
+      scale4(acc, a);
       ls *= a;
 #pragma unroll
       for (int u = 0; u < kBatch; ++u) {
         const float f = ex2(bm[u] - bse);
-        acc += bo[u] * f;
+        fma4(acc, bo[u], f);
         ls += bl[u] * f;
       }
       mx = mn;
     }
-    outp[i] = DT<T>::from_f(ls > 0.f ? acc / ls : 0.f);
-    if (d == 0 && p.stats != nullptr) {
-      p.stats[int64_t(seg) * 2 * G + g] = mx;
-      p.stats[int64_t(seg) * 2 * G + G + g] = ls;
+    attn_store4<T, D, G>(p, seg, i, mx, ls, acc);
+  }
+}
+
+// Write this CTA's (or cluster's) merged partial to global memory, arrive at
+// the segment's counter and, if last, merge all of the segment's partials.
+// The caller has stored its elements of `part` from this CTA's threads.
+template <typename T, int D, int G>
+__device__ __forceinline__ void attn_arrive_and_merge(const AttnParams& p, int seg, int j, int cid, int ncl) {
+  __shared__ int s_last;
+  __syncthreads();  // the CTA's partial is written (CTA scope) ...
+  if (threadIdx.x == 0) {
+    fence_acq_rel_gpu();  // ... and released at gpu scope (cumulative) before the arrival
+    const int old = atomicAdd(p.counters + seg, 1);
+    const int last = (old == ncl - 1) ? 1 : 0;
+    if (last) {
+      p.counters[seg] = 0;  // every partial of this launch has arrived
+      fence_acq_rel_gpu();  // acquire the other partials
+    }
+    s_last = last;
+  }
+  __syncthreads();
+  if (s_last) attn_merge_partials<T, D, G>(p, p.partials + int64_t(cid - j) * PartIO<D, G>::kStride, seg, ncl);
+}
+
+// Merge the 4 warp partials (wm, wl, wo at the start of `smem`) into the
+// output, or -- segments split over several clusters -- into a global
+// partial merged by the last-arriving cluster.  Clusters of several CTAs
+// first combine their CTAs through distributed shared memory: every CTA
+// parks its merged partial in its own shared memory, rank 0 gathers them
+// and carries on alone while the other ranks leave.
+template <typename T, int D, int G>
+__device__ __forceinline__ void attn_finish(const AttnParams& p, uint8_t* smem, int seg, int j, int cid, int ncl) {
+  using IO = PartIO<D, G>;
+  cg::cluster_group cluster = cg::this_cluster();
+  const int cs = static_cast<int>(cluster.num_blocks());
+  const int rank = static_cast<int>(cluster.block_rank());
+  const int tid = threadIdx.x;
+  const float* ws = reinterpret_cast<const float*>(smem);
+  float* part = p.partials + int64_t(cid) * IO::kStride;
+  if (cs == 1) {
+    for (int i = 4 * tid; i < G * D; i += 4 * kAttnThreads) {
+      float mx, ls;
+      float4 acc;
+      merge_warps4<D, G>(ws, i, mx, ls, acc);
+      if (ncl == 1) {
+        attn_store4<T, D, G>(p, seg, i, mx, ls, acc);
+      } else {
+        IO::st(part + i, acc);
+        if (i % D == 0) {
+          part[G * D + i / D] = mx;
+          part[G * D + G + i / D] = ls;
+        }
+      }
+    }
+    if (ncl > 1) attn_arrive_and_merge<T, D, G>(p, seg, j, cid, ncl);
+    return;
+  }
+  // CTA partial behind the warp partials: Po [G*D] (16-byte aligned), Pm, Pl [G]
+  float* Po = reinterpret_cast<float*>(smem) + 2 * kAttnWarps * G + kAttnWarps * G * D;
+  float* Pm = Po + G * D;
+  float* Pl = Pm + G;
+  for (int i = 4 * tid; i < G * D; i += 4 * kAttnThreads) {
+    float mx, ls;
+    float4 acc;
+    merge_warps4<D, G>(ws, i, mx, ls, acc);
+    *reinterpret_cast<float4*>(Po + i) = acc;
+    if (i % D == 0) {
+      Pm[i / D] = mx;
+      Pl[i / D] = ls;
     }
   }
+  cluster_arrive();  // CTA partials visible to the cluster
+  cluster_wait();
+  if (rank != 0) {
+    cluster_arrive();  // keep this CTA's shared memory until rank 0 has read it
+    cluster_wait();
+    return;
+  }
+  for (int i = 4 * tid; i < G * D; i += 4 * kAttnThreads) {
+    const int g = i / D;
+    // pull every rank's (max, sum, o) first so the remote loads overlap
+    float pm[kMaxCluster], pl[kMaxCluster];
+    float4 po[kMaxCluster];
+#pragma unroll
+    for (int r = 0; r < kMaxCluster; ++r) {
+      if (r < cs) {
+        pm[r] = *cluster.map_shared_rank(Pm + g, r);
+        pl[r] = *cluster.map_shared_rank(Pl + g, r);
+        po[r] = *reinterpret_cast<const float4*>(cluster.map_shared_rank(Po + i, r));
+      } else {
+        pm[r] = -INFINITY;
+        pl[r] = 0.f;
+        po[r] = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+    float mx = -INFINITY;
+#pragma unroll
+    for (int r = 0; r < kMaxCluster; ++r) mx = fmaxf(mx, pm[r]);
+    const float bse = (mx == -INFINITY) ? 0.f : mx;
+    float ls = 0.f;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int r = 0; r < kMaxCluster; ++r) {
+      const float f = ex2(pm[r] - bse);
+      fma4(acc, po[r], f);
+      ls += pl[r] * f;
+    }
+    if (ncl == 1) {
+      attn_store4<T, D, G>(p, seg, i, mx, ls, acc);
+    } else {
+      IO::st(part + i, acc);
+      if (i % D == 0) {
+        part[G * D + g] = mx;
+        part[G * D + G + g] = ls;
+      }
+    }
+  }
+  cluster_arrive();  // done with the other ranks' shared memory
+  if (ncl > 1) attn_arrive_and_merge<T, D, G>(p, seg, j, cid, ncl);
+  cluster_wait();
 }
 
 template <typename T, int D, int G>
@@ -558,5 +654,9 @@ wnw_status launch_attn(const wnw_decode_attn_args* a, cudaStream_t stream) {
 
 template <typename T>
 wnw_status dispatch_dtype(const wnw_decode_attn_args* a, cudaStream_t s);
+
+// co-resident clusters of `cs` CTAs of the tensor-core kernel with `nstages`
+// shared-memory stages (decode_attn_bf16.cu)
+wnw_status attn_mma_active_clusters_any(int head_dim, int cs, int nstages, int* n);
 
 }  // namespace wnw

@@ -22,6 +22,16 @@ def split_rows(dtype, head_dim):
     return N.lib.wnw_split_rows(N.dtype_code(dtype), int(head_dim))
 
 
+def attn_launch_shape(dtype, head_dim, seg_cap):
+    """(split_rows, cluster_size) for one layer's capacities
+    (``wnw_attn_launch_shape``; needs the CUDA device for 16-bit head_dim 64/128)."""
+    cap = np.ascontiguousarray(np.asarray(seg_cap, dtype=np.int32))
+    split, cs = C.c_int(), C.c_int()
+    N.call("wnw_attn_launch_shape", N.dtype_code(dtype), int(head_dim), N.ptr(cap), cap.size, C.byref(split),
+           C.byref(cs))
+    return split.value, cs.value
+
+
 def choose_cluster_size(max_rows, split):
     """Clusters of up to 8 CTAs; smaller when even the longest segment needs
     fewer splits (idle cluster members only cost a barrier)."""
@@ -59,7 +69,7 @@ class AttnScratch:
 
 
 def make_attn_args(dtype, S, G, D, k_store, v_store, seg_base, seg_len, work, cluster_size, scale, scratch,
-                   seg_cap=None, num_kv_heads=None, score=None):
+                   seg_cap=None, num_kv_heads=None, score=None, split=None):
     """A reusable ``wnw_decode_attn_args`` with everything but q / new rows /
     out filled in (the per-layer constant part of a decode step).  The struct
     keeps references to every tensor it points at, so temporaries passed in
@@ -75,7 +85,7 @@ def make_attn_args(dtype, S, G, D, k_store, v_store, seg_base, seg_len, work, cl
     a.work = work.data_ptr()
     a.n_clusters = work.shape[0]
     a.cluster_size = cluster_size
-    a.split_rows = split_rows(dtype, D)
+    a.split_rows = split or split_rows(dtype, D)
     a.scale = float(scale)
     if score is not None:
         a.score_slot = score["slot"].data_ptr()
@@ -123,8 +133,9 @@ def host_device_pointer(t):
 
 def decode_attention(q, k_store, v_store, seg_base, seg_len, work, cluster_size, scale, scratch,
                      new_k=None, new_v=None, seg_cap=None, out=None, num_kv_heads=None, score=None,
-                     stream=None):
-    """Launch ``wnw_decode_attn``.  q: [S, G, D]; work: device int32 [n, 2].
+                     stream=None, split=None):
+    """Launch ``wnw_decode_attn``.  q: [S, G, D]; work: device int32 [n, 2]
+    built with the same ``split`` (rows per CTA; default ``split_rows``).
     ``score`` (optional) = dict(slot=int32[S], audio_start=int32[B], audio_end=int32[B],
     logits=fp32 buffer, logits_off=int64[n_slots], stats=fp32 [S, 2, G])."""
     S, G, D = q.shape
@@ -143,7 +154,7 @@ def decode_attention(q, k_store, v_store, seg_base, seg_len, work, cluster_size,
     a.work = work.data_ptr()
     a.n_clusters = work.shape[0]
     a.cluster_size = cluster_size
-    a.split_rows = split_rows(q.dtype, D)
+    a.split_rows = split or split_rows(q.dtype, D)
     a.out = out.data_ptr()
     a.scale = float(scale)
     if score is not None:

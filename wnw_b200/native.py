@@ -65,6 +65,7 @@ _sig("wnw_last_error", C.c_char_p)
 _sig("wnw_decode_attn", _S, C.POINTER(DecodeAttnArgs), P)
 _sig("wnw_decode_attn_noalloc", _S, C.POINTER(DecodeAttnArgs), P)
 _sig("wnw_split_rows", C.c_int, C.c_int, C.c_int)
+_sig("wnw_attn_launch_shape", _S, C.c_int, C.c_int, P, C.c_int, C.POINTER(C.c_int), C.POINTER(C.c_int))
 _sig("wnw_build_work_table", _S, P, C.c_int, C.c_int, C.c_int, P, C.c_int, C.POINTER(C.c_int))
 _sig("wnw_advance_lengths", _S, P, C.c_int64, P)
 _sig("wnw_score_finalize", _S, P, P, P, P, P, P, C.c_int, C.c_int, P, C.c_int, P, P)
@@ -99,7 +100,7 @@ _sig("wnw_fetch_layers", _S, P, P, C.c_int64, P, P, P, C.c_int, P, P, C.c_int, P
 #: every symbol the header declares (checked by the CPU test suite)
 EXPORTS = [
     "wnw_abi_version", "wnw_status_string", "wnw_last_error", "wnw_decode_attn", "wnw_decode_attn_noalloc",
-    "wnw_split_rows",
+    "wnw_split_rows", "wnw_attn_launch_shape",
     "wnw_build_work_table", "wnw_advance_lengths", "wnw_score_finalize", "wnw_chunk_topk",
     "wnw_rebuild_segments", "wnw_copy_segments", "wnw_interleave_append", "wnw_planner_create",
     "wnw_planner_destroy", "wnw_planner_set_config", "wnw_planner_set_seg_count",

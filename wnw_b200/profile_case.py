@@ -6,7 +6,7 @@ and six class-B segments of 2,300 rows, bf16, head_dim 128, GQA 4 -- with
 class-A scoring on, and launches the decode-attention kernel over the layers
 round-robin (~180 MB for 8 layers: more than L2, so each launch reads HBM).
 
-    python -m wnw_b200.profile_case [--layers 8] [--reps 20] [--cluster 8]
+    python -m wnw_b200.profile_case [--layers 8] [--reps 20] [--cluster C --tiles T]
 
 Prints the mean launch time and the algorithmic-bytes bandwidth.
 """
@@ -21,7 +21,7 @@ import torch
 from wnw_b200 import kernels as Kx
 
 
-def build_layer(dev, lens, a0, a1, G, D, cluster, seed):
+def build_layer(dev, lens, a0, a1, G, D, cluster, seed, tiles=0):
     S = len(lens)
     dtype = torch.bfloat16
     g = torch.Generator(device=dev).manual_seed(seed)
@@ -32,7 +32,10 @@ def build_layer(dev, lens, a0, a1, G, D, cluster, seed):
     ks = torch.randn(rows, D, device=dev, generator=g).to(dtype)
     vs = torch.randn(rows, D, device=dev, generator=g).to(dtype)
     q = torch.randn(S, G, D, device=dev, generator=g).to(dtype)
-    split = Kx.split_rows(dtype, D)
+    if tiles <= 0 or cluster <= 0:  # the library's launch-shape choice
+        split, cluster = Kx.attn_launch_shape(dtype, D, cap)
+    else:
+        split = Kx.split_rows(dtype, D) * tiles
     work = torch.from_numpy(Kx.build_work_table(cap, split, cluster)).to(dev)
     scratch = Kx.AttnScratch(dev, work.shape[0], G, D, S)
     ca = [s for s in range(S) if lens[s] >= a1]
@@ -49,9 +52,9 @@ def build_layer(dev, lens, a0, a1, G, D, cluster, seed):
     args = Kx.make_attn_args(dtype, S, G, D, ks, vs, torch.from_numpy(base).to(dev),
                              torch.tensor(lens, dtype=torch.int32, device=dev), work, cluster, D ** -0.5,
                              scratch, seg_cap=torch.from_numpy(cap.astype(np.int32)).to(dev), num_kv_heads=S,
-                             score=score)
+                             score=score, split=split)
     nbytes = int(np.sum(lens)) * D * 2 * 2 + S * G * D * 2 * 2 + 8 * len(ca) * n_a
-    keep = (ks, vs, work, scratch, score, base)
+    keep = (ks, vs, work, scratch, score, base, split, cluster)
     return args, q, torch.empty_like(q), nbytes, keep
 
 
@@ -59,13 +62,14 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--layers", type=int, default=8)
     ap.add_argument("--reps", type=int, default=20)
-    ap.add_argument("--cluster", type=int, default=8)
+    ap.add_argument("--cluster", type=int, default=0, help="CTAs per cluster (0: library choice)")
     ap.add_argument("--class-a", type=int, default=15100)
     ap.add_argument("--class-b", type=int, default=2300)
+    ap.add_argument("--tiles", type=int, default=0, help="128-row tiles streamed per CTA (0: library choice)")
     a = ap.parse_args()
     dev = torch.device("cuda:0")
     lens = [a.class_a, a.class_a] + [a.class_b] * 6
-    layers = [build_layer(dev, lens, 4, 15004, 4, 128, a.cluster, seed=l) for l in range(a.layers)]
+    layers = [build_layer(dev, lens, 4, 15004, 4, 128, a.cluster, seed=l, tiles=a.tiles) for l in range(a.layers)]
     st = torch.cuda.current_stream().cuda_stream
     for args, q, out, _, _ in layers:
         Kx.launch_attn(args, q, None, None, out, st)
@@ -82,7 +86,7 @@ def main():
     us = e0.elapsed_time(e1) * 1e3 / n
     nbytes = layers[0][3]
     print(json.dumps({"us_per_launch": us, "bytes_per_launch": nbytes, "gbs": nbytes / (us * 1e-6) / 1e9,
-                      "launches": n, "cluster": a.cluster, "lens": lens}))
+                      "launches": n, "cluster": layers[0][4][7], "split_rows": layers[0][4][6], "lens": lens}))
 
 
 if __name__ == "__main__":
