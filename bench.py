@@ -30,7 +30,12 @@ so they do exactly the work the model run did.
 
 ``--impl reference`` times that CPU path alone (rank 0; other ranks exit).
 With torchrun, every rank runs its own replica (request sharding, weak
-scaling); value = all ranks' tokens / max-over-ranks time.
+scaling); value = all ranks' tokens / max-over-ranks time.  ``--parallel tp``
+instead shards the one request by kv head (wnw_b200.tp): rank r owns kv heads
+[r*8/N, (r+1)*8/N) of every layer, the step adds each layer's o_proj partial
+(the rank's query heads x its slice of a random o_proj weight) and its NCCL
+all-reduce, and the class-A scores are summed over the ranks before top-k
+(strong scaling; value = the request's tokens / max-over-ranks time).
 """
 from __future__ import annotations
 
@@ -63,6 +68,8 @@ def parse():
     ap.add_argument("--cpu-steps", type=int, default=3, help="oracle steps in the bounded CPU sample")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--profile", action="store_true", help="short run for ncu (no clocks, no CPU leg)")
+    ap.add_argument("--parallel", default="replicas", choices=["replicas", "tp"],
+                    help="N>1: independent per-request replicas, or one request sharded by kv head")
     return ap.parse_args()
 
 
@@ -164,14 +171,72 @@ def record(dev, n_steps, seed):
     return rec
 
 
-def fresh_cache(rec, dev, n_steps):
+class Shard:
+    """The slice of the hot path one rank runs: kv heads [h0, h1) of every
+    layer (all of them for replicas), plus -- tensor parallel -- the o_proj
+    slice of those heads' query heads and the NCCL group of the exchanges."""
+
+    def __init__(self, dev, rank=0, world=1, tp=False, seed=0):
+        from wnw_b200.tp import head_range
+        self.tp, self.rank, self.world = tp, rank, world
+        H, G, D = MODEL["Hkv"], MODEL["Hq"] // MODEL["Hkv"], MODEL["D"]
+        self.h0, self.h1 = head_range(rank, world, H) if tp else (0, H)
+        self.Hkv = self.h1 - self.h0
+        self.Hq = self.Hkv * G
+        self.wo = None
+        if tp:
+            g = torch.Generator(device=dev).manual_seed(seed + 17 * rank)
+            self.wo = [(torch.randn(MODEL["hidden"], self.Hq * D, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+                       for _ in range(MODEL["L"])]
+
+    def cfg(self, cfg):
+        from wnw_b200.tp import shard_config
+        if not self.tp:
+            return cfg
+        return shard_config(cfg, self.rank, self.world, MODEL["L"], MODEL["Hkv"], MODEL["Hq"])
+
+    def score_reduce(self):
+        from wnw_b200.tp import ScoreReducer
+        return ScoreReducer() if self.tp and self.world > 1 else None
+
+    def prefill(self, ca, ph, k, v):
+        """This rank's prefill hook inputs.  The recorded class-A scores are
+        the layer totals; under tensor parallelism the cache sums the ranks'
+        prefill scores, so rank 0 carries the totals and the others zeros."""
+        if not self.tp:
+            return ca, ph, k, v
+        if self.rank:
+            ca = [torch.zeros_like(x) if x is not None else None for x in ca]
+        return ca, [r[self.h0:self.h1] for r in ph], k[:, self.h0:self.h1], v[:, self.h0:self.h1]
+
+    def step_inputs(self, steps):
+        """Per step and layer (q_flat, k, v) of this rank's heads, contiguous."""
+        from wnw_b200.tp import slice_flat
+        if not self.tp:
+            return steps
+        H = MODEL["Hkv"]
+        return [[(slice_flat(q, self.h0, self.h1, H).contiguous(), k[:, self.h0:self.h1].contiguous(),
+                  v[:, self.h0:self.h1].contiguous()) for q, k, v in st] for st in steps]
+
+    def o_proj(self, l, out):
+        """The layer's row-parallel o_proj: this rank's partial sum, all-reduced."""
+        if not self.tp:
+            return out
+        y = out.reshape(1, -1) @ self.wo[l].t()
+        if self.world > 1:
+            torch.distributed.all_reduce(y)
+        return y
+
+
+def fresh_cache(rec, dev, n_steps, shard=None):
     from wnw_b200.cache import B200WnWCache
-    c = B200WnWCache(rec["cfg"], MODEL["L"], MODEL["Hkv"], MODEL["Hq"], MODEL["D"], dev,
-                     max_decode_tokens=n_steps + 8)
+    shard = shard or Shard(dev)
+    c = B200WnWCache(shard.cfg(rec["cfg"]), MODEL["L"], shard.Hkv, shard.Hq, MODEL["D"], dev,
+                     max_decode_tokens=n_steps + 8, score_reduce=shard.score_reduce())
     a0, a1 = rec["audio"]
     c.setup_audio(torch.tensor([a0]), torch.tensor([a1]), None)
     for l, ca, ph, k, v in rec["prefill"]:
-        c.prefill_after_attn(l, ca, ph, k, v)
+        c.prefill_after_attn(l, *shard.prefill(ca, ph, k, v))
     c.prefill_all_layers_done()
     return c
 
@@ -214,17 +279,18 @@ def attention_replay(cache, qs, reps):
     return us, nbytes, n
 
 
-def run_value(rec, dev, K, W):
+def run_value(rec, dev, K, W, shard=None):
     """Timed replay with the inputs resident in HBM."""
     from wnw_b200 import kernels as Kx
-    cache = fresh_cache(rec, dev, K + W)
-    steps, scale, L = rec["steps"], rec["scale"], MODEL["L"]
+    shard = shard or Shard(dev)
+    cache = fresh_cache(rec, dev, K + W, shard)
+    steps, scale, L = shard.step_inputs(rec["steps"]), rec["scale"], MODEL["L"]
 
     def one(i):
         for l in range(L):
             q, k, v = steps[i][l]
             kk, vv, cu, _ = cache.decode_before_attn(l, k, v)
-            cache.fused_decode_attention(l, q, None, kk, vv, cu, scale)
+            shard.o_proj(l, cache.fused_decode_attention(l, q, None, kk, vv, cu, scale))
         cache.decode_all_layers_done()
 
     for i in range(W):
@@ -232,6 +298,9 @@ def run_value(rec, dev, K, W):
     fetched = 0
     launches0 = Kx.LAUNCHES[0]
     torch.cuda.synchronize()
+    if shard.world > 1:
+        torch.distributed.barrier()
+        torch.cuda.synchronize()
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
     t0.record()
@@ -242,18 +311,22 @@ def run_value(rec, dev, K, W):
     torch.cuda.nvtx.range_pop()
     t1.record()
     torch.cuda.synchronize()
+    if shard.world > 1:
+        torch.distributed.barrier()
+        torch.cuda.synchronize()
     launches = Kx.LAUNCHES[0] - launches0
     total_ms = t0.elapsed_time(t1)
     us, nbytes, n = attention_replay(cache, [steps[W + K - 1][l][0] for l in range(L)], reps=10)
     return dict(ms=total_ms, attn_us=us, attn_bytes=nbytes, attn_n=n, launches=launches, fetched_rows=fetched)
 
 
-def run_e2e(rec, dev, K, W):
+def run_e2e(rec, dev, K, W, shard=None):
     """Hook API with host buffers: per step H2D of all layers' q/k/v from
-    pinned memory and D2H of all layers' attention outputs."""
-    cache = fresh_cache(rec, dev, K + W)
-    steps, scale, L = rec["steps"], rec["scale"], MODEL["L"]
-    q0, k0, _ = steps[0][0]
+    pinned memory and D2H of all layers' outputs (attention outputs; under
+    tensor parallelism the all-reduced o_proj rows)."""
+    shard = shard or Shard(dev)
+    cache = fresh_cache(rec, dev, K + W, shard)
+    steps, scale, L = shard.step_inputs(rec["steps"]), rec["scale"], MODEL["L"]
     host_in = [[torch.empty(x.shape, dtype=x.dtype).pin_memory() for x in steps[i][l]]
                for i in range(W + K) for l in range(L)]
     for i in range(W + K):
@@ -261,7 +334,8 @@ def run_e2e(rec, dev, K, W):
             for j in range(3):
                 host_in[i * L + l][j].copy_(steps[i][l][j])
     dev_in = [torch.empty_like(x, device=dev) for x in steps[0][0]]
-    host_out = torch.empty((L,) + tuple(q0.shape), dtype=q0.dtype).pin_memory()
+    out_shape = (1, MODEL["hidden"]) if shard.tp else tuple(steps[0][0][0].shape)
+    host_out = torch.empty((L,) + out_shape, dtype=torch.bfloat16).pin_memory()
     in_bytes = sum(x.numel() * x.element_size() for x in steps[0][0]) * L
     out_bytes = host_out.numel() * host_out.element_size()
     outs = [None] * L
@@ -270,7 +344,7 @@ def run_e2e(rec, dev, K, W):
         for l in range(L):
             q, k, v = (d.copy_(h, non_blocking=True) for d, h in zip(dev_in, host_in[i * L + l]))
             kk, vv, cu, _ = cache.decode_before_attn(l, k, v)
-            outs[l] = cache.fused_decode_attention(l, q, None, kk, vv, cu, scale)
+            outs[l] = shard.o_proj(l, cache.fused_decode_attention(l, q, None, kk, vv, cu, scale))
         cache.decode_all_layers_done()
         for l in range(L):
             host_out[l].copy_(outs[l], non_blocking=True)
@@ -279,7 +353,9 @@ def run_e2e(rec, dev, K, W):
     for i in range(W):
         one(i)
     torch.cuda.synchronize()
-    t0 = time.perf_counter()
+    if shard.world > 1:
+        torch.distributed.barrier()
+        torch.cuda.synchronize()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record()
@@ -287,7 +363,9 @@ def run_e2e(rec, dev, K, W):
         one(i)
     e1.record()
     torch.cuda.synchronize()
-    del t0
+    if shard.world > 1:
+        torch.distributed.barrier()
+        torch.cuda.synchronize()
     return dict(ms=e0.elapsed_time(e1), in_bytes=in_bytes, out_bytes=out_bytes)
 
 
@@ -442,7 +520,12 @@ def main():
                 "inputs": "q/k/v recorded from the random-init decoder, replayed",
                 "l2": "per-step K/V working set > L2 (30 layers x ~25 MB)",
                 "parallelism": f"request-sharded replicas x{world}"}
-    rec = record(dev, W + K, seed=1000 + rank)
+    tp = a.parallel == "tp" and a.impl == "b200"
+    if tp:
+        cfg_json["parallelism"] = f"tp{world} (kv heads sharded, o_proj all-reduce per layer)"
+    # replicas record their own request; tensor-parallel ranks share one
+    rec = record(dev, W + K, seed=1000 + (0 if tp else rank))
+    shard = Shard(dev, rank, world, tp=tp, seed=2000)
 
     if a.impl == "reference":
         n = max(1, min(a.cpu_steps, K))
@@ -459,8 +542,8 @@ def main():
         return
 
     with Clocks(local) as clk:
-        val = run_value(rec, dev, K, W)
-    e2e = run_e2e(rec, dev, K, W)
+        val = run_value(rec, dev, K, W, shard)
+    e2e = run_e2e(rec, dev, K, W, shard)
     ms = val["ms"]
     if dist:
         t = torch.tensor([ms, e2e["ms"]], device=dev)
@@ -469,7 +552,7 @@ def main():
         torch.distributed.barrier()
     else:
         e2e_ms = e2e["ms"]
-    tokens = world * 1 * K
+    tokens = (1 if tp else world) * 1 * K
     peak, peak_kind = peaks()
     link = h2d_link_probe(dev)
     fetch_bytes = val["fetched_rows"] / K * MODEL["D"] * 2 * 2
@@ -477,7 +560,7 @@ def main():
     line = {
         "metric": "decode tokens/s (WnW hot path) and decode-attention HBM GB/s", "value": tokens / (ms * 1e-3),
         "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": ms / K,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "higher_is_better": True, "scaling": "strong" if tp else "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (random-init decoder, N(0,0.02) audio embeddings)", "config": cfg_json,
         "e2e": {"value": tokens / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": e2e["in_bytes"],
                 "d2h_bytes_per_step": e2e["out_bytes"]},

@@ -284,6 +284,11 @@ wnw_status wnw_fetch_layers(const void* src_k, const void* src_v, int64_t row_by
                             int num_layers, void* dst_k, void* dst_v, int max_ctas, void* stream,
                             void* const* events);
 
+/* Make `stream` wait for `event` (cudaStreamWaitEvent; both as void*).  No
+ * reference counterpart: the per-layer "rows of layer l have landed" wait of
+ * the decode loop in one call. */
+wnw_status wnw_stream_wait_event(void* stream, void* event);
+
 /* Async H2D copy of n bytes for K and V on `stream`, then record `event`
  * (cudaEvent_t as void*, may be NULL) -- one per layer. */
 wnw_status wnw_h2d_async(void* dst_k, void* dst_v, const void* src_k, const void* src_v,

@@ -87,11 +87,14 @@ class B200WnWCache(FlatVarlenCache):
                            reads the offloaded rows straight from pinned host
                            memory; "dma": host threads gather them into pinned
                            staging and cudaMemcpyAsync copies each layer;
-      fetch_threads     -- host threads of the "dma" gather.
+      fetch_threads     -- host threads of the "dma" gather;
+      score_reduce      -- tensor parallelism by kv head (wnw_b200.tp): a
+                           callable that sums the class-A score accumulator
+                           over the ranks before every chunk selection.
     """
 
     def __init__(self, config, num_layers, num_kv_heads, num_q_heads, head_dim, device, adapter=None, *,
-                 max_decode_tokens=256, fetch_mode="zerocopy", fetch_threads=8, fetch_ctas=512):
+                 max_decode_tokens=256, fetch_mode="zerocopy", fetch_threads=8, fetch_ctas=512, score_reduce=None):
         super().__init__(num_layers, num_kv_heads, num_q_heads, head_dim, device, adapter)
         if self.device.type != "cuda":
             raise RuntimeError("B200WnWCache needs a CUDA device; the CPU oracle lives in the test suite")
@@ -106,6 +109,9 @@ class B200WnWCache(FlatVarlenCache):
         self.fetch_mode = fetch_mode
         self.fetch_threads = int(fetch_threads)
         self.fetch_ctas = int(fetch_ctas)
+        self.score_reduce = score_reduce
+        self._dev_index = self.device.index if self.device.index is not None else torch.cuda.current_device()
+        self._rb_args = [None] * num_layers
         self._class_b_heads_by_layer = [config.get_layer_class_b(l) for l in range(num_layers)]
         self.batch_size = 0
         self.prefilled = False
@@ -237,6 +243,8 @@ class B200WnWCache(FlatVarlenCache):
             else:
                 sel[o0:o1] = 1.0
             self._prefill_scores[b] = []
+        if self.score_reduce is not None:
+            sel = self.score_reduce(sel)
         top = self._select_topk(sel)
         for b in range(B):
             needed = sorted({s for c in top[b] for s in self.chunk_to_segs[b][c]})
@@ -359,6 +367,7 @@ class B200WnWCache(FlatVarlenCache):
             self._scratch = Kx.AttnScratch(dev, n_max, G, D, S)
         del max_rows
         self._attn_args = [None] * L  # launch arguments, built lazily per (layer, scale)
+        self._rb_args = [None] * L    # rebuild arguments, likewise
 
     def _grow(self, l):
         """Give layer l another ``max_decode_tokens`` rows per slot."""
@@ -474,15 +483,16 @@ class B200WnWCache(FlatVarlenCache):
         rows stored before this step's token (cache.py:487-515 contract)."""
         l = layer_idx
         if self._pending and self._layer_chg[l]:
-            recs = list(self._plan_records(l))
-            if any(nl + 1 > self._cap_host[l, seg] for seg, nl in recs):
+            new_lens = self._next_lens[l]
+            if (new_lens + 1 > self._cap_host[l]).any():
                 self._grow(l)
-            torch.cuda.current_stream(self.device).wait_event(self._events[l])
-            Kx.rebuild_layer(self.k_store[l], self.v_store[l], self._seg_base[l], self._seg_len[l],
-                             self._seg_cap[l], self._land_k, self._land_v, self._plan_dev, l,
-                             self._move_k, self._move_v, self._rb_status, self._scratch.err)
-            for seg, new_len in recs:
-                self._len_host[l, seg] = new_len
+            stream = self._raw_stream()
+            N.call("wnw_stream_wait_event", stream, self._event_handles[l])
+            st = N.lib.wnw_rebuild_segments(*self._rebuild_args(l), stream)
+            if st:
+                N.check(st, "wnw_rebuild_segments")
+            Kx.LAUNCHES[0] += 2
+            self._len_host[l] = new_lens
         if (self._len_host[l] + 1 > self._cap_host[l]).any():
             self._grow(l)
         if l == self.num_layers - 1:
@@ -495,9 +505,24 @@ class B200WnWCache(FlatVarlenCache):
         self.seq_lens[l] = (self._len_host[l] + 1).tolist()
         return self.k_store[l], self.v_store[l], self._seg_len[l], int(self._len_host[l].max()) + 1
 
-    def _plan_records(self, l):
-        r = Kx.plan_record(self._plan_np, l)
-        return zip(r["seg"].tolist(), r["new_len"].tolist())
+    def _raw_stream(self):
+        """cudaStream_t of the current torch stream on this cache's device."""
+        return torch._C._cuda_getCurrentRawStream(self._dev_index)
+
+    def _rebuild_args(self, l):
+        """wnw_rebuild_segments arguments of layer l (all but the stream);
+        rebuilt whenever a buffer they point at is reallocated."""
+        a = self._rb_args[l]
+        if a is None:
+            mk, mv = self._move_k, self._move_v
+            a = self._rb_args[l] = (
+                N.dtype_code(self.dtype), self.head_dim, self.k_store[l].data_ptr(), self.v_store[l].data_ptr(),
+                self._seg_base[l].data_ptr(), self._seg_len[l].data_ptr(), self._seg_cap[l].data_ptr(),
+                self._land_k.data_ptr() if self._land_k is not None else None,
+                self._land_v.data_ptr() if self._land_v is not None else None, self._plan_dev.data_ptr(), l,
+                mk.data_ptr() if mk is not None else None, mv.data_ptr() if mv is not None else None,
+                int(mk.shape[0]) if mk is not None else 0, self._rb_status.data_ptr(), self._scratch.err.data_ptr())
+        return a
 
     def _score_args(self, l):
         if not self._score_groups[l]:
@@ -532,7 +557,7 @@ class B200WnWCache(FlatVarlenCache):
             cached = self._attn_args[l] = (scale, sep, args)
         _, sep, args = cached
         out = torch.empty_like(qf)
-        Kx.launch_attn(args, qf, nk, nv, out, torch.cuda.current_stream(self.device).cuda_stream)
+        Kx.launch_attn(args, qf, nk, nv, out, self._raw_stream())
         if sep:
             score = self._score_args(l)  # rescore with the reference's 1/sqrt(d) (the append is idempotent)
             Kx.decode_attention(qf, self.k_store[l], self.v_store[l], self._seg_base[l], self._seg_len[l],
@@ -555,6 +580,8 @@ class B200WnWCache(FlatVarlenCache):
                               self.num_kv_groups, self.score_offsets, self.max_audio, self.score_accumulator)
         else:
             self.score_accumulator.zero_()
+        if self.score_reduce is not None:
+            self.score_accumulator.copy_(self.score_reduce(self.score_accumulator))
         if self.config.top_k_chunks > 0 and self.max_audio > 0:
             Kx.chunk_topk(self.score_accumulator, self.score_offsets, self.max_audio, self.config.stride_tokens,
                           self.segs_per_chunk, self.config.top_k_chunks, self._topk_dev)
@@ -591,12 +618,16 @@ class B200WnWCache(FlatVarlenCache):
             n = 1 << (plan.size - 1).bit_length()
             self._plan_host = torch.zeros(n, dtype=torch.int32).pin_memory()
             self._plan_dev = torch.zeros(n, dtype=torch.int32, device=self.device)
+            self._rb_args = [None] * L
         self._plan_host[:plan.size].copy_(torch.from_numpy(plan))
         self._plan_np = plan.copy()
         moved = 0
         for l in range(L):
             self._layer_chg[l] = int(plan[int(plan[l])])
             moved = max(moved, int(plan[int(plan[l]) + 1]))
+        # stored rows per slot after the rebuild: the planner's new lengths
+        # (planner.cpp:278-357) count this step's token, every slot of every layer
+        self._next_lens = self._plan_bufs[3].astype(np.int64) - 1
         self._ensure_move_capacity(moved)
         rows, rng = self._planner.layer_transfer()
         self._layer_rows = rows.astype(np.int64)
@@ -643,6 +674,7 @@ class B200WnWCache(FlatVarlenCache):
             n = 1 << max(0, rows - 1).bit_length()
             self._move_k = torch.empty(n, self.head_dim, dtype=self.dtype, device=self.device)
             self._move_v = torch.empty(n, self.head_dim, dtype=self.dtype, device=self.device)
+            self._rb_args = [None] * self.num_layers
 
     def _restore_dev_ptrs(self):
         if getattr(self, "_restore_ptrs", None) is None:
@@ -659,6 +691,7 @@ class B200WnWCache(FlatVarlenCache):
             n = 1 << max(0, rows - 1).bit_length()
             self._land_k = torch.empty(n, D, dtype=dt, device=self.device)
             self._land_v = torch.empty(n, D, dtype=dt, device=self.device)
+            self._rb_args = [None] * self.num_layers
             if self.fetch_mode == "dma":
                 self._stage_k = torch.empty(n, D, dtype=dt).pin_memory()
                 self._stage_v = torch.empty(n, D, dtype=dt).pin_memory()

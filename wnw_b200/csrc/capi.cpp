@@ -104,6 +104,16 @@ wnw_status wnw_gather_rows(const void* src_k, const void* src_v, int64_t row_byt
   return WNW_OK;
 }
 
+wnw_status wnw_stream_wait_event(void* stream, void* event) {
+  if (!event) {
+    wnw::set_error("null event");
+    return WNW_ERR_INVALID;
+  }
+  const cudaError_t e = cudaStreamWaitEvent(static_cast<cudaStream_t>(stream), static_cast<cudaEvent_t>(event), 0);
+  if (e != cudaSuccess) return wnw::cuda_status(e, "cudaStreamWaitEvent");
+  return WNW_OK;
+}
+
 wnw_status wnw_h2d_async(void* dst_k, void* dst_v, const void* src_k, const void* src_v, int64_t bytes,
                          void* stream, void* event) {
   cudaStream_t s = static_cast<cudaStream_t>(stream);

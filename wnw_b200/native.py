@@ -93,6 +93,7 @@ _sig("wnw_planner_get_changes", _S, P, C.c_int, P, C.c_int, C.POINTER(C.c_int), 
 _sig("wnw_planner_device_plan", _S, P, P, C.c_int64, C.POINTER(C.c_int64))
 _sig("wnw_gather_rows", _S, P, P, C.c_int64, P, C.c_int, P, P, C.c_int)
 _sig("wnw_h2d_async", _S, P, P, P, P, C.c_int64, P, P)
+_sig("wnw_stream_wait_event", _S, P, P)
 _sig("wnw_host_device_pointer", _S, P, C.POINTER(P))
 _sig("wnw_fetch_rows", _S, P, P, C.c_int64, P, P, C.c_int, P, P, C.c_int, P)
 _sig("wnw_fetch_layers", _S, P, P, C.c_int64, P, P, P, C.c_int, P, P, C.c_int, P, P)
@@ -108,7 +109,7 @@ EXPORTS = [
     "wnw_planner_set_loaded", "wnw_planner_set_seq_lens", "wnw_planner_get_loaded_segments",
     "wnw_planner_compute_and_prepare", "wnw_planner_get_evictions", "wnw_planner_get_cpu_ranges",
     "wnw_planner_get_layer_transfer", "wnw_planner_get_changes", "wnw_planner_device_plan",
-    "wnw_gather_rows", "wnw_h2d_async", "wnw_host_device_pointer", "wnw_fetch_rows",
+    "wnw_gather_rows", "wnw_h2d_async", "wnw_stream_wait_event", "wnw_host_device_pointer", "wnw_fetch_rows",
     "wnw_fetch_layers",
 ]
 
