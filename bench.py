@@ -70,6 +70,8 @@ def parse():
     ap.add_argument("--profile", action="store_true", help="short run for ncu (no clocks, no CPU leg)")
     ap.add_argument("--parallel", default="replicas", choices=["replicas", "tp"],
                     help="N>1: independent per-request replicas, or one request sharded by kv head")
+    ap.add_argument("--tp-exchange", default="fused", choices=["fused", "nccl"],
+                    help="tensor parallel: o_proj GEMV + all-reduce as one NVLink kernel, or cuBLAS + NCCL")
     return ap.parse_args()
 
 
@@ -176,8 +178,8 @@ class Shard:
     layer (all of them for replicas), plus -- tensor parallel -- the o_proj
     slice of those heads' query heads and the NCCL group of the exchanges."""
 
-    def __init__(self, dev, rank=0, world=1, tp=False, seed=0):
-        from wnw_b200.tp import head_range
+    def __init__(self, dev, rank=0, world=1, tp=False, seed=0, exchange="fused"):
+        from wnw_b200.tp import OprojAllReduce, head_range
         self.tp, self.rank, self.world = tp, rank, world
         H, G, D = MODEL["Hkv"], MODEL["Hq"] // MODEL["Hkv"], MODEL["D"]
         self.h0, self.h1 = head_range(rank, world, H) if tp else (0, H)
@@ -188,6 +190,12 @@ class Shard:
             g = torch.Generator(device=dev).manual_seed(seed + 17 * rank)
             self.wo = [(torch.randn(MODEL["hidden"], self.Hq * D, device=dev, generator=g) * 0.02).to(torch.bfloat16)
                        for _ in range(MODEL["L"])]
+        self.ex = OprojAllReduce(dev, MODEL["hidden"]) if tp and exchange == "fused" else None
+
+    def close(self):
+        if self.ex is not None:
+            self.ex.close()
+            self.ex = None
 
     def cfg(self, cfg):
         from wnw_b200.tp import shard_config
@@ -222,6 +230,8 @@ class Shard:
         """The layer's row-parallel o_proj: this rank's partial sum, all-reduced."""
         if not self.tp:
             return out
+        if self.ex is not None:  # one kernel: GEMV + all-reduce over NVLink peer memory
+            return self.ex(out.reshape(1, -1), self.wo[l])
         y = out.reshape(1, -1) @ self.wo[l].t()
         if self.world > 1:
             torch.distributed.all_reduce(y)
@@ -525,7 +535,9 @@ def main():
         cfg_json["parallelism"] = f"tp{world} (kv heads sharded, o_proj all-reduce per layer)"
     # replicas record their own request; tensor-parallel ranks share one
     rec = record(dev, W + K, seed=1000 + (0 if tp else rank))
-    shard = Shard(dev, rank, world, tp=tp, seed=2000)
+    shard = Shard(dev, rank, world, tp=tp, seed=2000, exchange=a.tp_exchange)
+    if tp:
+        cfg_json["parallelism"] += f", exchange {a.tp_exchange}"
 
     if a.impl == "reference":
         n = max(1, min(a.cpu_steps, K))
@@ -544,6 +556,8 @@ def main():
     with Clocks(local) as clk:
         val = run_value(rec, dev, K, W, shard)
     e2e = run_e2e(rec, dev, K, W, shard)
+    if shard.ex is not None:
+        shard.ex.check()
     ms = val["ms"]
     if dist:
         t = torch.tensor([ms, e2e["ms"]], device=dev)
@@ -588,6 +602,7 @@ def main():
                                 "sample": f"{n} decode steps (all 30 layers) replayed by the CPU oracle"}
     if rank == 0:
         print(json.dumps(line), flush=True)
+    shard.close()
     if dist:
         torch.distributed.destroy_process_group()
 

@@ -37,6 +37,7 @@ typedef enum wnw_dtype { WNW_F32 = 0, WNW_F16 = 1, WNW_BF16 = 2 } wnw_dtype;
 #define WNW_DEVERR_MBAR_TIMEOUT 1   /* a TMA mbarrier wait ran out           */
 #define WNW_DEVERR_LEN_MISMATCH 2   /* rebuild plan disagrees with seg_len   */
 #define WNW_DEVERR_CAPACITY 4       /* a segment would exceed its slot       */
+#define WNW_DEVERR_PEER_TIMEOUT 8   /* a tensor-parallel peer's partials did not arrive */
 
 int wnw_abi_version(void);
 const char* wnw_status_string(wnw_status s);
@@ -293,6 +294,49 @@ wnw_status wnw_stream_wait_event(void* stream, void* event);
  * (cudaEvent_t as void*, may be NULL) -- one per layer. */
 wnw_status wnw_h2d_async(void* dst_k, void* dst_v, const void* src_k, const void* src_v,
                          int64_t bytes, void* stream, void* event);
+
+/* ------------------------------------------------------------------------
+ * Tensor parallelism by kv head: the per-layer o_proj exchange (no reference
+ * counterpart -- the reference runs one request per GPU; its o_proj is the
+ * model's dense projection, src/algorithms/wnw/code/session.py drives it).
+ *
+ * y[B, N] = sum over ranks r of x_r[B, K] . W_r[N, K]^T, where x_r is rank
+ * r's attention output (its query heads) and W_r the matching column slice of
+ * o_proj, in one kernel per rank: each CTA computes its chunk of this rank's
+ * partial sums, stores them into every rank's receive buffer over NVLink,
+ * raises a per-chunk flag there, waits for every rank's flag in its own
+ * memory and adds the partials in rank order (bit-identical y on every rank).
+ * recv[p] / flags[p]: rank p's buffers as mapped in this process
+ * (wnw_ipc_open; p == rank: this rank's own allocation), sized
+ *   recv:  2 * world * batch * n_out fp32,
+ *   flags: world * wnw_oproj_allreduce_chunks(n_out) u32, zeroed once.
+ * epoch: 1, 2, 3, ... per call, the same on every rank.  A peer whose flag
+ * does not arrive within timeout_ns (0: 2 s) sets WNW_DEVERR_PEER_TIMEOUT in
+ * *err and the kernel returns with zeros in y. */
+#define WNW_TP_MAX_RANKS 8
+typedef struct {
+  int dtype;                            /* WNW_BF16 or WNW_F16 (x, W, y) */
+  int batch, n_out, k_in;               /* B <= 8, N, K (K % 8 == 0)     */
+  int rank, world;                      /* world <= WNW_TP_MAX_RANKS     */
+  const void* x;                        /* [B, K]                        */
+  const void* w;                        /* [N, K] row-major              */
+  void* y;                              /* [B, N]                        */
+  float* recv[WNW_TP_MAX_RANKS];
+  uint32_t* flags[WNW_TP_MAX_RANKS];
+  uint32_t epoch;
+  uint64_t timeout_ns;
+  int32_t* err;
+} wnw_oproj_allreduce_args;
+wnw_status wnw_oproj_allreduce(const wnw_oproj_allreduce_args* a, void* stream);
+/* CTAs (and flag slots per rank) of wnw_oproj_allreduce for n_out outputs. */
+int wnw_oproj_allreduce_chunks(int n_out);
+
+/* Device buffers shared across processes (CUDA IPC): allocate + zero + export
+ * a 64-byte handle; open a peer's handle; close (owned: cudaFree, else
+ * cudaIpcCloseMemHandle). */
+wnw_status wnw_ipc_alloc(int64_t bytes, void** ptr, void* handle);
+wnw_status wnw_ipc_open(const void* handle, void** ptr);
+wnw_status wnw_ipc_close(void* ptr, int owned);
 
 #ifdef __cplusplus
 }

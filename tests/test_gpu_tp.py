@@ -117,3 +117,108 @@ def test_two_gpu_tensor_parallel_cache_matches_oracle():
     for p in ps:
         p.join(timeout=120)
     assert res == {0: "ok", 1: "ok"}, res
+
+
+def _oproj_ref(xs, ws):
+    return sum(x.float().cpu() @ w.float().cpu().t() for x, w in zip(xs, ws))
+
+
+def test_oproj_allreduce_single_rank():
+    """world 1: the fused kernel is the o_proj GEMV (its own receive buffer)."""
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA GPU")
+    from wnw_b200.tp import OprojAllReduce
+    dev = torch.device("cuda:0")
+    g = torch.Generator(device="cpu").manual_seed(3)
+    for B, N, K in ((1, 3072, 1024), (3, 1000, 256), (8, 64, 4096)):
+        x = torch.randn(B, K, generator=g).to(torch.bfloat16).to(dev)
+        w = (torch.randn(N, K, generator=g) * 0.05).to(torch.bfloat16).to(dev)
+        ex = OprojAllReduce(dev, N, batch=B)
+        for _ in range(3):  # successive epochs reuse both receive parities
+            y = ex(x, w)
+        torch.cuda.synchronize()
+        ex.check()
+        ref = _oproj_ref([x], [w])
+        np.testing.assert_allclose(y.float().cpu().numpy(), ref.numpy(), atol=2e-2, rtol=2e-2)
+        ex.close()
+
+
+def test_oproj_allreduce_reports_missing_peer():
+    """A peer that never arrives: the wait runs out after its deadline, the
+    kernel sets WNW_DEVERR_PEER_TIMEOUT and returns zeros, and the context
+    stays usable (one GPU; the 'peer' is a second local buffer nobody fills)."""
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA GPU")
+    import ctypes as C
+    from wnw_b200 import native as N
+    dev = torch.device("cuda:0")
+    B, Nout, K, world = 1, 512, 256, 2
+    nch = N.lib.wnw_oproj_allreduce_chunks(Nout)
+    bufs = [torch.zeros(2 * world * B * Nout + world * nch + 64, dtype=torch.float32, device=dev) for _ in range(2)]
+    x = torch.ones(B, K, dtype=torch.bfloat16, device=dev)
+    w = torch.ones(Nout, K, dtype=torch.bfloat16, device=dev)
+    y = torch.full((B, Nout), 7.0, dtype=torch.bfloat16, device=dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    a = N.OprojAllReduceArgs()
+    a.dtype, a.batch, a.n_out, a.k_in, a.rank, a.world = N.BF16, B, Nout, K, 0, world
+    for p in range(world):
+        a.recv[p] = bufs[p].data_ptr()
+        a.flags[p] = bufs[p].data_ptr() + 4 * 2 * world * B * Nout
+    a.x, a.w, a.y, a.epoch, a.timeout_ns, a.err = x.data_ptr(), w.data_ptr(), y.data_ptr(), 1, 20_000_000, err.data_ptr()
+    N.check(N.lib.wnw_oproj_allreduce(C.byref(a), N.stream_ptr(None)))
+    torch.cuda.synchronize()
+    assert int(err.item()) & N.DEVERR_PEER_TIMEOUT
+    assert torch.count_nonzero(y).item() == 0
+    # the device is still usable
+    z = torch.arange(10, device=dev).sum()
+    assert int(z.item()) == 45
+
+
+def _oproj_rank(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    dev = torch.device(f"cuda:{rank}")
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                           timeout=datetime.timedelta(seconds=120))
+    ex = None
+    try:
+        from wnw_b200.tp import OprojAllReduce
+        B, Nout, K = 2, 3072, 512
+        xs = [torch.randn(B, K, generator=torch.Generator().manual_seed(10 + r)).to(torch.bfloat16)
+              for r in range(world)]
+        ws = [(torch.randn(Nout, K, generator=torch.Generator().manual_seed(20 + r)) * 0.05).to(torch.bfloat16)
+              for r in range(world)]
+        ex = OprojAllReduce(dev, Nout, batch=B)
+        x, w = xs[rank].to(dev), ws[rank].to(dev)
+        for _ in range(5):
+            y = ex(x, w)
+        torch.cuda.synchronize()
+        ex.check()
+        ys = [torch.empty_like(y) for _ in range(world)]
+        dist.all_gather(ys, y)
+        assert all(torch.equal(ys[0], t) for t in ys), "ranks disagree"
+        np.testing.assert_allclose(y.float().cpu().numpy(), _oproj_ref(xs, ws).numpy(), atol=3e-2, rtol=2e-2)
+        q.put((rank, "ok"))
+    except Exception as e:
+        q.put((rank, repr(e)))
+    finally:
+        if ex is not None:
+            ex.close()
+        torch.cuda.synchronize()
+        dist.destroy_process_group()
+
+
+def test_two_gpu_oproj_allreduce():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    ps = [ctx.Process(target=_oproj_rank, args=(r, world, port, q)) for r in range(world)]
+    for p in ps:
+        p.start()
+    res = dict(q.get(timeout=600) for _ in range(world))
+    for p in ps:
+        p.join(timeout=120)
+    assert res == {0: "ok", 1: "ok"}, res

@@ -21,6 +21,7 @@ STATUS_NAMES = {0: "ok", 1: "invalid argument", 2: "CUDA error", 3: "capacity ex
 DEVERR_MBAR_TIMEOUT = 1
 DEVERR_LEN_MISMATCH = 2
 DEVERR_CAPACITY = 4
+DEVERR_PEER_TIMEOUT = 8
 
 F32, F16, BF16 = 0, 1, 2
 
@@ -48,6 +49,18 @@ class DecodeAttnArgs(C.Structure):
         ("out", P), ("scale", C.c_float),
         ("score_slot", P), ("audio_start", P), ("audio_end", P), ("logits", P), ("logits_off", P),
         ("stats", P), ("partials", P), ("counters", P), ("err", P), ("store_rows", C.c_int64),
+    ]
+
+
+TP_MAX_RANKS = 8
+
+
+class OprojAllReduceArgs(C.Structure):
+    _fields_ = [
+        ("dtype", C.c_int), ("batch", C.c_int), ("n_out", C.c_int), ("k_in", C.c_int),
+        ("rank", C.c_int), ("world", C.c_int), ("x", P), ("w", P), ("y", P),
+        ("recv", P * TP_MAX_RANKS), ("flags", P * TP_MAX_RANKS), ("epoch", C.c_uint32),
+        ("timeout_ns", C.c_uint64), ("err", P),
     ]
 
 
@@ -94,6 +107,11 @@ _sig("wnw_planner_device_plan", _S, P, P, C.c_int64, C.POINTER(C.c_int64))
 _sig("wnw_gather_rows", _S, P, P, C.c_int64, P, C.c_int, P, P, C.c_int)
 _sig("wnw_h2d_async", _S, P, P, P, P, C.c_int64, P, P)
 _sig("wnw_stream_wait_event", _S, P, P)
+_sig("wnw_oproj_allreduce_chunks", C.c_int, C.c_int)
+_sig("wnw_oproj_allreduce", _S, C.POINTER(OprojAllReduceArgs), P)
+_sig("wnw_ipc_alloc", _S, C.c_int64, C.POINTER(C.c_void_p), P)
+_sig("wnw_ipc_open", _S, P, C.POINTER(C.c_void_p))
+_sig("wnw_ipc_close", _S, P, C.c_int)
 _sig("wnw_host_device_pointer", _S, P, C.POINTER(P))
 _sig("wnw_fetch_rows", _S, P, P, C.c_int64, P, P, C.c_int, P, P, C.c_int, P)
 _sig("wnw_fetch_layers", _S, P, P, C.c_int64, P, P, P, C.c_int, P, P, C.c_int, P, P)
@@ -109,7 +127,8 @@ EXPORTS = [
     "wnw_planner_set_loaded", "wnw_planner_set_seq_lens", "wnw_planner_get_loaded_segments",
     "wnw_planner_compute_and_prepare", "wnw_planner_get_evictions", "wnw_planner_get_cpu_ranges",
     "wnw_planner_get_layer_transfer", "wnw_planner_get_changes", "wnw_planner_device_plan",
-    "wnw_gather_rows", "wnw_h2d_async", "wnw_stream_wait_event", "wnw_host_device_pointer", "wnw_fetch_rows",
+    "wnw_gather_rows", "wnw_h2d_async", "wnw_stream_wait_event", "wnw_oproj_allreduce",
+    "wnw_oproj_allreduce_chunks", "wnw_ipc_alloc", "wnw_ipc_open", "wnw_ipc_close", "wnw_host_device_pointer", "wnw_fetch_rows",
     "wnw_fetch_layers",
 ]
 

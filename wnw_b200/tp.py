@@ -21,6 +21,7 @@ independent per-request replicas (src/eval/launch_wnw.py), which
 from __future__ import annotations
 
 import copy
+import ctypes as C
 
 import torch
 
@@ -90,3 +91,91 @@ def slice_flat(x, h0, h1, num_kv_heads):
     """kv heads [h0, h1) of a segment-major [B * Hkv, ...] tensor."""
     B = x.shape[0] // num_kv_heads
     return x.reshape(B, num_kv_heads, *x.shape[1:])[:, h0:h1].reshape(-1, *x.shape[1:])
+
+
+class OprojAllReduce:
+    """The per-layer tensor-parallel exchange as one kernel
+    (``wnw_oproj_allreduce``): y = sum over ranks of x_r . W_r^T, the o_proj
+    GEMV of this rank's query heads fused with an all-reduce over NVLink
+    peer memory.  Receive buffers and flags are one CUDA-IPC allocation per
+    rank, mapped into every other rank's process once, here.
+
+    ``__call__`` must be issued by every rank of the group in the same
+    order (each call is one epoch); a rank whose peers do not arrive within
+    ``timeout_s`` gets zeros and ``check()`` raises."""
+
+    def __init__(self, dev, n_out, batch=1, dtype=torch.bfloat16, group=None, timeout_s=2.0):
+        from wnw_b200 import native as N
+        self.N = N
+        self.dev = torch.device(dev)
+        dist = torch.distributed
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_available() and dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if self.world > 1 else 0
+        if self.world > N.TP_MAX_RANKS:
+            raise ValueError(f"at most {N.TP_MAX_RANKS} ranks")
+        self.batch, self.n_out, self.dtype = batch, n_out, dtype
+        nch = N.lib.wnw_oproj_allreduce_chunks(n_out)
+        recv_bytes = (2 * self.world * batch * n_out * 4 + 255) // 256 * 256
+        total = recv_bytes + self.world * nch * 4
+        with torch.cuda.device(self.dev):
+            own, handle = C.c_void_p(), (C.c_char * 64)()
+            N.call("wnw_ipc_alloc", total, C.byref(own), handle)
+            self._own = own.value
+            self._peers = {}
+            bases = [None] * self.world
+            bases[self.rank] = self._own
+            if self.world > 1:
+                handles = [None] * self.world
+                dist.all_gather_object(handles, bytes(handle), group=group)
+                for p in range(self.world):
+                    if p != self.rank:
+                        ptr = C.c_void_p()
+                        N.call("wnw_ipc_open", C.create_string_buffer(handles[p], 64), C.byref(ptr))
+                        self._peers[p] = ptr.value
+                        bases[p] = ptr.value
+                dist.barrier(group=group)
+        self.err = torch.zeros(1, dtype=torch.int32, device=self.dev)
+        a = self.args = N.OprojAllReduceArgs()
+        a.dtype = N.dtype_code(dtype)
+        a.batch, a.n_out, a.rank, a.world = batch, n_out, self.rank, self.world
+        for p in range(self.world):
+            a.recv[p] = bases[p]
+            a.flags[p] = bases[p] + recv_bytes
+        a.timeout_ns = int(timeout_s * 1e9)
+        a.err = self.err.data_ptr()
+        self.epoch = 0
+
+    def __call__(self, x, w, y=None, stream=None):
+        """x [B, K] (this rank's heads), w [N, K] -> y [B, N], summed over ranks."""
+        a = self.args
+        if y is None:
+            y = torch.empty(x.shape[0], self.n_out, dtype=self.dtype, device=self.dev)
+        self.epoch += 1
+        a.epoch = self.epoch
+        a.k_in = x.shape[-1]
+        a.batch = x.shape[0]
+        a.x, a.w, a.y = x.data_ptr(), w.data_ptr(), y.data_ptr()
+        sp = stream.cuda_stream if stream is not None else torch._C._cuda_getCurrentRawStream(self.dev.index)
+        st = self.N.lib.wnw_oproj_allreduce(C.byref(a), sp)
+        if st:
+            self.N.check(st, "wnw_oproj_allreduce")
+        return y
+
+    def check(self):
+        """Raise if a peer's partials ever failed to arrive (host sync)."""
+        if int(self.err.item()) & self.N.DEVERR_PEER_TIMEOUT:
+            raise RuntimeError("tensor-parallel o_proj exchange: a peer's partial sums did not arrive in time")
+
+    def close(self):
+        """Unmap the peers' buffers and free this rank's (after a device sync)."""
+        if self._own is None:
+            return
+        torch.cuda.synchronize(self.dev)
+        for ptr in self._peers.values():
+            self.N.call("wnw_ipc_close", ptr, 0)
+        self._peers = {}
+        if self.world > 1:
+            torch.distributed.barrier(group=self.group)  # no peer still maps our buffer
+        self.N.call("wnw_ipc_close", self._own, 1)
+        self._own = None
