@@ -108,6 +108,7 @@ class OprojAllReduce:
         from wnw_b200 import native as N
         self.N = N
         self.dev = torch.device(dev)
+        self._dev_index = self.dev.index if self.dev.index is not None else torch.cuda.current_device()
         dist = torch.distributed
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_available() and dist.is_initialized() else 1
@@ -156,7 +157,7 @@ class OprojAllReduce:
         a.k_in = x.shape[-1]
         a.batch = x.shape[0]
         a.x, a.w, a.y = x.data_ptr(), w.data_ptr(), y.data_ptr()
-        sp = stream.cuda_stream if stream is not None else torch._C._cuda_getCurrentRawStream(self.dev.index)
+        sp = stream.cuda_stream if stream is not None else torch._C._cuda_getCurrentRawStream(self._dev_index)
         st = self.N.lib.wnw_oproj_allreduce(C.byref(a), sp)
         if st:
             self.N.check(st, "wnw_oproj_allreduce")
