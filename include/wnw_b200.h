@@ -285,6 +285,29 @@ wnw_status wnw_fetch_layers(const void* src_k, const void* src_v, int64_t row_by
                             int num_layers, void* dst_k, void* dst_v, int max_ctas, void* stream,
                             void* const* events);
 
+/* After wnw_planner_compute_and_prepare reported a change, hand the plan to
+ * the device in one call (the reference's staging gather + side-stream copy,
+ * src/algorithms/wnw/code/cache.py:868-889 and planner.cpp:104-122, as one
+ * host call): writes the device-plan blob into plan_host (pinned) and copies
+ * it to plan_dev; writes the host ranges and their landing rows into
+ * ranges_host / dst_host (pinned) and copies them to ranges_dev / dst_dev;
+ * then wnw_fetch_layers from src_k / src_v (device addresses of the pinned
+ * restore store) into land_k / land_v, recording events[l] after layer l --
+ * all on `stream`.  info receives the sizes and, per layer, whether it
+ * changed; if a capacity (plan ints, range pairs, landing rows) is too small
+ * nothing is issued and WNW_ERR_CAPACITY is returned with info filled.
+ * The pinned buffers must not be read by copies still in flight from a
+ * previous call (synchronize `stream` first). */
+typedef struct {
+  int64_t plan_ints, total_rows, n_ranges, max_moved_rows;
+  int32_t* layer_changed; /* caller-owned [num_layers] */
+} wnw_fetch_info;
+wnw_status wnw_planner_issue_fetch(const wnw_planner* p, int32_t* plan_host, int32_t* plan_dev, int64_t plan_cap,
+                                   int32_t* ranges_host, int32_t* ranges_dev, int64_t* dst_host, int64_t* dst_dev,
+                                   int64_t ranges_cap, const void* src_k, const void* src_v, int64_t row_bytes,
+                                   void* land_k, void* land_v, int64_t land_rows, int max_ctas, void* stream,
+                                   void* const* events, wnw_fetch_info* info);
+
 /* Make `stream` wait for `event` (cudaStreamWaitEvent; both as void*).  No
  * reference counterpart: the per-layer "rows of layer l have landed" wait of
  * the decode loop in one call. */

@@ -25,6 +25,7 @@ Per decode step:
 """
 from __future__ import annotations
 
+import ctypes as C
 import math
 from itertools import accumulate
 
@@ -472,6 +473,7 @@ class B200WnWCache(FlatVarlenCache):
         self._move_k = self._move_v = None
         self._rb_status = torch.zeros(max(1, S), dtype=torch.int32, device=self.device)
         self._layer_chg = [0] * L
+        self._chg_buf = None
         self._layer_rows = np.zeros(L + 1, np.int64)
         self._new_kv = [None] * L
 
@@ -608,11 +610,62 @@ class B200WnWCache(FlatVarlenCache):
         """Device plan + fetch of the newly needed host rows, per layer on the
         copy stream, each layer followed by its own event (the reference's
         staging cat + side-stream copy, cache.py:868-889)."""
-        L, D = self.num_layers, self.head_dim
+        L = self.num_layers
         if self._copy_stream is None:
             self._copy_stream = torch.cuda.Stream(device=self.device)
         cs = self._copy_stream
         cs.synchronize()  # the previous plan's copies no longer read the pinned buffers
+        if self.fetch_mode == "zerocopy":
+            info = self._issue_fetch(cs)
+            moved, total = info.max_moved_rows, info.total_rows
+            self._layer_chg = self._chg_buf.tolist()
+            Kx.LAUNCHES[0] += int(np.count_nonzero(np.diff(self._planner.layer_transfer()[1]))) if total else 0
+        else:
+            moved, total = self._prepare_fetch_dma(cs, total, ranges)
+        self._ensure_move_capacity(moved)
+        # stored rows per slot after the rebuild: the planner's new lengths
+        # (planner.cpp:278-357) count this step's token, every slot of every layer
+        self._next_lens = self._plan_bufs[3].astype(np.int64) - 1
+        if self.stats.enabled and total > 0:
+            row_bytes = self.head_dim * self.cpu_restore_k.element_size()
+            self.stats.record_cpu_gpu_transfer(0, c2g_tokens=int(total), c2g_bytes=int(total) * row_bytes * 2)
+        self._fetched_rows = int(total)
+        self._pending = True
+
+    def _issue_fetch(self, cs):
+        """wnw_planner_issue_fetch; grows the plan / range / landing buffers
+        and retries when it reports a capacity shortfall (nothing issued)."""
+        row_bytes = self.head_dim * self.cpu_restore_k.element_size()
+        if self._chg_buf is None:
+            self._chg_buf = np.zeros(self.num_layers, np.int32)
+        info = N.FetchInfo()
+        info.layer_changed = self._chg_buf.ctypes.data
+        for _ in range(3):
+            rng_cap = self._rng_host.shape[0] if getattr(self, "_rng_host", None) is not None else 0
+            land = self._land_k.shape[0] if self._land_k is not None else 0
+            src_k, src_v = self._restore_dev_ptrs() if self.cpu_restore_k.shape[0] else (None, None)
+            st = N.lib.wnw_planner_issue_fetch(
+                self._planner._h, self._plan_host.data_ptr(), self._plan_dev.data_ptr(), self._plan_host.numel(),
+                self._rng_host.data_ptr() if rng_cap else None, self._rng_dev.data_ptr() if rng_cap else None,
+                self._dst_host.data_ptr() if rng_cap else None, self._dst_dev.data_ptr() if rng_cap else None,
+                rng_cap, src_k, src_v, row_bytes, self._land_k.data_ptr() if land else None,
+                self._land_v.data_ptr() if land else None, land, self.fetch_ctas, cs.cuda_stream,
+                self._event_handles, C.byref(info))
+            if st != N.WNW_ERR_CAPACITY:
+                N.check(st, "wnw_planner_issue_fetch")
+                return info
+            if info.plan_ints > self._plan_host.numel():
+                n = 1 << (int(info.plan_ints) - 1).bit_length()
+                self._plan_host = torch.zeros(n, dtype=torch.int32).pin_memory()
+                self._plan_dev = torch.zeros(n, dtype=torch.int32, device=self.device)
+                self._rb_args = [None] * self.num_layers
+            self._ensure_fetch_capacity(int(info.total_rows), int(info.n_ranges))
+        raise RuntimeError("wnw_planner_issue_fetch: buffers still too small after growing them")
+
+    def _prepare_fetch_dma(self, cs, total, ranges):
+        """fetch_mode="dma": host threads gather the ranges into pinned
+        staging, one cudaMemcpyAsync per layer and tensor."""
+        L, D = self.num_layers, self.head_dim
         plan = self._planner.device_plan()
         if plan.size > self._plan_host.numel():
             n = 1 << (plan.size - 1).bit_length()
@@ -620,54 +673,29 @@ class B200WnWCache(FlatVarlenCache):
             self._plan_dev = torch.zeros(n, dtype=torch.int32, device=self.device)
             self._rb_args = [None] * L
         self._plan_host[:plan.size].copy_(torch.from_numpy(plan))
-        self._plan_np = plan.copy()
         moved = 0
         for l in range(L):
             self._layer_chg[l] = int(plan[int(plan[l])])
             moved = max(moved, int(plan[int(plan[l]) + 1]))
-        # stored rows per slot after the rebuild: the planner's new lengths
-        # (planner.cpp:278-357) count this step's token, every slot of every layer
-        self._next_lens = self._plan_bufs[3].astype(np.int64) - 1
-        self._ensure_move_capacity(moved)
-        rows, rng = self._planner.layer_transfer()
+        rows, _ = self._planner.layer_transfer()
         self._layer_rows = rows.astype(np.int64)
         row_bytes = D * self.cpu_restore_k.element_size()
         with torch.cuda.stream(cs):
             self._plan_dev[:plan.size].copy_(self._plan_host[:plan.size], non_blocking=True)
             if total > 0:
                 self._ensure_fetch_capacity(total, len(ranges))
-                if self.fetch_mode == "zerocopy":
-                    nr = len(ranges)
-                    lens = (ranges[:, 1] - ranges[:, 0]).astype(np.int64)
-                    self._rng_host[:nr].copy_(torch.from_numpy(np.ascontiguousarray(ranges, np.int32)))
-                    self._dst_host[0] = 0
-                    if nr > 1:
-                        self._dst_host[1:nr].copy_(torch.from_numpy(np.cumsum(lens)[:-1]))
-                    self._rng_dev[:nr].copy_(self._rng_host[:nr], non_blocking=True)
-                    self._dst_dev[:nr].copy_(self._dst_host[:nr], non_blocking=True)
-                    src_k, src_v = self._restore_dev_ptrs()
-                    lr = np.ascontiguousarray(rng, np.int32)
-                    N.call("wnw_fetch_layers", src_k, src_v, int(row_bytes), self._rng_dev.data_ptr(),
-                           self._dst_dev.data_ptr(), N.ptr(lr), L, self._land_k.data_ptr(), self._land_v.data_ptr(),
-                           self.fetch_ctas, cs.cuda_stream, self._event_handles)
-                    Kx.LAUNCHES[0] += int(np.count_nonzero(np.diff(lr)))
-                else:
-                    gather_rows(self.cpu_restore_k, self.cpu_restore_v, ranges, self._stage_k, self._stage_v,
-                                self.fetch_threads)
-                    for l in range(L):
-                        r0, r1 = int(self._layer_rows[l]), int(self._layer_rows[l + 1])
-                        N.call("wnw_h2d_async", self._land_k[r0:].data_ptr(), self._land_v[r0:].data_ptr(),
-                               self._stage_k[r0:].data_ptr(), self._stage_v[r0:].data_ptr(),
-                               (r1 - r0) * row_bytes, cs.cuda_stream, None)
-                        self._events[l].record(cs)
-                if self.stats.enabled:
-                    n = int((ranges[:, 1] - ranges[:, 0]).sum())
-                    self.stats.record_cpu_gpu_transfer(0, c2g_tokens=n, c2g_bytes=n * row_bytes * 2)
+                gather_rows(self.cpu_restore_k, self.cpu_restore_v, ranges, self._stage_k, self._stage_v,
+                            self.fetch_threads)
+                for l in range(L):
+                    r0, r1 = int(self._layer_rows[l]), int(self._layer_rows[l + 1])
+                    N.call("wnw_h2d_async", self._land_k[r0:].data_ptr(), self._land_v[r0:].data_ptr(),
+                           self._stage_k[r0:].data_ptr(), self._stage_v[r0:].data_ptr(),
+                           (r1 - r0) * row_bytes, cs.cuda_stream, None)
+                    self._events[l].record(cs)
             else:
                 for l in range(L):
                     self._events[l].record(cs)
-        self._fetched_rows = int(total)
-        self._pending = True
+        return moved, total
 
     def _ensure_move_capacity(self, rows):
         if self._move_k is None or self._move_k.shape[0] < max(1, rows):

@@ -22,10 +22,13 @@
 #include <new>
 #include <vector>
 
+#include <cuda_runtime.h>
+
 #include "../../include/wnw_b200.h"
 
 namespace wnw {
 void set_error(const char* fmt, ...);
+wnw_status cuda_status(cudaError_t e, const char* what);
 }
 
 struct wnw_planner {
@@ -520,6 +523,63 @@ wnw_status wnw_planner_device_plan(const wnw_planner* p, int32_t* blob, int64_t 
   }
   blob[L] = static_cast<int32_t>(o);
   return WNW_OK;
+}
+
+wnw_status wnw_planner_issue_fetch(const wnw_planner* p, int32_t* plan_host, int32_t* plan_dev, int64_t plan_cap,
+                                   int32_t* ranges_host, int32_t* ranges_dev, int64_t* dst_host, int64_t* dst_dev,
+                                   int64_t ranges_cap, const void* src_k, const void* src_v, int64_t row_bytes,
+                                   void* land_k, void* land_v, int64_t land_rows, int max_ctas, void* stream,
+                                   void* const* events, wnw_fetch_info* info) {
+  if (!p || !info) return bad("null argument");
+  const int L = p->L;
+  // sizes first: nothing is issued unless every buffer is large enough
+  int64_t used = 0;
+  wnw_status st = wnw_planner_device_plan(p, nullptr, 0, &used);
+  if (st != WNW_OK) return st;
+  const int64_t nr = static_cast<int64_t>(p->cpu_ranges.size() / 2);
+  const int64_t rows = p->layer_rows.empty() ? 0 : p->layer_rows[L];
+  int64_t moved = 0;
+  for (int l = 0; l < L; ++l) {
+    int64_t m = 0;
+    for (const auto& c : p->chg[l]) {
+      const int n_ev = c.ev_hi - c.ev_lo;
+      if (n_ev > 0) m += (c.new_len - c.load_len) - p->ev_starts[c.ev_lo];
+    }
+    moved = std::max(moved, m);
+    info->layer_changed[l] = p->chg[l].empty() ? 0 : 1;
+  }
+  info->plan_ints = used;
+  info->total_rows = rows;
+  info->n_ranges = nr;
+  info->max_moved_rows = moved;
+  if (used > plan_cap || nr > ranges_cap || rows > land_rows) {
+    wnw::set_error("issue_fetch needs plan %lld / ranges %lld / rows %lld; capacity %lld / %lld / %lld",
+                   (long long)used, (long long)nr, (long long)rows, (long long)plan_cap, (long long)ranges_cap,
+                   (long long)land_rows);
+    return WNW_ERR_CAPACITY;
+  }
+  if (!plan_host || !plan_dev || (nr > 0 && (!ranges_host || !ranges_dev || !dst_host || !dst_dev || !src_k ||
+                                             !src_v || !land_k || !land_v)))
+    return bad("null buffer");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  st = wnw_planner_device_plan(p, plan_host, plan_cap, &used);
+  if (st != WNW_OK) return st;
+  cudaError_t e = cudaMemcpyAsync(plan_dev, plan_host, sizeof(int32_t) * used, cudaMemcpyHostToDevice, s);
+  if (e != cudaSuccess) return wnw::cuda_status(e, "cudaMemcpyAsync(plan)");
+  if (nr > 0) {
+    std::memcpy(ranges_host, p->cpu_ranges.data(), sizeof(int32_t) * 2 * nr);
+    int64_t acc = 0;
+    for (int64_t i = 0; i < nr; ++i) {
+      dst_host[i] = acc;
+      acc += p->cpu_ranges[2 * i + 1] - p->cpu_ranges[2 * i];
+    }
+    e = cudaMemcpyAsync(ranges_dev, ranges_host, sizeof(int32_t) * 2 * nr, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess)
+      e = cudaMemcpyAsync(dst_dev, dst_host, sizeof(int64_t) * nr, cudaMemcpyHostToDevice, s);
+    if (e != cudaSuccess) return wnw::cuda_status(e, "cudaMemcpyAsync(ranges)");
+  }
+  return wnw_fetch_layers(src_k, src_v, row_bytes, ranges_dev, dst_dev, p->layer_ranges.data(), L, land_k, land_v,
+                          max_ctas, stream, events);
 }
 
 }  // extern "C"
