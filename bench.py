@@ -21,8 +21,8 @@ so they do exactly the work the model run did.
 
 * value -- decode tokens/s with the inputs resident in HBM;
 * e2e   -- the same through the Python hook API with each step's q/k/v copied
-           from pinned host memory and each step's attention outputs copied
-           back (bytes per step reported);
+           from pinned host memory (one copy per step) and each step's
+           attention outputs copied back (one copy; bytes per step reported);
 * roofline -- the decode-attention kernel: algorithmic bytes (K+V rows
            attended + q in + o out + class-A logits) / CUDA-event time;
 * cpu_baseline -- the CPU oracle (numpy/torch restatement of the reference's
@@ -331,33 +331,42 @@ def run_value(rec, dev, K, W, shard=None):
 
 
 def run_e2e(rec, dev, K, W, shard=None):
-    """Hook API with host buffers: per step H2D of all layers' q/k/v from
-    pinned memory and D2H of all layers' outputs (attention outputs; under
-    tensor parallelism the all-reduced o_proj rows)."""
+    """Hook API with host buffers: per step one H2D copy of all layers' q/k/v
+    from pinned memory and one D2H copy of all layers' outputs (attention
+    outputs; under tensor parallelism the all-reduced o_proj rows)."""
     shard = shard or Shard(dev)
     cache = fresh_cache(rec, dev, K + W, shard)
     steps, scale, L = shard.step_inputs(rec["steps"]), rec["scale"], MODEL["L"]
-    host_in = [[torch.empty(x.shape, dtype=x.dtype).pin_memory() for x in steps[i][l]]
-               for i in range(W + K) for l in range(L)]
+    shapes = [tuple(x.shape) for x in steps[0][0]]
+    sizes = [math.prod(sh) for sh in shapes]
+    per_layer = sum(sizes)
+    host_in = [torch.empty(L * per_layer, dtype=torch.bfloat16).pin_memory() for _ in range(W + K)]
     for i in range(W + K):
-        for l in range(L):
-            for j in range(3):
-                host_in[i * L + l][j].copy_(steps[i][l][j])
-    dev_in = [torch.empty_like(x, device=dev) for x in steps[0][0]]
-    out_shape = (1, MODEL["hidden"]) if shard.tp else tuple(steps[0][0][0].shape)
-    host_out = torch.empty((L,) + out_shape, dtype=torch.bfloat16).pin_memory()
-    in_bytes = sum(x.numel() * x.element_size() for x in steps[0][0]) * L
+        host_in[i].copy_(torch.cat([x.reshape(-1).cpu() for l in range(L) for x in steps[i][l]]))
+    dev_in = torch.empty(L * per_layer, dtype=torch.bfloat16, device=dev)
+    views = []
+    for l in range(L):
+        o, v = l * per_layer, []
+        for sh, n in zip(shapes, sizes):
+            v.append(dev_in[o:o + n].view(sh))
+            o += n
+        views.append(v)
+    out_shape = (1, MODEL["hidden"]) if shard.tp else shapes[0]
+    dev_out = torch.empty((L,) + tuple(out_shape), dtype=torch.bfloat16, device=dev)
+    host_out = torch.empty_like(dev_out, device="cpu").pin_memory()
+    in_bytes = host_in[0].numel() * host_in[0].element_size()
     out_bytes = host_out.numel() * host_out.element_size()
-    outs = [None] * L
 
     def one(i):
+        dev_in.copy_(host_in[i], non_blocking=True)
+        outs = []
         for l in range(L):
-            q, k, v = (d.copy_(h, non_blocking=True) for d, h in zip(dev_in, host_in[i * L + l]))
+            q, k, v = views[l]
             kk, vv, cu, _ = cache.decode_before_attn(l, k, v)
-            outs[l] = shard.o_proj(l, cache.fused_decode_attention(l, q, None, kk, vv, cu, scale))
+            outs.append(shard.o_proj(l, cache.fused_decode_attention(l, q, None, kk, vv, cu, scale)))
         cache.decode_all_layers_done()
-        for l in range(L):
-            host_out[l].copy_(outs[l], non_blocking=True)
+        torch.stack(outs, out=dev_out)
+        host_out.copy_(dev_out, non_blocking=True)
         torch.cuda.current_stream().synchronize()
 
     for i in range(W):

@@ -89,13 +89,15 @@ class B200WnWCache(FlatVarlenCache):
                            memory; "dma": host threads gather them into pinned
                            staging and cudaMemcpyAsync copies each layer;
       fetch_threads     -- host threads of the "dma" gather;
+      fetch_ctas        -- CTAs of the zero-copy fetch (32 saturate the host
+                           link and leave the SMs to the layer kernels);
       score_reduce      -- tensor parallelism by kv head (wnw_b200.tp): a
                            callable that sums the class-A score accumulator
                            over the ranks before every chunk selection.
     """
 
     def __init__(self, config, num_layers, num_kv_heads, num_q_heads, head_dim, device, adapter=None, *,
-                 max_decode_tokens=256, fetch_mode="zerocopy", fetch_threads=8, fetch_ctas=512, score_reduce=None):
+                 max_decode_tokens=256, fetch_mode="zerocopy", fetch_threads=8, fetch_ctas=32, score_reduce=None):
         super().__init__(num_layers, num_kv_heads, num_q_heads, head_dim, device, adapter)
         if self.device.type != "cuda":
             raise RuntimeError("B200WnWCache needs a CUDA device; the CPU oracle lives in the test suite")
