@@ -112,6 +112,11 @@ __device__ inline void cluster_wait() { asm volatile("barrier.cluster.wait.acqui
 // Programmatic dependent launch: wait until the preceding kernel in the
 // stream has completed and its writes are visible / let the next kernel in
 // the stream start its prologue.
+// Bulk prefetch of [ptr, ptr + bytes) into L2 (16-byte aligned, bytes a
+// multiple of 16); a hint with no completion to wait for.
+__device__ inline void prefetch_l2(const void* ptr, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(ptr), "r"(bytes) : "memory");
+}
 __device__ inline void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ inline void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 

@@ -103,6 +103,21 @@ __global__ void __launch_bounds__(kAttnThreads)
   const int seg = __ldg(p.work + 2 * cid);
   const int j = __ldg(p.work + 2 * cid + 1);
   const int64_t base = __ldg(p.seg_base + seg);
+  // L2 prefetch of this CTA's first tiles (up to the slot capacity): it needs
+  // only layout constants, so it runs before the dependency wait and the rows
+  // stream into L2 while the preceding kernel finishes.  L2 is the point of
+  // coherence and nothing lands in shared memory, so rows the preceding
+  // kernel still writes are read correctly after the wait.
+  if (p.seg_cap != nullptr && threadIdx.x < 2 * kMmaMaxStages) {
+    const int cap = __ldg(p.seg_cap + seg);
+    const int i = threadIdx.x >> 1;
+    const int r0 = (j * cs + rank) * tiles * kMmaTileRows + i * kMmaTileRows;
+    const int r1 = min(min(r0 + kMmaTileRows, cap), (j * cs + rank + 1) * tiles * kMmaTileRows);
+    if (i < tiles && r1 > r0) {
+      const T* src = reinterpret_cast<const T*>((threadIdx.x & 1) ? p.v_store : p.k_store) + (base + r0) * D;
+      prefetch_l2(src, uint32_t(r1 - r0) * D * sizeof(T));
+    }
+  }
   if (threadIdx.x == 0) {
 #pragma unroll
     for (int st = 0; st < kMmaMaxStages; ++st)

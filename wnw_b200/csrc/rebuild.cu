@@ -117,6 +117,10 @@ __global__ void __launch_bounds__(kRbThreads)
     rebuild_scatter_kernel(uint4* k_store, uint4* v_store, const int64_t* seg_base, int32_t* seg_len,
                            const int32_t* seg_cap, const uint4* k_land, const uint4* v_land, const int32_t* blob,
                            int layer, const uint4* k_move, const uint4* v_move, const int32_t* status, int cpr) {
+  // the layer's decode attention (launched with programmatic dependent launch)
+  // may start its layout-only prologue now; it waits for this grid to finish
+  // before it reads anything written here
+  pdl_launch_dependents();
   const RbRec r(blob, layer);
   const int64_t gtid = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
   const int64_t nthreads = int64_t(gridDim.x) * blockDim.x;
