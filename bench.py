@@ -238,6 +238,9 @@ class Shard:
         return y
 
 
+PREFILL_MS = []  # prefill-side compression time of every cache built (ms)
+
+
 def fresh_cache(rec, dev, n_steps, shard=None):
     from wnw_b200.cache import B200WnWCache
     shard = shard or Shard(dev)
@@ -245,9 +248,13 @@ def fresh_cache(rec, dev, n_steps, shard=None):
                      max_decode_tokens=n_steps + 8, score_reduce=shard.score_reduce())
     a0, a1 = rec["audio"]
     c.setup_audio(torch.tensor([a0]), torch.tensor([a1]), None)
+    torch.cuda.synchronize()
+    t = time.perf_counter()
     for l, ca, ph, k, v in rec["prefill"]:
         c.prefill_after_attn(l, *shard.prefill(ca, ph, k, v))
     c.prefill_all_layers_done()
+    torch.cuda.synchronize()
+    PREFILL_MS.append((time.perf_counter() - t) * 1e3)
     return c
 
 
@@ -602,6 +609,11 @@ def main():
                       "how": "offloaded rows fetched per step over the host link (zero-copy kernel); link_gbs = "
                              "that kernel on 128 MB of random 128-row ranges, measured in this run"},
         "model_decode_ms_per_token": rec["model_ms"],
+        "prefill_compress_ms": {"first": PREFILL_MS[0] if PREFILL_MS else None,
+                                "warm": min(PREFILL_MS[1:]) if len(PREFILL_MS) > 1 else None,
+                                "how": "prefill_after_attn x 30 layers + prefill_all_layers_done on the recorded "
+                                       "prompt (15,064 tokens); first = including this process's first pinned "
+                                       "allocation of the host store"},
     }
     if rank == 0 and not a.no_cpu and not a.profile:
         n = max(1, min(a.cpu_steps, K))

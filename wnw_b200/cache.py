@@ -79,6 +79,43 @@ def topk_keep_global(scores, seg_ranges, ratio):
     return kept
 
 
+def keep_audio_indices(scores, seg_ranges, ratio, global_topk):
+    """Kept audio tokens of a group of heads sharing one retention ratio:
+    scores [n_heads, n_audio] -> int64 [n_heads, K], ascending per head.  Per
+    segment (cache.py:1114-1138) every segment keeps its max(1, int(len *
+    ratio)) best tokens; globally (cache.py:1141-1150) the span keeps the sum
+    of those counts.  Same choices as ``topk_keep_per_segment`` /
+    ``topk_keep_global``, for all the heads in one batched top-k."""
+    nh, n = scores.shape
+    if global_topk:
+        k = min(n, sum(max(1, int((b - a) * ratio)) for a, b in seg_ranges))
+        return scores.topk(k, dim=1).indices.sort(dim=1).values
+    stride = seg_ranges[0][1] - seg_ranges[0][0]
+    full = len(seg_ranges) if seg_ranges[-1][1] - seg_ranges[-1][0] == stride else len(seg_ranges) - 1
+    parts = []
+    if full:
+        k = max(1, int(stride * ratio))
+        idx = scores[:, :full * stride].reshape(nh, full, stride).topk(k, dim=2).indices.sort(dim=2).values
+        idx = idx + (torch.arange(full, device=scores.device) * stride).view(1, full, 1)
+        parts.append(idx.reshape(nh, full * k))
+    if full < len(seg_ranges):
+        a, b = seg_ranges[-1]
+        parts.append(scores[:, a:b].topk(max(1, int((b - a) * ratio)), dim=1).indices.sort(dim=1).values + a)
+    return torch.cat(parts, dim=1) if len(parts) > 1 else parts[0]
+
+
+def offload_counts(seg_ranges, ratio, global_topk):
+    """Rows a class-B head offloads per segment (per-segment keep rule), or
+    None per segment when the global rule makes them data-dependent; and
+    the head's total."""
+    if global_topk:
+        n = seg_ranges[-1][1] if seg_ranges else 0
+        k = min(n, sum(max(1, int((b - a) * ratio)) for a, b in seg_ranges))
+        return None, n - k
+    c = [(b - a) - max(1, int((b - a) * ratio)) for a, b in seg_ranges]
+    return c, sum(c)
+
+
 class B200WnWCache(FlatVarlenCache):
     """WnW KV cache on the B200 slot layout.
 
@@ -149,7 +186,8 @@ class B200WnWCache(FlatVarlenCache):
         self._pk = [None] * L          # packed prefill K / V (until the slot layout is built)
         self._pv = [None] * L
         self.seq_lens = [None] * L     # reference semantics: rows incl. this step's token once appended
-        self._offload = []             # (layer, b, kv, seg, k_rows_cpu, v_rows_cpu)
+        self._store_planned = False    # pinned restore store sized at the first prefill layer
+        self._nonaudio = {}
         self.restore_meta = None
         self._pending = False
         self._decode_step = 0
@@ -162,45 +200,126 @@ class B200WnWCache(FlatVarlenCache):
     def prefill_after_attn(self, layer_idx, class_a_scores, per_head_scores, key_states, value_states):
         """cache.py:257-349: class-A heads keep everything after the padding;
         other heads keep the non-audio rows plus a top-``ratio`` subset of every
-        audio segment; class-B heads offload the rest to host memory."""
-        cfg = self.config
-        for b in range(self.batch_size):
+        audio segment; class-B heads offload the rest to host memory.
+
+        One layer = a batched top-k per retention ratio, one row gather into
+        the packed layer and one into the offload rows, which are copied
+        (asynchronously) straight into their place in the pinned host store."""
+        cfg, l = self.config, layer_idx
+        B, H, D = self.batch_size, self.num_kv_heads, self.head_dim
+        for b in range(B):
             if class_a_scores[b] is not None:
                 self._prefill_scores[b].append(class_a_scores[b].float())
-        kp, vp, lens = [], [], []
-        for b in range(self.batch_size):
+        if not self._store_planned:
+            self._plan_restore_store(key_states.dtype)
+        Sq = key_states.shape[2]
+        dev = key_states.device
+        kflat = key_states.reshape(B * H * Sq, D)
+        vflat = value_states.reshape(B * H * Sq, D)
+        keep_rows = [None] * (B * H)   # source rows of each segment, reference order
+        off_rows = []                  # class-B offload source rows, store order
+        lens = [0] * (B * H)
+        g2c = [0] * B
+        for b in range(B):
             r0, r1, pad = self._raw_audio_starts[b], self._raw_audio_ends[b], self.pad_lens_list[b]
-            for h in range(self.num_kv_heads):
-                kf, vf = key_states[b, h], value_states[b, h]
-                if cfg.is_class_a_kv_head(layer_idx, h):
-                    kp.append(kf[pad:])
-                    vp.append(vf[pad:])
-                    lens.append(kf.shape[0] - pad)
-                    continue
-                ratio = cfg.get_retention(layer_idx, h)
-                pick = topk_keep_global if cfg.prefill_global_topk else topk_keep_per_segment
-                kept = pick(per_head_scores[b][h], self.segment_ranges[b], ratio)
-                audio_k, audio_v = kf[r0:r1], vf[r0:r1]
-                kp.append(torch.cat([kf[pad:r0], kf[r1:], audio_k[kept]]))
-                vp.append(torch.cat([vf[pad:r0], vf[r1:], audio_v[kept]]))
-                lens.append((r0 - pad) + (kf.shape[0] - r1) + int(kept.sum()))
-                if cfg.is_class_b(layer_idx, h):
-                    idx = (~kept).nonzero(as_tuple=True)[0]
-                    if idx.numel():
-                        rk = audio_k.index_select(0, idx).cpu()
-                        rv = audio_v.index_select(0, idx).cpu()
-                        self.stats.record_cpu_gpu_transfer(b, g2c_tokens=int(idx.numel()),
-                                                           g2c_bytes=int(rk.numel() + rv.numel()) * rk.element_size())
-                        counts = torch.bincount(idx // cfg.stride_tokens,
-                                                minlength=len(self.segment_ranges[b])).tolist()
-                        off = 0
-                        for si, n in enumerate(counts):
-                            if n:
-                                self._offload.append((layer_idx, b, h, si, rk[off:off + n], rv[off:off + n]))
-                                off += n
-        self._pk[layer_idx] = torch.cat(kp)
-        self._pv[layer_idx] = torch.cat(vp)
-        self.seq_lens[layer_idx] = lens
+            segs = self.segment_ranges[b]
+            key = (b, Sq)
+            if key not in self._nonaudio:
+                self._nonaudio[key] = torch.cat([torch.arange(pad, r0, device=dev),
+                                                 torch.arange(r1, Sq, device=dev)])
+            nonaudio = self._nonaudio[key]
+            groups = {}
+            for h in range(H):
+                fi = b * H + h
+                if cfg.is_class_a_kv_head(l, h):
+                    keep_rows[fi] = torch.arange(fi * Sq + pad, fi * Sq + Sq, device=dev)
+                    lens[fi] = Sq - pad
+                else:
+                    groups.setdefault(cfg.get_retention(l, h), []).append(h)
+            off_head = {}
+            for ratio, hs in groups.items():
+                sc = torch.stack([per_head_scores[b][h] for h in hs]).to(dev)
+                kept = keep_audio_indices(sc, segs, ratio, cfg.prefill_global_topk)
+                bases = torch.tensor([(b * H + h) * Sq for h in hs], device=dev).unsqueeze(1)
+                rows = torch.cat([nonaudio.unsqueeze(0).expand(len(hs), -1), kept + r0], dim=1) + bases
+                n_keep = kept.shape[1]
+                hb = [i for i, h in enumerate(hs) if cfg.is_class_b(l, h)]
+                if hb and n_keep < sc.shape[1]:
+                    mask = torch.ones(len(hb), sc.shape[1], dtype=torch.int8, device=dev)
+                    mask.scatter_(1, kept[hb], 0)
+                    # stable descending sort lists the offloaded tokens first, ascending
+                    off = torch.argsort(mask, dim=1, descending=True, stable=True)[:, :sc.shape[1] - n_keep]
+                    off = off + r0 + bases[hb]
+                    if cfg.prefill_global_topk:
+                        cnt = torch.stack([torch.bincount((off[i] - bases[hb[i]] - r0) // cfg.stride_tokens,
+                                                          minlength=len(segs)) for i in range(len(hb))]).cpu()
+                    for i, j in enumerate(hb):
+                        off_head[hs[j]] = (off[i], cnt[i].tolist() if cfg.prefill_global_topk else None)
+                for i, h in enumerate(hs):
+                    keep_rows[b * H + h] = rows[i]
+                    lens[b * H + h] = (r0 - pad) + (Sq - r1) + n_keep
+            for h in sorted(off_head):
+                fi = b * H + h
+                rows_h, cnt = off_head[h]
+                if cnt is None:
+                    cnt = offload_counts(segs, cfg.get_retention(l, h), False)[0]
+                o = int(self._store_off[l, fi])
+                m0 = self._meta_base[l, fi]
+                for si, n in enumerate(cnt):
+                    if n:
+                        self._meta["cpu_s"][m0 + si], self._meta["cpu_e"][m0 + si] = o, o + n
+                        o += n
+                off_rows.append(rows_h)
+                g2c[b] += rows_h.shape[0]
+        src = torch.cat(keep_rows)
+        self._pk[l] = kflat.index_select(0, src)
+        self._pv[l] = vflat.index_select(0, src)
+        if off_rows:
+            src = torch.cat(off_rows)
+            o0 = int(self._store_layer_off[l])
+            n = src.shape[0]
+            self.cpu_restore_k[o0:o0 + n].copy_(kflat.index_select(0, src), non_blocking=True)
+            self.cpu_restore_v[o0:o0 + n].copy_(vflat.index_select(0, src), non_blocking=True)
+        for b in range(B):
+            if g2c[b]:
+                self.stats.record_cpu_gpu_transfer(b, g2c_tokens=g2c[b],
+                                                   g2c_bytes=g2c[b] * D * 2 * key_states.element_size())
+        self.seq_lens[l] = lens
+
+    def _plan_restore_store(self, dtype):
+        """Sizes of everything the prefill offloads, known from the config and
+        the audio spans alone: the restore-metadata layout, each (layer,
+        segment)'s place in the host store, and the store itself (pinned,
+        allocated once; layer-major, then segment, then audio segment)."""
+        cfg = self.config
+        L, H, B, D = self.num_layers, self.num_kv_heads, self.batch_size, self.head_dim
+        S = B * H
+        self.seg_count = [len(self.segment_ranges[b]) for b in range(B)]
+        per_fi = np.array([self.seg_count[fi // H] for fi in range(S)], np.int64)
+        self._meta_base = (np.arange(L, dtype=np.int64)[:, None] * per_fi.sum()
+                           + np.concatenate([[0], np.cumsum(per_fi)[:-1]])[None, :])
+        acc = int(L * per_fi.sum())
+        self._meta = {k: np.full(acc, -1, np.int32) for k in ("cpu_s", "cpu_e", "gpu_s", "gpu_e")}
+        self._store_off = np.zeros((L, S), np.int64)
+        self._store_layer_off = np.zeros(L + 1, np.int64)
+        off = 0
+        for l in range(L):
+            self._store_layer_off[l] = off
+            for fi in range(S):
+                b, h = divmod(fi, H)
+                self._store_off[l, fi] = off
+                if cfg.is_class_b(l, h) and not cfg.is_class_a_kv_head(l, h):
+                    off += offload_counts(self.segment_ranges[b], cfg.get_retention(l, h),
+                                          cfg.prefill_global_topk)[1]
+        self._store_layer_off[L] = off
+        if off:
+            self.cpu_restore_k = torch.empty(off, D, dtype=dtype, pin_memory=True)
+            self.cpu_restore_v = torch.empty(off, D, dtype=dtype, pin_memory=True)
+        else:
+            self.cpu_restore_k = torch.empty(0, D, dtype=dtype)
+            self.cpu_restore_v = torch.empty(0, D, dtype=dtype)
+        self._restore_ptrs = None
+        self._store_planned = True
 
     def prefill_all_layers_done(self):
         """cache.py:351-390: host restore store, initial chunk selection and
@@ -209,32 +328,9 @@ class B200WnWCache(FlatVarlenCache):
         S = B * H
         dt = self._pk[0].dtype
         self.dtype = dt
-        # --- host restore store + metadata (flat, planner layout)
-        self.seg_count = [len(self.segment_ranges[b]) for b in range(B)]
-        self._meta_base = np.zeros((L, S), np.int64)
-        acc = 0
-        for l in range(L):
-            for fi in range(S):
-                self._meta_base[l, fi] = acc
-                acc += self.seg_count[fi // H]
-        self._meta = {k: np.full(acc, -1, np.int32) for k in ("cpu_s", "cpu_e", "gpu_s", "gpu_e")}
-        if self._offload:
-            self.cpu_restore_k = torch.cat([o[4] for o in self._offload])
-            self.cpu_restore_v = torch.cat([o[5] for o in self._offload])
-            try:
-                self.cpu_restore_k = self.cpu_restore_k.pin_memory()
-                self.cpu_restore_v = self.cpu_restore_v.pin_memory()
-            except RuntimeError:
-                pass
-            off = 0
-            for l, b, h, si, rk, _ in self._offload:
-                i = self._meta_base[l, b * H + h] + si
-                self._meta["cpu_s"][i], self._meta["cpu_e"][i] = off, off + rk.shape[0]
-                off += rk.shape[0]
-        else:
-            self.cpu_restore_k = torch.empty(0, D, dtype=dt)
-            self.cpu_restore_v = torch.empty(0, D, dtype=dt)
-        self._offload = []
+        if not self._store_planned:  # no layer offloaded anything
+            self._plan_restore_store(dt)
+        # the offload copies into the pinned store were queued on this stream
         # --- scoring geometry (needed by the initial selection)
         self._setup_scoring()
         # --- initial chunk selection from the summed prefill class-A scores
@@ -262,36 +358,49 @@ class B200WnWCache(FlatVarlenCache):
 
     def _initial_load(self, b, segs):
         """cache.py:651-714: append the selected host rows to sample b's
-        class-B segments, in ascending segment order."""
-        H = self.num_kv_heads
+        class-B segments, in ascending segment order -- per layer one copy of
+        the packed rows to their new places and one zero-copy fetch of the
+        selected rows from the pinned store."""
+        H, D = self.num_kv_heads, self.head_dim
         dev = self.device
+        c2g = 0
         for l in range(self.num_layers):
-            cu = [0] + list(accumulate(self.seq_lens[l]))
-            kp, vp = [], []
             lens = list(self.seq_lens[l])
-            for fi in range(self.batch_size * H):
-                bb, h = divmod(fi, H)
-                kp.append(self._pk[l][cu[fi]:cu[fi + 1]])
-                vp.append(self._pv[l][cu[fi]:cu[fi + 1]])
-                if bb != b or not self.config.is_class_b(l, h):
+            old = list(lens)
+            ranges, dst = [], []
+            for fi in range(b * H, (b + 1) * H):
+                if not self.config.is_class_b(l, fi - b * H):
                     continue
                 rel = lens[fi]
+                m0 = self._meta_base[l, fi]
                 for si in segs:
-                    i = self._meta_base[l, fi] + si
-                    cs, ce = int(self._meta["cpu_s"][i]), int(self._meta["cpu_e"][i])
+                    cs, ce = int(self._meta["cpu_s"][m0 + si]), int(self._meta["cpu_e"][m0 + si])
                     if cs < 0:
                         continue
-                    kp.append(self.cpu_restore_k[cs:ce].to(dev))
-                    vp.append(self.cpu_restore_v[cs:ce].to(dev))
-                    self._meta["gpu_s"][i], self._meta["gpu_e"][i] = rel, rel + ce - cs
+                    ranges.append((cs, ce))
+                    dst.append((fi, rel))
+                    self._meta["gpu_s"][m0 + si], self._meta["gpu_e"][m0 + si] = rel, rel + ce - cs
                     rel += ce - cs
-                    self.stats.record_cpu_gpu_transfer(b, c2g_tokens=ce - cs,
-                                                       c2g_bytes=(ce - cs) * self.head_dim * 2 *
-                                                       self.cpu_restore_k.element_size())
                 lens[fi] = rel
-            self._pk[l] = torch.cat(kp)
-            self._pv[l] = torch.cat(vp)
+            if not ranges:
+                continue
+            new_cu = np.concatenate([[0], np.cumsum(lens)]).astype(np.int64)
+            old_cu = np.concatenate([[0], np.cumsum(old)]).astype(np.int64)
+            nk = torch.empty(int(new_cu[-1]), D, dtype=self._pk[l].dtype, device=dev)
+            nv = torch.empty_like(nk)
+            Kx.copy_segments(self._pk[l], self._pv[l], torch.from_numpy(old_cu[:-1]).to(dev), nk, nv,
+                             torch.from_numpy(new_cu[:-1]).to(dev),
+                             torch.from_numpy(np.asarray(old, np.int32)).to(dev))
+            rng = torch.tensor(ranges, dtype=torch.int32, device=dev)
+            drow = torch.tensor([int(new_cu[fi]) + r for fi, r in dst], dtype=torch.int64, device=dev)
+            src_k, src_v = self._restore_dev_ptrs()
+            Kx.fetch_rows(src_k, src_v, D * nk.element_size(), rng, drow, nk, nv, max_ctas=self.fetch_ctas)
+            c2g += sum(e - s_ for s_, e in ranges)
+            self._pk[l], self._pv[l] = nk, nv
             self.seq_lens[l] = lens
+        if c2g:
+            self.stats.record_cpu_gpu_transfer(b, c2g_tokens=c2g,
+                                               c2g_bytes=c2g * D * 2 * self.cpu_restore_k.element_size())
 
     def _loaded_bound(self, l, fi):
         """Most host rows segment (l, fi) can hold at once: a segment stays
