@@ -111,8 +111,9 @@ def compute_prefill_scores(q, k, attention_mask, cache, layer_idx, B, S, H, G, s
     if attention_mask is not None and attention_mask.dim() == 4 and attention_mask.dtype == torch.bool:
         attention_mask = torch.where(attention_mask, 0.0, float("-inf")).to(q.dtype)
     if attention_mask is None:
-        causal = torch.full((S, S), float("-inf"), device=q.device, dtype=q.dtype).triu_(1)
-        attention_mask = causal.unsqueeze(0).unsqueeze(0).expand(B, 1, S, S)
+        # the causal mask's rows the scores read -- the last query, or the
+        # post-audio text queries -- instead of the whole S x S matrix
+        attention_mask = _CausalRows(S, q.device, q.dtype)
     cfg = cache.config
     ca_heads = cfg.get_layer_class_a(layer_idx)
     class_a, per_head = [], []
@@ -135,6 +136,25 @@ def compute_prefill_scores(q, k, attention_mask, cache, layer_idx, B, S, H, G, s
                                       cfg.prefill_score_mode))
         per_head.append(heads)
     return class_a, per_head
+
+
+class _CausalRows:
+    """Stand-in for a [B, 1, S, S] causal mask: indexing [b, :, rows, :]
+    builds only the requested rows (0 on and below the diagonal, -inf above)."""
+
+    def __init__(self, S, device, dtype):
+        self.S, self.device, self.dtype = S, device, dtype
+
+    def dim(self):
+        return 4
+
+    def __getitem__(self, idx):
+        _, _, rows, _ = idx
+        r = torch.arange(self.S, device=self.device)[rows]
+        cols = torch.arange(self.S, device=self.device)
+        m = torch.zeros(r.numel(), self.S, device=self.device, dtype=self.dtype)
+        m.masked_fill_(cols.unsqueeze(0) > r.unsqueeze(1), float("-inf"))
+        return m.unsqueeze(0)
 
 
 def _head_scores(q_all, k_one, mask, b, S, q0, q1, a0, a1, scaling, mode):
