@@ -50,42 +50,12 @@ def compute_chunks(segments, chunk_size, stride):
     return [list(range(i, min(i + spc, n))) for i in range(n)]
 
 
-def topk_keep_per_segment(scores, seg_ranges, ratio):
-    """Prefill audio selection per segment (cache.py:1114-1138): keep
-    ``max(1, int(len * ratio))`` highest-scoring tokens of every segment."""
-    n = scores.shape[0]
-    kept = torch.zeros(n, dtype=torch.bool, device=scores.device)
-    if not seg_ranges:
-        return kept
-    stride = seg_ranges[0][1] - seg_ranges[0][0]
-    full = len(seg_ranges) if seg_ranges[-1][1] - seg_ranges[-1][0] == stride else len(seg_ranges) - 1
-    if full:
-        k = max(1, int(stride * ratio))
-        idx = scores[:full * stride].view(full, stride).topk(k, dim=1).indices
-        idx = idx + torch.arange(full, device=scores.device).unsqueeze(1) * stride
-        kept[idx.reshape(-1)] = True
-    if full < len(seg_ranges):
-        a, b = seg_ranges[-1]
-        kept[scores[a:b].topk(max(1, int((b - a) * ratio))).indices + a] = True
-    return kept
-
-
-def topk_keep_global(scores, seg_ranges, ratio):
-    """Prefill audio selection over the whole span (cache.py:1141-1150)."""
-    n = scores.shape[0]
-    k = min(n, sum(max(1, int((b - a) * ratio)) for a, b in seg_ranges))
-    kept = torch.zeros(n, dtype=torch.bool, device=scores.device)
-    kept[scores.topk(k).indices] = True
-    return kept
-
-
 def keep_audio_indices(scores, seg_ranges, ratio, global_topk):
     """Kept audio tokens of a group of heads sharing one retention ratio:
     scores [n_heads, n_audio] -> int64 [n_heads, K], ascending per head.  Per
     segment (cache.py:1114-1138) every segment keeps its max(1, int(len *
     ratio)) best tokens; globally (cache.py:1141-1150) the span keeps the sum
-    of those counts.  Same choices as ``topk_keep_per_segment`` /
-    ``topk_keep_global``, for all the heads in one batched top-k."""
+    of those counts -- for all the heads in one batched top-k."""
     nh, n = scores.shape
     if global_topk:
         k = min(n, sum(max(1, int((b - a) * ratio)) for a, b in seg_ranges))
