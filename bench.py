@@ -62,7 +62,7 @@ WNW = dict(frac_a=0.30, chunk=128, top_k=16, lag=1, retention=0.0, seed=1234)
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=24)
+    ap.add_argument("--steps", type=int, default=64)
     ap.add_argument("--warmup", type=int, default=4)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--cpu-steps", type=int, default=3, help="oracle steps in the bounded CPU sample")
@@ -320,6 +320,7 @@ def run_value(rec, dev, K, W, shard=None):
         torch.cuda.synchronize()
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
+    wall0 = time.time()
     t0.record()
     torch.cuda.nvtx.range_push("wnw_timed")
     for i in range(W, W + K):
@@ -328,13 +329,15 @@ def run_value(rec, dev, K, W, shard=None):
     torch.cuda.nvtx.range_pop()
     t1.record()
     torch.cuda.synchronize()
+    wall1 = time.time()
     if shard.world > 1:
         torch.distributed.barrier()
         torch.cuda.synchronize()
     launches = Kx.LAUNCHES[0] - launches0
     total_ms = t0.elapsed_time(t1)
     us, nbytes, n = attention_replay(cache, [steps[W + K - 1][l][0] for l in range(L)], reps=10)
-    return dict(ms=total_ms, attn_us=us, attn_bytes=nbytes, attn_n=n, launches=launches, fetched_rows=fetched)
+    return dict(ms=total_ms, attn_us=us, attn_bytes=nbytes, attn_n=n, launches=launches, fetched_rows=fetched,
+                window=(wall0, wall1))
 
 
 def run_e2e(rec, dev, K, W, shard=None):
@@ -364,8 +367,17 @@ def run_e2e(rec, dev, K, W, shard=None):
     in_bytes = host_in[0].numel() * host_in[0].element_size()
     out_bytes = host_out.numel() * host_out.element_size()
 
+    from wnw_b200 import kernels as Kx
+    from wnw_b200 import native as N
+    host_ptr = [Kx.host_device_pointer(h) for h in host_in]
+
     def one(i):
-        dev_in.copy_(host_in[i], non_blocking=True)
+        # the step's inputs: a kernel copy from mapped pinned memory (SM loads
+        # share the host link with the zero-copy fetch; a copy-engine transfer
+        # can queue behind it for the whole fetch)
+        N.call("wnw_copy_mapped", dev_in.data_ptr(), host_ptr[i], in_bytes, 32,
+               torch._C._cuda_getCurrentRawStream(dev.index if dev.index is not None else 0))
+        Kx.LAUNCHES[0] += 1
         outs = []
         for l in range(L):
             q, k, v = views[l]
@@ -455,24 +467,27 @@ def _cpu_step(c, step, scale):
 class Clocks:
     """nvidia-smi sampling during the timed region."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, index):
         self.index = index
         self.proc = None
+        self.lines = []
 
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
         return self
 
     def __exit__(self, *exc):
+        if self.proc is None:
+            return
         self.lines = []
         if self.proc is not None:
             self.proc.terminate()
@@ -482,24 +497,33 @@ class Clocks:
                 self.proc.kill()
                 out, _ = self.proc.communicate()
             self.lines = [x for x in out.splitlines() if x.strip()]
+            self.proc = None
 
-    def summary(self):
+    def summary(self, window=None):
+        """Median SM clock, max clock and active throttle reasons over the
+        samples taken inside ``window`` = (t0, t1) in time.time() seconds
+        (the timed region; all samples when None)."""
+        import datetime
         sm, mx, reasons = [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for ln in self.lines:
             p = [x.strip() for x in ln.split(",")]
             try:
-                sm.append(float(p[1]))
-                mx.append(float(p[2]))
+                ts = datetime.datetime.strptime(p[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                clk, cmax = float(p[2]), float(p[3])
             except (ValueError, IndexError):
                 continue
-            for n, v in zip(names, p[5:9]):
+            if window is not None and not window[0] <= ts <= window[1]:
+                continue
+            sm.append(clk)
+            mx.append(cmax)
+            for n, v in zip(names, p[6:10]):
                 if v.lower().startswith("active"):
                     reasons.add(n)
         if not sm:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "samples": len(sm), "window": "timed region" if window is not None else "whole leg"}
 
 
 def peaks():
@@ -549,6 +573,18 @@ def main():
     tp = a.parallel == "tp" and a.impl == "b200"
     if tp:
         cfg_json["parallelism"] = f"tp{world} (kv heads sharded, o_proj all-reduce per layer)"
+    # the clock sampler starts now so its start-up is long over by the timed
+    # region; only the samples inside that region are reported
+    clk = Clocks(local)
+    if a.impl == "b200" and not a.profile:
+        clk.__enter__()
+    try:
+        return _main(a, rank, world, local, dist, dev, K, W, cfg_json, tp, clk)
+    finally:
+        clk.__exit__(None, None, None)
+
+
+def _main(a, rank, world, local, dist, dev, K, W, cfg_json, tp, clk):
     # replicas record their own request; tensor-parallel ranks share one
     rec = record(dev, W + K, seed=1000 + (0 if tp else rank))
     shard = Shard(dev, rank, world, tp=tp, seed=2000, exchange=a.tp_exchange)
@@ -569,8 +605,8 @@ def main():
         print(json.dumps(line), flush=True)
         return
 
-    with Clocks(local) as clk:
-        val = run_value(rec, dev, K, W, shard)
+    val = run_value(rec, dev, K, W, shard)
+    clk.__exit__(None, None, None)
     e2e = run_e2e(rec, dev, K, W, shard)
     if shard.ex is not None:
         shard.ex.check()
@@ -602,7 +638,7 @@ def main():
                      "launches_timed": val["attn_n"],
                      "how": "all 30 layers' launches back to back on the timed run's final state, CUDA events"},
         "gpu_launches": val["launches"],
-        "clocks": clk.summary(),
+        "clocks": clk.summary(val["window"]),
         "fetched_rows_per_step": val["fetched_rows"] / K,
         "host_link": {"fetch_bytes_per_step": fetch_bytes, "link_gbs": link,
                       "fetch_ms_at_link": fetch_bytes / (link * 1e9) * 1e3 if link else None,

@@ -300,13 +300,26 @@ wnw_status wnw_fetch_layers(const void* src_k, const void* src_v, int64_t row_by
  * previous call (synchronize `stream` first). */
 typedef struct {
   int64_t plan_ints, total_rows, n_ranges, max_moved_rows;
-  int32_t* layer_changed; /* caller-owned [num_layers] */
+  int64_t fetch_launches; /* layers with rows to fetch (one launch each)   */
+  int32_t* layer_changed; /* caller-owned [num_layers]                     */
 } wnw_fetch_info;
 wnw_status wnw_planner_issue_fetch(const wnw_planner* p, int32_t* plan_host, int32_t* plan_dev, int64_t plan_cap,
                                    int32_t* ranges_host, int32_t* ranges_dev, int64_t* dst_host, int64_t* dst_dev,
                                    int64_t ranges_cap, const void* src_k, const void* src_v, int64_t row_bytes,
                                    void* land_k, void* land_v, int64_t land_rows, int max_ctas, void* stream,
                                    void* const* events, wnw_fetch_info* info);
+
+/* Kernel copy of `bytes` (a multiple of 16, 16-byte aligned) from `src` --
+ * typically the device address of pinned host memory (wnw_host_device_pointer)
+ * -- to `dst`, on `stream`.  No reference counterpart: a host->device copy
+ * made of SM loads, which share the host link with the zero-copy fetch instead
+ * of queueing behind it as a copy-engine transfer can. */
+wnw_status wnw_copy_mapped(void* dst, const void* src, int64_t bytes, int max_ctas, void* stream);
+
+/* Async copy of n bytes in either direction (cudaMemcpyDefault: unified
+ * addressing tells host from device) on `stream`.  No reference counterpart:
+ * the step's small host<->device copies in one call each. */
+wnw_status wnw_copy_async(void* dst, const void* src, int64_t bytes, void* stream);
 
 /* Make `stream` wait for `event` (cudaStreamWaitEvent; both as void*).  No
  * reference counterpart: the per-layer "rows of layer l have landed" wait of

@@ -122,6 +122,7 @@ class B200WnWCache(FlatVarlenCache):
         self.score_reduce = score_reduce
         self._dev_index = self.device.index if self.device.index is not None else torch.cuda.current_device()
         self._rb_args = [None] * num_layers
+        self._tail_args = None
         self._class_b_heads_by_layer = [config.get_layer_class_b(l) for l in range(num_layers)]
         self.batch_size = 0
         self.prefilled = False
@@ -323,6 +324,7 @@ class B200WnWCache(FlatVarlenCache):
         # --- slot layout, planner, per-step buffers
         self._build_slots()
         self._init_planner()
+        self._tail_args = None
         self.prefilled = True
         self.stats.record_prefill(self._snapshot_cache_stats)
 
@@ -447,6 +449,7 @@ class B200WnWCache(FlatVarlenCache):
             n_max = max(n_max, w.shape[0])
         if getattr(self, "_scratch", None) is None or not self._scratch.fits(n_max, G, D, S):
             self._scratch = Kx.AttnScratch(dev, n_max, G, D, S)
+            self._tail_args = None  # the step tail copies the scratch's error word
         del max_rows
         self._attn_args = [None] * L  # launch arguments, built lazily per (layer, scale)
         self._rb_args = [None] * L    # rebuild arguments, likewise
@@ -557,6 +560,34 @@ class B200WnWCache(FlatVarlenCache):
         self._chg_buf = None
         self._layer_rows = np.zeros(L + 1, np.int64)
         self._new_kv = [None] * L
+        self._presize_step_buffers()
+
+    def _presize_step_buffers(self):
+        """Size the per-step fetch and rebuild buffers for the worst step the
+        planner can produce, so the decode loop never allocates (a pinned
+        allocation is a slow, synchronising driver call): one step loads at
+        most every segment a slot can hold, moves at most those rows plus the
+        decoded ones, and the plan blob holds at most one record per slot."""
+        L, S = self.num_layers, self.batch_size * self.num_kv_heads
+        lag = max(1, self.config.eviction_lag)
+        segs = lag * self.config.top_k_chunks * self.segs_per_chunk
+        bound = np.zeros((L, S), np.int64)
+        for l in range(L):
+            for fi in range(S):
+                if self.config.is_class_b(l, fi % self.num_kv_heads):
+                    bound[l, fi] = self._loaded_bound(l, fi)
+        rows = int(bound.sum())
+        if rows == 0:
+            return
+        n_ranges = L * S * segs
+        self._ensure_fetch_capacity(rows, n_ranges)
+        self._ensure_move_capacity(int((bound + self.max_decode_tokens * (bound > 0)).sum(axis=1).max()))
+        plan_ints = (L + 1) + L * (6 + 8 * S) + 2 * n_ranges
+        if plan_ints > self._plan_host.numel():
+            n = 1 << (plan_ints - 1).bit_length()
+            self._plan_host = torch.zeros(n, dtype=torch.int32).pin_memory()
+            self._plan_dev = torch.zeros(n, dtype=torch.int32, device=self.device)
+            self._rb_args = [None] * L
 
     # ------------------------------------------------------------- decode
     def decode_before_attn(self, layer_idx, new_k, new_v):
@@ -655,37 +686,73 @@ class B200WnWCache(FlatVarlenCache):
         self.stats.flush_decode_step(self._decode_step)
         if self.stats.enabled and self._decode_step % self.stats.interval == 0:
             self.stats.record_decode(self._decode_step, self._snapshot_cache_stats)
-        Kx.advance_lengths(self._seg_len)
-        self._len_host += 1
         B = self.batch_size
+        st = self._raw_stream()
+        a = self._tail_args if self._tail_args is not None else self._make_tail_args()
+        select = self.config.top_k_chunks > 0 and self.max_audio > 0
+        self._tail_call("wnw_advance_lengths", a["adv"], st)
+        self._len_host += 1
         if self._has_scoring:
-            Kx.score_finalize(self._logits, self._stats, self._t_logit, self._t_stat, self._t_mask, self._t_off,
-                              self.num_kv_groups, self.score_offsets, self.max_audio, self.score_accumulator)
+            self._tail_call("wnw_score_finalize", a["fin"], st)
         else:
             self.score_accumulator.zero_()
         if self.score_reduce is not None:
             self.score_accumulator.copy_(self.score_reduce(self.score_accumulator))
-        if self.config.top_k_chunks > 0 and self.max_audio > 0:
-            Kx.chunk_topk(self.score_accumulator, self.score_offsets, self.max_audio, self.config.stride_tokens,
-                          self.segs_per_chunk, self.config.top_k_chunks, self._topk_dev)
-        self._topk_host.copy_(self._topk_dev, non_blocking=True)
-        self._err_host.copy_(self._scratch.err, non_blocking=True)
+            st = self._raw_stream()
+        if select:
+            self._tail_call("wnw_chunk_topk", a["topk"], st)
+        Kx.LAUNCHES[0] += 1 + int(self._has_scoring) + int(select)
+        self._tail_call("wnw_copy_async", a["topk_d2h"], st)
+        self._tail_call("wnw_copy_async", a["err_d2h"], st)
         self._ready.record()
         self._ready.synchronize()
-        if int(self._err_host[0]):
+        if int(a["err_np"][0]):
             Kx.check_device_error(self._scratch.err)
-        rows = self._topk_host.tolist()
-        flat, off = [], [0]
-        for b in range(B):
-            if self.config.top_k_chunks > 0 and self.max_audio > 0:
-                flat.extend(c for c in rows[b] if c >= 0)
-            off.append(len(flat))
-        self.last_topk = [sorted(flat[off[b]:off[b + 1]]) for b in range(B)]
-        ch, total, _, _, ranges = self._planner.compute_and_prepare(flat, off, *self._plan_bufs)
+        if select:
+            t = a["topk_np"]
+            keep = t >= 0
+            flat = np.ascontiguousarray(t[keep], np.int32)
+            off = np.concatenate([[0], np.cumsum(keep.sum(axis=1))]).astype(np.int32)
+        else:
+            flat, off = np.zeros(0, np.int32), np.zeros(B + 1, np.int32)
+        self.last_topk = [sorted(flat[off[b]:off[b + 1]].tolist()) for b in range(B)]
+        if self.fetch_mode == "zerocopy":
+            ch, total = self._planner.compute(flat, off, a["plan_ptrs"])
+            ranges = None
+        else:
+            ch, total, _, _, ranges = self._planner.compute_and_prepare(flat, off, *self._plan_bufs)
         for b in range(B):
             self.loaded_segments[b] = set(self._planner.get_loaded_segments(b))
         if ch:
             self._prepare_fetch(total, ranges)
+
+    def _tail_call(self, name, args, stream):
+        st = getattr(N.lib, name)(*args, stream)
+        if st:
+            N.check(st, name)
+
+    def _make_tail_args(self):
+        """Launch arguments of the step's tail (length advance, score
+        finalisation, chunk top-k, two small device-to-host copies), taken
+        once: every buffer they name lives as long as the prefilled state."""
+        B = self.batch_size
+        a = {"adv": (self._seg_len.data_ptr(), self._seg_len.numel())}
+        if self._has_scoring:
+            a["fin"] = (self._logits.data_ptr(), self._stats.data_ptr(), self._t_logit.data_ptr(),
+                        self._t_stat.data_ptr(), self._t_mask.data_ptr(), self._t_off.data_ptr(),
+                        self.num_kv_groups, B, self.score_offsets.data_ptr(), int(self.max_audio),
+                        self.score_accumulator.data_ptr())
+        a["topk"] = (self.score_accumulator.data_ptr(), self.score_offsets.data_ptr(), B, int(self.max_audio),
+                     int(self.config.stride_tokens), int(self.segs_per_chunk), int(self.config.top_k_chunks),
+                     self._topk_dev.data_ptr(), None, None)
+        a["topk_d2h"] = (self._topk_host.data_ptr(), self._topk_dev.data_ptr(),
+                         self._topk_dev.numel() * self._topk_dev.element_size())
+        a["err_d2h"] = (self._err_host.data_ptr(), self._scratch.err.data_ptr(), 4)
+        a["topk_np"] = self._topk_host.numpy()
+        a["err_np"] = self._err_host.numpy()
+        a["plan_ptrs"] = [b.ctypes.data for b in self._plan_bufs]
+        self._tail_args = a
+        return a
 
     def _prepare_fetch(self, total, ranges):
         """Device plan + fetch of the newly needed host rows, per layer on the
@@ -700,7 +767,7 @@ class B200WnWCache(FlatVarlenCache):
             info = self._issue_fetch(cs)
             moved, total = info.max_moved_rows, info.total_rows
             self._layer_chg = self._chg_buf.tolist()
-            Kx.LAUNCHES[0] += int(np.count_nonzero(np.diff(self._planner.layer_transfer()[1]))) if total else 0
+            Kx.LAUNCHES[0] += int(info.fetch_launches)
         else:
             moved, total = self._prepare_fetch_dma(cs, total, ranges)
         self._ensure_move_capacity(moved)

@@ -104,6 +104,17 @@ wnw_status wnw_gather_rows(const void* src_k, const void* src_v, int64_t row_byt
   return WNW_OK;
 }
 
+wnw_status wnw_copy_async(void* dst, const void* src, int64_t bytes, void* stream) {
+  if (bytes <= 0) return WNW_OK;
+  if (!dst || !src) {
+    wnw::set_error("null argument");
+    return WNW_ERR_INVALID;
+  }
+  const cudaError_t e = cudaMemcpyAsync(dst, src, size_t(bytes), cudaMemcpyDefault, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return wnw::cuda_status(e, "cudaMemcpyAsync");
+  return WNW_OK;
+}
+
 wnw_status wnw_stream_wait_event(void* stream, void* event) {
   if (!event) {
     wnw::set_error("null event");

@@ -51,7 +51,28 @@ __global__ void __launch_bounds__(kFetchThreads)
   }
 }
 
+// Plain copy of n 16-byte words (the source may be mapped host memory).
+__global__ void __launch_bounds__(kFetchThreads) copy_words_kernel(const uint4* __restrict__ src,
+                                                                    uint4* __restrict__ dst, int64_t n) {
+  for (int64_t i = int64_t(blockIdx.x) * kFetchThreads + threadIdx.x; i < n; i += int64_t(gridDim.x) * kFetchThreads)
+    dst[i] = src[i];
+}
+
 }  // namespace wnw
+
+extern "C" wnw_status wnw_copy_mapped(void* dst, const void* src, int64_t bytes, int max_ctas, void* stream) {
+  using namespace wnw;
+  if (bytes <= 0) return WNW_OK;
+  WNW_CHECK_ARG(dst && src, "null pointer argument");
+  WNW_CHECK_ARG(bytes % 16 == 0 && aligned16(dst) && aligned16(src), "16-byte aligned sizes and addresses only");
+  const int64_t n = bytes / 16;
+  const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(max_ctas > 0 ? max_ctas : 32,
+                                                                           (n + kFetchThreads - 1) / kFetchThreads)));
+  copy_words_kernel<<<grid, kFetchThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint4*>(src), static_cast<uint4*>(dst), n);
+  WNW_CUDA_TRY(cudaGetLastError());
+  return WNW_OK;
+}
 
 extern "C" wnw_status wnw_host_device_pointer(const void* host_ptr, void** dev_ptr) {
   using namespace wnw;

@@ -550,6 +550,8 @@ wnw_status wnw_planner_issue_fetch(const wnw_planner* p, int32_t* plan_host, int
   }
   info->plan_ints = used;
   info->total_rows = rows;
+  info->fetch_launches = 0;
+  for (int l = 0; l < L; ++l) info->fetch_launches += p->layer_ranges[l + 1] > p->layer_ranges[l] ? 1 : 0;
   info->n_ranges = nr;
   info->max_moved_rows = moved;
   if (used > plan_cap || nr > ranges_cap || rows > land_rows) {

@@ -89,6 +89,15 @@ class Planner:
         ev_s, ev_e = self.evictions()
         return ch.value, tot.value, ev_s, ev_e, self.cpu_ranges()
 
+    def compute(self, topk_idx, topk_off, out_ptrs):
+        """``compute_and_prepare`` for callers that keep the plan on the
+        planner (wnw_planner_issue_fetch): int32 numpy top-k input, the seven
+        output arrays as pre-taken pointers; returns (any_change, total)."""
+        ch, tot = C.c_int(), C.c_int()
+        N.call("wnw_planner_compute_and_prepare", self._h, topk_idx.ctypes.data if topk_idx.size else None,
+               topk_off.ctypes.data, *out_ptrs, C.byref(ch), C.byref(tot))
+        return ch.value, tot.value
+
     def evictions(self):
         n = C.c_int()
         N.call("wnw_planner_get_evictions", self._h, None, None, 0, C.byref(n))

@@ -9,14 +9,27 @@ from collections import defaultdict
 import torch
 
 
+_TOTAL = {}
+
+
 def gpu_snapshot(index):
+    """Device memory in the reference's GPUMonitor fields
+    (src/common/monitoring/gpu_monitor.py:10-31), read without a driver
+    query: total = the device's memory (looked up once), used = the bytes
+    this process's allocator holds.  The reference calls cudaMemGetInfo
+    (device-wide); that call took from 0.1 to ~55 ms on a shared B200 while
+    another process queried the driver, and the snapshot sits inside the
+    decode step every ``interval`` steps."""
     try:
-        free, total = torch.cuda.mem_get_info(index)
+        if index not in _TOTAL:
+            _TOTAL[index] = int(torch.cuda.get_device_properties(index).total_memory)
+        total = _TOTAL[index]
+        used = int(torch.cuda.memory_reserved(index))
     except Exception:
         return {"gpu_index": index, "memory_total_bytes": None, "memory_free_bytes": None,
                 "memory_used_bytes": None}
-    return {"gpu_index": index, "memory_total_bytes": int(total), "memory_free_bytes": int(free),
-            "memory_used_bytes": int(total - free)}
+    return {"gpu_index": index, "memory_total_bytes": total, "memory_free_bytes": total - used,
+            "memory_used_bytes": used}
 
 
 class InferenceStats:
