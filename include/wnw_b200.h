@@ -293,14 +293,16 @@ wnw_status wnw_fetch_layers(const void* src_k, const void* src_v, int64_t row_by
  * ranges_host / dst_host (pinned) and copies them to ranges_dev / dst_dev;
  * then wnw_fetch_layers from src_k / src_v (device addresses of the pinned
  * restore store) into land_k / land_v, recording events[l] after layer l --
- * all on `stream`.  info receives the sizes and, per layer, whether it
+ * all on `stream`.  With all buffers given, the copies, the per-layer
+ * fetches and the event records run as one CUDA graph built once per set of
+ * buffers (one graph launch per call).  info receives the sizes and, per layer, whether it
  * changed; if a capacity (plan ints, range pairs, landing rows) is too small
  * nothing is issued and WNW_ERR_CAPACITY is returned with info filled.
  * The pinned buffers must not be read by copies still in flight from a
  * previous call (synchronize `stream` first). */
 typedef struct {
   int64_t plan_ints, total_rows, n_ranges, max_moved_rows;
-  int64_t fetch_launches; /* layers with rows to fetch (one launch each)   */
+  int64_t fetch_launches; /* fetch kernels this call ran                   */
   int32_t* layer_changed; /* caller-owned [num_layers]                     */
 } wnw_fetch_info;
 wnw_status wnw_planner_issue_fetch(const wnw_planner* p, int32_t* plan_host, int32_t* plan_dev, int64_t plan_cap,

@@ -25,6 +25,7 @@
 #include <cuda_runtime.h>
 
 #include "../../include/wnw_b200.h"
+#include "fetch_graph.h"
 
 namespace wnw {
 void set_error(const char* fmt, ...);
@@ -100,7 +101,10 @@ wnw_status wnw_planner_create(int num_layers, int num_kv_heads, int batch_size, 
   return WNW_OK;
 }
 
-void wnw_planner_destroy(wnw_planner* p) { delete p; }
+void wnw_planner_destroy(wnw_planner* p) {
+  if (p) wnw::fetch_graph_release(p);
+  delete p;
+}
 
 wnw_status wnw_planner_set_config(wnw_planner* p, int top_k_chunks, int eviction_lag) {
   if (!p) return bad("null planner");
@@ -566,6 +570,33 @@ wnw_status wnw_planner_issue_fetch(const wnw_planner* p, int32_t* plan_host, int
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   st = wnw_planner_device_plan(p, plan_host, plan_cap, &used);
   if (st != WNW_OK) return st;
+  if (ranges_cap > 0 && ranges_host && ranges_dev && dst_host && dst_dev && land_k && land_v && src_k && src_v) {
+    // one graph launch: tables up, then per layer its fetch and its event
+    int64_t acc = 0;
+    for (int64_t i = 0; i < nr; ++i) {
+      ranges_host[2 * i] = p->cpu_ranges[2 * i];
+      ranges_host[2 * i + 1] = p->cpu_ranges[2 * i + 1];
+      dst_host[i] = acc;
+      acc += p->cpu_ranges[2 * i + 1] - p->cpu_ranges[2 * i];
+    }
+    wnw::FetchGraphKey k;
+    k.src_k = src_k;
+    k.src_v = src_v;
+    k.row_bytes = row_bytes;
+    k.plan_host = plan_host;
+    k.plan_dev = plan_dev;
+    k.ranges_host = ranges_host;
+    k.ranges_dev = ranges_dev;
+    k.dst_host = dst_host;
+    k.dst_dev = dst_dev;
+    k.land_k = land_k;
+    k.land_v = land_v;
+    k.max_ctas = max_ctas > 0 ? max_ctas : 32;
+    k.L = L;
+    k.events = events;
+    info->fetch_launches = L;  // the graph runs every layer's fetch kernel
+    return wnw::fetch_graph_issue(p, k, used, nr, p->layer_ranges.data(), stream, events);
+  }
   cudaError_t e = cudaMemcpyAsync(plan_dev, plan_host, sizeof(int32_t) * used, cudaMemcpyHostToDevice, s);
   if (e != cudaSuccess) return wnw::cuda_status(e, "cudaMemcpyAsync(plan)");
   if (nr > 0) {
