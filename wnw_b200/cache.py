@@ -325,6 +325,7 @@ class B200WnWCache(FlatVarlenCache):
         self._build_slots()
         self._init_planner()
         self._tail_args = None
+        self._plan_layer_checks()
         self.prefilled = True
         self.stats.record_prefill(self._snapshot_cache_stats)
 
@@ -596,19 +597,18 @@ class B200WnWCache(FlatVarlenCache):
         Returns (k_store, v_store, seg_len, max_seqlen_k); seg_len counts the
         rows stored before this step's token (cache.py:487-515 contract)."""
         l = layer_idx
+        if self._grow_flags[l]:
+            self._grow(l)
+            self._grow_flags[l] = False
         if self._pending and self._layer_chg[l]:
-            new_lens = self._next_lens[l]
-            if (new_lens + 1 > self._cap_host[l]).any():
-                self._grow(l)
             stream = self._raw_stream()
-            N.call("wnw_stream_wait_event", stream, self._event_handles[l])
-            st = N.lib.wnw_rebuild_segments(*self._rebuild_args(l), stream)
+            st = N.lib.wnw_stream_wait_event(stream, self._event_handles[l])
+            if st == 0:
+                st = N.lib.wnw_rebuild_segments(*self._rebuild_args(l), stream)
             if st:
                 N.check(st, "wnw_rebuild_segments")
             Kx.LAUNCHES[0] += 2
-            self._len_host[l] = new_lens
-        if (self._len_host[l] + 1 > self._cap_host[l]).any():
-            self._grow(l)
+            self._len_host[l] = self._next_lens[l]
         if l == self.num_layers - 1:
             self._pending = False
         S = self.batch_size * self.num_kv_heads
@@ -616,8 +616,23 @@ class B200WnWCache(FlatVarlenCache):
         nv = new_v.reshape(S, self.head_dim)
         self._new_kv[l] = (nk if nk.is_contiguous() else nk.contiguous(),
                            nv if nv.is_contiguous() else nv.contiguous())
-        self.seq_lens[l] = (self._len_host[l] + 1).tolist()
-        return self.k_store[l], self.v_store[l], self._seg_len[l], int(self._len_host[l].max()) + 1
+        self.seq_lens[l] = self._step_seq[l]
+        return self.k_store[l], self.v_store[l], self._seg_len[l], self._step_max[l]
+
+    def _plan_layer_checks(self):
+        """Per-layer facts of the coming step, computed once for all layers:
+        the rows each slot will hold before this step's token (after any
+        rebuild), whether a slot would overflow (grow first), the reference's
+        seq_lens (rows including the token) and their maximum."""
+        eff = self._len_host
+        if self._pending:
+            chg = np.asarray(self._layer_chg, bool)
+            if chg.any():
+                eff = eff.copy()
+                eff[chg] = self._next_lens[chg]
+        self._grow_flags = ((eff + 1) > self._cap_host).any(axis=1).tolist()
+        self._step_seq = eff + 1
+        self._step_max = (eff.max(axis=1) + 1).tolist() if eff.shape[1] else [1] * self.num_layers
 
     def _raw_stream(self):
         """cudaStream_t of the current torch stream on this cache's device."""
@@ -725,6 +740,7 @@ class B200WnWCache(FlatVarlenCache):
             self.loaded_segments[b] = set(self._planner.get_loaded_segments(b))
         if ch:
             self._prepare_fetch(total, ranges)
+        self._plan_layer_checks()
 
     def _tail_call(self, name, args, stream):
         st = getattr(N.lib, name)(*args, stream)
