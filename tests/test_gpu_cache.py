@@ -45,13 +45,13 @@ def _packed_with_token(cache, l):
     return k, v, cu
 
 
-def _drive(dev, trace_rec=None):
+def _drive(dev, trace_rec=None, **kw):
     from wnw_b200.cache import B200WnWCache
     from wnw_b200.config import WnWConfig
     sc = CACHE_SCENARIO
     cfg = WnWConfig(**make_config_dict(sc))
     inp = make_cache_inputs(sc)
-    cache = B200WnWCache(cfg, sc["L"], sc["Hkv"], sc["Hq"], sc["D"], dev, max_decode_tokens=3)
+    cache = B200WnWCache(cfg, sc["L"], sc["Hkv"], sc["Hq"], sc["D"], dev, max_decode_tokens=3, **kw)
     cache.setup_audio(torch.tensor(inp["audio_starts"]), torch.tensor(inp["audio_ends"]),
                       torch.tensor(inp["attention_mask"]))
     for l in range(sc["L"]):
@@ -63,9 +63,12 @@ def _drive(dev, trace_rec=None):
     return cache, inp, sc
 
 
-def test_cache_reproduces_reference_trace(dev, golden_dir):
+@pytest.mark.parametrize("tier", ["host", "hbm"])
+def test_cache_reproduces_reference_trace(dev, golden_dir, tier):
+    """offload_tier "hbm" keeps the offloaded rows in device memory; the
+    layouts, selections and outputs must not change."""
     tz = np.load(os.path.join(golden_dir, "cache_trace.npz"), allow_pickle=True)
-    cache, inp, sc = _drive(dev)
+    cache, inp, sc = _drive(dev, offload_tier=tier)
     G = sc["Hq"] // sc["Hkv"]
     for l in range(sc["L"]):
         k, v, cu = cache.packed_layer(l)

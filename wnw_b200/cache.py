@@ -98,13 +98,19 @@ class B200WnWCache(FlatVarlenCache):
       fetch_threads     -- host threads of the "dma" gather;
       fetch_ctas        -- CTAs of the zero-copy fetch (32 saturate the host
                            link and leave the SMs to the layer kernels);
+      offload_tier      -- where class-B offloaded rows live: "host" (pinned
+                           host memory, the reference's CPU offload; default)
+                           or "hbm" (device memory, for deployments whose HBM
+                           budget holds them: the same gather then reads HBM
+                           instead of crossing the host link);
       score_reduce      -- tensor parallelism by kv head (wnw_b200.tp): a
                            callable that sums the class-A score accumulator
                            over the ranks before every chunk selection.
     """
 
     def __init__(self, config, num_layers, num_kv_heads, num_q_heads, head_dim, device, adapter=None, *,
-                 max_decode_tokens=256, fetch_mode="zerocopy", fetch_threads=8, fetch_ctas=32, score_reduce=None):
+                 max_decode_tokens=256, fetch_mode="zerocopy", fetch_threads=8, fetch_ctas=32, score_reduce=None,
+                 offload_tier="host"):
         super().__init__(num_layers, num_kv_heads, num_q_heads, head_dim, device, adapter)
         if self.device.type != "cuda":
             raise RuntimeError("B200WnWCache needs a CUDA device; the CPU oracle lives in the test suite")
@@ -117,6 +123,11 @@ class B200WnWCache(FlatVarlenCache):
         if fetch_mode not in ("zerocopy", "dma"):
             raise ValueError(f"fetch_mode must be 'zerocopy' or 'dma', not {fetch_mode!r}")
         self.fetch_mode = fetch_mode
+        if offload_tier not in ("host", "hbm"):
+            raise ValueError(f"offload_tier must be 'host' or 'hbm', not {offload_tier!r}")
+        if offload_tier == "hbm" and fetch_mode != "zerocopy":
+            raise ValueError("offload_tier='hbm' is fetched by the gather kernel (fetch_mode='zerocopy')")
+        self.offload_tier = offload_tier
         self.fetch_threads = int(fetch_threads)
         self.fetch_ctas = int(fetch_ctas)
         self.score_reduce = score_reduce
@@ -284,8 +295,12 @@ class B200WnWCache(FlatVarlenCache):
                                           cfg.prefill_global_topk)[1]
         self._store_layer_off[L] = off
         if off:
-            self.cpu_restore_k = torch.empty(off, D, dtype=dtype, pin_memory=True)
-            self.cpu_restore_v = torch.empty(off, D, dtype=dtype, pin_memory=True)
+            if self.offload_tier == "hbm":
+                self.cpu_restore_k = torch.empty(off, D, dtype=dtype, device=self.device)
+                self.cpu_restore_v = torch.empty(off, D, dtype=dtype, device=self.device)
+            else:
+                self.cpu_restore_k = torch.empty(off, D, dtype=dtype, pin_memory=True)
+                self.cpu_restore_v = torch.empty(off, D, dtype=dtype, pin_memory=True)
         else:
             self.cpu_restore_k = torch.empty(0, D, dtype=dtype)
             self.cpu_restore_v = torch.empty(0, D, dtype=dtype)
@@ -870,6 +885,9 @@ class B200WnWCache(FlatVarlenCache):
 
     def _restore_dev_ptrs(self):
         if getattr(self, "_restore_ptrs", None) is None:
+            if self.cpu_restore_k.is_cuda:  # offload_tier="hbm"
+                self._restore_ptrs = (self.cpu_restore_k.data_ptr(), self.cpu_restore_v.data_ptr())
+                return self._restore_ptrs
             if not self.cpu_restore_k.is_pinned():
                 raise RuntimeError("zero-copy fetch needs the host restore store in pinned memory "
                                    "(use fetch_mode='dma')")
