@@ -407,6 +407,62 @@ def run_e2e(rec, dev, K, W, shard=None):
     return dict(ms=e0.elapsed_time(e1), in_bytes=in_bytes, out_bytes=out_bytes)
 
 
+def run_reference_gpu(rec, dev, K, W):
+    """The reference's own cache (its Python planner and Triton kernels, from
+    the offline install in baseline/_ref) on this GPU, driven by the same
+    replay -- for comparison only (the reference arm times its CPU path)."""
+    import importlib
+    ref = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref, "algorithms")):
+        return {"unavailable": "baseline/_ref (offline install of the reference) not present"}
+    sys.path.insert(0, ref)
+    try:
+        RefCache = importlib.import_module("algorithms.wnw.code.cache").WnWCache
+        RefConfig = importlib.import_module("algorithms.wnw.code.config").WnWConfig
+        c0 = rec["cfg"]
+        rcfg = RefConfig(chunk_size_s=c0.chunk_size_s, overlap_s=c0.overlap_s, token_rate=c0.token_rate,
+                         class_a=list(c0.class_a), class_b=list(c0.class_b),
+                         retention_ratios=list(c0.retention_ratios), top_k_chunks=c0.top_k_chunks,
+                         eviction_lag=c0.eviction_lag, prefill_score_mode=c0.prefill_score_mode,
+                         prefill_global_topk=c0.prefill_global_topk, num_layers=c0.num_layers,
+                         num_kv_heads=c0.num_kv_heads, num_q_heads=c0.num_q_heads)
+        cache = RefCache(rcfg, MODEL["L"], MODEL["Hkv"], MODEL["Hq"], MODEL["D"], dev, None)
+        a0, a1 = rec["audio"]
+        cache.setup_audio(torch.tensor([a0]), torch.tensor([a1]), None)
+        torch.cuda.synchronize()
+        t = time.perf_counter()
+        for l, ca, ph, k, v in rec["prefill"]:
+            cache.prefill_after_attn(l, ca, ph, k, v)
+        cache.prefill_all_layers_done()
+        torch.cuda.synchronize()
+        pre = (time.perf_counter() - t) * 1e3
+        steps, scale, L = rec["steps"], rec["scale"], MODEL["L"]
+
+        def one(i):
+            for l in range(L):
+                q, k, v = steps[i][l]
+                kk, vv, cu, _ = cache.decode_before_attn(l, k, v)
+                cache.fused_decode_attention(l, q, None, kk, vv, cu, scale)
+            cache.decode_all_layers_done()
+
+        for i in range(W):
+            one(i)
+        n = min(K, 16)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(W, W + n):
+            one(i)
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / n
+        return {"value": 1e3 / ms, "unit": "tokens/s", "ms_per_step": ms, "steps": n, "prefill_compress_ms": pre,
+                "how": "the reference's WnWCache (Python planner, Triton kernels; fused attention + scoring) "
+                       "from baseline/_ref, same replay on this GPU; informational"}
+    except Exception as e:  # report, never fail the bench on the comparison leg
+        return {"unavailable": f"{type(e).__name__}: {e}"[:300]}
+
+
 def h2d_link_probe(dev, mb=128, reps=5):
     """Zero-copy H2D bandwidth of this GPU's host link right now (the fetch
     kernel reading 128-row ranges of a pinned buffer), GB/s.  The decode step
@@ -613,6 +669,7 @@ def _main(a, rank, world, local, dist, dev, K, W, cfg_json, tp, clk):
     # the same step with the offloaded rows kept in HBM (offload_tier="hbm"),
     # for comparison only: the reference offloads to host memory
     hbm = run_value(rec, dev, K, W, shard, tier="hbm") if not dist and not a.profile else None
+    ref_gpu = run_reference_gpu(rec, dev, K, W) if not dist and not a.profile and not tp else None
     ms = val["ms"]
     if dist:
         t = torch.tensor([ms, e2e["ms"]], device=dev)
@@ -648,6 +705,7 @@ def _main(a, rank, world, local, dist, dev, K, W, cfg_json, tp, clk):
                       "how": "offloaded rows fetched per step over the host link (zero-copy kernel); link_gbs = "
                              "that kernel on 128 MB of random 128-row ranges, measured in this run"},
         "model_decode_ms_per_token": rec["model_ms"],
+        "reference_gpu": ref_gpu,
         "offload_tier_hbm": ({"value": tokens / (hbm["ms"] * 1e-3), "ms_per_step": hbm["ms"] / K,
                               "how": "same replay with offload_tier='hbm' (class-B rows in device memory, no "
                                      "host-link traffic); not the headline, which offloads to host memory as "
