@@ -101,6 +101,13 @@ typedef struct wnw_decode_attn_args {
 
 wnw_status wnw_decode_attn(const wnw_decode_attn_args* a, void* stream);
 
+/* wnw_decode_attn with the four per-step pointers given separately: `a`
+ * holds the layer's constant part (layout, work table, scratch, scoring) and
+ * is not modified.  No reference counterpart: saves the host from rewriting
+ * the argument block every layer of every step. */
+wnw_status wnw_decode_attn_step(const wnw_decode_attn_args* a, const void* q, const void* new_k,
+                                const void* new_v, void* out, void* stream);
+
 /* Allocation-free variant of wnw_decode_attn.  It has no counterpart in the
  * reference.  It is for callers that cannot allocate device memory because
  * their host owns every byte of it (a serving engine with a fixed, pre-split

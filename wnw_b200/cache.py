@@ -626,11 +626,10 @@ class B200WnWCache(FlatVarlenCache):
             self._len_host[l] = self._next_lens[l]
         if l == self.num_layers - 1:
             self._pending = False
-        S = self.batch_size * self.num_kv_heads
-        nk = new_k.reshape(S, self.head_dim)
-        nv = new_v.reshape(S, self.head_dim)
-        self._new_kv[l] = (nk if nk.is_contiguous() else nk.contiguous(),
-                           nv if nv.is_contiguous() else nv.contiguous())
+        # the kernel reads the step's rows as [S, head_dim]: any contiguous
+        # [B, Hkv, 1, D] (or [S, D]) tensor is that already
+        self._new_kv[l] = (new_k if new_k.is_contiguous() else new_k.contiguous(),
+                           new_v if new_v.is_contiguous() else new_v.contiguous())
         self.seq_lens[l] = self._step_seq[l]
         return self.k_store[l], self.v_store[l], self._seg_len[l], self._step_max[l]
 
@@ -698,10 +697,14 @@ class B200WnWCache(FlatVarlenCache):
                                      self._seg_len[l], self._work[l], self._shape[l][1], scale, self._scratch,
                                      seg_cap=self._seg_cap[l], num_kv_heads=self.num_kv_heads,
                                      score=None if sep else score, split=self._shape[l][0])
-            cached = self._attn_args[l] = (scale, sep, args)
-        _, sep, args = cached
+            cached = self._attn_args[l] = (scale, sep, args, C.byref(args))
+        _, sep, args, ref = cached
         out = torch.empty_like(qf)
-        Kx.launch_attn(args, qf, nk, nv, out, self._raw_stream())
+        st = N.lib.wnw_decode_attn_step(ref, qf.data_ptr(), nk.data_ptr(), nv.data_ptr(), out.data_ptr(),
+                                        self._raw_stream())
+        if st:
+            N.check(st, "wnw_decode_attn_step")
+        Kx.LAUNCHES[0] += 1
         if sep:
             score = self._score_args(l)  # rescore with the reference's 1/sqrt(d) (the append is idempotent)
             Kx.decode_attention(qf, self.k_store[l], self.v_store[l], self._seg_base[l], self._seg_len[l],

@@ -145,6 +145,18 @@ extern "C" wnw_status wnw_decode_attn(const wnw_decode_attn_args* a, void* strea
   }
 }
 
+extern "C" wnw_status wnw_decode_attn_step(const wnw_decode_attn_args* a, const void* q, const void* new_k,
+                                           const void* new_v, void* out, void* stream) {
+  using namespace wnw;
+  WNW_CHECK_ARG(a != nullptr, "null args");
+  wnw_decode_attn_args b = *a;
+  b.q = q;
+  b.new_k = new_k;
+  b.new_v = new_v;
+  b.out = out;
+  return wnw_decode_attn(&b, stream);
+}
+
 extern "C" wnw_status wnw_build_work_table(const int32_t* seg_cap, int num_segs, int split_rows,
                                            int cluster_size, int32_t* work, int max_clusters,
                                            int* n_clusters) {

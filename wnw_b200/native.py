@@ -115,6 +115,7 @@ _sig("wnw_h2d_async", _S, P, P, P, P, C.c_int64, P, P)
 _sig("wnw_stream_wait_event", _S, P, P)
 _sig("wnw_copy_async", _S, P, P, C.c_int64, P)
 _sig("wnw_copy_mapped", _S, P, P, C.c_int64, C.c_int, P)
+_sig("wnw_decode_attn_step", _S, C.POINTER(DecodeAttnArgs), P, P, P, P, P)
 _sig("wnw_planner_issue_fetch", _S, P, P, P, C.c_int64, P, P, P, P, C.c_int64, P, P, C.c_int64, P, P, C.c_int64,
      C.c_int, P, P, C.POINTER(FetchInfo))
 _sig("wnw_oproj_allreduce_chunks", C.c_int, C.c_int)
@@ -137,7 +138,7 @@ EXPORTS = [
     "wnw_planner_set_loaded", "wnw_planner_set_seq_lens", "wnw_planner_get_loaded_segments",
     "wnw_planner_compute_and_prepare", "wnw_planner_get_evictions", "wnw_planner_get_cpu_ranges",
     "wnw_planner_get_layer_transfer", "wnw_planner_get_changes", "wnw_planner_device_plan",
-    "wnw_gather_rows", "wnw_h2d_async", "wnw_stream_wait_event", "wnw_planner_issue_fetch", "wnw_copy_async", "wnw_copy_mapped", "wnw_oproj_allreduce",
+    "wnw_gather_rows", "wnw_h2d_async", "wnw_stream_wait_event", "wnw_planner_issue_fetch", "wnw_copy_async", "wnw_copy_mapped", "wnw_decode_attn_step", "wnw_oproj_allreduce",
     "wnw_oproj_allreduce_chunks", "wnw_ipc_alloc", "wnw_ipc_open", "wnw_ipc_close", "wnw_host_device_pointer", "wnw_fetch_rows",
     "wnw_fetch_layers",
 ]
