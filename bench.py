@@ -57,6 +57,7 @@ import torch  # noqa: E402
 MODEL = dict(L=30, hidden=3072, Hq=32, Hkv=8, D=128, inter=8192, vocab=131072, theta=1e8)
 PROMPT = dict(sink=4, audio=15000, tail=60)
 WNW = dict(frac_a=0.30, chunk=128, top_k=16, lag=1, retention=0.0, seed=1234)
+METRIC = "decode tokens/s (WnW hot path) and decode-attention HBM GB/s"
 
 
 def parse():
@@ -651,7 +652,7 @@ def _main(a, rank, world, local, dist, dev, K, W, cfg_json, tp, clk):
         n = max(1, min(a.cpu_steps, K))
         sec = cpu_replay(rec, n, start=W)
         v = 1.0 / sec
-        line = {"impl": "reference", "metric": "decode tokens/s (WnW hot path)", "value": v, "unit": "tokens/s",
+        line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s",
                 "n_gpus": a.gpus, "steps": n, "warmup": W, "ms_per_step": sec * 1e3, "higher_is_better": True,
                 "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
                 "config": cfg_json,
@@ -684,7 +685,7 @@ def _main(a, rank, world, local, dist, dev, K, W, cfg_json, tp, clk):
     fetch_bytes = val["fetched_rows"] / K * MODEL["D"] * 2 * 2
     achieved = val["attn_bytes"] / (val["attn_us"] * 1e-6) / 1e9
     line = {
-        "metric": "decode tokens/s (WnW hot path) and decode-attention HBM GB/s", "value": tokens / (ms * 1e-3),
+        "metric": METRIC, "value": tokens / (ms * 1e-3),
         "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": ms / K,
         "higher_is_better": True, "scaling": "strong" if tp else "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (random-init decoder, N(0,0.02) audio embeddings)", "config": cfg_json,
