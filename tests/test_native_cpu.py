@@ -133,3 +133,49 @@ def test_launch_shape_cuda_core_kernel():
     assert attn_launch_shape(torch.float32, 128, [100000, 5]) == (base, 8)
     with pytest.raises(N.WnwError, match="negative capacity"):
         attn_launch_shape(torch.float32, 128, [-1])
+
+
+def test_issue_fetch_reports_sizes_without_issuing(golden_dir):
+    """wnw_planner_issue_fetch checks every capacity before touching the
+    device: with empty buffers it returns WNW_ERR_CAPACITY and reports the
+    plan, range and row counts the step needs (equal to the planner's own
+    outputs), so the caller can grow its buffers and retry."""
+    from wnw_b200.planner import Planner
+    ps = PLANNER_SCENARIOS[0]
+    inp = make_planner_inputs(ps)
+    P = _planner_from(ps, inp, Planner)
+    L, S = ps["L"], ps["B"] * ps["H"]
+    bufs = [np.zeros((L, S), np.int32), np.zeros((L, S), np.int32), np.zeros((L, S + 1), np.int32),
+            np.zeros((L, S), np.int32), np.zeros((L, S + 1), np.int32), np.zeros(L, np.int32),
+            np.zeros(L + 1, np.int32)]
+    for tk, toff in inp["steps"]:
+        ch, total, _, _, ranges = P.compute_and_prepare(tk, toff, *bufs)
+        if ch and total:
+            break
+    assert ch and total
+    chg = np.full(L, -1, np.int32)
+    info = N.FetchInfo()
+    info.layer_changed = chg.ctypes.data
+    st = N.lib.wnw_planner_issue_fetch(P._h, None, None, 0, None, None, None, None, 0, None, None, 256, None, None,
+                                       0, 32, None, None, ctypes.byref(info))
+    assert st == N.WNW_ERR_CAPACITY
+    assert info.total_rows == total and info.n_ranges == len(ranges)
+    assert info.plan_ints == P.device_plan().size
+    blob = P.device_plan()
+    for l in range(L):
+        assert chg[l] == (1 if blob[blob[l]] > 0 else 0)
+    assert b"capacity" in N.lib.wnw_last_error()
+
+
+def test_oproj_allreduce_rejects_bad_arguments():
+    """Argument checks of the tensor-parallel exchange run before any launch."""
+    a = N.OprojAllReduceArgs()
+    a.dtype, a.batch, a.n_out, a.k_in, a.rank, a.world = N.BF16, 1, 64, 60, 0, 1
+    st = N.lib.wnw_oproj_allreduce(ctypes.byref(a), None)
+    assert st == 1 and b"multiple of 8" in N.lib.wnw_last_error()
+    a.k_in, a.world, a.rank = 64, 9, 0
+    assert N.lib.wnw_oproj_allreduce(ctypes.byref(a), None) == 1
+    a.world, a.batch = 1, 9
+    assert N.lib.wnw_oproj_allreduce(ctypes.byref(a), None) == 1
+    assert N.lib.wnw_oproj_allreduce_chunks(3072) == 384
+    assert N.lib.wnw_oproj_allreduce_chunks(0) == 0
