@@ -192,12 +192,19 @@ wnw_status wnw_chunk_topk(const float* acc, const int32_t* score_off, int batch,
  * validated against seg_len / seg_cap (status[n_chg] scratch); then moved and
  * fetched (`landing`) rows are written to their final slot rows and seg_len
  * is set.  A record that fails validation moves nothing and sets
- * WNW_DEVERR_LEN_MISMATCH (or _CAPACITY) in *err. */
+ * WNW_DEVERR_LEN_MISMATCH (or _CAPACITY) in *err.  Every index the blob
+ * holds is checked against the sizes given here before it is used: the
+ * layer record against blob_ints (ints in plan_blob), segment numbers against
+ * num_segs (the entries of seg_base / seg_len / seg_cap, and of status),
+ * landing rows against land_rows (rows of k_landing / v_landing), moved rows
+ * against move_rows -- a malformed layer record makes the whole call a no-op
+ * with the error bit set. */
 wnw_status wnw_rebuild_segments(int dtype, int head_dim, void* k_store, void* v_store,
                                 const int64_t* seg_base, int32_t* seg_len, const int32_t* seg_cap,
-                                const void* k_landing, const void* v_landing,
-                                const int32_t* plan_blob, int layer, void* k_move, void* v_move,
-                                int64_t move_rows, int32_t* status, int32_t* err, void* stream);
+                                int num_segs, const void* k_landing, const void* v_landing,
+                                int64_t land_rows, const int32_t* plan_blob, int64_t blob_ints,
+                                int layer, void* k_move, void* v_move, int64_t move_rows,
+                                int32_t* status, int32_t* err, void* stream);
 
 /* Copy rows [0, len[s]) of every segment from src (+src_base[s]) to dst
  * (+dst_base[s]); src and dst must not overlap.  Used to pack a slot layout

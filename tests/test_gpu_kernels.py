@@ -302,6 +302,59 @@ def test_rebuild_matches_oracle(dev):
     assert torch.equal(ks, snap)
 
 
+def test_rebuild_refuses_malformed_plans(dev):
+    """Host-side fault injection: corrupted plan blobs (a layer offset past the
+    blob, more records than segments, a segment number out of range, landing
+    rows past the landing buffer, more moved rows than the move buffer) are
+    refused by the kernels' own checks -- error bit set, nothing written."""
+    from wnw_b200 import kernels as Kx
+    from wnw_b200 import native as N
+    D, dtype = 64, torch.bfloat16
+    lens = [300, 50, 900]
+    ks, vs, base, cap = _slots(lens, 400, D, dtype, dev, seed=21)
+    base_d = torch.from_numpy(base).to(dev)
+    cap_d = torch.from_numpy(cap.astype(np.int32)).to(dev)
+    land_k = torch.randn(64, D, device=dev).to(dtype)
+    land_v = torch.randn(64, D, device=dev).to(dtype)
+    move_k = torch.empty(1024, D, dtype=dtype, device=dev)
+    move_v = torch.empty_like(move_k)
+    status = torch.zeros(len(lens), dtype=torch.int32, device=dev)
+
+    def good(seg=0, ls=0, ll=10):
+        return (seg, lens[0], lens[0] - 20 + ll, ls, ll, [(100, 120)])
+
+    cases = {}
+    b = Kx.pack_plan([[good()]]).copy()
+    b[0] = 10 ** 6
+    cases["layer offset past the blob"] = (b, 1024)
+    b = Kx.pack_plan([[good()]]).copy()
+    b[b[0]] = 1000
+    cases["more records than segments"] = (b, 1024)
+    cases["segment out of range"] = (Kx.pack_plan([[good(seg=99)]]), 1024)
+    cases["landing rows past the buffer"] = (Kx.pack_plan([[good(ls=60, ll=10)]]), 1024)
+    cases["moved rows past the move buffer"] = (Kx.pack_plan([[good()]]), 8)
+    for name, (blob, move_rows) in cases.items():
+        snap_k, snap_v = ks.clone(), vs.clone()
+        seg_len = torch.tensor(lens, dtype=torch.int32, device=dev)
+        err = torch.zeros(1, dtype=torch.int32, device=dev)
+        N.call("wnw_rebuild_segments", N.BF16, D, ks.data_ptr(), vs.data_ptr(), base_d.data_ptr(),
+               seg_len.data_ptr(), cap_d.data_ptr(), len(lens), land_k.data_ptr(), land_v.data_ptr(),
+               land_k.shape[0], torch.from_numpy(blob).to(dev).data_ptr(), int(blob.size), 0, move_k.data_ptr(),
+               move_v.data_ptr(), move_rows, status.data_ptr(), err.data_ptr(), N.stream_ptr(None))
+        torch.cuda.synchronize()
+        assert int(err.item()) & (N.DEVERR_LEN_MISMATCH | N.DEVERR_CAPACITY), name
+        assert torch.equal(ks, snap_k) and torch.equal(vs, snap_v), name
+        assert seg_len.cpu().tolist() == lens, name
+    # the same record, well formed, is applied
+    seg_len = torch.tensor(lens, dtype=torch.int32, device=dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    blob = Kx.pack_plan([[good()]])
+    Kx.rebuild_layer(ks, vs, base_d, seg_len, cap_d, land_k, land_v, torch.from_numpy(blob).to(dev), 0,
+                     move_k, move_v, status, err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0 and seg_len.cpu().tolist()[0] == lens[0] - 10
+
+
 def test_copy_segments_and_interleave_append_exact(dev):
     from wnw_b200 import kernels as Kx
     rng = np.random.default_rng(2)

@@ -661,8 +661,11 @@ class B200WnWCache(FlatVarlenCache):
             a = self._rb_args[l] = (
                 N.dtype_code(self.dtype), self.head_dim, self.k_store[l].data_ptr(), self.v_store[l].data_ptr(),
                 self._seg_base[l].data_ptr(), self._seg_len[l].data_ptr(), self._seg_cap[l].data_ptr(),
+                int(self._seg_len[l].numel()),
                 self._land_k.data_ptr() if self._land_k is not None else None,
-                self._land_v.data_ptr() if self._land_v is not None else None, self._plan_dev.data_ptr(), l,
+                self._land_v.data_ptr() if self._land_v is not None else None,
+                int(self._land_k.shape[0]) if self._land_k is not None else 0,
+                self._plan_dev.data_ptr(), int(self._plan_dev.numel()), l,
                 mk.data_ptr() if mk is not None else None, mv.data_ptr() if mv is not None else None,
                 int(mk.shape[0]) if mk is not None else 0, self._rb_status.data_ptr(), self._scratch.err.data_ptr())
         return a

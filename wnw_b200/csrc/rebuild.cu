@@ -50,6 +50,40 @@ struct RbRec {
   }
 };
 
+// Whether layer `layer`'s record lies inside the blob and its offset arrays
+// are well formed (start at 0, non-decreasing, end at the totals), with at
+// most num_segs records -- checked before anything else reads the record.
+__device__ inline bool record_well_formed(const int32_t* blob, int64_t blob_ints, int layer, int num_segs) {
+  if (layer < 0 || int64_t(layer) >= blob_ints) return false;
+  const int64_t o = blob[layer];
+  if (o < 0 || o + 3 > blob_ints) return false;
+  const int64_t n = blob[o];
+  if (n < 0 || n > num_segs) return false;
+  const int64_t fixed = 3 + 5 * n + 3 * (n + 1);
+  if (o + fixed > blob_ints) return false;
+  const int32_t* h = blob + o;
+  const int32_t* mov_off = h + 3 + 5 * n;
+  const int32_t* out_off = mov_off + n + 1;
+  const int32_t* ev_off = out_off + n + 1;
+  if (h[1] < 0 || h[2] < 0 || mov_off[0] != 0 || out_off[0] != 0 || ev_off[0] != 0) return false;
+  for (int64_t i = 0; i < n; ++i)
+    if (mov_off[i + 1] < mov_off[i] || out_off[i + 1] < out_off[i] || ev_off[i + 1] < ev_off[i]) return false;
+  if (mov_off[n] != h[1] || out_off[n] != h[2]) return false;
+  return o + fixed + 2 * int64_t(ev_off[n]) <= blob_ints;
+}
+
+// Every CTA checks the layer record once; on a malformed record the block 0
+// thread 0 raises the error bit and every CTA returns before reading it.
+__device__ inline bool cta_record_ok(const int32_t* blob, int64_t blob_ints, int layer, int num_segs, int32_t* err) {
+  __shared__ int s_ok;
+  if (threadIdx.x == 0) {
+    s_ok = record_well_formed(blob, blob_ints, layer, num_segs) ? 1 : 0;
+    if (!s_ok && blockIdx.x == 0) atomicOr(err, WNW_DEVERR_LEN_MISMATCH);
+  }
+  __syncthreads();
+  return s_ok != 0;
+}
+
 // Kept-row index k (0-based among the kept rows after the first evicted
 // range) -> slot-relative source row.
 __device__ inline int kept_source_row(const RbRec& r, int i, int k) {
@@ -68,14 +102,21 @@ __device__ inline int kept_source_row(const RbRec& r, int i, int k) {
 // Phase 1: validate every record, gather the moving kept rows into scratch.
 __global__ void __launch_bounds__(kRbThreads)
     rebuild_gather_kernel(const uint4* k_store, const uint4* v_store, const int64_t* seg_base, const int32_t* seg_len,
-                          const int32_t* seg_cap, const int32_t* blob, int layer, uint4* k_move, uint4* v_move,
-                          int64_t move_rows, int32_t* status, int32_t* err, int cpr) {
+                          const int32_t* seg_cap, const int32_t* blob, int64_t blob_ints, int layer, int num_segs,
+                          int64_t land_rows, uint4* k_move, uint4* v_move, int64_t move_rows, int32_t* status,
+                          int32_t* err, int cpr) {
+  if (!cta_record_ok(blob, blob_ints, layer, num_segs, err)) return;
   const RbRec r(blob, layer);
   const int64_t gtid = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
   const int64_t nthreads = int64_t(gridDim.x) * blockDim.x;
   for (int i = static_cast<int>(gtid); i < r.n; i += static_cast<int>(nthreads)) {
     const int seg = r.seg[i];
     const int e0 = r.ev_off[i], e1 = r.ev_off[i + 1];
+    if (seg < 0 || seg >= num_segs) {  // nothing of this record is read or written
+      atomicOr(err, WNW_DEVERR_LEN_MISMATCH);
+      status[i] = 0;
+      continue;
+    }
     int ok = seg_len[seg] == r.old_len[i] ? 1 : 0;
     int prev = 0, evicted = 0;
     for (int e = e0; e < e1 && ok; ++e) {
@@ -85,7 +126,9 @@ __global__ void __launch_bounds__(kRbThreads)
     }
     const int moved = r.mov_off[i + 1] - r.mov_off[i];
     if (ok && (r.old_len[i] - evicted + r.llen[i] != r.new_len[i] || r.llen[i] < 0 || r.lsrc[i] < 0 ||
-               moved != (e1 > e0 ? r.old_len[i] - evicted - r.ev_s[e0] : 0)))
+               moved != (e1 > e0 ? r.old_len[i] - evicted - r.ev_s[e0] : 0) ||
+               r.out_off[i + 1] - r.out_off[i] != moved + r.llen[i] ||
+               int64_t(r.lsrc[i]) + r.llen[i] > (r.llen[i] > 0 ? land_rows : int64_t(INT32_MAX))))
       ok = 0;
     if (!ok) atomicOr(err, WNW_DEVERR_LEN_MISMATCH);
     if (ok && r.new_len[i] + 1 > seg_cap[seg]) {
@@ -103,9 +146,10 @@ __global__ void __launch_bounds__(kRbThreads)
     const int row = static_cast<int>(x / cpr);
     const int c = static_cast<int>(x % cpr);
     const int i = r.find(r.mov_off, row);
-    const int src = kept_source_row(r, i, row - r.mov_off[i]);
     const int seg = r.seg[i];
-    if (src < 0 || src >= seg_cap[seg]) continue;  // malformed record: refused by status[i]
+    if (seg < 0 || seg >= num_segs) continue;  // malformed record: refused by status[i]
+    const int src = kept_source_row(r, i, row - r.mov_off[i]);
+    if (src < 0 || src >= seg_cap[seg]) continue;
     const int64_t s = (seg_base[seg] + src) * cpr + c;
     k_move[int64_t(row) * cpr + c] = k_store[s];
     v_move[int64_t(row) * cpr + c] = v_store[s];
@@ -116,12 +160,15 @@ __global__ void __launch_bounds__(kRbThreads)
 __global__ void __launch_bounds__(kRbThreads)
     rebuild_scatter_kernel(uint4* k_store, uint4* v_store, const int64_t* seg_base, int32_t* seg_len,
                            const int32_t* seg_cap, const uint4* k_land, const uint4* v_land, const int32_t* blob,
-                           int layer, const uint4* k_move, const uint4* v_move, const int32_t* status, int cpr) {
+                           int64_t blob_ints, int layer, int num_segs, int64_t move_rows, const uint4* k_move,
+                           const uint4* v_move, const int32_t* status, int32_t* err, int cpr) {
   // the layer's decode attention (launched with programmatic dependent launch)
   // may start its layout-only prologue now; it waits for this grid to finish
   // before it reads anything written here
   pdl_launch_dependents();
+  if (!cta_record_ok(blob, blob_ints, layer, num_segs, err)) return;
   const RbRec r(blob, layer);
+  if (r.moved_total > move_rows) return;  // refused by the gather (error bit set there)
   const int64_t gtid = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
   const int64_t nthreads = int64_t(gridDim.x) * blockDim.x;
   const int64_t total = int64_t(r.out_total) * cpr;
@@ -188,13 +235,15 @@ inline int row_bytes_of(int dtype, int head_dim) { return head_dim * (dtype == W
 
 extern "C" wnw_status wnw_rebuild_segments(int dtype, int head_dim, void* k_store, void* v_store,
                                            const int64_t* seg_base, int32_t* seg_len, const int32_t* seg_cap,
-                                           const void* k_landing, const void* v_landing, const int32_t* plan_blob,
+                                           int num_segs, const void* k_landing, const void* v_landing,
+                                           int64_t land_rows, const int32_t* plan_blob, int64_t blob_ints,
                                            int layer, void* k_move, void* v_move, int64_t move_rows,
                                            int32_t* status, int32_t* err, void* stream) {
   using namespace wnw;
   WNW_CHECK_ARG(k_store && v_store && seg_base && seg_len && seg_cap && plan_blob && status && err,
                 "null pointer argument");
-  WNW_CHECK_ARG(layer >= 0, "negative layer");
+  WNW_CHECK_ARG(layer >= 0 && num_segs >= 0 && land_rows >= 0 && blob_ints > layer,
+                "negative layer / sizes, or a blob too small for the layer table");
   WNW_CHECK_ARG(aligned16(k_store) && aligned16(v_store), "stores must be 16-byte aligned");
   WNW_CHECK_ARG(k_landing == nullptr || (aligned16(k_landing) && aligned16(v_landing)),
                 "landing buffers must be 16-byte aligned");
@@ -205,12 +254,14 @@ extern "C" wnw_status wnw_rebuild_segments(int dtype, int head_dim, void* k_stor
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   rebuild_gather_kernel<<<kRbMaxBlocks, kRbThreads, 0, s>>>(
       static_cast<const uint4*>(k_store), static_cast<const uint4*>(v_store), seg_base, seg_len, seg_cap, plan_blob,
-      layer, static_cast<uint4*>(k_move), static_cast<uint4*>(v_move), move_rows, status, err, rb / 16);
+      blob_ints, layer, num_segs, k_landing ? land_rows : 0, static_cast<uint4*>(k_move),
+      static_cast<uint4*>(v_move), move_rows, status, err, rb / 16);
   WNW_CUDA_TRY(cudaGetLastError());
   rebuild_scatter_kernel<<<kRbMaxBlocks, kRbThreads, 0, s>>>(
       static_cast<uint4*>(k_store), static_cast<uint4*>(v_store), seg_base, seg_len, seg_cap,
-      static_cast<const uint4*>(k_landing), static_cast<const uint4*>(v_landing), plan_blob, layer,
-      static_cast<const uint4*>(k_move), static_cast<const uint4*>(v_move), status, rb / 16);
+      static_cast<const uint4*>(k_landing), static_cast<const uint4*>(v_landing), plan_blob, blob_ints, layer,
+      num_segs, move_rows, static_cast<const uint4*>(k_move), static_cast<const uint4*>(v_move), status, err,
+      rb / 16);
   WNW_CUDA_TRY(cudaGetLastError());
   return WNW_OK;
 }

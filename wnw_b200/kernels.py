@@ -201,10 +201,12 @@ def rebuild_layer(k_store, v_store, seg_base, seg_len, seg_cap, k_landing, v_lan
                   k_move, v_move, status, err, stream=None):
     """Compaction + splice of one layer's changed slots (two launches)."""
     N.call("wnw_rebuild_segments", N.dtype_code(k_store.dtype), k_store.shape[1], k_store.data_ptr(),
-           v_store.data_ptr(), seg_base.data_ptr(), seg_len.data_ptr(), seg_cap.data_ptr(),
+           v_store.data_ptr(), seg_base.data_ptr(), seg_len.data_ptr(), seg_cap.data_ptr(), int(seg_len.numel()),
            k_landing.data_ptr() if k_landing is not None else None,
-           v_landing.data_ptr() if v_landing is not None else None, plan_blob.data_ptr(), int(layer),
-           k_move.data_ptr() if k_move is not None else None, v_move.data_ptr() if v_move is not None else None,
+           v_landing.data_ptr() if v_landing is not None else None,
+           int(k_landing.shape[0]) if k_landing is not None else 0, plan_blob.data_ptr(), int(plan_blob.numel()),
+           int(layer), k_move.data_ptr() if k_move is not None else None,
+           v_move.data_ptr() if v_move is not None else None,
            int(k_move.shape[0]) if k_move is not None else 0, status.data_ptr(), err.data_ptr(),
            N.stream_ptr(stream))
     _count(2)

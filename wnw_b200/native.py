@@ -89,7 +89,8 @@ _sig("wnw_build_work_table", _S, P, C.c_int, C.c_int, C.c_int, P, C.c_int, C.POI
 _sig("wnw_advance_lengths", _S, P, C.c_int64, P)
 _sig("wnw_score_finalize", _S, P, P, P, P, P, P, C.c_int, C.c_int, P, C.c_int, P, P)
 _sig("wnw_chunk_topk", _S, P, P, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, P, P, P, P)
-_sig("wnw_rebuild_segments", _S, C.c_int, C.c_int, P, P, P, P, P, P, P, P, C.c_int, P, P, C.c_int64, P, P, P)
+_sig("wnw_rebuild_segments", _S, C.c_int, C.c_int, P, P, P, P, P, C.c_int, P, P, C.c_int64, P, C.c_int64, C.c_int,
+     P, P, C.c_int64, P, P, P)
 _sig("wnw_copy_segments", _S, C.c_int, C.c_int, P, P, P, P, P, P, P, C.c_int, P)
 _sig("wnw_interleave_append", _S, C.c_int, C.c_int, P, P, P, C.c_int, P, P)
 _sig("wnw_planner_create", _S, C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(P))
