@@ -2,8 +2,9 @@
 INFRASTRUCTURE ONLY (the checker, never the product).
 
 The source compiles in place from the reference checkout
-(``src/algorithms/wnw_cpp/code/planner.cpp``; default root
-``/root/reference``, override with ``WNW_REFERENCE_ROOT``) with torch's
+(``src/algorithms/wnw_cpp/code/planner.cpp``; the checkout named by
+``WNW_REFERENCE_ROOT``, by default a ``reference`` directory beside this
+repository) with torch's
 extension builder, exactly as the reference's ``_ext.py:18-47`` does (-O3),
 but with the build directory under ``oracle/_ref`` so the module travels with
 the repository snapshot and never lands in a user cache.  No reference source
@@ -24,7 +25,8 @@ NAME = "wnw_ref_planner"
 
 
 def source_path():
-    root = os.environ.get("WNW_REFERENCE_ROOT", "/root/reference")
+    root = os.environ.get("WNW_REFERENCE_ROOT",
+                          os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference"))
     return os.path.join(root, "src", "algorithms", "wnw_cpp", "code", "planner.cpp")
 
 

@@ -1,7 +1,8 @@
 """Generate golden fixtures by EXECUTING the XMUDeepLIT/WnW reference on CPU.
 
-Run in a container that has the reference checked out (default
-``/root/reference/src``, override with ``WNW_REFERENCE_SRC``)::
+Run in a container that has the reference checked out (its ``src``
+directory named by ``WNW_REFERENCE_SRC``, by default ``reference/src`` beside
+this repository)::
 
     python tests/golden/make_golden.py
 
@@ -27,7 +28,8 @@ import sys
 os.environ["TRITON_INTERPRET"] = "1"
 os.environ["WNW_FUSED_ATTN"] = "1"
 os.environ.setdefault("TORCH_EXTENSIONS_DIR", "/tmp/wnw_golden_ext")
-REF = os.environ.get("WNW_REFERENCE_SRC", "/root/reference/src")
+REF = os.environ.get("WNW_REFERENCE_SRC", os.path.join(
+    os.path.dirname(os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))), "reference", "src"))
 sys.path.insert(0, REF)
 
 import numpy as np  # noqa: E402

@@ -179,3 +179,27 @@ def test_oproj_allreduce_rejects_bad_arguments():
     assert N.lib.wnw_oproj_allreduce(ctypes.byref(a), None) == 1
     assert N.lib.wnw_oproj_allreduce_chunks(3072) == 384
     assert N.lib.wnw_oproj_allreduce_chunks(0) == 0
+
+
+def test_step_wait_times_out_instead_of_blocking():
+    """The decode step's host wait has a deadline: a device that never gets
+    there (a fake event that never completes) raises a timeout error."""
+    import time
+    from wnw_b200.cache import wait_event
+
+    class Never:
+        def query(self):
+            return False
+
+    class Later:
+        def __init__(self):
+            self.t = time.perf_counter() + 0.05
+
+        def query(self):
+            return time.perf_counter() > self.t
+
+    t0 = time.perf_counter()
+    with pytest.raises(N.WnwError, match="timed out"):
+        wait_event(Never(), 0.2)
+    assert time.perf_counter() - t0 < 5
+    wait_event(Later(), 5.0)  # completes in time: no error

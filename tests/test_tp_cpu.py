@@ -132,3 +132,40 @@ def test_two_rank_oracle_matches_single_process():
     for p in ps:
         p.join(timeout=60)
     assert res == {0: "ok", 1: "ok"}, res
+
+
+def _dead_peer(rank, world, port, q):
+    import datetime
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
+    if rank == 1:
+        q.put((1, "left"))
+        q.close()
+        q.join_thread()  # the message is out before the process dies
+        os._exit(0)  # leaves between steps, before the score reduction
+    t0 = __import__("time").perf_counter()
+    try:
+        ScoreReducer()(torch.ones(4))
+        q.put((0, "no error"))
+    except Exception:
+        q.put((0, f"raised after {__import__('time').perf_counter() - t0:.1f} s"))
+
+
+def test_dead_rank_fails_the_score_reduction():
+    """Failure detection on the host: a tensor-parallel rank that leaves
+    between steps makes the survivors' next score reduction raise (a closed
+    peer or the process group's timeout) instead of hanging."""
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    ps = [ctx.Process(target=_dead_peer, args=(r, world, port, q)) for r in range(world)]
+    for p in ps:
+        p.start()
+    res = dict(q.get(timeout=60) for _ in range(world))
+    for p in ps:
+        p.join(timeout=30)
+        if p.is_alive():
+            p.kill()
+    assert res[1] == "left"
+    assert res[0].startswith("raised"), res

@@ -27,6 +27,7 @@ from __future__ import annotations
 
 import ctypes as C
 import math
+import time
 from itertools import accumulate
 
 import numpy as np
@@ -48,6 +49,18 @@ def compute_chunks(segments, chunk_size, stride):
     spc = math.ceil(chunk_size / stride)
     n = len(segments)
     return [list(range(i, min(i + spc, n))) for i in range(n)]
+
+
+def wait_event(event, timeout_s):
+    """Wait for a CUDA event with a host deadline: WnwError(WNW_ERR_TIMEOUT)
+    instead of blocking forever when the device never gets there."""
+    if event.query():
+        return
+    deadline = time.perf_counter() + timeout_s
+    while not event.query():
+        if time.perf_counter() > deadline:
+            raise N.WnwError(5, "decode step", f"device work not finished after {timeout_s:g} s")
+        time.sleep(0)
 
 
 def keep_audio_indices(scores, seg_ranges, ratio, global_topk):
@@ -98,6 +111,8 @@ class B200WnWCache(FlatVarlenCache):
       fetch_threads     -- host threads of the "dma" gather;
       fetch_ctas        -- CTAs of the zero-copy fetch (32 saturate the host
                            link and leave the SMs to the layer kernels);
+      wait_timeout_s    -- the step waits this long for its scores and
+                           errors on the device, then raises a timeout error;
       offload_tier      -- where class-B offloaded rows live: "host" (pinned
                            host memory, the reference's CPU offload; default)
                            or "hbm" (device memory, for deployments whose HBM
@@ -110,7 +125,7 @@ class B200WnWCache(FlatVarlenCache):
 
     def __init__(self, config, num_layers, num_kv_heads, num_q_heads, head_dim, device, adapter=None, *,
                  max_decode_tokens=256, fetch_mode="zerocopy", fetch_threads=8, fetch_ctas=32, score_reduce=None,
-                 offload_tier="host"):
+                 offload_tier="host", wait_timeout_s=60.0):
         super().__init__(num_layers, num_kv_heads, num_q_heads, head_dim, device, adapter)
         if self.device.type != "cuda":
             raise RuntimeError("B200WnWCache needs a CUDA device; the CPU oracle lives in the test suite")
@@ -128,6 +143,7 @@ class B200WnWCache(FlatVarlenCache):
         if offload_tier == "hbm" and fetch_mode != "zerocopy":
             raise ValueError("offload_tier='hbm' is fetched by the gather kernel (fetch_mode='zerocopy')")
         self.offload_tier = offload_tier
+        self.wait_timeout_s = float(wait_timeout_s)
         self.fetch_threads = int(fetch_threads)
         self.fetch_ctas = int(fetch_ctas)
         self.score_reduce = score_reduce
@@ -741,7 +757,7 @@ class B200WnWCache(FlatVarlenCache):
         self._tail_call("wnw_copy_async", a["topk_d2h"], st)
         self._tail_call("wnw_copy_async", a["err_d2h"], st)
         self._ready.record()
-        self._ready.synchronize()
+        wait_event(self._ready, self.wait_timeout_s)
         if int(a["err_np"][0]):
             Kx.check_device_error(self._scratch.err)
         if select:
