@@ -351,6 +351,10 @@ class OracleWnWCache:
             self._prepare_pending()
         self.score_accumulator[:] = 0
 
+    def _select(self, b, cs, k):
+        """The k chunks of sample b to keep loaded (cache.py:641-642)."""
+        return K.topk_lower_index(cs, k)
+
     def _chunk_changes(self, b, scores):
         """cache.py:632-649 then 609-630."""
         bounds = self.chunk_bounds[b]
@@ -362,7 +366,7 @@ class OracleWnWCache:
         if k == 0:
             self.last_topk[b] = []
             return set(), set()
-        top = K.topk_lower_index(cs, k)
+        top = self._select(b, cs, k)
         self.last_topk[b] = sorted(top)
         needed = {si for ci in top for si in self.chunk_to_segs[b][ci]}
         loaded = self.loaded_segments[b]
