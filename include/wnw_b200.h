@@ -38,6 +38,7 @@ typedef enum wnw_dtype { WNW_F32 = 0, WNW_F16 = 1, WNW_BF16 = 2 } wnw_dtype;
 #define WNW_DEVERR_LEN_MISMATCH 2   /* rebuild plan disagrees with seg_len   */
 #define WNW_DEVERR_CAPACITY 4       /* a segment would exceed its slot       */
 #define WNW_DEVERR_PEER_TIMEOUT 8   /* a tensor-parallel peer's partials did not arrive */
+#define WNW_DEVERR_BAD_INDEX 16     /* device fetch plan: top-k chunk or segment index out of range */
 
 int wnw_abi_version(void);
 const char* wnw_status_string(wnw_status s);
@@ -324,6 +325,49 @@ wnw_status wnw_planner_issue_fetch(const wnw_planner* p, int32_t* plan_host, int
                                    int64_t ranges_cap, const void* src_k, const void* src_v, int64_t row_bytes,
                                    void* land_k, void* land_v, int64_t land_rows, int max_ctas, void* stream,
                                    void* const* events, wnw_fetch_info* info);
+
+/* The step's rebuild plan only: after wnw_planner_compute_and_prepare
+ * reported a change, write the device-plan blob into plan_host (pinned) and
+ * copy it to plan_dev on `stream`; fill info (plan ints, landed rows, ranges,
+ * moved rows, changed layers).  The fetch itself is not issued: this is the
+ * host half of the device-planned step (wnw_dplan_step below).  Replaces the
+ * plan-blob part of the reference's staging path
+ * (src/algorithms/wnw/code/cache.py:868-889).  WNW_ERR_CAPACITY (nothing
+ * copied, info filled) when plan_cap is too small. */
+wnw_status wnw_planner_upload_plan(const wnw_planner* p, int32_t* plan_host, int32_t* plan_dev, int64_t plan_cap,
+                                   void* stream, wnw_fetch_info* info);
+
+/* Device mirror of the planner's selection state, so that a step's fetch is
+ * planned on the GPU straight from the device top-k and starts with no host
+ * round trip.  No reference counterpart as a call: it restates, on the
+ * device, the selection diff and range emission of the reference planner
+ * (src/algorithms/wnw_cpp/code/planner.cpp:124-306; the Python path's
+ * cache.py:609-630 and 771-823) for the fetch only; the host planner still
+ * plans the rebuild and checks the device's result (wnw_dplan_verify).
+ *
+ * create: copies the planner's tables and current loaded sets / eviction
+ *   counters to the device (synchronous; call after the prefill state is
+ *   handed to the planner).  WNW_ERR_UNSUPPORTED when the per-step state does
+ *   not fit one thread block's shared memory (the caller keeps the host path).
+ * step: on compute_stream, one kernel turns the top-k rows topk_dev
+ *   ([B][topk_stride] chunk ids, -1 padded) into this step's loads (updating
+ *   the mirrored loaded sets and counters exactly as the planner does) and
+ *   their host ranges and landing rows; then copy_stream waits for it and runs
+ *   the per-layer fetch (src_k / src_v -> land_k / land_v, events[l] after
+ *   layer l) as one CUDA graph.  Bad indices or a landing overflow set
+ *   WNW_DEVERR_BAD_INDEX / WNW_DEVERR_CAPACITY in *err and fetch nothing.
+ * verify: after the host has waited for the step and run
+ *   wnw_planner_compute_and_prepare on the same top-k, compare the device's
+ *   per-layer landing rows, loaded sets and counters with the planner's;
+ *   WNW_ERR_STATE on any difference. */
+typedef struct wnw_dplan wnw_dplan;
+wnw_status wnw_dplan_create(const wnw_planner* p, wnw_dplan** out);
+void wnw_dplan_destroy(wnw_dplan* dp);
+wnw_status wnw_dplan_step(wnw_dplan* dp, const int32_t* topk_dev, int topk_stride, int32_t* err,
+                          const void* src_k, const void* src_v, int64_t row_bytes, void* land_k, void* land_v,
+                          int64_t land_rows, int max_ctas, void* compute_stream, void* copy_stream,
+                          void* const* events);
+wnw_status wnw_dplan_verify(const wnw_dplan* dp, const wnw_planner* p);
 
 /* Kernel copy of `bytes` (a multiple of 16, 16-byte aligned) from `src` --
  * typically the device address of pinned host memory (wnw_host_device_pointer)

@@ -63,13 +63,16 @@ def _drive(dev, trace_rec=None, **kw):
     return cache, inp, sc
 
 
-@pytest.mark.parametrize("tier,fetch", [("host", "zerocopy"), ("hbm", "zerocopy"), ("host", "dma")])
-def test_cache_reproduces_reference_trace(dev, golden_dir, tier, fetch):
-    """offload_tier "hbm" keeps the offloaded rows in device memory and
-    fetch_mode "dma" gathers them on the host and copies them with the copy
-    engine; the layouts, selections and outputs must not change."""
+@pytest.mark.parametrize("tier,fetch,plan", [("host", "zerocopy", "device"), ("hbm", "zerocopy", "device"),
+                                             ("host", "zerocopy", "host"), ("host", "dma", "host")])
+def test_cache_reproduces_reference_trace(dev, golden_dir, tier, fetch, plan):
+    """offload_tier "hbm" keeps the offloaded rows in device memory, fetch_mode
+    "dma" gathers them on the host and copies them with the copy engine, and
+    fetch_plan "host" plans the fetch on the host instead of the device; the
+    layouts, selections and outputs must not change."""
     tz = np.load(os.path.join(golden_dir, "cache_trace.npz"), allow_pickle=True)
-    cache, inp, sc = _drive(dev, offload_tier=tier, fetch_mode=fetch)
+    cache, inp, sc = _drive(dev, offload_tier=tier, fetch_mode=fetch, fetch_plan=plan)
+    assert (cache._dplan is not None) == (plan == "device")
     G = sc["Hq"] // sc["Hkv"]
     for l in range(sc["L"]):
         k, v, cu = cache.packed_layer(l)

@@ -36,7 +36,7 @@ import torch
 from wnw_b200 import kernels as Kx
 from wnw_b200 import native as N
 from wnw_b200.flat_cache import FlatVarlenCache
-from wnw_b200.planner import Planner, gather_rows
+from wnw_b200.planner import DevicePlan, Planner, gather_rows
 
 
 def compute_segments(num_audio, stride):
@@ -110,8 +110,15 @@ class B200WnWCache(FlatVarlenCache):
                            memory; "dma": host threads gather them into pinned
                            staging and cudaMemcpyAsync copies each layer;
       fetch_threads     -- host threads of the "dma" gather;
-      fetch_ctas        -- CTAs of the zero-copy fetch (32 saturate the host
-                           link and leave the SMs to the layer kernels);
+      fetch_ctas        -- CTAs of the zero-copy fetch: 12 (~0.8 MB of host
+                           reads in flight) keep the link saturated; more only
+                           queue requests in the memory system and slow the
+                           layer kernels running beside the fetch;
+      fetch_plan        -- "device" (default): each step's fetch is planned
+                           on the GPU from the device top-k and starts at
+                           once, while the host planner plans the rebuild and
+                           checks the device's result; "host": the host plans
+                           the fetch after reading the top-k back;
       wait_timeout_s    -- the step waits this long for its scores and
                            errors on the device, then raises a timeout error;
       offload_tier      -- where class-B offloaded rows live: "host" (pinned
@@ -125,8 +132,8 @@ class B200WnWCache(FlatVarlenCache):
     """
 
     def __init__(self, config, num_layers, num_kv_heads, num_q_heads, head_dim, device, adapter=None, *,
-                 max_decode_tokens=256, fetch_mode="zerocopy", fetch_threads=8, fetch_ctas=32, score_reduce=None,
-                 offload_tier="host", wait_timeout_s=60.0):
+                 max_decode_tokens=256, fetch_mode="zerocopy", fetch_threads=8, fetch_ctas=12, score_reduce=None,
+                 offload_tier="host", wait_timeout_s=60.0, fetch_plan="device"):
         super().__init__(num_layers, num_kv_heads, num_q_heads, head_dim, device, adapter)
         if self.device.type != "cuda":
             raise RuntimeError("B200WnWCache needs a CUDA device; the CPU oracle lives in the test suite")
@@ -144,6 +151,11 @@ class B200WnWCache(FlatVarlenCache):
         if offload_tier == "hbm" and fetch_mode != "zerocopy":
             raise ValueError("offload_tier='hbm' is fetched by the gather kernel (fetch_mode='zerocopy')")
         self.offload_tier = offload_tier
+        if fetch_plan not in ("device", "host"):
+            raise ValueError(f"fetch_plan must be 'device' or 'host', not {fetch_plan!r}")
+        self.fetch_plan = fetch_plan
+        self._dplan = None
+        self._dplan_args = None
         self.wait_timeout_s = float(wait_timeout_s)
         self.fetch_threads = int(fetch_threads)
         self.fetch_ctas = int(fetch_ctas)
@@ -594,6 +606,10 @@ class B200WnWCache(FlatVarlenCache):
         self._layer_rows = np.zeros(L + 1, np.int64)
         self._new_kv = [None] * L
         self._presize_step_buffers()
+        self._dplan, self._dplan_args = None, None
+        if (self.fetch_mode == "zerocopy" and self.fetch_plan == "device" and self.config.top_k_chunks > 0
+                and self.max_audio > 0 and self.cpu_restore_k.shape[0] and self._land_k is not None):
+            self._dplan = DevicePlan.create(P)
 
     def _presize_step_buffers(self):
         """Size the per-step fetch and rebuild buffers for the worst step the
@@ -754,6 +770,9 @@ class B200WnWCache(FlatVarlenCache):
             st = self._raw_stream()
         if select:
             self._tail_call("wnw_chunk_topk", a["topk"], st)
+        dplan = self._dplan if select else None
+        if dplan is not None:  # the fetch starts now, planned on the device
+            self._dplan_step(st)
         Kx.LAUNCHES[0] += 1 + int(self._has_scoring) + int(select)
         self._tail_call("wnw_copy_async", a["topk_d2h"], st)
         self._tail_call("wnw_copy_async", a["err_d2h"], st)
@@ -774,10 +793,14 @@ class B200WnWCache(FlatVarlenCache):
             ranges = None
         else:
             ch, total, _, _, ranges = self._planner.compute_and_prepare(flat, off, *self._plan_bufs)
+        if dplan is not None:
+            dplan.verify(self._planner)  # the fetch already in flight is the planner's
+            if ch:
+                self._upload_plan(st)
+        elif ch:
+            self._prepare_fetch(total, ranges)
         for b in range(B):
             self.loaded_segments[b] = set(self._planner.get_loaded_segments(b))
-        if ch:
-            self._prepare_fetch(total, ranges)
         self._plan_layer_checks()
 
     def _tail_call(self, name, args, stream):
@@ -808,6 +831,59 @@ class B200WnWCache(FlatVarlenCache):
         self._tail_args = a
         return a
 
+    def _dplan_step(self, stream):
+        """wnw_dplan_step: plan this step's loads on the device from the
+        top-k just computed on `stream` and launch their fetch on the copy
+        stream (per-layer events, as in _prepare_fetch)."""
+        a = self._dplan_args
+        if a is None:
+            src_k, src_v = self._restore_dev_ptrs()
+            a = self._dplan_args = (
+                self._dplan._h, self._topk_dev.data_ptr(), int(self._topk_dev.shape[1]),
+                self._scratch.err.data_ptr(), src_k, src_v, self.head_dim * self.cpu_restore_k.element_size(),
+                self._land_k.data_ptr(), self._land_v.data_ptr(), int(self._land_k.shape[0]), self.fetch_ctas)
+        st = N.lib.wnw_dplan_step(*a, stream, self._copy_stream.cuda_stream, self._event_handles)
+        if st:
+            N.check(st, "wnw_dplan_step")
+        Kx.LAUNCHES[0] += 1 + self.num_layers
+
+    def _upload_plan(self, stream):
+        """The host half of a device-planned step: the rebuild plan blob to
+        the device on `stream` (ahead of the next step's rebuilds)."""
+        if self._chg_buf is None:
+            self._chg_buf = np.zeros(self.num_layers, np.int32)
+        info = N.FetchInfo()
+        info.layer_changed = self._chg_buf.ctypes.data
+        for _ in range(2):
+            st = N.lib.wnw_planner_upload_plan(self._planner._h, self._plan_host.data_ptr(),
+                                               self._plan_dev.data_ptr(), self._plan_host.numel(), stream,
+                                               C.byref(info))
+            if st != N.WNW_ERR_CAPACITY:
+                N.check(st, "wnw_planner_upload_plan")
+                break
+            self._grow_plan(int(info.plan_ints))
+        else:
+            raise RuntimeError("wnw_planner_upload_plan: plan buffer still too small after growing it")
+        self._layer_chg = self._chg_buf.tolist()
+        self._after_plan(int(info.max_moved_rows), int(info.total_rows))
+
+    def _grow_plan(self, ints):
+        n = 1 << (ints - 1).bit_length()
+        self._plan_host = torch.zeros(n, dtype=torch.int32).pin_memory()
+        self._plan_dev = torch.zeros(n, dtype=torch.int32, device=self.device)
+        self._rb_args = [None] * self.num_layers
+
+    def _after_plan(self, moved, total):
+        self._ensure_move_capacity(moved)
+        # stored rows per slot after the rebuild: the planner's new lengths
+        # (planner.cpp:278-357) count this step's token, every slot of every layer
+        self._next_lens = self._plan_bufs[3].astype(np.int64) - 1
+        if self.stats.enabled and total > 0:
+            row_bytes = self.head_dim * self.cpu_restore_k.element_size()
+            self.stats.record_cpu_gpu_transfer(0, c2g_tokens=int(total), c2g_bytes=int(total) * row_bytes * 2)
+        self._fetched_rows = int(total)
+        self._pending = True
+
     def _prepare_fetch(self, total, ranges):
         """Device plan + fetch of the newly needed host rows, per layer on the
         copy stream, each layer followed by its own event (the reference's
@@ -824,15 +900,7 @@ class B200WnWCache(FlatVarlenCache):
             Kx.LAUNCHES[0] += int(info.fetch_launches)
         else:
             moved, total = self._prepare_fetch_dma(cs, total, ranges)
-        self._ensure_move_capacity(moved)
-        # stored rows per slot after the rebuild: the planner's new lengths
-        # (planner.cpp:278-357) count this step's token, every slot of every layer
-        self._next_lens = self._plan_bufs[3].astype(np.int64) - 1
-        if self.stats.enabled and total > 0:
-            row_bytes = self.head_dim * self.cpu_restore_k.element_size()
-            self.stats.record_cpu_gpu_transfer(0, c2g_tokens=int(total), c2g_bytes=int(total) * row_bytes * 2)
-        self._fetched_rows = int(total)
-        self._pending = True
+        self._after_plan(moved, total)
 
     def _issue_fetch(self, cs):
         """wnw_planner_issue_fetch; grows the plan / range / landing buffers
@@ -857,10 +925,7 @@ class B200WnWCache(FlatVarlenCache):
                 N.check(st, "wnw_planner_issue_fetch")
                 return info
             if info.plan_ints > self._plan_host.numel():
-                n = 1 << (int(info.plan_ints) - 1).bit_length()
-                self._plan_host = torch.zeros(n, dtype=torch.int32).pin_memory()
-                self._plan_dev = torch.zeros(n, dtype=torch.int32, device=self.device)
-                self._rb_args = [None] * self.num_layers
+                self._grow_plan(int(info.plan_ints))
             self._ensure_fetch_capacity(int(info.total_rows), int(info.n_ranges))
         raise RuntimeError("wnw_planner_issue_fetch: buffers still too small after growing them")
 
@@ -925,6 +990,7 @@ class B200WnWCache(FlatVarlenCache):
             self._land_k = torch.empty(n, D, dtype=dt, device=self.device)
             self._land_v = torch.empty(n, D, dtype=dt, device=self.device)
             self._rb_args = [None] * self.num_layers
+            self._dplan_args = None
             if self.fetch_mode == "dma":
                 self._stage_k = torch.empty(n, D, dtype=dt).pin_memory()
                 self._stage_v = torch.empty(n, D, dtype=dt).pin_memory()

@@ -100,29 +100,37 @@ static std::map<const void*, std::unique_ptr<FetchGraph>> g_graphs;
 
 static wnw_status build_graph(FetchGraph* fg, const FetchGraphKey& k, void* const* events) {
   fg->key = k;
-  WNW_CUDA_TRY(cudaHostAlloc(reinterpret_cast<void**>(&fg->lr_host), sizeof(int32_t) * (k.L + 1),
-                             cudaHostAllocDefault));
-  WNW_CUDA_TRY(cudaMalloc(reinterpret_cast<void**>(&fg->lr_dev), sizeof(int32_t) * (k.L + 1)));
+  const bool planned = k.layer_ranges_dev != nullptr;
   WNW_CUDA_TRY(cudaGraphCreate(&fg->graph, 0));
   cudaGraph_t g = fg->graph;
-  // placeholder sizes (16 bytes); the real ones are set before every launch
-  WNW_CUDA_TRY(cudaGraphAddMemcpyNode1D(&fg->cp_plan, g, nullptr, 0, k.plan_dev, k.plan_host, 16,
-                                        cudaMemcpyHostToDevice));
-  WNW_CUDA_TRY(cudaGraphAddMemcpyNode1D(&fg->cp_rng, g, nullptr, 0, k.ranges_dev, k.ranges_host, 16,
-                                        cudaMemcpyHostToDevice));
-  WNW_CUDA_TRY(cudaGraphAddMemcpyNode1D(&fg->cp_dst, g, nullptr, 0, k.dst_dev, k.dst_host, 16,
-                                        cudaMemcpyHostToDevice));
-  WNW_CUDA_TRY(cudaGraphAddMemcpyNode1D(&fg->cp_lr, g, nullptr, 0, fg->lr_dev, fg->lr_host,
-                                        sizeof(int32_t) * (k.L + 1), cudaMemcpyHostToDevice));
-  cudaGraphNode_t prev[4] = {fg->cp_plan, fg->cp_rng, fg->cp_dst, fg->cp_lr};
-  int nprev = 4;
+  cudaGraphNode_t prev[4] = {};
+  int nprev = 0;
+  if (!planned) {
+    WNW_CUDA_TRY(cudaHostAlloc(reinterpret_cast<void**>(&fg->lr_host), sizeof(int32_t) * (k.L + 1),
+                               cudaHostAllocDefault));
+    WNW_CUDA_TRY(cudaMalloc(reinterpret_cast<void**>(&fg->lr_dev), sizeof(int32_t) * (k.L + 1)));
+    // placeholder sizes (16 bytes); the real ones are set before every launch
+    WNW_CUDA_TRY(cudaGraphAddMemcpyNode1D(&fg->cp_plan, g, nullptr, 0, k.plan_dev, k.plan_host, 16,
+                                          cudaMemcpyHostToDevice));
+    WNW_CUDA_TRY(cudaGraphAddMemcpyNode1D(&fg->cp_rng, g, nullptr, 0, k.ranges_dev, k.ranges_host, 16,
+                                          cudaMemcpyHostToDevice));
+    WNW_CUDA_TRY(cudaGraphAddMemcpyNode1D(&fg->cp_dst, g, nullptr, 0, k.dst_dev, k.dst_host, 16,
+                                          cudaMemcpyHostToDevice));
+    WNW_CUDA_TRY(cudaGraphAddMemcpyNode1D(&fg->cp_lr, g, nullptr, 0, fg->lr_dev, fg->lr_host,
+                                          sizeof(int32_t) * (k.L + 1), cudaMemcpyHostToDevice));
+    prev[0] = fg->cp_plan;
+    prev[1] = fg->cp_rng;
+    prev[2] = fg->cp_dst;
+    prev[3] = fg->cp_lr;
+    nprev = 4;
+  }
   const int cpr = static_cast<int>(k.row_bytes / 16);
   for (int l = 0; l < k.L; ++l) {
     const uint4* sk = static_cast<const uint4*>(k.src_k);
     const uint4* sv = static_cast<const uint4*>(k.src_v);
     const int32_t* rng = static_cast<const int32_t*>(k.ranges_dev);
     const int64_t* dst = static_cast<const int64_t*>(k.dst_dev);
-    const int32_t* lr = fg->lr_dev;
+    const int32_t* lr = planned ? k.layer_ranges_dev : fg->lr_dev;
     int layer = l;
     uint4* dk = static_cast<uint4*>(k.land_k);
     uint4* dv = static_cast<uint4*>(k.land_v);
@@ -169,6 +177,25 @@ wnw_status fetch_graph_issue(const void* owner, const FetchGraphKey& k, int64_t 
   WNW_CUDA_TRY(cudaGraphExecMemcpyNodeSetParams1D(fg->exec, fg->cp_dst, k.dst_dev, k.dst_host, sizeof(int64_t) * nr,
                                                    cudaMemcpyHostToDevice));
   WNW_CUDA_TRY(cudaGraphLaunch(fg->exec, static_cast<cudaStream_t>(stream)));
+  return WNW_OK;
+}
+
+wnw_status fetch_graph_issue_planned(const void* owner, const FetchGraphKey& k, void* stream) {
+  if (!k.layer_ranges_dev) {
+    set_error("fetch_graph_issue_planned: no device layer offsets");
+    return WNW_ERR_INVALID;
+  }
+  std::lock_guard<std::mutex> lock(g_graph_mu);
+  auto& slot = g_graphs[owner];
+  if (!slot || !(slot->key == k)) {
+    slot.reset(new FetchGraph());
+    const wnw_status st = build_graph(slot.get(), k, k.events);
+    if (st != WNW_OK) {
+      slot.reset();
+      return st;
+    }
+  }
+  WNW_CUDA_TRY(cudaGraphLaunch(slot->exec, static_cast<cudaStream_t>(stream)));
   return WNW_OK;
 }
 

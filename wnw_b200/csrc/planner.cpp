@@ -26,6 +26,7 @@
 
 #include "../../include/wnw_b200.h"
 #include "fetch_graph.h"
+#include "planner_tables.h"
 
 namespace wnw {
 void set_error(const char* fmt, ...);
@@ -466,6 +467,109 @@ wnw_status wnw_planner_get_changes(const wnw_planner* p, int b, int32_t* to_load
   return WNW_OK;
 }
 
+}  // extern "C"
+
+namespace {
+
+// Sizes of the last plan (blob ints, landed rows, ranges, most rows a layer
+// moves) and which layers it changes.
+wnw_status fill_fetch_info(const wnw_planner* p, wnw_fetch_info* info) {
+  const int L = p->L;
+  int64_t used = 0;
+  wnw_status st = wnw_planner_device_plan(p, nullptr, 0, &used);
+  if (st != WNW_OK) return st;
+  int64_t moved = 0;
+  for (int l = 0; l < L; ++l) {
+    int64_t m = 0;
+    for (const auto& c : p->chg[l]) {
+      const int n_ev = c.ev_hi - c.ev_lo;
+      if (n_ev > 0) m += (c.new_len - c.load_len) - p->ev_starts[c.ev_lo];
+    }
+    moved = std::max(moved, m);
+    if (info->layer_changed) info->layer_changed[l] = p->chg[l].empty() ? 0 : 1;
+  }
+  info->plan_ints = used;
+  info->total_rows = p->layer_rows.empty() ? 0 : p->layer_rows[L];
+  info->fetch_launches = 0;
+  for (int l = 0; l < L; ++l) info->fetch_launches += p->layer_ranges[l + 1] > p->layer_ranges[l] ? 1 : 0;
+  info->n_ranges = static_cast<int64_t>(p->cpu_ranges.size() / 2);
+  info->max_moved_rows = moved;
+  return WNW_OK;
+}
+
+}  // namespace
+
+namespace wnw {
+
+wnw_status planner_tables(const wnw_planner* p, PlannerTables* t) {
+  if (!p || !t) return bad("null argument");
+  if (!p->have_seg_count || !p->have_meta) return bad("planner state incomplete");
+  t->L = p->L;
+  t->H = p->H;
+  t->B = p->B;
+  t->evict_lag = p->evict_lag;
+  t->chunk_base.assign(1, 0);
+  t->c2s_off.clear();
+  t->c2s_flat.clear();
+  t->seg_base.assign(1, 0);
+  t->seg_sample.clear();
+  t->loaded.clear();
+  t->counters.clear();
+  for (int b = 0; b < p->B; ++b) {
+    const int fb = static_cast<int>(t->c2s_flat.size());
+    if (p->c2s_off[b].empty()) {
+      t->c2s_off.push_back(fb);  // no chunks
+    } else {
+      for (int o : p->c2s_off[b]) t->c2s_off.push_back(fb + o);
+      t->c2s_flat.insert(t->c2s_flat.end(), p->c2s_flat[b].begin(), p->c2s_flat[b].end());
+    }
+    t->chunk_base.push_back(static_cast<int32_t>(t->c2s_off.size()));
+    const int nsb = p->seg_count[b];
+    t->seg_base.push_back(t->seg_base.back() + nsb);
+    for (int s = 0; s < nsb; ++s) {
+      t->seg_sample.push_back(b);
+      t->loaded.push_back(p->loaded[b][s]);
+      t->counters.push_back(p->counters[b][s]);
+    }
+  }
+  t->meta_base = p->meta_base;
+  t->cpu_s = p->cpu_s;
+  t->cpu_e = p->cpu_e;
+  t->classb_off.assign(1, 0);
+  t->classb.clear();
+  for (int l = 0; l < p->L; ++l) {
+    t->classb.insert(t->classb.end(), p->class_b[l].begin(), p->class_b[l].end());
+    t->classb_off.push_back(static_cast<int32_t>(t->classb.size()));
+  }
+  return WNW_OK;
+}
+
+wnw_status planner_check_mirror(const wnw_planner* p, const int32_t* layer_rows, const uint8_t* loaded,
+                                const int32_t* counters) {
+  if (!p || !layer_rows || !loaded || !counters) return bad("null argument");
+  for (int l = 0; l <= p->L; ++l) {
+    const int32_t want = p->layer_rows.empty() ? 0 : p->layer_rows[l];
+    if (layer_rows[l] != want) {
+      wnw::set_error("device fetch plan: layer %d lands at row %d, the planner's plan at %d", l, layer_rows[l],
+                     want);
+      return WNW_ERR_STATE;
+    }
+  }
+  int64_t i = 0;
+  for (int b = 0; b < p->B; ++b)
+    for (int s = 0; s < p->seg_count[b]; ++s, ++i)
+      if (loaded[i] != p->loaded[b][s] || counters[i] != p->counters[b][s]) {
+        wnw::set_error("device fetch plan: sample %d segment %d loaded/counter %d/%d, planner %d/%d", b, s,
+                       int(loaded[i]), counters[i], int(p->loaded[b][s]), p->counters[b][s]);
+        return WNW_ERR_STATE;
+      }
+  return WNW_OK;
+}
+
+}  // namespace wnw
+
+extern "C" {
+
 wnw_status wnw_planner_device_plan(const wnw_planner* p, int32_t* blob, int64_t cap, int64_t* used) {
   if (!p || !used) return bad("null argument");
   const int L = p->L;
@@ -529,6 +633,25 @@ wnw_status wnw_planner_device_plan(const wnw_planner* p, int32_t* blob, int64_t 
   return WNW_OK;
 }
 
+wnw_status wnw_planner_upload_plan(const wnw_planner* p, int32_t* plan_host, int32_t* plan_dev, int64_t plan_cap,
+                                   void* stream, wnw_fetch_info* info) {
+  if (!p || !info) return bad("null argument");
+  wnw_status st = fill_fetch_info(p, info);
+  if (st != WNW_OK) return st;
+  if (info->plan_ints > plan_cap) {
+    wnw::set_error("upload_plan needs %lld ints, capacity %lld", (long long)info->plan_ints, (long long)plan_cap);
+    return WNW_ERR_CAPACITY;
+  }
+  if (!plan_host || !plan_dev) return bad("null buffer");
+  int64_t used = 0;
+  st = wnw_planner_device_plan(p, plan_host, plan_cap, &used);
+  if (st != WNW_OK) return st;
+  info->fetch_launches = 0;
+  const cudaError_t e = cudaMemcpyAsync(plan_dev, plan_host, sizeof(int32_t) * used, cudaMemcpyHostToDevice,
+                                        static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? WNW_OK : wnw::cuda_status(e, "cudaMemcpyAsync(plan)");
+}
+
 wnw_status wnw_planner_issue_fetch(const wnw_planner* p, int32_t* plan_host, int32_t* plan_dev, int64_t plan_cap,
                                    int32_t* ranges_host, int32_t* ranges_dev, int64_t* dst_host, int64_t* dst_dev,
                                    int64_t ranges_cap, const void* src_k, const void* src_v, int64_t row_bytes,
@@ -537,27 +660,10 @@ wnw_status wnw_planner_issue_fetch(const wnw_planner* p, int32_t* plan_host, int
   if (!p || !info) return bad("null argument");
   const int L = p->L;
   // sizes first: nothing is issued unless every buffer is large enough
-  int64_t used = 0;
-  wnw_status st = wnw_planner_device_plan(p, nullptr, 0, &used);
+  wnw_status st = fill_fetch_info(p, info);
   if (st != WNW_OK) return st;
-  const int64_t nr = static_cast<int64_t>(p->cpu_ranges.size() / 2);
-  const int64_t rows = p->layer_rows.empty() ? 0 : p->layer_rows[L];
-  int64_t moved = 0;
-  for (int l = 0; l < L; ++l) {
-    int64_t m = 0;
-    for (const auto& c : p->chg[l]) {
-      const int n_ev = c.ev_hi - c.ev_lo;
-      if (n_ev > 0) m += (c.new_len - c.load_len) - p->ev_starts[c.ev_lo];
-    }
-    moved = std::max(moved, m);
-    info->layer_changed[l] = p->chg[l].empty() ? 0 : 1;
-  }
-  info->plan_ints = used;
-  info->total_rows = rows;
-  info->fetch_launches = 0;
-  for (int l = 0; l < L; ++l) info->fetch_launches += p->layer_ranges[l + 1] > p->layer_ranges[l] ? 1 : 0;
-  info->n_ranges = nr;
-  info->max_moved_rows = moved;
+  int64_t used = info->plan_ints;
+  const int64_t nr = info->n_ranges, rows = info->total_rows;
   if (used > plan_cap || nr > ranges_cap || rows > land_rows) {
     wnw::set_error("issue_fetch needs plan %lld / ranges %lld / rows %lld; capacity %lld / %lld / %lld",
                    (long long)used, (long long)nr, (long long)rows, (long long)plan_cap, (long long)ranges_cap,

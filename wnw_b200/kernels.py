@@ -284,7 +284,9 @@ def check_device_error(err_tensor):
     if v:
         names = [n for bit, n in ((N.DEVERR_MBAR_TIMEOUT, "mbarrier wait timed out"),
                                   (N.DEVERR_LEN_MISMATCH, "segment length disagrees with the plan"),
-                                  (N.DEVERR_CAPACITY, "segment exceeds its slot capacity")) if v & bit]
+                                  (N.DEVERR_CAPACITY, "segment exceeds its slot capacity"),
+                                  (N.DEVERR_PEER_TIMEOUT, "tensor-parallel peer timed out"),
+                                  (N.DEVERR_BAD_INDEX, "device fetch plan: index out of range")) if v & bit]
         raise N.WnwError(5 if v & N.DEVERR_MBAR_TIMEOUT else 4, "device", ", ".join(names))
 
 

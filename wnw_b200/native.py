@@ -23,6 +23,7 @@ DEVERR_MBAR_TIMEOUT = 1
 DEVERR_LEN_MISMATCH = 2
 DEVERR_CAPACITY = 4
 DEVERR_PEER_TIMEOUT = 8
+DEVERR_BAD_INDEX = 16
 
 F32, F16, BF16 = 0, 1, 2
 
@@ -119,6 +120,11 @@ _sig("wnw_copy_mapped", _S, P, P, C.c_int64, C.c_int, P)
 _sig("wnw_decode_attn_step", _S, C.POINTER(DecodeAttnArgs), P, P, P, P, P)
 _sig("wnw_planner_issue_fetch", _S, P, P, P, C.c_int64, P, P, P, P, C.c_int64, P, P, C.c_int64, P, P, C.c_int64,
      C.c_int, P, P, C.POINTER(FetchInfo))
+_sig("wnw_planner_upload_plan", _S, P, P, P, C.c_int64, P, C.POINTER(FetchInfo))
+_sig("wnw_dplan_create", _S, P, C.POINTER(C.c_void_p))
+_sig("wnw_dplan_destroy", None, P)
+_sig("wnw_dplan_step", _S, P, P, C.c_int, P, P, P, C.c_int64, P, P, C.c_int64, C.c_int, P, P, P)
+_sig("wnw_dplan_verify", _S, P, P)
 _sig("wnw_oproj_allreduce_chunks", C.c_int, C.c_int)
 _sig("wnw_oproj_allreduce", _S, C.POINTER(OprojAllReduceArgs), P)
 _sig("wnw_ipc_alloc", _S, C.c_int64, C.POINTER(C.c_void_p), P)
@@ -141,7 +147,8 @@ EXPORTS = [
     "wnw_planner_get_layer_transfer", "wnw_planner_get_changes", "wnw_planner_device_plan",
     "wnw_gather_rows", "wnw_h2d_async", "wnw_stream_wait_event", "wnw_planner_issue_fetch", "wnw_copy_async", "wnw_copy_mapped", "wnw_decode_attn_step", "wnw_oproj_allreduce",
     "wnw_oproj_allreduce_chunks", "wnw_ipc_alloc", "wnw_ipc_open", "wnw_ipc_close", "wnw_host_device_pointer", "wnw_fetch_rows",
-    "wnw_fetch_layers",
+    "wnw_fetch_layers", "wnw_planner_upload_plan", "wnw_dplan_create", "wnw_dplan_destroy", "wnw_dplan_step",
+    "wnw_dplan_verify",
 ]
 
 

@@ -147,6 +147,35 @@ class Planner:
         return out[:used.value]
 
 
+class DevicePlan:
+    """Device mirror of a Planner's selection state (wnw_dplan_*): plans each
+    step's fetch on the GPU from the device top-k and launches it on the copy
+    stream with no host round trip; ``verify`` checks it against the host
+    planner once that has planned the same step.  ``create`` returns None
+    when the state does not fit the planning kernel (the host path is used)."""
+
+    def __init__(self, h):
+        self._h = h
+
+    @classmethod
+    def create(cls, planner):
+        h = C.c_void_p()
+        st = N.lib.wnw_dplan_create(planner._h, C.byref(h))
+        if st == 6:  # WNW_ERR_UNSUPPORTED
+            return None
+        N.check(st, "wnw_dplan_create")
+        return cls(h)
+
+    def __del__(self):
+        h = getattr(self, "_h", None)
+        if h is not None and h.value:
+            N.lib.wnw_dplan_destroy(h)
+            self._h = None
+
+    def verify(self, planner):
+        N.check(N.lib.wnw_dplan_verify(self._h, planner._h), "wnw_dplan_verify")
+
+
 def gather_rows(src_k, src_v, ranges, dst_k, dst_v, n_threads=8):
     """planner.cpp:113-122: copy the rows of each planned CPU range, in order,
     into ``dst`` (host memory, e.g. pinned staging)."""
