@@ -465,9 +465,11 @@ def run_reference_gpu(rec, dev, K, W):
 
 
 def h2d_link_probe(dev, mb=128, reps=5):
-    """Zero-copy H2D bandwidth of this GPU's host link right now (the fetch
-    kernel reading 128-row ranges of a pinned buffer), GB/s.  The decode step
-    fetches its offloaded rows over this link, so it bounds the step."""
+    """H2D bandwidth of this GPU's host link right now, GB/s: (the fetch
+    kernel reading 128-row ranges of a pinned buffer, a copy-engine copy of
+    the same bytes from contiguous pinned memory).  The decode step fetches
+    its offloaded rows over this link, so it bounds the step; the copy engine
+    on contiguous memory is the link's practical ceiling."""
     from wnw_b200 import kernels as Kx
     D = MODEL["D"]
     rows = mb * (1 << 20) // (2 * D * 2)
@@ -489,7 +491,17 @@ def h2d_link_probe(dev, mb=128, reps=5):
         Kx.fetch_rows(pk, pv, D * 2, ranges, dst, dk, dv, max_ctas=512)
     e1.record()
     torch.cuda.synchronize()
-    return 2 * rows * D * 2 * reps / (e0.elapsed_time(e1) * 1e-3) / 1e9
+    zero_copy = 2 * rows * D * 2 * reps / (e0.elapsed_time(e1) * 1e-3) / 1e9
+    dk.copy_(hk, non_blocking=True)
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(reps):
+        dk.copy_(hk, non_blocking=True)
+        dv.copy_(hv, non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    dma = 2 * rows * D * 2 * reps / (e0.elapsed_time(e1) * 1e-3) / 1e9
+    return zero_copy, dma
 
 
 def cpu_replay(rec, n_steps, start=0):
@@ -681,7 +693,7 @@ def _main(a, rank, world, local, dist, dev, K, W, cfg_json, tp, clk):
         e2e_ms = e2e["ms"]
     tokens = (1 if tp else world) * 1 * K
     peak, peak_kind = peaks()
-    link = h2d_link_probe(dev)
+    link, link_dma = h2d_link_probe(dev)
     fetch_bytes = val["fetched_rows"] / K * MODEL["D"] * 2 * 2
     achieved = val["attn_bytes"] / (val["attn_us"] * 1e-6) / 1e9
     line = {
@@ -702,9 +714,15 @@ def _main(a, rank, world, local, dist, dev, K, W, cfg_json, tp, clk):
         "clocks": clk.summary(val["window"]),
         "fetched_rows_per_step": val["fetched_rows"] / K,
         "host_link": {"fetch_bytes_per_step": fetch_bytes, "link_gbs": link,
+                      "dma_contiguous_gbs": link_dma,
+                      "fetch_kernel_frac_of_dma": link / link_dma if link and link_dma else None,
                       "fetch_ms_at_link": fetch_bytes / (link * 1e9) * 1e3 if link else None,
+                      "step_frac_of_link_bound": (fetch_bytes / (link * 1e9) * 1e3) / (ms / K)
+                      if link else None,
                       "how": "offloaded rows fetched per step over the host link (zero-copy kernel); link_gbs = "
-                             "that kernel on 128 MB of random 128-row ranges, measured in this run"},
+                             "that kernel on 128 MB of random 128-row ranges, dma_contiguous_gbs = a copy-engine "
+                             "copy of the same bytes from contiguous pinned memory (the link's practical "
+                             "ceiling), both measured in this run"},
         "model_decode_ms_per_token": rec["model_ms"],
         "reference_gpu": ref_gpu,
         "offload_tier_hbm": ({"value": tokens / (hbm["ms"] * 1e-3), "ms_per_step": hbm["ms"] / K,
