@@ -232,3 +232,42 @@ def test_device_fetch_plan_follows_planner(dev, variant):
         loads += sum(len(x) for x in orc.last_to_load)
         evicts += sum(len(x) for x in orc.last_to_evict)
     assert loads > 0 and (evicts > 0 or sc["lag"] > sc["steps"])
+
+
+def test_cache_serves_a_second_request(dev, golden_dir):
+    """One cache, two requests back to back: the first request's last step
+    has already fetched ahead for a step that never comes; the second
+    request's prefill waits for that fetch, replans from scratch and must
+    reproduce the reference trace exactly as a fresh cache does."""
+    from wnw_b200.cache import B200WnWCache
+    from wnw_b200.config import WnWConfig
+    tz = np.load(os.path.join(golden_dir, "cache_trace.npz"), allow_pickle=True)
+    sc = CACHE_SCENARIO
+    inp = make_cache_inputs(sc)
+    G = sc["Hq"] // sc["Hkv"]
+    cache = B200WnWCache(WnWConfig(**make_config_dict(sc)), sc["L"], sc["Hkv"], sc["Hq"], sc["D"], dev,
+                         max_decode_tokens=3)
+    for _ in range(2):
+        cache.setup_audio(torch.tensor(inp["audio_starts"]), torch.tensor(inp["audio_ends"]),
+                          torch.tensor(inp["attention_mask"]))
+        for l in range(sc["L"]):
+            cache.prefill_after_attn(l, [x.to(dev) if x is not None else None for x in inp["class_a_scores"][l]],
+                                     [[x.to(dev) if x is not None else None for x in row]
+                                      for row in inp["per_head_scores"][l]],
+                                     torch.from_numpy(inp["prefill_k"][l]).to(dev),
+                                     torch.from_numpy(inp["prefill_v"][l]).to(dev))
+        cache.prefill_all_layers_done()
+        assert [sorted(s) for s in cache.loaded_segments] == [list(x) for x in tz["prefill_loaded"]]
+        for t in range(4):
+            for l in range(sc["L"]):
+                q = torch.from_numpy(inp["dec_q"][t][l]).to(dev)
+                kk, vv, cu, _ = cache.decode_before_attn(l, torch.from_numpy(inp["dec_k"][t][l]).to(dev),
+                                                         torch.from_numpy(inp["dec_v"][t][l]).to(dev))
+                qf = q.squeeze(2).reshape(sc["B"], sc["Hkv"], G, sc["D"]).reshape(-1, G, sc["D"])
+                out = cache.fused_decode_attention(l, qf, q, kk, vv, cu, sc["D"] ** -0.5)
+                pk, pv, pcu = _packed_with_token(cache, l)
+                assert np.array_equal(pcu, tz[f"s{t}_l{l}_cu"]), (t, l)
+                assert _digest(pk) == str(tz[f"s{t}_l{l}_khash"]), (t, l)
+                np.testing.assert_allclose(out.cpu().numpy(), tz[f"s{t}_l{l}_out"], atol=1e-5, rtol=1e-5)
+            cache.decode_all_layers_done()
+            assert [sorted(s) for s in cache.loaded_segments] == [list(x) for x in tz[f"s{t}_loaded"]], t

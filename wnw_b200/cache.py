@@ -171,6 +171,11 @@ class B200WnWCache(FlatVarlenCache):
     # ------------------------------------------------------------- set-up
     def setup_audio(self, audio_starts, audio_ends, attention_mask=None):
         """cache.py:144-250: segments, chunks, score buffers, fresh state."""
+        if self._copy_stream is not None:
+            # the previous request's last step fetched ahead for a step that
+            # never came: let it land before its buffers and plan go away
+            self._copy_stream.synchronize()
+        self._dplan = self._dplan_args = None
         super().setup_audio(audio_starts, audio_ends, attention_mask)
         a_s = [int(x) for x in audio_starts.tolist()]
         a_e = [int(x) for x in audio_ends.tolist()]
@@ -989,6 +994,9 @@ class B200WnWCache(FlatVarlenCache):
             n = 1 << max(0, rows - 1).bit_length()
             self._land_k = torch.empty(n, D, dtype=dt, device=self.device)
             self._land_v = torch.empty(n, D, dtype=dt, device=self.device)
+            if self._copy_stream is not None:  # written there: not reused until that work is done
+                self._land_k.record_stream(self._copy_stream)
+                self._land_v.record_stream(self._copy_stream)
             self._rb_args = [None] * self.num_layers
             self._dplan_args = None
             if self.fetch_mode == "dma":
