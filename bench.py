@@ -57,7 +57,7 @@ import torch  # noqa: E402
 MODEL = dict(L=30, hidden=3072, Hq=32, Hkv=8, D=128, inter=8192, vocab=131072, theta=1e8)
 PROMPT = dict(sink=4, audio=15000, tail=60)
 WNW = dict(frac_a=0.30, chunk=128, top_k=16, lag=1, retention=0.0, seed=1234)
-METRIC = "decode tokens/s (WnW hot path) and decode-attention HBM GB/s"
+METRIC = "decode tokens/s and varlen-attn HBM GB/s (frac of peak) at 1/2/4/8 B200"
 
 
 def parse():
