@@ -203,3 +203,38 @@ def test_step_wait_times_out_instead_of_blocking():
         wait_event(Never(), 0.2)
     assert time.perf_counter() - t0 < 5
     wait_event(Later(), 5.0)  # completes in time: no error
+
+
+def test_upload_plan_and_device_plan_argument_checks(golden_dir):
+    """The device-planned step's host entry points refuse bad calls before
+    any CUDA call: wnw_planner_upload_plan reports the plan size and
+    WNW_ERR_CAPACITY for a too-small buffer; wnw_dplan_* reject null handles
+    and an incomplete planner."""
+    from wnw_b200.planner import Planner
+    ps = PLANNER_SCENARIOS[0]
+    inp = make_planner_inputs(ps)
+    P = _planner_from(ps, inp, Planner)
+    L, S = ps["L"], ps["B"] * ps["H"]
+    bufs = [np.zeros((L, S), np.int32), np.zeros((L, S), np.int32), np.zeros((L, S + 1), np.int32),
+            np.zeros((L, S), np.int32), np.zeros((L, S + 1), np.int32), np.zeros(L, np.int32),
+            np.zeros(L + 1, np.int32)]
+    for tk, toff in inp["steps"]:
+        ch, total, _, _, _ = P.compute_and_prepare(tk, toff, *bufs)
+        if ch and total:
+            break
+    chg = np.full(L, -1, np.int32)
+    info = N.FetchInfo()
+    info.layer_changed = chg.ctypes.data
+    st = N.lib.wnw_planner_upload_plan(P._h, None, None, 0, None, ctypes.byref(info))
+    assert st == N.WNW_ERR_CAPACITY
+    assert info.plan_ints == P.device_plan().size and info.total_rows == total
+    assert N.lib.wnw_planner_upload_plan(None, None, None, 0, None, ctypes.byref(info)) == N.WNW_ERR_INVALID
+    h = ctypes.c_void_p()
+    assert N.lib.wnw_dplan_create(None, ctypes.byref(h)) == N.WNW_ERR_INVALID
+    bare = Planner(2, 2, 1)  # no segments or metadata yet
+    assert N.lib.wnw_dplan_create(bare._h, ctypes.byref(h)) == N.WNW_ERR_INVALID
+    assert b"incomplete" in N.lib.wnw_last_error()
+    assert N.lib.wnw_dplan_step(None, None, 1, None, None, None, 256, None, None, 0, 12, None, None,
+                                None) == N.WNW_ERR_INVALID
+    assert N.lib.wnw_dplan_verify(None, P._h) == N.WNW_ERR_INVALID
+    N.lib.wnw_dplan_destroy(None)  # a null handle is a no-op

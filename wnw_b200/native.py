@@ -16,7 +16,9 @@ if not os.path.exists(LIB_PATH):
 lib = C.CDLL(LIB_PATH)
 
 WNW_OK = 0
+WNW_ERR_INVALID = 1
 WNW_ERR_CAPACITY = 3
+WNW_ERR_UNSUPPORTED = 6
 STATUS_NAMES = {0: "ok", 1: "invalid argument", 2: "CUDA error", 3: "capacity exceeded",
                 4: "invalid state", 5: "timed out", 6: "unsupported"}
 DEVERR_MBAR_TIMEOUT = 1

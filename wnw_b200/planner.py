@@ -161,7 +161,7 @@ class DevicePlan:
     def create(cls, planner):
         h = C.c_void_p()
         st = N.lib.wnw_dplan_create(planner._h, C.byref(h))
-        if st == 6:  # WNW_ERR_UNSUPPORTED
+        if st == N.WNW_ERR_UNSUPPORTED:
             return None
         N.check(st, "wnw_dplan_create")
         return cls(h)
