@@ -16,7 +16,8 @@ are needed to run its CUDA-oriented code on CPU (neither changes arithmetic):
   (``src/algorithms/wnw_cpp/code/cache.py:258-265``).
 
 Outputs (all small, committed): ``kernels.npz``, ``cache_trace.npz``,
-``cache_cpp_trace.npz``, ``planner.npz``, ``session_trace.json``.
+``cache_cpp_trace.npz``, ``planner.npz``, ``session_trace.json``,
+``session_degqa_trace.json``.
 """
 from __future__ import annotations
 
@@ -265,16 +266,11 @@ def gen_planner():
     np.savez_compressed(os.path.join(HERE, "planner.npz"), **out)
 
 
-def gen_session_trace():
-    """Drive the reference WnWSession over a tiny random-init Llama (fp32) and
-    record the hook call sequence and the greedy tokens."""
-    from transformers import LlamaConfig, LlamaForCausalLM
+def _tiny_adapter(ss):
+    """The reference's BaseModelAdapter completed for a tiny random-init
+    Llama whose audio span is fixed by the scenario."""
     from transformers.models.llama.modeling_llama import apply_rotary_pos_emb
-    from algorithms.wnw.code.config import WnWConfig
-    from algorithms.wnw.code.cache import WnWCache
-    from algorithms.wnw.code.session import WnWSession
     from common.adapters.base import BaseModelAdapter
-    from tests.golden.scenario import SESSION_SCENARIO as ss, make_tiny_llama_config, session_inputs
 
     class TinyAdapter(BaseModelAdapter):
         name = "tiny"
@@ -308,6 +304,19 @@ def gen_session_trace():
         def get_audio_token_id(self, model): return 0
         def build_analysis_inputs(self, *a, **k): raise NotImplementedError
 
+    return TinyAdapter()
+
+
+def gen_session_trace():
+    """Drive the reference WnWSession over a tiny random-init Llama (fp32) and
+    record the hook call sequence and the greedy tokens."""
+    from transformers import LlamaConfig, LlamaForCausalLM
+    from algorithms.wnw.code.config import WnWConfig
+    from algorithms.wnw.code.cache import WnWCache
+    from algorithms.wnw.code.session import WnWSession
+    from tests.golden.scenario import SESSION_SCENARIO as ss, make_tiny_llama_config, session_inputs
+
+    adapter = _tiny_adapter(ss)
     calls = []
 
     class TracingCache(WnWCache):
@@ -334,7 +343,6 @@ def gen_session_trace():
     torch.manual_seed(ss["seed"])
     mcfg = LlamaConfig(**make_tiny_llama_config(ss))
     model = LlamaForCausalLM(mcfg).eval()
-    adapter = TinyAdapter()
     cfg = WnWConfig(**make_config_dict(ss))
     cache = TracingCache(config=cfg, num_layers=ss["L"], num_kv_heads=ss["Hkv"], num_q_heads=ss["Hq"],
                          head_dim=ss["D"], device=torch.device("cpu"), adapter=adapter)
@@ -349,8 +357,55 @@ def gen_session_trace():
         json.dump(res, f)
 
 
+def gen_degqa_trace():
+    """The reference's GQA -> MHA path: its config expansion
+    (analysis/wnw_config/scripts/expand_wnw_config.py) on the session
+    scenario's config, then its degqa_model on the same tiny Llama and its
+    session in MHA mode (one kv head per q head) with the expanded config:
+    hook calls, greedy tokens, loaded sets."""
+    from analysis.wnw_config.scripts.expand_wnw_config import expand_config
+    from common.adapters.degqa import degqa_model
+    from transformers import LlamaConfig, LlamaForCausalLM
+    from algorithms.wnw.code.config import WnWConfig
+    from algorithms.wnw.code.cache import WnWCache
+    from algorithms.wnw.code.session import WnWSession
+    from tests.golden.scenario import SESSION_SCENARIO as ss, make_tiny_llama_config, session_inputs
+    from wnw_b200.config import WnWConfig as OurConfig
+
+    cfg_in = OurConfig(**make_config_dict(ss)).to_dict()
+    cfg_out = expand_config(cfg_in, ss["L"], ss["Hkv"], ss["Hq"])
+    torch.manual_seed(ss["seed"])
+    model = LlamaForCausalLM(LlamaConfig(**make_tiny_llama_config(ss))).eval()
+    ad = _tiny_adapter(ss)
+    degqa_model(model, ad)
+    kw = dict(make_config_dict(ss), class_b=cfg_out["heads"]["class_b"],
+              retention_ratios=cfg_out["heads"]["retention_ratios"], num_kv_heads=ss["Hq"])
+    calls = []
+
+    class TracingCache(WnWCache):
+        def decode_before_attn(self, l, k, v):
+            calls.append(["decode_before_attn", l, list(k.shape)])
+            return super().decode_before_attn(l, k, v)
+
+        def decode_all_layers_done(self):
+            calls.append(["decode_all_layers_done"])
+            return super().decode_all_layers_done()
+
+    cache = TracingCache(config=WnWConfig(**kw), num_layers=ss["L"], num_kv_heads=ss["Hq"], num_q_heads=ss["Hq"],
+                         head_dim=ss["D"], device=torch.device("cpu"), adapter=ad)
+    ids = session_inputs(ss)
+    with WnWSession(model, ad, cache) as sess:
+        sess.setup_audio(ids)
+        with torch.no_grad():
+            out = sess.generate({"input_ids": ids}, max_new_tokens=ss["new_tokens"], do_sample=False)
+    res = {"config_in": cfg_in, "config_out": cfg_out, "calls": calls, "tokens": out.tolist(),
+           "loaded": [sorted(s) for s in cache.loaded_segments]}
+    with open(os.path.join(HERE, "session_degqa_trace.json"), "w") as f:
+        json.dump(res, f)
+
+
 if __name__ == "__main__":
-    which = sys.argv[1:] or ["kernels", "cache", "planner", "session"]
+    which = sys.argv[1:] or ["kernels", "cache", "planner", "session", "degqa"]
     if "kernels" in which:
         gen_kernels()
     if "cache" in which:
@@ -359,4 +414,6 @@ if __name__ == "__main__":
         gen_planner()
     if "session" in which:
         gen_session_trace()
+    if "degqa" in which:
+        gen_degqa_trace()
     print("golden fixtures written to", HERE)

@@ -271,3 +271,41 @@ def test_cache_serves_a_second_request(dev, golden_dir):
                 np.testing.assert_allclose(out.cpu().numpy(), tz[f"s{t}_l{l}_out"], atol=1e-5, rtol=1e-5)
             cache.decode_all_layers_done()
             assert [sorted(s) for s in cache.loaded_segments] == [list(x) for x in tz[f"s{t}_loaded"]], t
+
+
+def test_mha_mode_session_reproduces_reference_generation(dev, golden_dir):
+    """GQA -> MHA mode (wnw_b200.degqa: the expanded model and config, one kv
+    head per q head) through our session and B200WnWCache on the GPU gives
+    the reference's MHA-mode hook calls, greedy tokens and loaded sets."""
+    from transformers import LlamaConfig, LlamaForCausalLM
+    from tests.golden.scenario import SESSION_SCENARIO as ss, make_tiny_llama_config, session_inputs
+    from tests.oracle_hf import TracingMixin
+    from wnw_b200.adapters import LlamaFamilyAdapter
+    from wnw_b200.cache import B200WnWCache
+    from wnw_b200.config import WnWConfig
+    from wnw_b200.degqa import degqa_model, expand_wnw_config
+    from wnw_b200.session import WnWSession
+
+    with open(os.path.join(golden_dir, "session_degqa_trace.json")) as f:
+        ref = json.load(f)
+    torch.manual_seed(ss["seed"])
+    model = LlamaForCausalLM(LlamaConfig(**make_tiny_llama_config(ss))).eval().to(dev)
+    adapter = LlamaFamilyAdapter(ss["audio_start"], ss["audio_end"])
+    degqa_model(model, adapter)
+    heads = expand_wnw_config(WnWConfig(**make_config_dict(ss)).to_dict(), ss["L"], ss["Hkv"], ss["Hq"])["heads"]
+    cfg = WnWConfig(**dict(make_config_dict(ss), class_b=heads["class_b"],
+                           retention_ratios=heads["retention_ratios"], num_kv_heads=ss["Hq"]))
+
+    class Tracing(TracingMixin, B200WnWCache):
+        pass
+
+    cache = Tracing(cfg, ss["L"], ss["Hq"], ss["Hq"], ss["D"], dev, max_decode_tokens=4)
+    ids = session_inputs(ss).to(dev)
+    with WnWSession(model, adapter, cache) as sess:
+        sess.setup_audio(ids)
+        with torch.no_grad():
+            out = sess.generate({"input_ids": ids}, max_new_tokens=ss["new_tokens"], do_sample=False)
+    calls = [c for c in cache.calls if c[0] in ("decode_before_attn", "decode_all_layers_done")]
+    assert calls == ref["calls"]
+    assert out.cpu().tolist() == ref["tokens"]
+    assert [sorted(s) for s in cache.loaded_segments] == ref["loaded"]
