@@ -17,7 +17,7 @@ are needed to run its CUDA-oriented code on CPU (neither changes arithmetic):
 
 Outputs (all small, committed): ``kernels.npz``, ``cache_trace.npz``,
 ``cache_cpp_trace.npz``, ``planner.npz``, ``session_trace.json``,
-``session_degqa_trace.json``.
+``session_degqa_trace.json``, ``stats.json``.
 """
 from __future__ import annotations
 
@@ -211,6 +211,7 @@ def run_cache_trace(cache_cls, cpp):
         rec[f"s{t}_loaded"] = np.array(
             [sorted(cache._planner.get_loaded_segments(b)) if cpp else sorted(cache.loaded_segments[b])
              for b in range(sc["B"])], dtype=object)
+    run_cache_trace.last_cache = cache
     return rec
 
 
@@ -224,6 +225,49 @@ def gen_cache_traces():
         np.savez_compressed(os.path.join(HERE, "cache_cpp_trace.npz"), **rec2)
     except Exception as e:  # the C++ JIT needs a compiler; report and continue
         print("C++ cache trace skipped:", e)
+
+
+def _jsonable(x):
+    if isinstance(x, dict):
+        return {k: _jsonable(v) for k, v in x.items()}
+    if isinstance(x, (list, tuple)):
+        return [_jsonable(v) for v in x]
+    if isinstance(x, (np.integer,)):
+        return int(x)
+    if isinstance(x, (np.floating,)):
+        return float(x)
+    return x
+
+
+def gen_stats():
+    """InferenceStats as the reference records them: (1) its InferenceStats
+    driven by a scripted call sequence, (2) its Python cache's stats after the
+    seeded cache scenario (prefill offload, initial loads, per-step loads, the
+    interval snapshots).  GPU-memory fields are None here (no CUDA)."""
+    from common.monitoring.inference_stats import InferenceStats
+    st = InferenceStats(torch.device("cpu"), interval=2)
+    st.reset(3)
+
+    def snap(step=-1):
+        return [{"step": step, "b": b, "x": b * 10 + max(step, 0)} for b in range(3)]
+
+    st.record_prefill_before(snap)
+    st.record_prefill_before(snap)  # guarded: once
+    st.record_cpu_gpu_transfer(0, g2c_tokens=7, g2c_bytes=70)
+    st.record_cpu_gpu_transfer(2, c2g_tokens=3, c2g_bytes=30)
+    st.record_prefill(snap)
+    for step in range(1, 6):
+        st.record_cpu_gpu_transfer(step % 3, c2g_tokens=step, c2g_bytes=step * 11)
+        st.record_cpu_gpu_transfer(1, c2g_tokens=0)  # all-zero: no event
+        st.flush_decode_step(step)
+        if step % st.interval == 0:
+            st.record_decode(step, snap)
+    scripted = st.get_all_stats()
+    from algorithms.wnw.code.cache import WnWCache
+    run_cache_trace(WnWCache, cpp=False)
+    cache_stats = run_cache_trace.last_cache.stats.get_all_stats()
+    with open(os.path.join(HERE, "stats.json"), "w") as f:
+        json.dump(_jsonable({"scripted": scripted, "cache_trace": cache_stats}), f)
 
 
 def gen_planner():
@@ -352,7 +396,7 @@ def gen_session_trace():
         with torch.no_grad():
             out = sess.generate({"input_ids": ids}, max_new_tokens=ss["new_tokens"], do_sample=False)
     res = {"calls": calls, "tokens": out.tolist(),
-           "loaded": [sorted(s) for s in cache.loaded_segments]}
+           "loaded": [sorted(s) for s in cache.loaded_segments], "stats": _jsonable(sess.get_stats())}
     with open(os.path.join(HERE, "session_trace.json"), "w") as f:
         json.dump(res, f)
 
@@ -405,7 +449,7 @@ def gen_degqa_trace():
 
 
 if __name__ == "__main__":
-    which = sys.argv[1:] or ["kernels", "cache", "planner", "session", "degqa"]
+    which = sys.argv[1:] or ["kernels", "cache", "planner", "session", "degqa", "stats"]
     if "kernels" in which:
         gen_kernels()
     if "cache" in which:
@@ -416,4 +460,6 @@ if __name__ == "__main__":
         gen_session_trace()
     if "degqa" in which:
         gen_degqa_trace()
+    if "stats" in which:
+        gen_stats()
     print("golden fixtures written to", HERE)

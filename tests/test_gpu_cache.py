@@ -97,6 +97,11 @@ def test_cache_reproduces_reference_trace(dev, golden_dir, tier, fetch, plan):
         assert [sorted(s) for s in cache.loaded_segments] == [list(x) for x in tz[f"s{t}_loaded"]], t
     # slots grew past the initial decode reservation (3 rows) without losing rows
     assert (cache._cap_host >= cache._len_host + 1).all()
+    # InferenceStats: the reference's snapshots and per-sample transfer events
+    from tests.stats_compare import normalise
+    with open(os.path.join(golden_dir, "stats.json")) as f:
+        want = json.load(f)["cache_trace"]
+    assert normalise(cache.stats.get_all_stats()) == normalise(want)
 
 
 def test_cache_matches_oracle_in_bf16(dev):
@@ -179,6 +184,8 @@ def test_session_reproduces_reference_generation(dev, golden_dir):
     assert cache.calls == ref["calls"]
     assert out.cpu().tolist() == ref["tokens"]
     assert [sorted(s) for s in cache.loaded_segments] == ref["loaded"]
+    from tests.stats_compare import normalise
+    assert normalise(sess.get_stats()) == normalise(ref["stats"])
 
 
 @pytest.mark.parametrize("variant", [dict(lag=0), dict(lag=1), dict(lag=3, top_k=1),

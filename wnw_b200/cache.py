@@ -176,6 +176,7 @@ class B200WnWCache(FlatVarlenCache):
             # never came: let it land before its buffers and plan go away
             self._copy_stream.synchronize()
         self._dplan = self._dplan_args = None
+        self._seg_rows = None
         super().setup_audio(audio_starts, audio_ends, attention_mask)
         a_s = [int(x) for x in audio_starts.tolist()]
         a_e = [int(x) for x in audio_ends.tolist()]
@@ -575,6 +576,7 @@ class B200WnWCache(FlatVarlenCache):
         """Hand the prefill state to the native planner (wnw_cpp/code/cache.py:40-116)."""
         L, H, B = self.num_layers, self.num_kv_heads, self.batch_size
         P = self._planner = Planner(L, H, B, self.num_kv_groups)
+        self._seg_rows = self._segment_host_rows()
         P.set_config(self.config.top_k_chunks, self.config.eviction_lag)
         P.set_seg_count(self.seg_count)
         for b in range(B):
@@ -805,7 +807,14 @@ class B200WnWCache(FlatVarlenCache):
         elif ch:
             self._prepare_fetch(total, ranges)
         for b in range(B):
-            self.loaded_segments[b] = set(self._planner.get_loaded_segments(b))
+            now = set(self._planner.get_loaded_segments(b))
+            if ch and self.stats.enabled:  # cache.py:816-820: each sample's loads
+                new = sorted(now - self.loaded_segments[b])
+                n = int(self._seg_rows[b][new].sum()) if new else 0
+                if n:
+                    row_bytes = self.head_dim * self.cpu_restore_k.element_size()
+                    self.stats.record_cpu_gpu_transfer(b, c2g_tokens=n, c2g_bytes=n * row_bytes * 2)
+            self.loaded_segments[b] = now
         self._plan_layer_checks()
 
     def _tail_call(self, name, args, stream):
@@ -883,9 +892,6 @@ class B200WnWCache(FlatVarlenCache):
         # stored rows per slot after the rebuild: the planner's new lengths
         # (planner.cpp:278-357) count this step's token, every slot of every layer
         self._next_lens = self._plan_bufs[3].astype(np.int64) - 1
-        if self.stats.enabled and total > 0:
-            row_bytes = self.head_dim * self.cpu_restore_k.element_size()
-            self.stats.record_cpu_gpu_transfer(0, c2g_tokens=int(total), c2g_bytes=int(total) * row_bytes * 2)
         self._fetched_rows = int(total)
         self._pending = True
 
@@ -1030,16 +1036,57 @@ class B200WnWCache(FlatVarlenCache):
             sorted(self.loaded_segments[b])
 
     def _snapshot_cache_stats(self, step=-1):
-        """Cache occupancy snapshot with the reference's keys (cache.py:1013-1080)."""
+        """Cache occupancy snapshot, the reference's fields and arithmetic
+        (cache.py:1013-1080): GPU rows per sample (all, audio, per layer),
+        retention against the full audio span of every (layer, kv head), and
+        the host store (all rows, this sample's class-B rows, those loaded)."""
         out = []
         L, H = self.num_layers, self.num_kv_heads
+        seg_rows = getattr(self, "_seg_rows", None)
+        cpu_total = int(sum(int(r.sum()) for r in seg_rows)) if seg_rows is not None else 0
+        dt = self._decode_step if self.prefilled else 0
+        padded_prefill = (self._seq_lengths[0] - self._decode_step) if self._seq_lengths else 0
         for b in range(self.batch_size):
             n_audio = self._audio_ends_list[b] - self._audio_starts_list[b]
-            tot = 0
-            if getattr(self, "_len_host", None) is not None:
-                tot = int(self._len_host[:, b * H:(b + 1) * H].sum())
-            elif self.seq_lens and self.seq_lens[0] is not None:
-                tot = sum(sum(x[b * H:(b + 1) * H]) for x in self.seq_lens if x is not None)
-            out.append({"step": step, "num_audio": n_audio, "gpu_total_tokens": tot,
-                        "full_audio_tokens": L * H * n_audio})
+            full = L * H * n_audio
+            post_text = max(0, max(0, padded_prefill - self.pad_lens_list[b]) - self._audio_ends_list[b])
+            non_audio = self._audio_starts_list[b] + post_text
+            tot, aud, per_layer = 0, 0, []
+            for l in range(L):
+                lens = self.seq_lens[l]
+                if lens is None:
+                    per_layer.append(0)
+                    continue
+                row = np.asarray(lens[b * H:(b + 1) * H], dtype=np.int64)
+                a = int(np.maximum(row - non_audio - dt, 0).sum())
+                tot += int(row.sum())
+                aud += a
+                per_layer.append(a)
+            restore = int(seg_rows[b].sum()) if seg_rows is not None else 0
+            loaded = 0
+            if self.prefilled and seg_rows is not None and self.loaded_segments[b]:
+                loaded = int(seg_rows[b][sorted(self.loaded_segments[b])].sum())
+            out.append({"step": step, "num_audio": n_audio, "gpu_audio_tokens": aud, "gpu_total_tokens": tot,
+                        "audio_retention": aud / full if full > 0 else 1.0, "per_layer_audio_tokens": per_layer,
+                        "cpu_total_tokens": cpu_total, "cpu_loaded_tokens": loaded,
+                        "cpu_restore_tokens": restore,
+                        "gpu_plus_cpu_retention": (aud + restore) / full if full > 0 else 1.0})
         return out
+
+    def _segment_host_rows(self):
+        """Per sample, the host rows of each segment summed over every class-B
+        (layer, kv head): what loading or evicting that segment moves."""
+        L, H = self.num_layers, self.num_kv_heads
+        cs, ce = self._meta["cpu_s"], self._meta["cpu_e"]
+        rows = []
+        for b in range(self.batch_size):
+            n = self.seg_count[b]
+            r = np.zeros(n, np.int64)
+            for l in range(L):
+                for h in range(H):
+                    if self.config.is_class_b(l, h):
+                        m0 = int(self._meta_base[l, b * H + h])
+                        s, e = cs[m0:m0 + n].astype(np.int64), ce[m0:m0 + n].astype(np.int64)
+                        r += np.where(s >= 0, e - s, 0)
+            rows.append(r)
+        return rows
