@@ -238,3 +238,37 @@ def test_upload_plan_and_device_plan_argument_checks(golden_dir):
                                 None) == N.WNW_ERR_INVALID
     assert N.lib.wnw_dplan_verify(None, P._h) == N.WNW_ERR_INVALID
     N.lib.wnw_dplan_destroy(None)  # a null handle is a no-op
+
+
+def test_planner_gather_restore_matches_oracle(golden_dir):
+    """Planner.set_restore_buffers / gather_restore (planner.cpp:104-122): the
+    last plan's host ranges, in planner order, land at the front of the
+    staging buffers; a staging buffer too small is refused."""
+    import torch
+    from oracle import kernels as K
+    from wnw_b200.planner import Planner
+    ps = PLANNER_SCENARIOS[0]
+    inp = make_planner_inputs(ps)
+    P = _planner_from(ps, inp, Planner)
+    L, S = ps["L"], ps["B"] * ps["H"]
+    bufs = [np.zeros((L, S), np.int32), np.zeros((L, S), np.int32), np.zeros((L, S + 1), np.int32),
+            np.zeros((L, S), np.int32), np.zeros((L, S + 1), np.int32), np.zeros(L, np.int32),
+            np.zeros(L + 1, np.int32)]
+    for tk, toff in inp["steps"]:
+        ch, total, _, _, ranges = P.compute_and_prepare(tk, toff, *bufs)
+        if ch and total:
+            break
+    rows = int(np.max(ranges)) + 4
+    g = torch.Generator().manual_seed(5)
+    ck, cv = torch.randn(rows, 8, generator=g), torch.randn(rows, 8, generator=g)
+    sk, sv = torch.full((total + 3, 8), -1.0), torch.full((total + 3, 8), -1.0)
+    with pytest.raises(RuntimeError):
+        P.gather_restore()
+    P.set_restore_buffers(ck, cv, sk, sv)
+    P.gather_restore()
+    wk, wv = K.gather_restore(ck.numpy(), cv.numpy(), ranges)
+    assert np.array_equal(sk[:total].numpy(), wk) and np.array_equal(sv[:total].numpy(), wv)
+    assert (sk[total:] == -1).all()
+    P.set_restore_buffers(ck, cv, sk[:total - 1], sv[:total - 1])
+    with pytest.raises(N.WnwError):
+        P.gather_restore()

@@ -71,6 +71,28 @@ class Planner:
         return out[:n.value].tolist()
 
     # planner.cpp:124-306 -------------------------------------------------
+    # planner.cpp:104-122 ----------------------------------------------
+    def set_restore_buffers(self, cpu_k, cpu_v, stg_k, stg_v):
+        """The host restore store and the staging buffers ``gather_restore``
+        copies between; as in the reference, the caller keeps them alive
+        (their addresses are used, not copies)."""
+        if cpu_k.dim() != 2 or cpu_v.shape != cpu_k.shape or stg_k.shape[1:] != cpu_k.shape[1:] \
+                or stg_v.shape != stg_k.shape:
+            raise ValueError("restore buffers: [rows, head_dim] tensors of matching shapes expected")
+        self._restore = (cpu_k, cpu_v, stg_k, stg_v)
+
+    def gather_restore(self, n_threads=8):
+        """Copy the last plan's host ranges, in planner order, to the front of
+        the staging buffers."""
+        cpu_k, cpu_v, stg_k, stg_v = getattr(self, "_restore", (None,) * 4)
+        if cpu_k is None:
+            raise RuntimeError("gather_restore before set_restore_buffers")
+        r = self.cpu_ranges()
+        need = int((r[:, 1] - r[:, 0]).sum()) if r.size else 0
+        if need > stg_k.shape[0]:
+            raise N.WnwError(3, "gather_restore", f"staging holds {stg_k.shape[0]} rows, the plan needs {need}")
+        gather_rows(cpu_k, cpu_v, r, stg_k, stg_v, n_threads)
+
     def compute_and_prepare(self, topk_idx, topk_off, load_starts_2d, load_lens_2d, cu_new_2d,
                             new_lens_2d, evict_offsets_2d, evict_max, evict_layer_ptr):
         """Fills the caller's int32 output arrays (numpy or CPU tensors) in
