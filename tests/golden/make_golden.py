@@ -17,7 +17,7 @@ are needed to run its CUDA-oriented code on CPU (neither changes arithmetic):
 
 Outputs (all small, committed): ``kernels.npz``, ``cache_trace.npz``,
 ``cache_cpp_trace.npz``, ``planner.npz``, ``session_trace.json``,
-``session_degqa_trace.json``, ``stats.json``.
+``session_degqa_trace.json``, ``stats.json``, ``cache_cpp_dropin_trace.npz``.
 """
 from __future__ import annotations
 
@@ -270,6 +270,22 @@ def gen_stats():
         json.dump(_jsonable({"scripted": scripted, "cache_trace": cache_stats}), f)
 
 
+def gen_dropin():
+    """The reference's own C++-planner cache (WnWCppCache) run with OUR
+    Planner class in place of its pybind11 module: the same seeded trace,
+    recorded without the big layout arrays, to be compared with
+    cache_cpp_trace.npz (the reference's planner) by the CPU tests."""
+    import types
+    import algorithms.wnw_cpp.code._ext as ext
+    from algorithms.wnw_cpp.code.cache import WnWCppCache
+    from wnw_b200.planner import Planner
+    ext.get_planner_module = lambda: types.SimpleNamespace(Planner=Planner)
+    rec = run_cache_trace(WnWCppCache, cpp=True)
+    keep = {k: v for k, v in rec.items() if not (k.startswith("prefill_k") or k.startswith("prefill_v")
+                                                  or k.endswith("_k") or k.endswith("_v"))}
+    np.savez_compressed(os.path.join(HERE, "cache_cpp_dropin_trace.npz"), **keep)
+
+
 def gen_planner():
     from algorithms.wnw_cpp.code._ext import get_planner_module
     mod = get_planner_module()
@@ -449,7 +465,7 @@ def gen_degqa_trace():
 
 
 if __name__ == "__main__":
-    which = sys.argv[1:] or ["kernels", "cache", "planner", "session", "degqa", "stats"]
+    which = sys.argv[1:] or ["kernels", "cache", "planner", "session", "degqa", "stats", "dropin"]
     if "kernels" in which:
         gen_kernels()
     if "cache" in which:
@@ -462,4 +478,6 @@ if __name__ == "__main__":
         gen_degqa_trace()
     if "stats" in which:
         gen_stats()
+    if "dropin" in which:
+        gen_dropin()
     print("golden fixtures written to", HERE)

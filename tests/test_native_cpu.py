@@ -272,3 +272,42 @@ def test_planner_gather_restore_matches_oracle(golden_dir):
     P.set_restore_buffers(ck, cv, sk[:total - 1], sv[:total - 1])
     with pytest.raises(N.WnwError):
         P.gather_restore()
+
+
+def test_planner_returns_tensors_for_tensor_inputs(golden_dir):
+    """The reference's C++ cache calls .to(device) / .numel() on the plan's
+    evictions and ranges (wnw_cpp/code/cache.py:254-268): given torch inputs,
+    compute_and_prepare returns int32 CPU tensors equal to the numpy path."""
+    import torch
+    from wnw_b200.planner import Planner
+    ps = PLANNER_SCENARIOS[0]
+    inp = make_planner_inputs(ps)
+    L, S = ps["L"], ps["B"] * ps["H"]
+    shapes = [(L, S), (L, S), (L, S + 1), (L, S), (L, S + 1), (L,), (L + 1,)]
+    Pn, Pt = _planner_from(ps, inp, Planner), _planner_from(ps, inp, Planner)
+    for tk, toff in inp["steps"]:
+        rn = Pn.compute_and_prepare(tk, toff, *[np.zeros(s, np.int32) for s in shapes])
+        outs = [torch.zeros(s, dtype=torch.int32) for s in shapes]
+        rt = Pt.compute_and_prepare(torch.as_tensor(tk), torch.as_tensor(toff), *outs)
+        assert rt[:2] == rn[:2]
+        for a, b in zip(rt[2:], rn[2:]):
+            assert isinstance(a, torch.Tensor) and a.dtype == torch.int32
+            assert np.array_equal(a.numpy(), b)
+        assert rt[4].dim() == 2 and rt[4].shape[1] == 2
+
+
+def test_planner_is_a_drop_in_for_the_reference_cpp_cache(golden_dir):
+    """tests/golden/cache_cpp_dropin_trace.npz was recorded by running the
+    reference's own WnWCppCache with wnw_b200.planner.Planner in place of its
+    pybind11 planner (make_golden.py dropin): every layout digest, cu_seqlens,
+    output and loaded set equals the run with the reference's planner."""
+    ours = np.load(os.path.join(golden_dir, "cache_cpp_dropin_trace.npz"), allow_pickle=True)
+    ref = np.load(os.path.join(golden_dir, "cache_cpp_trace.npz"), allow_pickle=True)
+    keys = [k for k in ours.files]
+    assert any(k.endswith("_khash") for k in keys) and any(k.endswith("_loaded") for k in keys)
+    for k in keys:
+        a, b = ours[k], ref[k]
+        if a.dtype == object:
+            assert [list(x) for x in a] == [list(x) for x in b], k
+        else:
+            assert np.array_equal(a, b), k

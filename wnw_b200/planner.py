@@ -97,7 +97,9 @@ class Planner:
                             new_lens_2d, evict_offsets_2d, evict_max, evict_layer_ptr):
         """Fills the caller's int32 output arrays (numpy or CPU tensors) in
         place and returns ``(any_change, total_tokens, ev_starts, ev_ends,
-        cpu_ranges[nr, 2])`` like the reference."""
+        cpu_ranges[nr, 2])`` like the reference (planner.cpp:124-306): int32
+        CPU tensors when the top-k input is a tensor, as the reference's cache
+        expects (wnw_cpp/code/cache.py:254-268), numpy arrays otherwise."""
         tk, to = _i32(topk_idx), _i32(topk_off)
         outs = [load_starts_2d, load_lens_2d, cu_new_2d, new_lens_2d, evict_offsets_2d, evict_max,
                 evict_layer_ptr]
@@ -109,7 +111,11 @@ class Planner:
         N.call("wnw_planner_compute_and_prepare", self._h, N.ptr(tk) if tk.size else None, N.ptr(to),
                *[N.ptr(o) for o in outs], C.byref(ch), C.byref(tot))
         ev_s, ev_e = self.evictions()
-        return ch.value, tot.value, ev_s, ev_e, self.cpu_ranges()
+        ranges = self.cpu_ranges()
+        if hasattr(topk_idx, "numpy"):
+            import torch
+            ev_s, ev_e, ranges = (torch.from_numpy(x) for x in (ev_s, ev_e, ranges))
+        return ch.value, tot.value, ev_s, ev_e, ranges
 
     def compute(self, topk_idx, topk_off, out_ptrs):
         """``compute_and_prepare`` for callers that keep the plan on the
