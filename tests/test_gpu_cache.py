@@ -316,3 +316,38 @@ def test_mha_mode_session_reproduces_reference_generation(dev, golden_dir):
     assert calls == ref["calls"]
     assert out.cpu().tolist() == ref["tokens"]
     assert [sorted(s) for s in cache.loaded_segments] == ref["loaded"]
+
+
+def test_reference_session_drives_our_cache(dev, golden_dir):
+    """Drop-in check at the session boundary: the reference's OWN session
+    (the offline install in baseline/_ref, fused-attention path) driving
+    B200WnWCache on the GPU gives the reference session + reference cache's
+    hook calls, greedy tokens, loaded sets and stats."""
+    from transformers import LlamaConfig, LlamaForCausalLM
+    from tests.golden.scenario import SESSION_SCENARIO as ss, make_tiny_llama_config, session_inputs
+    from tests.oracle_hf import TracingMixin
+    from tests.reference_session import reference_session_or_skip
+    from tests.stats_compare import normalise
+    from wnw_b200.cache import B200WnWCache
+    from wnw_b200.config import WnWConfig
+
+    rsess, adapter = reference_session_or_skip(ss)
+    with open(os.path.join(golden_dir, "session_trace.json")) as f:
+        ref = json.load(f)
+    torch.manual_seed(ss["seed"])
+    model = LlamaForCausalLM(LlamaConfig(**make_tiny_llama_config(ss))).eval().to(dev)
+
+    class Tracing(TracingMixin, B200WnWCache):
+        pass
+
+    cache = Tracing(WnWConfig(**make_config_dict(ss)), ss["L"], ss["Hkv"], ss["Hq"], ss["D"], dev,
+                    max_decode_tokens=4)
+    ids = session_inputs(ss).to(dev)
+    with rsess.WnWSession(model, adapter, cache) as sess:
+        sess.setup_audio(ids)
+        with torch.no_grad():
+            out = sess.generate({"input_ids": ids}, max_new_tokens=ss["new_tokens"], do_sample=False)
+    assert cache.calls == ref["calls"]
+    assert out.cpu().tolist() == ref["tokens"]
+    assert [sorted(s) for s in cache.loaded_segments] == ref["loaded"]
+    assert normalise(sess.get_stats()) == normalise(ref["stats"])
