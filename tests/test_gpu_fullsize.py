@@ -86,3 +86,80 @@ def test_config2_full_size_matches_oracle(dev):
         changes += bool(orc.last_to_load[0] or orc.last_to_evict[0])
     assert changes >= 2
     assert near_ties < STEPS  # at least one step agreed on its own
+
+
+def _config3_scenario(seed=31):
+    """BASELINE config 3's shape, reduced to 2 layers: Qwen2.5-Omni-7B-like
+    heads (4 kv / 28 q, GQA 7, head_dim 128), batch 8 with seeded lognormal
+    prompt lengths (median 3k, clipped to [1k, 6k]) left-padded to the
+    longest, 50 % class-A kv heads, class-B retention 0.25 (~60 % of the KV
+    kept), chunks of 128 tokens, top-8, lag 1."""
+    rng = np.random.default_rng(seed)
+    B, L, H, Hq = 8, 2, 4, 28
+    lens = np.clip(np.round(np.exp(rng.normal(np.log(3000), 0.5, B))), 1000, 6000).astype(int)
+    S = int(lens.max())
+    pad = [int(S - n) for n in lens]
+    G = Hq // H
+    return dict(seed=seed, L=L, Hkv=H, Hq=Hq, D=128, B=B, steps=3, S=S,
+                audio_starts=[p + 4 for p in pad], audio_ends=[S - 30] * B, pad=pad,
+                chunk_size_s=128.0, overlap_s=0.0, token_rate=1.0,
+                class_a=[l * Hq + q for l in range(L) for q in range(2 * G)],
+                class_b=[l * H + h for l in range(L) for h in (2, 3)],
+                retention={(l, h): 0.25 for l in range(L) for h in (2, 3)},
+                top_k=8, lag=1, prefill_mode="last")
+
+
+def test_config3_shape_matches_oracle(dev):
+    """Batch 8 with ragged, left-padded prompts and GQA 7 through the whole
+    decode path (device fetch plan, fetch, rebuild, attention with scoring,
+    top-k) against the oracle: layouts bit for bit, loaded sets exactly,
+    attention within bf16 tolerance, class-A scores within fp32 tolerance."""
+    from tests.follow_oracle import FollowOracle, sync_selection
+    from tests.golden.scenario import make_cache_inputs, make_config_dict
+    from tests.test_gpu_cache import _packed_with_token
+    from wnw_b200.cache import B200WnWCache
+    from wnw_b200.config import WnWConfig
+
+    sc = _config3_scenario()
+    cfg = WnWConfig(**make_config_dict(sc))
+    inp = make_cache_inputs(sc)
+    L, H, Hq, D, B = sc["L"], sc["Hkv"], sc["Hq"], sc["D"], sc["B"]
+    G = Hq // H
+    bf = lambda a: torch.from_numpy(a).to(torch.bfloat16)  # noqa: E731
+    cache = B200WnWCache(cfg, L, H, Hq, D, dev, max_decode_tokens=sc["steps"] + 2)
+    orc = FollowOracle(cfg, L, H, Hq, D)
+    cache.setup_audio(torch.tensor(inp["audio_starts"]), torch.tensor(inp["audio_ends"]),
+                      torch.tensor(inp["attention_mask"]))
+    orc.setup_audio(inp["audio_starts"], inp["audio_ends"], inp["pad"])
+    for l in range(L):
+        ca, ph = inp["class_a_scores"][l], inp["per_head_scores"][l]
+        k, v = bf(inp["prefill_k"][l]), bf(inp["prefill_v"][l])
+        cache.prefill_after_attn(l, [x.to(dev) if x is not None else None for x in ca],
+                                 [[x.to(dev) if x is not None else None for x in r] for r in ph], k.to(dev), v.to(dev))
+        orc.prefill_after_attn(l, ca, ph, k, v)
+    cache.prefill_all_layers_done()
+    orc.prefill_all_layers_done()
+    assert cache._dplan is not None
+    assert [sorted(s) for s in cache.loaded_segments] == [sorted(s) for s in orc.loaded_segments]
+    loads = 0
+    for t in range(sc["steps"]):
+        for l in range(L):
+            q = bf(inp["dec_q"][t][l])
+            k, v = bf(inp["dec_k"][t][l]), bf(inp["dec_v"][t][l])
+            kk, vv, cu, _ = cache.decode_before_attn(l, k.to(dev), v.to(dev))
+            orc.decode_before_attn(l, k, v)
+            qf = q.squeeze(2).reshape(B, H, G, D).reshape(-1, G, D)
+            out = cache.fused_decode_attention(l, qf.to(dev), q.to(dev), kk, vv, cu, D ** -0.5)
+            orc.fused_decode_attention(l, qf, scale=D ** -0.5)
+            np.testing.assert_allclose(out.float().cpu().numpy(), orc.last_out64, atol=2e-2, rtol=2e-2)
+            pk, _, pcu = _packed_with_token(cache, l)
+            assert np.array_equal(pcu, orc.cu(l)), (t, l)
+            assert torch.equal(pk.cpu(), orc.layer_k[l]), (t, l)
+        cache.decode_all_layers_done()
+        sync_selection(orc, cache.last_topk)
+        orc.decode_all_layers_done()
+        np.testing.assert_allclose(cache.score_accumulator.cpu().numpy(), orc.last_scores, atol=1e-4, rtol=1e-3)
+        assert cache.last_topk == orc.last_topk, t
+        assert [sorted(s) for s in cache.loaded_segments] == [sorted(s) for s in orc.loaded_segments], t
+        loads += sum(len(x) for x in orc.last_to_load)
+    assert loads > 0
