@@ -50,8 +50,13 @@ def make_cache_inputs(sc):
     n_audio = [e - s for s, e in zip(sc["audio_starts"], sc["audio_ends"])]
     inp = dict(audio_starts=list(sc["audio_starts"]), audio_ends=list(sc["audio_ends"]),
                attention_mask=mask, pad=list(sc["pad"]))
-    inp["prefill_k"] = [rng.standard_normal((B, H, S, D)).astype(np.float32) for _ in range(L)]
-    inp["prefill_v"] = [rng.standard_normal((B, H, S, D)).astype(np.float32) for _ in range(L)]
+    if sc.get("torch_kv"):  # long contexts: torch's generator draws fp32 directly, ~10x faster
+        g = torch.Generator().manual_seed(sc["seed"])
+        inp["prefill_k"] = [torch.randn(B, H, S, D, generator=g).numpy() for _ in range(L)]
+        inp["prefill_v"] = [torch.randn(B, H, S, D, generator=g).numpy() for _ in range(L)]
+    else:
+        inp["prefill_k"] = [rng.standard_normal((B, H, S, D)).astype(np.float32) for _ in range(L)]
+        inp["prefill_v"] = [rng.standard_normal((B, H, S, D)).astype(np.float32) for _ in range(L)]
     cas, phs = [], []
     for l in range(L):
         ca_kv = _class_a_kv(sc, l)

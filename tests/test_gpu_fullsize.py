@@ -163,3 +163,78 @@ def test_config3_shape_matches_oracle(dev):
         assert [sorted(s) for s in cache.loaded_segments] == [sorted(s) for s in orc.loaded_segments], t
         loads += sum(len(x) for x in orc.last_to_load)
     assert loads > 0
+
+
+def _config4_scenario(seed=41):
+    """BASELINE config 4's per-layer shape, reduced to one layer:
+    Voxtral-Small-24B-like heads (8 kv / 32 q, head_dim 128), batch 2 at a
+    120k-token context (a 119,900-token audio span), class-B chunks of 128
+    tokens offloaded to pinned host memory, top-32; a quarter of the kv heads
+    class A (full 120k context, scored), the rest class B at retention 0.05."""
+    B, L, H, Hq = 2, 1, 8, 32
+    S = 120064
+    G = Hq // H
+    return dict(seed=seed, L=L, Hkv=H, Hq=Hq, D=128, B=B, steps=3, S=S,
+                audio_starts=[4, 4], audio_ends=[S - 160, S - 160], pad=[0, 0],
+                chunk_size_s=128.0, overlap_s=0.0, token_rate=1.0,
+                class_a=[q for q in range(2 * G)], class_b=list(range(2, H)),
+                retention={(0, h): 0.05 for h in range(2, H)},
+                top_k=32, lag=1, prefill_mode="last", torch_kv=True)
+
+
+def test_config4_long_context_layer_matches_oracle(dev):
+    """120k-token context through the whole decode path: ~940 chunks per
+    sample, top-32 loads per step fetched from pinned host memory, two
+    120k-row class-A segments per sample attended and scored."""
+    from tests.follow_oracle import FollowOracle, sync_selection
+    from tests.golden.scenario import make_cache_inputs, make_config_dict
+    from tests.test_gpu_cache import _packed_with_token
+    from wnw_b200.cache import B200WnWCache
+    from wnw_b200.config import WnWConfig
+
+    sc = _config4_scenario()
+    cfg = WnWConfig(**make_config_dict(sc))
+    inp = make_cache_inputs(sc)
+    L, H, Hq, D, B = sc["L"], sc["Hkv"], sc["Hq"], sc["D"], sc["B"]
+    G = Hq // H
+    bf = lambda a: torch.from_numpy(a).to(torch.bfloat16)  # noqa: E731
+    pk16 = [bf(x) for x in inp.pop("prefill_k")]
+    pv16 = [bf(x) for x in inp.pop("prefill_v")]
+    cache = B200WnWCache(cfg, L, H, Hq, D, dev, max_decode_tokens=sc["steps"] + 2)
+    orc = FollowOracle(cfg, L, H, Hq, D)
+    cache.setup_audio(torch.tensor(inp["audio_starts"]), torch.tensor(inp["audio_ends"]),
+                      torch.tensor(inp["attention_mask"]))
+    orc.setup_audio(inp["audio_starts"], inp["audio_ends"], inp["pad"])
+    for l in range(L):
+        ca, ph = inp["class_a_scores"][l], inp["per_head_scores"][l]
+        cache.prefill_after_attn(l, [x.to(dev) if x is not None else None for x in ca],
+                                 [[x.to(dev) if x is not None else None for x in r] for r in ph],
+                                 pk16[l].to(dev), pv16[l].to(dev))
+        orc.prefill_after_attn(l, ca, ph, pk16[l], pv16[l])
+    del pk16, pv16
+    cache.prefill_all_layers_done()
+    orc.prefill_all_layers_done()
+    assert cache._dplan is not None
+    assert [sorted(s) for s in cache.loaded_segments] == [sorted(s) for s in orc.loaded_segments]
+    loads = 0
+    for t in range(sc["steps"]):
+        for l in range(L):
+            q = bf(inp["dec_q"][t][l])
+            k, v = bf(inp["dec_k"][t][l]), bf(inp["dec_v"][t][l])
+            kk, vv, cu, _ = cache.decode_before_attn(l, k.to(dev), v.to(dev))
+            orc.decode_before_attn(l, k, v)
+            qf = q.squeeze(2).reshape(B, H, G, D).reshape(-1, G, D)
+            out = cache.fused_decode_attention(l, qf.to(dev), q.to(dev), kk, vv, cu, D ** -0.5)
+            orc.fused_decode_attention(l, qf, scale=D ** -0.5)
+            np.testing.assert_allclose(out.float().cpu().numpy(), orc.last_out64, atol=2e-2, rtol=2e-2)
+            pk, _, pcu = _packed_with_token(cache, l)
+            assert np.array_equal(pcu, orc.cu(l)), (t, l)
+            assert torch.equal(pk.cpu(), orc.layer_k[l]), (t, l)
+        cache.decode_all_layers_done()
+        sync_selection(orc, cache.last_topk)
+        orc.decode_all_layers_done()
+        np.testing.assert_allclose(cache.score_accumulator.cpu().numpy(), orc.last_scores, atol=1e-4, rtol=1e-3)
+        assert cache.last_topk == orc.last_topk, t
+        assert [sorted(s) for s in cache.loaded_segments] == [sorted(s) for s in orc.loaded_segments], t
+        loads += sum(len(x) for x in orc.last_to_load)
+    assert loads > 0
