@@ -238,3 +238,75 @@ def test_config4_long_context_layer_matches_oracle(dev):
         assert [sorted(s) for s in cache.loaded_segments] == [sorted(s) for s in orc.loaded_segments], t
         loads += sum(len(x) for x in orc.last_to_load)
     assert loads > 0
+
+
+def _config1_scenario(seed=0):
+    """BASELINE config 1 (the reference's CPU-runnable case): one layer, batch
+    4, 8 kv / 32 q heads, head_dim 128, fp32, context lengths U[512, 4096]
+    per request (left-padded), layout [4 sink][audio][256 window], chunks of
+    64 tokens, top-8, kv heads 0 and 1 class A (all 8 of their q heads), the
+    other 6 class B at a small retention (the reference keeps >= 1 audio row
+    per segment)."""
+    rng = np.random.default_rng(seed)
+    B, L, H, Hq = 4, 1, 8, 32
+    lens = rng.integers(512, 4097, B)
+    S = int(lens.max())
+    pad = [int(S - n) for n in lens]
+    G = Hq // H
+    return dict(seed=seed, L=L, Hkv=H, Hq=Hq, D=128, B=B, steps=4, S=S,
+                audio_starts=[p + 4 for p in pad], audio_ends=[S - 256] * B, pad=pad,
+                chunk_size_s=64.0, overlap_s=0.0, token_rate=1.0,
+                class_a=list(range(2 * G)), class_b=list(range(2, H)),
+                retention={(0, h): 0.02 for h in range(2, H)},
+                top_k=8, lag=1, prefill_mode="last")
+
+
+def test_config1_matches_oracle_fp32(dev):
+    """fp32 at config 1's shape: attention and class-A scores within 1e-5 of
+    the oracle, layouts bit for bit, loaded sets exactly."""
+    from tests.follow_oracle import FollowOracle, sync_selection
+    from tests.golden.scenario import make_cache_inputs, make_config_dict
+    from tests.test_gpu_cache import _packed_with_token
+    from wnw_b200.cache import B200WnWCache
+    from wnw_b200.config import WnWConfig
+
+    sc = _config1_scenario()
+    cfg = WnWConfig(**make_config_dict(sc))
+    inp = make_cache_inputs(sc)
+    L, H, Hq, D, B = sc["L"], sc["Hkv"], sc["Hq"], sc["D"], sc["B"]
+    G = Hq // H
+    t32 = torch.from_numpy
+    cache = B200WnWCache(cfg, L, H, Hq, D, dev, max_decode_tokens=sc["steps"] + 2)
+    orc = FollowOracle(cfg, L, H, Hq, D)
+    cache.setup_audio(torch.tensor(inp["audio_starts"]), torch.tensor(inp["audio_ends"]),
+                      torch.tensor(inp["attention_mask"]))
+    orc.setup_audio(inp["audio_starts"], inp["audio_ends"], inp["pad"])
+    ca, ph = inp["class_a_scores"][0], inp["per_head_scores"][0]
+    k, v = t32(inp["prefill_k"][0]), t32(inp["prefill_v"][0])
+    cache.prefill_after_attn(0, [x.to(dev) if x is not None else None for x in ca],
+                             [[x.to(dev) if x is not None else None for x in r] for r in ph], k.to(dev), v.to(dev))
+    orc.prefill_after_attn(0, ca, ph, k, v)
+    cache.prefill_all_layers_done()
+    orc.prefill_all_layers_done()
+    assert [sorted(s) for s in cache.loaded_segments] == [sorted(s) for s in orc.loaded_segments]
+    loads = 0
+    for t in range(sc["steps"]):
+        q = t32(inp["dec_q"][t][0])
+        k, v = t32(inp["dec_k"][t][0]), t32(inp["dec_v"][t][0])
+        kk, vv, cu, _ = cache.decode_before_attn(0, k.to(dev), v.to(dev))
+        orc.decode_before_attn(0, k, v)
+        qf = q.squeeze(2).reshape(B, H, G, D).reshape(-1, G, D)
+        out = cache.fused_decode_attention(0, qf.to(dev), q.to(dev), kk, vv, cu, D ** -0.5)
+        orc.fused_decode_attention(0, qf, scale=D ** -0.5)
+        np.testing.assert_allclose(out.cpu().numpy(), orc.last_out64, atol=1e-5, rtol=1e-5)
+        pk, _, pcu = _packed_with_token(cache, 0)
+        assert np.array_equal(pcu, orc.cu(0)), t
+        assert torch.equal(pk.cpu(), orc.layer_k[0]), t
+        cache.decode_all_layers_done()
+        sync_selection(orc, cache.last_topk)
+        orc.decode_all_layers_done()
+        np.testing.assert_allclose(cache.score_accumulator.cpu().numpy(), orc.last_scores, atol=1e-5, rtol=1e-4)
+        assert cache.last_topk == orc.last_topk, t
+        assert [sorted(s) for s in cache.loaded_segments] == [sorted(s) for s in orc.loaded_segments], t
+        loads += sum(len(x) for x in orc.last_to_load)
+    assert loads > 0
