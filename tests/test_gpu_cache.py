@@ -189,10 +189,12 @@ def test_session_reproduces_reference_generation(dev, golden_dir):
 
 
 @pytest.mark.parametrize("variant", [dict(lag=0), dict(lag=1), dict(lag=3, top_k=1),
-                                     dict(top_k=5, chunk_size_s=16.0, overlap_s=0.0), dict(steps=12, top_k=2)])
+                                     dict(top_k=5, chunk_size_s=16.0, overlap_s=0.0), dict(steps=12, top_k=2),
+                                     dict(audio_starts=[5, 305], audio_ends=[305, 305])])
 def test_device_fetch_plan_follows_planner(dev, variant):
     """The device fetch plan mirrors the planner's selection diff (eviction
-    lag, chunks of one or two segments, several loads per step): every step
+    lag, chunks of one or two segments, several loads per step, a sample
+    with no audio at all): every step
     the cache checks its landing rows, loaded maps and counters against the
     host planner's (a difference raises), and the fp32 run must match the
     oracle's layouts, loaded sets and outputs."""

@@ -71,6 +71,8 @@ def keep_audio_indices(scores, seg_ranges, ratio, global_topk):
     ratio)) best tokens; globally (cache.py:1141-1150) the span keeps the sum
     of those counts -- for all the heads in one batched top-k."""
     nh, n = scores.shape
+    if not seg_ranges:  # a sample with no audio keeps (and offloads) nothing
+        return torch.empty(nh, 0, dtype=torch.int64, device=scores.device)
     if global_topk:
         k = min(n, sum(max(1, int((b - a) * ratio)) for a, b in seg_ranges))
         return scores.topk(k, dim=1).indices.sort(dim=1).values
