@@ -353,3 +353,52 @@ def test_reference_session_drives_our_cache(dev, golden_dir):
     assert out.cpu().tolist() == ref["tokens"]
     assert [sorted(s) for s in cache.loaded_segments] == ref["loaded"]
     assert normalise(sess.get_stats()) == normalise(ref["stats"])
+
+
+@pytest.mark.parametrize("variant", [dict(audio_starts=[305, 305], audio_ends=[305, 305]),  # no audio at all
+                                     dict(top_k=40),                   # top-k covers every chunk
+                                     dict(lag=50, steps=10)])          # nothing is ever evicted
+def test_cache_edge_cases_match_oracle(dev, variant):
+    """Edge cases of the selection: a batch without audio (no scoring, no
+    selection), a top-k that covers every chunk (everything loaded at
+    prefill, nothing moves), an eviction lag longer than the run (loads
+    only, slots grow): layouts, loaded sets and outputs as the oracle's."""
+    from tests.follow_oracle import FollowOracle, sync_selection
+    from wnw_b200.cache import B200WnWCache
+    from wnw_b200.config import WnWConfig
+    sc = dict(CACHE_SCENARIO, **variant)
+    cfg = WnWConfig(**make_config_dict(sc))
+    inp = make_cache_inputs(sc)
+    G = sc["Hq"] // sc["Hkv"]
+    cache = B200WnWCache(cfg, sc["L"], sc["Hkv"], sc["Hq"], sc["D"], dev, max_decode_tokens=2)
+    orc = FollowOracle(cfg, sc["L"], sc["Hkv"], sc["Hq"], sc["D"])
+    cache.setup_audio(torch.tensor(inp["audio_starts"]), torch.tensor(inp["audio_ends"]),
+                      torch.tensor(inp["attention_mask"]))
+    orc.setup_audio(inp["audio_starts"], inp["audio_ends"], inp["pad"])
+    for l in range(sc["L"]):
+        ca, ph = inp["class_a_scores"][l], inp["per_head_scores"][l]
+        k, v = torch.from_numpy(inp["prefill_k"][l]), torch.from_numpy(inp["prefill_v"][l])
+        cache.prefill_after_attn(l, [x.to(dev) if x is not None else None for x in ca],
+                                 [[x.to(dev) if x is not None else None for x in r] for r in ph], k.to(dev), v.to(dev))
+        orc.prefill_after_attn(l, ca, ph, k, v)
+    cache.prefill_all_layers_done()
+    orc.prefill_all_layers_done()
+    assert [sorted(s) for s in cache.loaded_segments] == [sorted(s) for s in orc.loaded_segments]
+    for t in range(sc["steps"]):
+        for l in range(sc["L"]):
+            q = torch.from_numpy(inp["dec_q"][t][l])
+            k, v = torch.from_numpy(inp["dec_k"][t][l]), torch.from_numpy(inp["dec_v"][t][l])
+            kk, vv, cu, _ = cache.decode_before_attn(l, k.to(dev), v.to(dev))
+            orc.decode_before_attn(l, k, v)
+            qf = q.squeeze(2).reshape(sc["B"], sc["Hkv"], G, sc["D"]).reshape(-1, G, sc["D"])
+            out = cache.fused_decode_attention(l, qf.to(dev), q.to(dev), kk, vv, cu, sc["D"] ** -0.5)
+            orc.fused_decode_attention(l, qf, scale=sc["D"] ** -0.5)
+            np.testing.assert_allclose(out.cpu().numpy(), orc.last_out64, atol=1e-5, rtol=1e-5)
+            pk, _, pcu = _packed_with_token(cache, l)
+            assert np.array_equal(pcu, orc.cu(l)), (t, l)
+            assert torch.equal(pk.cpu(), orc.layer_k[l]), (t, l)
+        cache.decode_all_layers_done()
+        sync_selection(orc, cache.last_topk)
+        orc.decode_all_layers_done()
+        assert cache.last_topk == orc.last_topk, t
+        assert [sorted(s) for s in cache.loaded_segments] == [sorted(s) for s in orc.loaded_segments], t

@@ -523,7 +523,7 @@ class B200WnWCache(FlatVarlenCache):
         self._score_groups = []
         for l in range(L):
             by_kv = {}
-            for qh in self.config.get_layer_class_a(l):
+            for qh in self.config.get_layer_class_a(l) if sum(audio) > 0 else ():  # no audio: nothing to score
                 by_kv.setdefault(qh // G, []).append(qh % G)
             self._score_groups.append(sorted(by_kv.items()))
         self._has_scoring = any(self._score_groups)
