@@ -17,7 +17,7 @@ are needed to run its CUDA-oriented code on CPU (neither changes arithmetic):
 
 Outputs (all small, committed): ``kernels.npz``, ``cache_trace.npz``,
 ``cache_cpp_trace.npz``, ``planner.npz``, ``session_trace.json``,
-``session_degqa_trace.json``, ``stats.json``, ``cache_cpp_dropin_trace.npz``.
+``session_degqa_trace.json``, ``stats.json``, ``cache_cpp_dropin_trace.npz``, ``cache_trace_global.npz``.
 """
 from __future__ import annotations
 
@@ -155,9 +155,8 @@ class _Adapter:
     """Minimal stand-in: the cache only stores its adapter."""
 
 
-def run_cache_trace(cache_cls, cpp):
+def run_cache_trace(cache_cls, cpp, sc=CACHE_SCENARIO):
     from algorithms.wnw.code.config import WnWConfig
-    sc = CACHE_SCENARIO
     cfg = WnWConfig(**make_config_dict(sc))
     cache = cache_cls(config=cfg, num_layers=sc["L"], num_kv_heads=sc["Hkv"],
                       num_q_heads=sc["Hq"], head_dim=sc["D"], device=torch.device("cpu"),
@@ -284,6 +283,21 @@ def gen_dropin():
     keep = {k: v for k, v in rec.items() if not (k.startswith("prefill_k") or k.startswith("prefill_v")
                                                   or k.endswith("_k") or k.endswith("_v"))}
     np.savez_compressed(os.path.join(HERE, "cache_cpp_dropin_trace.npz"), **keep)
+
+
+def gen_global_trace():
+    """The reference's Python cache on the seeded scenario with the global
+    per-head prefill top-k (cache.py:1141-1150) instead of the per-segment
+    rule; layouts as digests only (no raw arrays)."""
+    from algorithms.wnw.code.cache import WnWCache
+    from tests.golden.scenario import GLOBAL_TOPK_SCENARIO
+    rec = run_cache_trace(WnWCache, cpp=False, sc=GLOBAL_TOPK_SCENARIO)
+    for k in list(rec):
+        if k.startswith("prefill_k") or k.startswith("prefill_v") or k.endswith("_k") or k.endswith("_v"):
+            arr = rec.pop(k)
+            if k.startswith("prefill_k"):
+                rec[k.replace("prefill_k", "prefill_khash")] = np.array(_digest(arr))
+    np.savez_compressed(os.path.join(HERE, "cache_trace_global.npz"), **rec)
 
 
 def gen_planner():
@@ -465,7 +479,7 @@ def gen_degqa_trace():
 
 
 if __name__ == "__main__":
-    which = sys.argv[1:] or ["kernels", "cache", "planner", "session", "degqa", "stats", "dropin"]
+    which = sys.argv[1:] or ["kernels", "cache", "planner", "session", "degqa", "stats", "dropin", "global"]
     if "kernels" in which:
         gen_kernels()
     if "cache" in which:
@@ -480,4 +494,6 @@ if __name__ == "__main__":
         gen_stats()
     if "dropin" in which:
         gen_dropin()
+    if "global" in which:
+        gen_global_trace()
     print("golden fixtures written to", HERE)

@@ -20,6 +20,10 @@ CACHE_SCENARIO = dict(
 )
 
 
+# the same scenario with the global per-head prefill top-k (cache.py:1141-1150)
+GLOBAL_TOPK_SCENARIO = dict(CACHE_SCENARIO, global_topk=True)
+
+
 def make_config_dict(sc):
     """Keyword arguments for the reference ``WnWConfig`` (config.py:6-30)."""
     L, H, Hq = sc["L"], sc["Hkv"], sc["Hq"]

@@ -402,3 +402,47 @@ def test_cache_edge_cases_match_oracle(dev, variant):
         orc.decode_all_layers_done()
         assert cache.last_topk == orc.last_topk, t
         assert [sorted(s) for s in cache.loaded_segments] == [sorted(s) for s in orc.loaded_segments], t
+
+
+def test_cache_reproduces_reference_trace_global_prefill_topk(dev, golden_dir):
+    """The global per-head prefill top-k (cache.py:1141-1150): the B200 cache
+    reproduces the reference's trace recorded with it (layout digests,
+    cu_seqlens, loaded sets; outputs and class-A scores within fp32
+    tolerance)."""
+    from tests.golden.scenario import GLOBAL_TOPK_SCENARIO as sc
+    from wnw_b200.cache import B200WnWCache
+    from wnw_b200.config import WnWConfig
+    tz = np.load(os.path.join(golden_dir, "cache_trace_global.npz"), allow_pickle=True)
+    inp = make_cache_inputs(sc)
+    G = sc["Hq"] // sc["Hkv"]
+    cache = B200WnWCache(WnWConfig(**make_config_dict(sc)), sc["L"], sc["Hkv"], sc["Hq"], sc["D"], dev,
+                         max_decode_tokens=3)
+    cache.setup_audio(torch.tensor(inp["audio_starts"]), torch.tensor(inp["audio_ends"]),
+                      torch.tensor(inp["attention_mask"]))
+    for l in range(sc["L"]):
+        cache.prefill_after_attn(l, [x.to(dev) if x is not None else None for x in inp["class_a_scores"][l]],
+                                 [[x.to(dev) if x is not None else None for x in row]
+                                  for row in inp["per_head_scores"][l]],
+                                 torch.from_numpy(inp["prefill_k"][l]).to(dev),
+                                 torch.from_numpy(inp["prefill_v"][l]).to(dev))
+    cache.prefill_all_layers_done()
+    for l in range(sc["L"]):
+        k, _, cu = cache.packed_layer(l)
+        assert np.array_equal(cu.cpu().numpy(), tz["prefill_cu"][l])
+        assert _digest(k) == str(tz[f"prefill_khash{l}"])
+    assert [sorted(s) for s in cache.loaded_segments] == [list(x) for x in tz["prefill_loaded"]]
+    for t in range(sc["steps"]):
+        for l in range(sc["L"]):
+            q = torch.from_numpy(inp["dec_q"][t][l]).to(dev)
+            kk, vv, cu, _ = cache.decode_before_attn(l, torch.from_numpy(inp["dec_k"][t][l]).to(dev),
+                                                     torch.from_numpy(inp["dec_v"][t][l]).to(dev))
+            qf = q.squeeze(2).reshape(sc["B"], sc["Hkv"], G, sc["D"]).reshape(-1, G, sc["D"])
+            out = cache.fused_decode_attention(l, qf, q, kk, vv, cu, sc["D"] ** -0.5)
+            pk, pv, pcu = _packed_with_token(cache, l)
+            assert np.array_equal(pcu, tz[f"s{t}_l{l}_cu"]), (t, l)
+            assert _digest(pk) == str(tz[f"s{t}_l{l}_khash"]), (t, l)
+            assert _digest(pv) == str(tz[f"s{t}_l{l}_vhash"]), (t, l)
+            np.testing.assert_allclose(out.cpu().numpy(), tz[f"s{t}_l{l}_out"], atol=1e-5, rtol=1e-5)
+        cache.decode_all_layers_done()
+        np.testing.assert_allclose(cache.score_accumulator.cpu().numpy(), tz[f"s{t}_scores"], atol=1e-5, rtol=1e-4)
+        assert [sorted(s) for s in cache.loaded_segments] == [list(x) for x in tz[f"s{t}_loaded"]], t
