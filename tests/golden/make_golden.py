@@ -17,7 +17,9 @@ are needed to run its CUDA-oriented code on CPU (neither changes arithmetic):
 
 Outputs (all small, committed): ``kernels.npz``, ``cache_trace.npz``,
 ``cache_cpp_trace.npz``, ``planner.npz``, ``session_trace.json``,
-``session_degqa_trace.json``, ``stats.json``, ``cache_cpp_dropin_trace.npz``, ``cache_trace_global.npz``.
+``session_degqa_trace.json``, ``stats.json``, ``cache_cpp_dropin_trace.npz``, ``cache_trace_global.npz``,
+``session_mean_text_trace.json`` (each session trace with its prefill K
+layouts, ``*_prefill_k.npz``).
 """
 from __future__ import annotations
 
@@ -381,17 +383,19 @@ def _tiny_adapter(ss):
     return TinyAdapter()
 
 
-def gen_session_trace():
+def gen_session_trace(ss=None, name="session_trace.json"):
     """Drive the reference WnWSession over a tiny random-init Llama (fp32) and
     record the hook call sequence and the greedy tokens."""
     from transformers import LlamaConfig, LlamaForCausalLM
     from algorithms.wnw.code.config import WnWConfig
     from algorithms.wnw.code.cache import WnWCache
     from algorithms.wnw.code.session import WnWSession
-    from tests.golden.scenario import SESSION_SCENARIO as ss, make_tiny_llama_config, session_inputs
+    from tests.golden.scenario import SESSION_SCENARIO, make_tiny_llama_config, session_inputs
+    ss = ss or SESSION_SCENARIO
 
     adapter = _tiny_adapter(ss)
     calls = []
+    prefill_hash, prefill_k = [], []
 
     class TracingCache(WnWCache):
         def prefill_after_attn(self, l, a, p, k, v):
@@ -400,7 +404,10 @@ def gen_session_trace():
 
         def prefill_all_layers_done(self):
             calls.append(["prefill_all_layers_done"])
-            return super().prefill_all_layers_done()
+            r = super().prefill_all_layers_done()
+            prefill_hash.extend(_digest(self.layer_k[l].numpy()) for l in range(self.num_layers))
+            prefill_k.extend(self.layer_k[l].numpy().copy() for l in range(self.num_layers))
+            return r
 
         def decode_before_attn(self, l, k, v):
             calls.append(["decode_before_attn", l, list(k.shape)])
@@ -426,8 +433,11 @@ def gen_session_trace():
         with torch.no_grad():
             out = sess.generate({"input_ids": ids}, max_new_tokens=ss["new_tokens"], do_sample=False)
     res = {"calls": calls, "tokens": out.tolist(),
-           "loaded": [sorted(s) for s in cache.loaded_segments], "stats": _jsonable(sess.get_stats())}
-    with open(os.path.join(HERE, "session_trace.json"), "w") as f:
+           "loaded": [sorted(s) for s in cache.loaded_segments], "stats": _jsonable(sess.get_stats()),
+           "prefill_khash": prefill_hash}
+    np.savez_compressed(os.path.join(HERE, name.replace(".json", "_prefill_k.npz")),
+                        **{f"l{l}": k for l, k in enumerate(prefill_k)})
+    with open(os.path.join(HERE, name), "w") as f:
         json.dump(res, f)
 
 
@@ -479,7 +489,8 @@ def gen_degqa_trace():
 
 
 if __name__ == "__main__":
-    which = sys.argv[1:] or ["kernels", "cache", "planner", "session", "degqa", "stats", "dropin", "global"]
+    which = sys.argv[1:] or ["kernels", "cache", "planner", "session", "degqa", "stats", "dropin", "global",
+                             "mean_text"]
     if "kernels" in which:
         gen_kernels()
     if "cache" in which:
@@ -488,6 +499,9 @@ if __name__ == "__main__":
         gen_planner()
     if "session" in which:
         gen_session_trace()
+    if "mean_text" in which:
+        from tests.golden.scenario import MEAN_TEXT_SESSION_SCENARIO
+        gen_session_trace(MEAN_TEXT_SESSION_SCENARIO, "session_mean_text_trace.json")
     if "degqa" in which:
         gen_degqa_trace()
     if "stats" in which:

@@ -151,6 +151,11 @@ SESSION_SCENARIO = dict(
 )
 
 
+# the session scenario with the reference's default prefill score mode (the
+# mean over the post-audio text queries, session.py:185-196)
+MEAN_TEXT_SESSION_SCENARIO = dict(SESSION_SCENARIO, prefill_mode="mean_text")
+
+
 def make_tiny_llama_config(ss):
     return dict(vocab_size=ss["vocab"], hidden_size=ss["hidden"], intermediate_size=ss["inter"],
                 num_hidden_layers=ss["L"], num_attention_heads=ss["Hq"], num_key_value_heads=ss["Hkv"],

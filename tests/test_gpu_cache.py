@@ -154,25 +154,33 @@ def test_cache_matches_oracle_in_bf16(dev):
         assert [sorted(s) for s in cache.loaded_segments] == [sorted(s) for s in orc.loaded_segments], t
 
 
-def test_session_reproduces_reference_generation(dev, golden_dir):
+@pytest.mark.parametrize("mode", ["last", "mean_text"])
+def test_session_reproduces_reference_generation(dev, golden_dir, mode):
     """Tiny random-init Llama in fp32 on the GPU: model.generate through our
-    session and B200WnWCache gives the reference session's hook calls and
-    greedy tokens."""
+    session and B200WnWCache gives the reference session's hook calls,
+    prefill layouts (under either prefill score mode), greedy tokens and
+    stats."""
     from transformers import LlamaConfig, LlamaForCausalLM
-    from tests.golden.scenario import SESSION_SCENARIO as ss, make_tiny_llama_config, session_inputs
+    from tests.golden.scenario import (MEAN_TEXT_SESSION_SCENARIO, SESSION_SCENARIO, make_tiny_llama_config,
+                                       session_inputs)
     from tests.oracle_hf import TracingMixin
     from wnw_b200.adapters import LlamaFamilyAdapter
     from wnw_b200.cache import B200WnWCache
     from wnw_b200.config import WnWConfig
     from wnw_b200.session import WnWSession
 
-    with open(os.path.join(golden_dir, "session_trace.json")) as f:
+    ss = SESSION_SCENARIO if mode == "last" else MEAN_TEXT_SESSION_SCENARIO
+    name = "session_trace.json" if mode == "last" else "session_mean_text_trace.json"
+    with open(os.path.join(golden_dir, name)) as f:
         ref = json.load(f)
     torch.manual_seed(ss["seed"])
     model = LlamaForCausalLM(LlamaConfig(**make_tiny_llama_config(ss))).eval().to(dev)
+    prefill_k = []  # prefill K layouts, per layer
 
     class Tracing(TracingMixin, B200WnWCache):
-        pass
+        def prefill_all_layers_done(self):
+            super().prefill_all_layers_done()
+            prefill_k.extend(self.packed_layer(l)[0].float().cpu().numpy() for l in range(ss["L"]))
 
     cache = Tracing(WnWConfig(**make_config_dict(ss)), ss["L"], ss["Hkv"], ss["Hq"], ss["D"], dev,
                     max_decode_tokens=4)
@@ -182,6 +190,13 @@ def test_session_reproduces_reference_generation(dev, golden_dir):
         with torch.no_grad():
             out = sess.generate({"input_ids": ids}, max_new_tokens=ss["new_tokens"], do_sample=False)
     assert cache.calls == ref["calls"]
+    # the model's K on the GPU differs from the reference's CPU run in the low
+    # bits, so the kept rows are compared by value within fp32 tolerance (a
+    # different choice of kept rows differs by O(1))
+    want = np.load(os.path.join(golden_dir, name.replace(".json", "_prefill_k.npz")))
+    for l, k in enumerate(prefill_k):
+        assert k.shape == want[f"l{l}"].shape, l
+        np.testing.assert_allclose(k, want[f"l{l}"], atol=1e-4, rtol=1e-4)
     assert out.cpu().tolist() == ref["tokens"]
     assert [sorted(s) for s in cache.loaded_segments] == ref["loaded"]
     from tests.stats_compare import normalise
