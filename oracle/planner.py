@@ -235,3 +235,61 @@ class OraclePlanner:
                    ev_starts=np.asarray(ev_s, np.int32), ev_ends=np.asarray(ev_e, np.int32),
                    cpu_ranges=np.asarray(self.cpu_ranges, np.int32).reshape(-1, 2))
         return res
+
+
+def device_fetch_plan(P, topk_rows):
+    """Restates, in plain Python, what the device fetch plan kernel
+    (wnw_b200/csrc/device_plan.cu) computes from one step's top-k, for the
+    planner state ``P`` (an ``OraclePlanner``, whose loaded sets and counters
+    are advanced in place as the kernel advances its device copy):
+
+    * per sample with at least one top-k chunk: needed = union of the chunks'
+      segments, loads = needed - loaded (ascending); a loaded, unneeded
+      segment bumps its counter and is evicted at the lag (counter reset);
+      a needed one resets its counter -- the selection diff of
+      planner.cpp:124-160 / cache.py:609-630;
+    * ranges in the planner's emission order (layer, sample, class-B kv head,
+      loaded segment; (layer, head, segment)s without host rows skipped,
+      planner.cpp:231-260), each landing at the running row count.
+
+    Returns ``ranges`` [(start, end)], ``dst`` landing rows, ``layer_ranges``
+    and ``layer_rows`` ([L+1] offsets)."""
+    B, L, H = P.B, P.L, P.H
+    loads = []
+    for b in range(B):
+        chunks = [int(c) for c in topk_rows[b] if int(c) >= 0]
+        if not chunks:
+            loads.append([])
+            continue
+        needed = set(s for c in chunks for s in P.c2s[b][c])
+        before = set(P.loaded[b])
+        cnt = P.counters[b]
+        for s in range(P.seg_count[b]):
+            if s in before:
+                if s in needed:
+                    cnt[s] = 0
+                else:
+                    cnt[s] += 1
+                    if cnt[s] >= P.evict_lag:
+                        P.loaded[b].discard(s)
+                        cnt[s] = 0
+        new = sorted(needed - before)
+        P.loaded[b] |= set(new)
+        loads.append(new)
+    ranges, dst, layer_ranges, layer_rows = [], [], [], []
+    row = 0
+    for l in range(L):
+        layer_ranges.append(len(ranges))
+        layer_rows.append(row)
+        for b in range(B):
+            for h in P.class_b[l]:
+                cs, ce = P.cpu_s[l][b * H + h], P.cpu_e[l][b * H + h]
+                for s in loads[b]:
+                    if cs[s] < 0:
+                        continue
+                    ranges.append((cs[s], ce[s]))
+                    dst.append(row)
+                    row += ce[s] - cs[s]
+    layer_ranges.append(len(ranges))
+    layer_rows.append(row)
+    return dict(ranges=ranges, dst=dst, layer_ranges=layer_ranges, layer_rows=layer_rows)
