@@ -1075,6 +1075,10 @@ class B200WnWCache(FlatVarlenCache):
                         "gpu_plus_cpu_retention": (aud + restore) / full if full > 0 else 1.0})
         return out
 
+    def get_snapshot_stats(self, step=-1):
+        """The snapshot under its public name (cache.py:1082-1084)."""
+        return self._snapshot_cache_stats(step=step)
+
     def _segment_host_rows(self):
         """Per sample, the host rows of each segment summed over every class-B
         (layer, kv head): what loading or evicting that segment moves."""
