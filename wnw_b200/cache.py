@@ -1079,6 +1079,19 @@ class B200WnWCache(FlatVarlenCache):
         """The snapshot under its public name (cache.py:1082-1084)."""
         return self._snapshot_cache_stats(step=step)
 
+    def get_compression_stats(self):
+        """The snapshot at step -1 (cache.py:1086-1088)."""
+        return self._snapshot_cache_stats(step=-1)
+
+    def collect_stats(self, interval=20):
+        """Collect InferenceStats every ``interval`` decode steps; 0 turns
+        collection off (cache.py:136-138)."""
+        self.stats.set_interval(interval)
+
+    def get_all_stats(self):
+        """Per-sample stats of the run (cache.py:140-142)."""
+        return self.stats.get_all_stats()
+
     def _segment_host_rows(self):
         """Per sample, the host rows of each segment summed over every class-B
         (layer, kv head): what loading or evicting that segment moves."""
