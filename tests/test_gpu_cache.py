@@ -101,7 +101,9 @@ def test_cache_reproduces_reference_trace(dev, golden_dir, tier, fetch, plan):
     from tests.stats_compare import normalise
     with open(os.path.join(golden_dir, "stats.json")) as f:
         want = json.load(f)["cache_trace"]
-    assert normalise(cache.stats.get_all_stats()) == normalise(want)
+    assert normalise(cache.get_all_stats()) == normalise(want)
+    assert cache.get_compression_stats()[0]["step"] == -1
+    assert cache.get_snapshot_stats(7)[1]["num_audio"] == want[1]["prefill"]["num_audio"]
 
 
 def test_cache_matches_oracle_in_bf16(dev):
