@@ -311,3 +311,28 @@ def test_planner_is_a_drop_in_for_the_reference_cpp_cache(golden_dir):
             assert [list(x) for x in a] == [list(x) for x in b], k
         else:
             assert np.array_equal(a, b), k
+
+
+@pytest.mark.parametrize("seed", range(30))
+def test_work_table_properties_random(seed):
+    """wnw_build_work_table on random capacities, splits and cluster sizes:
+    every segment gets exactly the clusters its capacity (+1 appended row)
+    needs, numbered 0..n-1 and consecutive; segments needing more clusters
+    come first (a stable sort by decreasing cluster count), so the ones with
+    a cross-cluster merge start earliest."""
+    from wnw_b200.kernels import build_work_table
+    rng = np.random.default_rng(700 + seed)
+    cap = rng.integers(0, 40000, int(rng.integers(1, 70))).astype(np.int32)
+    split = int(rng.choice([32, 64, 128, 256, 384, 512, 1024]))
+    cs = int(rng.choice([1, 2, 4, 8, 16]))
+    w = build_work_table(cap, split, cs).tolist()
+    need = [max(1, -(-(-(-(int(c) + 1) // split)) // cs)) for c in cap]
+    assert len(w) == sum(need)
+    segs_in_order = []
+    for seg, j in w:
+        if not segs_in_order or segs_in_order[-1] != seg:
+            segs_in_order.append(seg)
+    assert sorted(segs_in_order) == list(range(len(cap)))  # each segment's clusters are consecutive
+    for s in range(len(cap)):
+        assert [j for seg, j in w if seg == s] == list(range(need[s]))
+    assert segs_in_order == sorted(range(len(cap)), key=lambda s: -need[s])
