@@ -93,9 +93,12 @@ def _check_device_plan(P, bufs, evs, eve, L, S):
         assert r["moved_total"] == r["mov_off"][-1] and r["out_total"] == r["out_off"][-1]
 
 
-def test_gather_rows_matches_oracle():
+@pytest.mark.parametrize("threads", [1, 4, 16])
+def test_gather_rows_matches_oracle(threads):
+    """The host gather of the pinned-copy fetch mode (any thread count, empty
+    ranges included) copies the planned ranges in order, like the oracle."""
     from wnw_b200.planner import gather_rows
-    rng = np.random.default_rng(0)
+    rng = np.random.default_rng(threads)
     for rows, n_ranges, dtype in ((500, 40, np.float32), (70000, 300, np.float16)):
         ck = rng.standard_normal((rows, 64)).astype(dtype)
         cv = rng.standard_normal((rows, 64)).astype(dtype)
@@ -104,7 +107,7 @@ def test_gather_rows_matches_oracle():
         ek, ev = K.gather_restore(ck, cv, ranges)
         dk = np.zeros_like(ek)
         dv = np.zeros_like(ev)
-        gather_rows(ck, cv, ranges, dk, dv, n_threads=4)
+        gather_rows(ck, cv, ranges, dk, dv, n_threads=threads)
         assert np.array_equal(dk, ek) and np.array_equal(dv, ev)
 
 
