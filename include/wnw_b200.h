@@ -120,8 +120,10 @@ wnw_status wnw_decode_attn_step(const wnw_decode_attn_args* a, const void* q, co
  * and a->counters are ignored, every other field means what it means for
  * wnw_decode_attn, and a->err is required.  Larger requests return
  * WNW_ERR_CAPACITY.  Calls share the array: calls that overlap on the GPU race.
- * The first call on a device looks up the array's address (make it before any
- * stream capture); each call clears the counters it uses. */
+ * The first call in a CUDA context looks up the array's address there (make it
+ * before any stream capture), and a call made after the device's context
+ * changed (a cudaDeviceReset) looks it up again; each call clears the
+ * counters it uses. */
 #define WNW_NOALLOC_MAX_PARTIAL_FLOATS (1 << 20)
 #define WNW_NOALLOC_MAX_SEGS (1 << 16)
 wnw_status wnw_decode_attn_noalloc(const wnw_decode_attn_args* a, void* stream);
@@ -404,7 +406,7 @@ wnw_status wnw_h2d_async(void* dst_k, void* dst_v, const void* src_k, const void
  * memory and adds the partials in rank order (bit-identical y on every rank).
  * recv[p] / flags[p]: rank p's buffers as mapped in this process
  * (wnw_ipc_open; p == rank: this rank's own allocation), sized
- *   recv:  2 * world * batch * n_out fp32,
+ *   recv:  2 * world * recv_batch * n_out fp32,
  *   flags: world * wnw_oproj_allreduce_chunks(n_out) u32, zeroed once.
  * epoch: 1, 2, 3, ... per call, the same on every rank.  A peer whose flag
  * does not arrive within timeout_ns (0: 2 s) sets WNW_DEVERR_PEER_TIMEOUT in
@@ -413,6 +415,10 @@ wnw_status wnw_h2d_async(void* dst_k, void* dst_v, const void* src_k, const void
 typedef struct {
   int dtype;                            /* WNW_BF16 or WNW_F16 (x, W, y) */
   int batch, n_out, k_in;               /* B <= 8, N, K (K % 8 == 0)     */
+  int recv_batch;                       /* rows per rank and parity the recv
+                                           buffers were sized for (their
+                                           layout stride); batch > recv_batch
+                                           returns WNW_ERR_CAPACITY      */
   int rank, world;                      /* world <= WNW_TP_MAX_RANKS     */
   const void* x;                        /* [B, K]                        */
   const void* w;                        /* [N, K] row-major              */

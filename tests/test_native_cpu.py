@@ -182,6 +182,42 @@ def test_oproj_allreduce_rejects_bad_arguments():
     assert N.lib.wnw_oproj_allreduce(ctypes.byref(a), None) == 1
     assert N.lib.wnw_oproj_allreduce_chunks(3072) == 384
     assert N.lib.wnw_oproj_allreduce_chunks(0) == 0
+    # a batch above the receive buffers' rows would store past a peer's buffer:
+    # refused as a capacity error before anything is launched
+    buf = (ctypes.c_uint8 * 4096)()
+    base = (ctypes.addressof(buf) + 255) // 256 * 256
+    a.x, a.w, a.y, a.err = base, base + 256, base + 512, base + 768
+    a.recv[0], a.flags[0] = base + 1024, base + 2048
+    a.batch, a.recv_batch = 2, 1
+    assert N.lib.wnw_oproj_allreduce(ctypes.byref(a), None) == 3
+    assert b"exceeds the receive buffers" in N.lib.wnw_last_error()
+    a.recv_batch = 0
+    assert N.lib.wnw_oproj_allreduce(ctypes.byref(a), None) == 1
+
+
+def test_oproj_exchange_refuses_shapes_it_was_not_built_for():
+    """OprojAllReduce checks every call's tensors against the receive
+    buffers it was built for before it launches anything."""
+    import torch
+    from wnw_b200.tp import OprojAllReduce
+
+    ex = object.__new__(OprojAllReduce)  # the checks only, no IPC buffers
+    ex.dev, ex.batch, ex.n_out, ex.dtype = torch.device("cpu"), 2, 16, torch.bfloat16
+    x = torch.zeros(2, 32, dtype=torch.bfloat16)
+    w = torch.zeros(16, 32, dtype=torch.bfloat16)
+    ex._check_shapes(x, w, None)
+    with pytest.raises(ValueError, match="batch 3 not in 1..2"):
+        ex._check_shapes(torch.zeros(3, 32, dtype=torch.bfloat16), w, None)
+    with pytest.raises(ValueError, match="w must be"):
+        ex._check_shapes(x, torch.zeros(16, 24, dtype=torch.bfloat16), None)
+    with pytest.raises(ValueError, match="w must be"):
+        ex._check_shapes(x, torch.zeros(8, 32, dtype=torch.bfloat16), None)
+    with pytest.raises(TypeError, match="must be torch.bfloat16"):
+        ex._check_shapes(x.half(), w, None)
+    with pytest.raises(ValueError, match="contiguous"):
+        ex._check_shapes(torch.zeros(32, 2, dtype=torch.bfloat16).t(), w, None)
+    with pytest.raises(ValueError, match="y must be"):
+        ex._check_shapes(x, w, torch.zeros(2, 8, dtype=torch.bfloat16))
 
 
 def test_step_wait_times_out_instead_of_blocking():

@@ -33,3 +33,22 @@ def test_reference_session_drives_the_oracle_cache(golden_dir):
     assert cache.calls == ref["calls"]
     assert out.tolist() == ref["tokens"]
     assert [sorted(s) for s in cache.oracle.loaded_segments] == ref["loaded"]
+
+
+def test_non_fused_reference_session_is_refused():
+    """The reference session's default branch (WNW_FUSED_ATTN unset) would
+    attend with varlen_attn over packed K/V the B200 cache does not build:
+    the integration refuses such a module instead of running it wrong, and
+    switches it to the fused branch only when asked to."""
+    import pytest
+
+    from wnw_b200.integration import NonFusedSessionError, accept_in_reference_session
+    rsess, _ = reference_session_or_skip(ss)
+    try:
+        rsess._FUSED_ATTN = False
+        with pytest.raises(NonFusedSessionError, match="non-fused mode"):
+            accept_in_reference_session(rsess)
+        accept_in_reference_session(rsess, enable_fused=True)
+        assert rsess._FUSED_ATTN is True
+    finally:
+        rsess._FUSED_ATTN = True

@@ -3,10 +3,12 @@
 ``wnw_decode_attn_noalloc`` serves callers whose host owns all device memory
 (a serving engine with a fixed memory budget, a plugin host that passes in
 only its own buffers) and therefore cannot let this library call cudaMalloc:
-its scratch lives in a fixed device array inside the library.  This test
-calls it through the C ABI twice in a row and checks both results against the
-regular entry point (which takes caller-allocated scratch), with the same
-tolerance as the other bf16 attention tests, and checks the size limit.
+its scratch lives in a fixed device array inside the library.  These tests
+call it through the C ABI, twice in a row and interleaved with calls of other
+sizes and dtypes, and check every result against the regular entry point
+(which takes caller-allocated scratch).  Both run the same kernel on the same
+work table, so the outputs -- and, with scoring on, the class-A logits and
+softmax statistics -- must be bit-identical.  The size limits are checked too.
 
 The file name makes pytest collect it last; it needs no state from other tests.
 """
@@ -26,7 +28,10 @@ def dev():
     return torch.device("cuda:0")
 
 
-def _case(dev, dtype, lens, G=4, D=128, cluster=8, seed=0):
+def _case(dev, dtype, lens, G=4, D=128, split=None, cluster=8, score=False, seed=0):
+    """One layer's arguments.  With ``score``, segment 0 of every sample (two
+    kv heads per sample) is a class-A segment whose audio rows [4, len - 60)
+    get their logits and softmax statistics stored."""
     from wnw_b200 import kernels as Kx
     g = torch.Generator(device="cpu").manual_seed(seed)
     S = len(lens)
@@ -44,38 +49,84 @@ def _case(dev, dtype, lens, G=4, D=128, cluster=8, seed=0):
         len=torch.tensor(lens, dtype=torch.int32, device=dev),
         cap=torch.from_numpy(cap.astype(np.int32)).to(dev),
     )
-    split = Kx.split_rows(dtype, D)
+    split = split or Kx.split_rows(dtype, D)
     t["work"] = torch.from_numpy(Kx.build_work_table(cap, split, cluster)).to(dev)
     t["scratch"] = Kx.AttnScratch(dev, t["work"].shape[0], G, D, S)
     t["err"] = torch.zeros(1, dtype=torch.int32, device=dev)
+    sc = None
+    if score:
+        H = 2
+        B = S // H
+        a0 = [4] * B
+        a1 = [max(4, lens[b * H] - 60) for b in range(B)]
+        slot = [-1] * S
+        offs = []
+        o = 0
+        for b in range(B):
+            slot[b * H] = b
+            offs.append(o)
+            o += (a1[b] - a0[b]) * G
+        sc = dict(slot=torch.tensor(slot, dtype=torch.int32, device=dev),
+                  audio_start=torch.tensor(a0, dtype=torch.int32, device=dev),
+                  audio_end=torch.tensor(a1, dtype=torch.int32, device=dev),
+                  logits=torch.zeros(max(o, 1), dtype=torch.float32, device=dev),
+                  logits_off=torch.tensor(offs, dtype=torch.int64, device=dev),
+                  stats=torch.zeros(S * 2 * G, dtype=torch.float32, device=dev))
+    t["score"] = sc
     t["args"] = Kx.make_attn_args(dtype, S, G, D, t["ks"], t["vs"], t["base"], t["len"], t["work"], cluster,
-                                  D ** -0.5, t["scratch"], seg_cap=t["cap"], num_kv_heads=S)
+                                  D ** -0.5, t["scratch"], seg_cap=t["cap"], num_kv_heads=2 if score else S,
+                                  score=sc, split=split)
     return t
 
 
 def _call(name, t, out):
+    """Run one entry point; returns copies of (out, logits, stats)."""
     from wnw_b200 import native as N
     a = t["args"]
     a.q, a.new_k, a.new_v, a.out = t["q"].data_ptr(), t["nk"].data_ptr(), t["nv"].data_ptr(), out.data_ptr()
-    if name == "wnw_decode_attn_noalloc":
-        a.err = t["err"].data_ptr()
+    err = t["err"] if name == "wnw_decode_attn_noalloc" else t["scratch"].err
+    a.err = err.data_ptr()
+    sc = t["score"]
+    if sc is not None:
+        sc["logits"].fill_(float("nan"))
+        sc["stats"].fill_(float("nan"))
     st = getattr(N.lib, name)(ctypes.byref(a), torch.cuda.current_stream().cuda_stream)
     N.check(st, name)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0, name
+    return (out.clone(),) + ((sc["logits"].clone(), sc["stats"].clone()) if sc is not None else ())
 
 
-@pytest.mark.parametrize("dtype,lens", [(torch.bfloat16, [15100, 2300, 1, 700, 129, 4097, 2300, 60]),
-                                        (torch.float32, [3000, 64, 65, 1])])
-def test_noalloc_matches_regular_entry_point_twice(dev, dtype, lens):
-    t = _case(dev, dtype, lens)
-    ref = torch.empty_like(t["q"])
-    _call("wnw_decode_attn", t, ref)
-    tol = 2e-2 if dtype == torch.bfloat16 else 1e-5
-    for _ in range(2):  # the static scratch keeps the last call's contents
-        out = torch.full_like(t["q"], float("nan"))
-        _call("wnw_decode_attn_noalloc", t, out)
-        torch.cuda.synchronize()
-        assert int(t["err"].item()) == 0 and int(t["scratch"].err.item()) == 0
-        np.testing.assert_allclose(out.float().cpu().numpy(), ref.float().cpu().numpy(), atol=tol, rtol=tol)
+def _check(t):
+    """The regular entry point once, then the allocation-free one twice in a
+    row (the static scratch keeps the last call's contents): bit-identical."""
+    ref = _call("wnw_decode_attn", t, torch.empty_like(t["q"]))
+    for _ in range(2):
+        got = _call("wnw_decode_attn_noalloc", t, torch.full_like(t["q"], float("nan")))
+        for r, x in zip(ref, got):
+            assert torch.equal(r, x)
+
+
+@pytest.mark.parametrize("dtype,lens,split,cluster,score", [
+    # tensor-core kernel: 3 tiles of 128 rows per CTA, clusters of 4, class-A
+    # scoring on; 15,100-row segments span ten clusters (global merge)
+    (torch.bfloat16, [15100, 2300, 1, 700, 129, 4097, 2300, 60], 384, 4, True),
+    (torch.bfloat16, [15100, 2300, 1, 700, 129, 4097, 2300, 60], None, 8, False),
+    (torch.float32, [3000, 64, 65, 1], None, 8, False),
+])
+def test_noalloc_bit_identical_to_regular_entry_point(dev, dtype, lens, split, cluster, score):
+    _check(_case(dev, dtype, lens, split=split, cluster=cluster, score=score))
+
+
+def test_noalloc_clears_the_counters_each_call_uses(dev):
+    """Calls of growing and shrinking segment counts, alternating dtypes:
+    each starts from the counters the previous call left and must still
+    merge every segment's partials correctly."""
+    cases = [(torch.bfloat16, [9000, 17]), (torch.float32, [3000, 5, 1200, 2, 800, 64, 4000, 3]),
+             (torch.bfloat16, [5000] * 12 + [130, 7]), (torch.float32, [2500]),
+             (torch.bfloat16, [12000, 64, 3000, 1])]
+    for i, (dtype, lens) in enumerate(cases):
+        _check(_case(dev, dtype, lens, cluster=2 if dtype == torch.bfloat16 else 4, seed=i))
 
 
 def test_noalloc_rejects_oversized_requests(dev):

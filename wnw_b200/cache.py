@@ -675,6 +675,20 @@ class B200WnWCache(FlatVarlenCache):
         self.seq_lens[l] = self._step_seq[l]
         return self.k_store[l], self.v_store[l], self._seg_len[l], self._step_max[l]
 
+    def decode_after_attn(self, layer_idx, q):
+        """Not supported: this hook belongs to the reference session's
+        non-fused branch (session.py:90-112), which attends with torch's
+        varlen_attn over packed K/V and then scores here (cache.py:517-544).
+        This cache attends, appends and scores in fused_decode_attention
+        (the session's WNW_FUSED_ATTN=1 branch); reaching this hook means the
+        session just attended over the slot stores as if they were packed,
+        so it raises instead of returning a wrong result."""
+        from wnw_b200.integration import NonFusedSessionError
+        raise NonFusedSessionError(
+            "B200WnWCache supports the fused-attention session path only (WNW_FUSED_ATTN=1): "
+            "decode_after_attn was called, so the session attended with varlen_attn over K/V this cache "
+            "does not pack")
+
     def _plan_layer_checks(self):
         """Per-layer facts of the coming step, computed once for all layers:
         the rows each slot will hold before this step's token (after any

@@ -13,8 +13,12 @@
 // The array is one per device per process, shared by every call: calls that
 // overlap on the GPU (different streams, or concurrent host threads) race on
 // it.  Each call clears the counters it uses before the launch.  The device
-// address of the array is looked up once per device, on the first call made
-// with that device current; make that first call before any stream capture.
+// address of the array is looked up on the first call made in a CUDA context
+// (with that context current) and again whenever the current context of the
+// device changes (after a cudaDeviceReset, say); make the first call of a
+// context before any stream capture.
+#include <cuda.h>
+
 #include <mutex>
 
 #include "decode_attn.cuh"
@@ -29,19 +33,52 @@ constexpr int kMaxDevices = 64;
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kScratchBytes];
 
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+
 std::mutex g_mu;
 void* g_addr[kMaxDevices] = {};
+CUcontext g_ctx[kMaxDevices] = {};
 
-// device address of g_noalloc_scratch on the current device
+// the driver's cuCtxGetCurrent (this library links only the CUDA runtime)
+CtxGetCurrentFn ctx_get_current() {
+  static CtxGetCurrentFn fn = nullptr;
+  if (fn == nullptr) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &p, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<CtxGetCurrentFn>(p);
+  }
+  return fn;
+}
+
+// device address of g_noalloc_scratch in the current context of the current
+// device; an address taken in a context that has since been destroyed is
+// never reused
 wnw_status scratch_address(void** out) {
   int dev = 0;
   WNW_CUDA_TRY(cudaGetDevice(&dev));
   WNW_CHECK_ARG(dev >= 0 && dev < kMaxDevices, "device index %d out of range", dev);
+  const CtxGetCurrentFn get = ctx_get_current();
+  if (get == nullptr) {
+    set_error("cuCtxGetCurrent is not available from the driver");
+    return WNW_ERR_CUDA;
+  }
+  CUcontext ctx = nullptr;
+  if (get(&ctx) == CUDA_SUCCESS && ctx == nullptr) {
+    WNW_CUDA_TRY(cudaSetDevice(dev));  // makes the device's primary context current
+    get(&ctx);
+  }
+  if (ctx == nullptr) {
+    set_error("no current CUDA context on device %d", dev);
+    return WNW_ERR_CUDA;
+  }
   std::lock_guard<std::mutex> lk(g_mu);
-  if (g_addr[dev] == nullptr) {
+  if (g_addr[dev] == nullptr || g_ctx[dev] != ctx) {
     void* p = nullptr;
     WNW_CUDA_TRY(cudaGetSymbolAddress(&p, g_noalloc_scratch));
     g_addr[dev] = p;
+    g_ctx[dev] = ctx;
   }
   *out = g_addr[dev];
   return WNW_OK;

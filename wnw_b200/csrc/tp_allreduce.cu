@@ -46,13 +46,13 @@ struct TpParams {
   void* y;
   float* recv[WNW_TP_MAX_RANKS];
   uint32_t* flags[WNW_TP_MAX_RANKS];
-  int batch, n_out, k_in, rank, world, chunk;
+  int batch, recv_batch, n_out, k_in, rank, world, chunk;
   uint32_t epoch;
   uint64_t timeout_ns;
   int32_t* err;
 };
 
-// recv layout on every rank: [2 parities][world][batch][n_out] fp32
+// recv layout on every rank: [2 parities][world][recv_batch][n_out] fp32
 // flags layout on every rank: [world][n_chunks] u32 (last epoch received)
 template <typename T>
 __global__ void __launch_bounds__(kTpThreads) oproj_allreduce_kernel(const TpParams p) {
@@ -109,7 +109,7 @@ __global__ void __launch_bounds__(kTpThreads) oproj_allreduce_kernel(const TpPar
     const int dst = idx / (p.batch * m);
     const int rem = idx % (p.batch * m);
     const int b = rem / m, j = rem % m;
-    float* r = p.recv[dst] + ((int64_t(par) * p.world + p.rank) * p.batch + b) * p.n_out + c0 + j;
+    float* r = p.recv[dst] + ((int64_t(par) * p.world + p.rank) * p.recv_batch + b) * p.n_out + c0 + j;
     *r = part[b][j];
   }
   __syncthreads();
@@ -138,11 +138,11 @@ __global__ void __launch_bounds__(kTpThreads) oproj_allreduce_kernel(const TpPar
 
   // ---- rank-order sum of the chunk -> y
   T* y = static_cast<T*>(p.y);
-  const float* own = p.recv[p.rank] + int64_t(par) * p.world * p.batch * p.n_out;
+  const float* own = p.recv[p.rank] + int64_t(par) * p.world * p.recv_batch * p.n_out;
   for (int idx = threadIdx.x; idx < p.batch * m; idx += kTpThreads) {
     const int b = idx / m, j = idx % m;
     float s = 0.f;
-    for (int r = 0; r < p.world; ++r) s += __ldcg(own + (int64_t(r) * p.batch + b) * p.n_out + c0 + j);
+    for (int r = 0; r < p.world; ++r) s += __ldcg(own + (int64_t(r) * p.recv_batch + b) * p.n_out + c0 + j);
     y[int64_t(b) * p.n_out + c0 + j] = DT<T>::from_f(s_timeout ? 0.f : s);
   }
 }
@@ -164,6 +164,12 @@ extern "C" wnw_status wnw_oproj_allreduce(const wnw_oproj_allreduce_args* a, voi
                 "rank %d / world %d out of range (world <= %d)", a->rank, a->world, WNW_TP_MAX_RANKS);
   WNW_CHECK_ARG(a->batch >= 1 && a->batch <= kTpMaxBatch, "batch %d not in 1..%d", a->batch, kTpMaxBatch);
   WNW_CHECK_ARG(a->n_out > 0 && a->k_in > 0 && a->k_in % 8 == 0, "n_out > 0 and k_in a multiple of 8 required");
+  WNW_CHECK_ARG(a->recv_batch >= 1 && a->recv_batch <= kTpMaxBatch, "recv_batch %d not in 1..%d", a->recv_batch,
+                kTpMaxBatch);
+  if (a->batch > a->recv_batch) {
+    wnw::set_error("wnw_oproj_allreduce: batch %d exceeds the receive buffers' %d rows", a->batch, a->recv_batch);
+    return WNW_ERR_CAPACITY;
+  }
   WNW_CHECK_ARG(a->x && a->w && a->y && a->err, "null pointer argument");
   WNW_CHECK_ARG(aligned16(a->x) && aligned16(a->w), "x and w must be 16-byte aligned");
   WNW_CHECK_ARG(a->dtype == WNW_BF16 || a->dtype == WNW_F16, "dtype must be bf16 or f16");
@@ -179,6 +185,7 @@ extern "C" wnw_status wnw_oproj_allreduce(const wnw_oproj_allreduce_args* a, voi
     p.flags[r] = r < a->world ? a->flags[r] : nullptr;
   }
   p.batch = a->batch;
+  p.recv_batch = a->recv_batch;
   p.n_out = a->n_out;
   p.k_in = a->k_in;
   p.rank = a->rank;

@@ -62,7 +62,7 @@ TP_MAX_RANKS = 8
 class OprojAllReduceArgs(C.Structure):
     _fields_ = [
         ("dtype", C.c_int), ("batch", C.c_int), ("n_out", C.c_int), ("k_in", C.c_int),
-        ("rank", C.c_int), ("world", C.c_int), ("x", P), ("w", P), ("y", P),
+        ("recv_batch", C.c_int), ("rank", C.c_int), ("world", C.c_int), ("x", P), ("w", P), ("y", P),
         ("recv", P * TP_MAX_RANKS), ("flags", P * TP_MAX_RANKS), ("epoch", C.c_uint32),
         ("timeout_ns", C.c_uint64), ("err", P),
     ]

@@ -107,8 +107,9 @@ class OprojAllReduce:
     def __init__(self, dev, n_out, batch=1, dtype=torch.bfloat16, group=None, timeout_s=2.0):
         from wnw_b200 import native as N
         self.N = N
-        self.dev = torch.device(dev)
-        self._dev_index = self.dev.index if self.dev.index is not None else torch.cuda.current_device()
+        dev = torch.device(dev)
+        self._dev_index = dev.index if dev.index is not None else torch.cuda.current_device()
+        self.dev = torch.device("cuda", self._dev_index)
         dist = torch.distributed
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_available() and dist.is_initialized() else 1
@@ -139,7 +140,7 @@ class OprojAllReduce:
         self.err = torch.zeros(1, dtype=torch.int32, device=self.dev)
         a = self.args = N.OprojAllReduceArgs()
         a.dtype = N.dtype_code(dtype)
-        a.batch, a.n_out, a.rank, a.world = batch, n_out, self.rank, self.world
+        a.batch, a.recv_batch, a.n_out, a.rank, a.world = batch, batch, n_out, self.rank, self.world
         for p in range(self.world):
             a.recv[p] = bases[p]
             a.flags[p] = bases[p] + recv_bytes
@@ -148,7 +149,13 @@ class OprojAllReduce:
         self.epoch = 0
 
     def __call__(self, x, w, y=None, stream=None):
-        """x [B, K] (this rank's heads), w [N, K] -> y [B, N], summed over ranks."""
+        """x [B, K] (this rank's heads), w [N, K] -> y [B, N], summed over ranks.
+
+        B may not exceed the batch the receive buffers were built for (the
+        kernel stores B rows into every peer's buffer); x, w and y must be
+        contiguous device tensors of this exchange's dtype, with w [n_out,
+        K] and y [B, n_out]."""
+        self._check_shapes(x, w, y)
         a = self.args
         if y is None:
             y = torch.empty(x.shape[0], self.n_out, dtype=self.dtype, device=self.dev)
@@ -162,6 +169,23 @@ class OprojAllReduce:
         if st:
             self.N.check(st, "wnw_oproj_allreduce")
         return y
+
+    def _check_shapes(self, x, w, y):
+        if x.dim() != 2 or w.dim() != 2:
+            raise ValueError(f"x must be [B, K] and w [N, K]; got {tuple(x.shape)} and {tuple(w.shape)}")
+        if not 1 <= x.shape[0] <= self.batch:
+            raise ValueError(f"batch {x.shape[0]} not in 1..{self.batch} (the receive buffers' rows)")
+        if tuple(w.shape) != (self.n_out, x.shape[1]):
+            raise ValueError(f"w must be [{self.n_out}, {x.shape[1]}]; got {tuple(w.shape)}")
+        if x.dtype != self.dtype or w.dtype != self.dtype:
+            raise TypeError(f"x and w must be {self.dtype}; got {x.dtype} and {w.dtype}")
+        if not (x.is_contiguous() and w.is_contiguous()):
+            raise ValueError("x and w must be contiguous")
+        if x.device != self.dev or w.device != self.dev:
+            raise ValueError(f"x and w must live on {self.dev}")
+        if y is not None and (tuple(y.shape) != (x.shape[0], self.n_out) or y.dtype != self.dtype
+                              or not y.is_contiguous() or y.device != self.dev):
+            raise ValueError(f"y must be a contiguous [{x.shape[0]}, {self.n_out}] {self.dtype} tensor on {self.dev}")
 
     def check(self):
         """Raise if a peer's partials ever failed to arrive (host sync)."""
