@@ -277,10 +277,13 @@ def attention_replay(cache, qs, reps):
     launching stream; the 30-layer working set (~770 MB) exceeds L2, so each
     launch reads its layer from HBM."""
     from wnw_b200 import kernels as Kx
+    from wnw_b200 import native as N
     L = cache.num_layers
     st = torch.cuda.current_stream()
     outs = [torch.empty_like(q) for q in qs]
     args = [cache._attn_args[l][2] for l in range(L)]
+    for a in args:  # nothing between the launches writes a layer's rows or lengths
+        a.flags = N.ATTN_ROWS_READY
     for l in range(L):
         Kx.launch_attn(args[l], qs[l], None, None, outs[l], st.cuda_stream)
     e0 = torch.cuda.Event(enable_timing=True)

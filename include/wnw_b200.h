@@ -55,10 +55,21 @@ const char* wnw_last_error(void);
  * new_k/new_v are given, the step's new token is attended as row seg_len[s]
  * and written there (fused append; src/common/kv/kernels.py:7-73), so the
  * caller advances seg_len by one afterwards (wnw_advance_lengths).
- * Work is split into `split_rows`-row pieces grouped into clusters of
- * `cluster_size` CTAs; `work` lists (segment, cluster index within the
- * segment) pairs covering every cluster a segment may need
- * (wnw_build_work_table).  Outputs o[s, g, :] = softmax(q.K^T*scale).V in the
+ * Two launch layouts:
+ *  - tensor-core path (16-bit K/V, head_dim 64 or 128): `plan` (device) is
+ *    the layer's work plan from wnw_attn_plan -- every CTA attends one row
+ *    range of one segment, a segment's CTAs share one thread-block cluster of
+ *    `cluster_size` CTAs and merge through distributed shared memory, and a
+ *    segment too long for one cluster spans several whose partials a second
+ *    kernel (launched here, after the first) merges in order -- with
+ *    plan_ctas / cluster_size / plan_parts / plan_combine copied from its
+ *    wnw_attn_plan_info.  work / n_clusters / split_rows / counters are not
+ *    used.
+ *  - CUDA-core path (fp32, or head_dim 16 / 32): work is split into
+ *    `split_rows`-row pieces grouped into clusters of `cluster_size` CTAs;
+ *    `work` lists (segment, cluster index within the segment) pairs covering
+ *    every cluster a segment may need (wnw_build_work_table).
+ * Outputs o[s, g, :] = softmax(q.K^T*scale).V in the
  * q dtype with fp32 accumulation.  For segments with score_slot[s] >= 0 the
  * kernel also stores the base-2 logits of the audio rows
  * [audio_start[b], audio_end[b]) into logits + logits_off[slot] ([t][g]) and
@@ -81,7 +92,8 @@ typedef struct wnw_decode_attn_args {
   const int32_t* seg_cap;   /* [num_segs] slot capacity or NULL (unchecked)  */
   const int32_t* work;      /* [n_clusters][2] (segment, cluster-in-segment) */
   int n_clusters;
-  int cluster_size;         /* 1, 2, 4, 8 or 16 (16: non-portable size)      */
+  int cluster_size;         /* 1, 2, 4, 8 or 16 (16: non-portable size); the
+                               plan's cluster on the tensor-core path          */
   int split_rows;           /* rows per CTA; wnw_split_rows()                */
   void* out;                /* [num_segs, group, head_dim]                   */
   float scale;
@@ -92,13 +104,27 @@ typedef struct wnw_decode_attn_args {
   float* logits;                 /* base-2 logits, see above                 */
   const int64_t* logits_off;     /* [n_slots] element offset of each slot    */
   float* stats;                  /* [num_segs][2][group] or NULL             */
-  /* scratch: partials [n_clusters][group][head_dim + 2] fp32, counters
-     [num_segs] int32 (zero before first use; kernels leave them zero) */
+  /* scratch: partials [n_clusters, or plan_parts][group][head_dim + 2]
+     fp32, counters [num_segs] int32 (CUDA-core path; zero before first use,
+     kernels leave them zero) */
   float* partials;
   int32_t* counters;
   int32_t* err;                  /* device error word (WNW_DEVERR_* bits)    */
   int64_t store_rows;            /* rows of k_store / v_store (the TMA extent) */
+  /* tensor-core path: the layer's plan (see above) */
+  const int32_t* plan;           /* wnw_attn_plan output, on the device      */
+  int plan_ctas, plan_parts, plan_combine;
+  int flags;                     /* WNW_ATTN_ROWS_READY or 0                 */
 } wnw_decode_attn_args;
+
+/* flags: the caller guarantees that seg_len and the stored K/V rows
+ * [seg_base, seg_base + seg_len) are not being written by any kernel that may
+ * still run when this launch starts (they were final before the preceding
+ * kernels in the stream started; q, new_k and new_v may still come from
+ * them).  The tensor-core kernel then reads the lengths and starts streaming
+ * rows before it waits for the preceding kernel (programmatic dependent
+ * launch). */
+#define WNW_ATTN_ROWS_READY 1
 
 wnw_status wnw_decode_attn(const wnw_decode_attn_args* a, void* stream);
 
@@ -128,17 +154,45 @@ wnw_status wnw_decode_attn_step(const wnw_decode_attn_args* a, const void* q, co
 #define WNW_NOALLOC_MAX_SEGS (1 << 16)
 wnw_status wnw_decode_attn_noalloc(const wnw_decode_attn_args* a, void* stream);
 
-/* Smallest rows per CTA of wnw_decode_attn for a dtype / head_dim (16-bit
- * K/V with head_dim 64 or 128 take the tensor-core kernel, whose CTAs stream
- * any positive multiple of its 128-row tile: split_rows = 128 * tiles). */
+/* Rows per CTA of the CUDA-core decode attention for a dtype / head_dim;
+ * 0 for the tensor-core path (16-bit K/V with head_dim 64 or 128), which
+ * takes a plan instead (wnw_attn_plan). */
 int wnw_split_rows(int dtype, int head_dim);
+
+/* Work plan of the tensor-core decode attention for one layer (no reference
+ * counterpart: the reference's kernels take one CTA per segment).  Segment s
+ * may hold up to seg_cap[s] + 1 rows at a launch (its capacity plus the
+ * step's token), counted in 32-row units.  Every CTA takes about the same
+ * units -- an equal share of `sm_count` SMs, raised (to at most 1,536 rows)
+ * so the longest segment fits one cluster of `max_cluster` CTAs -- and a
+ * segment needing k CTAs gets k consecutive ranks of one cluster (clusters
+ * hold the smallest power of two >= the largest such k, at most
+ * max_cluster; short segments share clusters).  A segment needing more
+ * CTAs than a cluster holds takes whole clusters, each writing a partial
+ * that the combine kernel merges.  sm_count <= 0: the current device's;
+ * max_cluster <= 0: 16 when the device holds clusters of 16 of the kernel,
+ * else 8.  Layout of `plan` (int32):
+ *   [0..7]  ctas, cluster, parts, combine, 0, 0, 0, 0
+ *   [8 ..]  ctas x {segment (-1: idle rank), row_begin, row_end, meta}
+ *           meta = leader rank | ranks << 5 | writes a partial << 10 |
+ *                  partial slot << 11
+ *   then    parts x first row of the partial's range (padded to 4 ints)
+ *   then    combine x {segment, first partial, partials, 0}
+ * Writes info (sizes) always and the plan when max_ints >= info->ints; with
+ * plan == NULL and max_ints == 0 it only sizes; otherwise a plan too small
+ * returns WNW_ERR_CAPACITY. */
+typedef struct {
+  int ctas, cluster, parts, combine;
+  int64_t ints;
+} wnw_attn_plan_info;
+wnw_status wnw_attn_plan(const int32_t* seg_cap, int num_segs, int sm_count, int max_cluster, int32_t* plan,
+                         int64_t max_ints, wnw_attn_plan_info* info);
 
 /* Launch shape for one layer (no reference counterpart: the reference's
  * kernels take one CTA per segment).  From the per-segment row capacities,
- * picks split_rows (a multiple of wnw_split_rows) and cluster_size so the
- * layer's CTAs fit the device's resident clusters in as few waves and tiles
- * per SM as possible (cudaOccupancyMaxActiveClusters on the current device;
- * the CUDA-core kernel keeps its fixed split and needs no device). */
+ * gives the CUDA-core kernel's split_rows and the cluster size (the
+ * smallest power of two, up to 8, covering the longest segment's splits);
+ * the tensor-core path takes a plan instead (WNW_ERR_INVALID here). */
 wnw_status wnw_attn_launch_shape(int dtype, int head_dim, const int32_t* seg_cap, int num_segs,
                                  int* split_rows, int* cluster_size);
 

@@ -75,28 +75,34 @@ CASES = [
 
 @pytest.mark.parametrize("dtype,D,G,cs,lens", CASES)
 @pytest.mark.parametrize("append", [True, False])
-@pytest.mark.parametrize("tiles", [1, 3])
-def test_decode_attention_matches_oracle(dev, dtype, D, G, cs, lens, append, tiles):
-    """``tiles`` > 1: each CTA of the tensor-core kernel streams that many
-    128-row tiles of its segment (two-stage pipeline, online softmax)."""
+@pytest.mark.parametrize("sms,ready", [(None, False), ((4, 4), True), ((600, 2), True)])
+def test_decode_attention_matches_oracle(dev, dtype, D, G, cs, lens, append, sms, ready):
+    """Tensor-core path: ``sms`` = (SM count, largest cluster) the plan is cut
+    for -- the device's own (the library default); 4 SMs with clusters of 4
+    (long per-CTA shares, segments spanning several clusters, merged by the
+    combine kernel); 600 SMs with clusters of 2 (32-row shares, dozens of
+    cluster partials per long segment); ``ready`` lets the kernel read
+    lengths and rows before its dependency wait.  The CUDA-core path (fp32,
+    head_dim 16 / 32) takes its cluster table ``cs``."""
     from wnw_b200 import kernels as Kx
     S = len(lens)
-    if tiles > 1 and (dtype == torch.float32 or D not in (64, 128)):
-        pytest.skip("multi-tile CTAs are a tensor-core kernel mode")
-    split = Kx.split_rows(dtype, D) * tiles
+    plan = Kx.uses_plan(dtype, D)
+    if not plan and sms is not None:
+        pytest.skip("the SM count of a plan is a tensor-core kernel mode")
     ks, vs, base, cap = _slots(lens, 40, D, dtype, dev, seed=sum(lens) + G)
     g = torch.Generator(device="cpu").manual_seed(7)
     q = torch.randn(S, G, D, generator=g).to(dtype).to(dev)
     nk = torch.randn(S, D, generator=g).to(dtype).to(dev) if append else None
     nv = torch.randn(S, D, generator=g).to(dtype).to(dev) if append else None
-    work = torch.from_numpy(Kx.build_work_table(cap, split, cs)).to(dev)
-    scratch = Kx.AttnScratch(dev, work.shape[0], G, D, S)
+    work = Kx.AttnWork(dtype, D, cap, dev, sm_count=sms[0] if sms else None, max_cluster=sms[1] if sms else None,
+                       split=None if plan else Kx.split_rows(dtype, D), cluster_size=None if plan else cs)
+    scratch = Kx.AttnScratch(dev, work.slots, G, D, S)
     seg_len = torch.tensor(lens, dtype=torch.int32, device=dev)
     before_k = ks.clone()
     scale = D ** -0.5
-    out = Kx.decode_attention(q, ks, vs, torch.from_numpy(base).to(dev), seg_len, work, cs, scale, scratch,
+    out = Kx.decode_attention(q, ks, vs, torch.from_numpy(base).to(dev), seg_len, work, scale, scratch,
                               new_k=nk, new_v=nv, seg_cap=torch.from_numpy(cap.astype(np.int32)).to(dev),
-                              split=split)
+                              flags=1 if ready else 0)
     torch.cuda.synchronize()
     assert int(scratch.err.item()) == 0
     assert int(scratch.counters.abs().sum()) == 0  # left zero for the next launch
@@ -119,23 +125,23 @@ def test_decode_attention_matches_oracle(dev, dtype, D, G, cs, lens, append, til
 
 
 @pytest.mark.parametrize("lens", [[15100, 15100, 2300, 2300, 2300, 2300, 2300, 2300], [120000, 4000, 3],
-                                  [1, 2, 3, 300], [5000] * 64])
-def test_library_launch_shape_matches_oracle(dev, lens):
-    """The shape wnw_attn_launch_shape picks (tiles per CTA, cluster size) is
-    valid and its output matches the oracle."""
+                                  [1, 2, 3, 300], [5000] * 64, [700] * 2048])
+def test_library_plan_matches_oracle(dev, lens):
+    """The library's default plan (this device's SMs and clusters) is valid
+    and its output matches the oracle -- including 2,048 segments (batch 256
+    x 8 kv heads, where the reference's row-gather kernels break down)."""
     from wnw_b200 import kernels as Kx
     dtype, D, G = torch.bfloat16, 128, 4
     S = len(lens)
     ks, vs, base, cap = _slots(lens, 64, D, dtype, dev, seed=len(lens))
-    split, cs = Kx.attn_launch_shape(dtype, D, cap)
-    assert split % 128 == 0 and split >= 128 and cs in (1, 2, 4, 8)
+    work = Kx.AttnWork(dtype, D, cap, dev)
+    assert work.plan and work.ctas >= S and work.ctas % work.cluster_size == 0
     g = torch.Generator(device="cpu").manual_seed(5)
     q = torch.randn(S, G, D, generator=g).to(dtype).to(dev)
-    work = torch.from_numpy(Kx.build_work_table(cap, split, cs)).to(dev)
-    scratch = Kx.AttnScratch(dev, work.shape[0], G, D, S)
+    scratch = Kx.AttnScratch(dev, work.slots, G, D, S)
     out = Kx.decode_attention(q, ks, vs, torch.from_numpy(base).to(dev),
-                              torch.tensor(lens, dtype=torch.int32, device=dev), work, cs, D ** -0.5, scratch,
-                              seg_cap=torch.from_numpy(cap.astype(np.int32)).to(dev), split=split)
+                              torch.tensor(lens, dtype=torch.int32, device=dev), work, D ** -0.5, scratch,
+                              seg_cap=torch.from_numpy(cap.astype(np.int32)).to(dev))
     torch.cuda.synchronize()
     assert int(scratch.err.item()) == 0
     pk, pv = _packed(ks, base, lens), _packed(vs, base, lens)
@@ -143,8 +149,8 @@ def test_library_launch_shape_matches_oracle(dev, lens):
     np.testing.assert_allclose(out.float().cpu().numpy(), ref, atol=TOL[dtype], rtol=TOL[dtype])
 
 
-@pytest.mark.parametrize("dtype,tiles", [(torch.float32, 1), (torch.bfloat16, 1), (torch.bfloat16, 4)])
-def test_scoring_logits_and_finalize_match_oracle(dev, dtype, tiles):
+@pytest.mark.parametrize("dtype,sms", [(torch.float32, None), (torch.bfloat16, None), (torch.bfloat16, (6, 2))])
+def test_scoring_logits_and_finalize_match_oracle(dev, dtype, sms):
     """Fused class-A logits + stats, then wnw_score_finalize, equal the
     reference's per-token probabilities summed over kv heads and q heads
     (bf16: the same inputs as fp32 values, logits accumulated in fp32)."""
@@ -155,9 +161,10 @@ def test_scoring_logits_and_finalize_match_oracle(dev, dtype, tiles):
     ks, vs, base, cap = _slots(lens, 16, D, dtype, dev, seed=3)
     g = torch.Generator(device="cpu").manual_seed(11)
     q = torch.randn(B * H, G, D, generator=g).to(dtype).to(dev)
-    split = Kx.split_rows(dtype, D) * tiles
-    work = torch.from_numpy(Kx.build_work_table(cap, split, 8)).to(dev)
-    scratch = Kx.AttnScratch(dev, work.shape[0], G, D, B * H)
+    plan = Kx.uses_plan(dtype, D)
+    work = Kx.AttnWork(dtype, D, cap, dev, sm_count=sms[0] if sms else None, max_cluster=sms[1] if sms else None,
+                       split=None if plan else Kx.split_rows(dtype, D), cluster_size=None if plan else 8)
+    scratch = Kx.AttnScratch(dev, work.slots, G, D, B * H)
     ca_kv = [0, 2]                       # class-A kv heads (all q heads of each)
     slot = np.full(B * H, -1, np.int32)
     offs, t_logit, t_stat, t_mask, t_off = [], [], [], [], [0]
@@ -177,7 +184,7 @@ def test_scoring_logits_and_finalize_match_oracle(dev, dtype, tiles):
                  audio_end=torch.tensor(a_e, dtype=torch.int32, device=dev), logits=logits,
                  logits_off=torch.tensor(offs, dtype=torch.int64, device=dev), stats=stats)
     Kx.decode_attention(q, ks, vs, torch.from_numpy(base).to(dev), torch.tensor(lens, dtype=torch.int32, device=dev),
-                        work, 8, D ** -0.5, scratch, num_kv_heads=H, score=score, split=split)
+                        work, D ** -0.5, scratch, num_kv_heads=H, score=score)
     n_audio = [e - s for s, e in zip(a_s, a_e)]
     score_off = torch.tensor([0, n_audio[0], sum(n_audio)], dtype=torch.int32, device=dev)
     acc = torch.full((sum(n_audio),), -1.0, device=dev)

@@ -24,7 +24,7 @@ def test_library_exports_every_header_symbol():
         assert hasattr(N.lib, name), name
     assert declared == set(N.EXPORTS)
     assert N.lib.wnw_abi_version() == 1
-    assert N.lib.wnw_split_rows(N.BF16, 128) == 128 and N.lib.wnw_split_rows(N.F32, 128) == 64
+    assert N.lib.wnw_split_rows(N.BF16, 128) == 0 and N.lib.wnw_split_rows(N.F32, 128) == 64
 
 
 def test_status_and_error_reporting():
@@ -136,6 +136,174 @@ def test_launch_shape_cuda_core_kernel():
     assert attn_launch_shape(torch.float32, 128, [100000, 5]) == (base, 8)
     with pytest.raises(N.WnwError, match="negative capacity"):
         attn_launch_shape(torch.float32, 128, [-1])
+    with pytest.raises(N.WnwError, match="launched from a plan"):
+        attn_launch_shape(torch.bfloat16, 128, [100])
+
+
+def _parse_plan(plan):
+    ctas, C, parts, ncomb = (int(x) for x in plan[:4])
+    cta = plan[8:8 + 4 * ctas].reshape(-1, 4)
+    at = 8 + 4 * ctas
+    part_r0 = plan[at:at + parts]
+    at += (parts + 3) // 4 * 4
+    comb = plan[at:at + 4 * ncomb].reshape(-1, 4)
+    assert plan.size == at + 4 * ncomb
+    return C, cta, part_r0, comb
+
+
+def _meta(m):
+    m = int(m) & 0xFFFFFFFF
+    return m & 31, (m >> 5) & 31, (m >> 10) & 1, m >> 11
+
+
+@pytest.mark.parametrize("seed", range(40))
+def test_attn_plan_properties_random(seed):
+    """wnw_attn_plan on random capacities, SM counts and cluster limits:
+    every segment's rows (capacity + the step's token, in 32-row units) are
+    covered exactly once, by consecutive ranks of one cluster that name their
+    leader and count -- or, for a segment longer than a cluster's CTAs take,
+    by whole clusters in order, each with a partial slot and its first row,
+    listed once in the combine table; the cluster size is a power of two no
+    larger than allowed and divides the CTA count."""
+    from wnw_b200.kernels import attn_plan
+    rng = np.random.default_rng(900 + seed)
+    nseg = int(rng.choice([1, 3, 8, 64, 700, 2048]))
+    hi = int(rng.choice([40, 3000, 130000]))
+    cap = rng.integers(0, hi, nseg).astype(np.int32)
+    sm, mc = int(rng.choice([1, 7, 148, 600])), int(rng.choice([1, 2, 4, 8, 16]))
+    plan, info = attn_plan(cap, sm, mc)
+    C, cta, part_r0, comb = _parse_plan(plan)
+    assert C == info["cluster"] and C <= mc and C & (C - 1) == 0
+    assert len(cta) == info["ctas"] and len(cta) % C == 0
+    assert len(part_r0) == info["parts"] and len(comb) == info["combine"]
+    units = (cap.astype(np.int64) + 1 + 31) // 32
+    covered = {s: [] for s in range(nseg)}
+    parts_of = {}
+    for c in range(0, len(cta), C):
+        cl = cta[c:c + C]
+        r = 0
+        while r < C:
+            seg = int(cl[r, 0])
+            if seg < 0:
+                r += 1
+                continue
+            leader, n, to_part, part = _meta(cl[r, 3])
+            assert leader == r and 1 <= n <= C - r
+            for i in range(n):  # the segment's ranks: consecutive, same leader and count
+                assert int(cl[r + i, 0]) == seg and _meta(cl[r + i, 3]) == (leader, n, to_part, part)
+                covered[seg].append((int(cl[r + i, 1]), int(cl[r + i, 2])))
+            if to_part:
+                assert n == C and part < len(part_r0) and part_r0[part] == cl[r, 1]
+                parts_of.setdefault(seg, []).append(part)
+            r += n
+    for s in range(nseg):
+        rngs = sorted(covered[s])
+        assert rngs[0][0] == 0 and rngs[-1][1] == units[s] * 32
+        assert all(a[1] == b[0] for a, b in zip(rngs, rngs[1:]))
+        assert all(r0 % 32 == 0 and r1 >= r0 for r0, r1 in rngs)
+    assert sorted(parts_of) == sorted(int(e[0]) for e in comb)
+    for seg, first, n, _ in comb:
+        assert parts_of[int(seg)] == list(range(int(first), int(first) + int(n)))
+        assert list(part_r0[first:first + n]) == sorted(part_r0[first:first + n]) and part_r0[first] == 0
+
+
+def test_attn_plan_config2_layer_fits_one_cluster_per_segment():
+    """The config-2 layer (two 15,100-row class-A and six 2,300-row class-B
+    segments) on a 148-SM device with clusters of 16: every segment merges
+    inside its cluster (no partials, no combine kernel)."""
+    from wnw_b200.kernels import attn_plan
+    cap = np.array([15100 + 40] * 2 + [2300 + 40] * 6, np.int32)
+    plan, info = attn_plan(cap, 148, 16)
+    assert info["cluster"] == 16 and info["parts"] == 0 and info["combine"] == 0
+    C, cta, _, _ = _parse_plan(plan)
+    for seg in range(8):
+        ranks = cta[cta[:, 0] == seg]
+        assert len(ranks) == (16 if seg < 2 else 3)
+
+
+def test_attn_plan_checks_arguments():
+    from wnw_b200.kernels import attn_plan
+    with pytest.raises(N.WnwError, match="out of range"):
+        attn_plan([5, -1], 4, 4)
+    with pytest.raises(N.WnwError, match="max_cluster"):
+        attn_plan([5], 4, 17)
+    info = N.AttnPlanInfo()
+    cap = np.array([100, 200], np.int32)
+    N.call("wnw_attn_plan", N.ptr(cap), 2, 4, 4, None, 0, ctypes.byref(info))
+    small = np.zeros(int(info.ints) - 1, np.int32)
+    st = N.lib.wnw_attn_plan(N.ptr(cap), 2, 4, 4, N.ptr(small), small.size, ctypes.byref(info))
+    assert st == 3 and b"capacity" in N.lib.wnw_last_error()
+
+
+@pytest.mark.parametrize("seed", range(12))
+def test_attn_plan_semantics_restate_attention(seed):
+    """The kernels' use of a plan, restated in numpy: every CTA attends rows
+    [row_begin, min(row_end, total)) of its segment; the leader of a
+    segment's ranks merges their (max, sum, o) states -- into the output, or,
+    for a segment spanning clusters, into the cluster's partial unless the
+    cluster starts at or past the segment's rows; the combine step merges a
+    segment's partials whose ranges start below its row count (a prefix; the
+    first always counts).  On random lengths at or below the capacities, with
+    and without the step's token, the result equals the oracle's attention."""
+    from wnw_b200.kernels import attn_plan
+    rng = np.random.default_rng(40 + seed)
+    S, G, D = int(rng.integers(1, 9)), int(rng.integers(1, 5)), 16
+    cap = rng.integers(0, 700, S).astype(np.int32)
+    append = bool(rng.integers(0, 2))
+    lens = np.array([rng.integers(0, c + 1) if c else 0 for c in cap], np.int64)
+    if append:
+        lens = np.minimum(lens, cap)  # the token fits: len + 1 <= cap + 1
+    total = lens + int(append)
+    plan, _ = attn_plan(cap, int(rng.choice([1, 3, 9, 40])), int(rng.choice([1, 2, 4])))
+    C, cta, part_r0, comb = _parse_plan(plan)
+    q = rng.standard_normal((S, G, D))
+    kv = [(rng.standard_normal((max(int(t), 1), D)), rng.standard_normal((max(int(t), 1), D))) for t in total]
+
+    def attend(seg, r0, r1):
+        rows = max(0, min(r1, int(total[seg])) - r0)
+        k, v = kv[seg][0][r0:r0 + rows], kv[seg][1][r0:r0 + rows]
+        x = q[seg] @ k.T / np.sqrt(D)
+        m = x.max(axis=1) if rows else np.full(G, -np.inf)
+        p = np.exp(x - m[:, None]) if rows else np.zeros((G, 0))
+        return m, p.sum(axis=1), p @ v
+
+    def merge(states):
+        ms = np.stack([s[0] for s in states])
+        mx = ms.max(axis=0)
+        w = np.where(np.isinf(ms), 0.0, np.exp(ms - np.where(np.isinf(mx), 0.0, mx)))
+        return mx, sum(w[j] * states[j][1] for j in range(len(states))), \
+            sum(w[j][:, None] * states[j][2] for j in range(len(states)))
+
+    out = np.full((S, G, D), np.nan)
+    parts = {}
+    for c in range(0, len(cta), C):
+        cl = cta[c:c + C]
+        for r in range(C):
+            seg = int(cl[r, 0])
+            if seg < 0:
+                continue
+            leader, n, to_part, part = _meta(cl[r, 3])
+            if r != leader:
+                continue
+            mx, l, o = merge([attend(seg, int(cl[r + i, 1]), int(cl[r + i, 2])) for i in range(n)])
+            if not to_part:
+                out[seg] = np.where(l[:, None] > 0, o / np.where(l > 0, l, 1)[:, None], 0.0)
+            elif not (cl[r, 1] >= total[seg] and cl[r, 1] > 0):
+                parts[part] = (mx, l, o)
+    for seg, first, n, _ in comb:
+        act = 1
+        while act < n and part_r0[first + act] < total[seg]:
+            act += 1
+        mx, l, o = merge([parts[first + j] for j in range(act)])
+        out[seg] = np.where(l[:, None] > 0, o / np.where(l > 0, l, 1)[:, None], 0.0)
+    cu = np.concatenate([[0], np.cumsum(total)])
+    pk = np.concatenate([kv[s][0][:total[s]] for s in range(S)]) if total.sum() else np.zeros((0, D))
+    pv = np.concatenate([kv[s][1][:total[s]] for s in range(S)]) if total.sum() else np.zeros((0, D))
+    ref, _, _ = K.decode_attn(q.astype(np.float32), pk.astype(np.float32), pv.astype(np.float32), cu, D ** -0.5)
+    nz = total > 0
+    assert not np.isnan(out).any()
+    np.testing.assert_allclose(out[nz], ref[nz], atol=1e-5, rtol=1e-5)
+    assert np.all(out[~nz] == 0)
 
 
 def test_issue_fetch_reports_sizes_without_issuing(golden_dir):

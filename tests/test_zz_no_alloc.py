@@ -6,8 +6,8 @@ only its own buffers) and therefore cannot let this library call cudaMalloc:
 its scratch lives in a fixed device array inside the library.  These tests
 call it through the C ABI, twice in a row and interleaved with calls of other
 sizes and dtypes, and check every result against the regular entry point
-(which takes caller-allocated scratch).  Both run the same kernel on the same
-work table, so the outputs -- and, with scoring on, the class-A logits and
+(which takes caller-allocated scratch).  Both run the same kernels on the same
+work layout, so the outputs -- and, with scoring on, the class-A logits and
 softmax statistics -- must be bit-identical.  The size limits are checked too.
 
 The file name makes pytest collect it last; it needs no state from other tests.
@@ -28,7 +28,7 @@ def dev():
     return torch.device("cuda:0")
 
 
-def _case(dev, dtype, lens, G=4, D=128, split=None, cluster=8, score=False, seed=0):
+def _case(dev, dtype, lens, G=4, D=128, sms=None, cluster=8, score=False, seed=0):
     """One layer's arguments.  With ``score``, segment 0 of every sample (two
     kv heads per sample) is a class-A segment whose audio rows [4, len - 60)
     get their logits and softmax statistics stored."""
@@ -49,9 +49,11 @@ def _case(dev, dtype, lens, G=4, D=128, split=None, cluster=8, score=False, seed
         len=torch.tensor(lens, dtype=torch.int32, device=dev),
         cap=torch.from_numpy(cap.astype(np.int32)).to(dev),
     )
-    split = split or Kx.split_rows(dtype, D)
-    t["work"] = torch.from_numpy(Kx.build_work_table(cap, split, cluster)).to(dev)
-    t["scratch"] = Kx.AttnScratch(dev, t["work"].shape[0], G, D, S)
+    plan = Kx.uses_plan(dtype, D)
+    t["work"] = Kx.AttnWork(dtype, D, cap, dev, sm_count=sms[0] if sms else None,
+                            max_cluster=sms[1] if sms else None, split=None if plan else Kx.split_rows(dtype, D),
+                            cluster_size=None if plan else cluster)
+    t["scratch"] = Kx.AttnScratch(dev, t["work"].slots, G, D, S)
     t["err"] = torch.zeros(1, dtype=torch.int32, device=dev)
     sc = None
     if score:
@@ -73,9 +75,9 @@ def _case(dev, dtype, lens, G=4, D=128, split=None, cluster=8, score=False, seed
                   logits_off=torch.tensor(offs, dtype=torch.int64, device=dev),
                   stats=torch.zeros(S * 2 * G, dtype=torch.float32, device=dev))
     t["score"] = sc
-    t["args"] = Kx.make_attn_args(dtype, S, G, D, t["ks"], t["vs"], t["base"], t["len"], t["work"], cluster,
+    t["args"] = Kx.make_attn_args(dtype, S, G, D, t["ks"], t["vs"], t["base"], t["len"], t["work"],
                                   D ** -0.5, t["scratch"], seg_cap=t["cap"], num_kv_heads=2 if score else S,
-                                  score=sc, split=split)
+                                  score=sc)
     return t
 
 
@@ -107,26 +109,31 @@ def _check(t):
             assert torch.equal(r, x)
 
 
-@pytest.mark.parametrize("dtype,lens,split,cluster,score", [
-    # tensor-core kernel: 3 tiles of 128 rows per CTA, clusters of 4, class-A
-    # scoring on; 15,100-row segments span ten clusters (global merge)
-    (torch.bfloat16, [15100, 2300, 1, 700, 129, 4097, 2300, 60], 384, 4, True),
-    (torch.bfloat16, [15100, 2300, 1, 700, 129, 4097, 2300, 60], None, 8, False),
+@pytest.mark.parametrize("dtype,lens,sms,cluster,score", [
+    # tensor-core kernel, class-A scoring on: the device's plan (a cluster
+    # per segment, merged in distributed shared memory); and a plan for 6 SMs
+    # in clusters of 2, where long segments span several clusters whose
+    # partials go through the scratch and the combine kernel
+    (torch.bfloat16, [15100, 2300, 1, 700, 129, 4097, 2300, 60], None, 8, True),
+    (torch.bfloat16, [15100, 2300, 1, 700, 129, 4097, 2300, 60], (6, 2), 8, True),
+    # CUDA-core kernel: clusters of 8 and the global counter merge
     (torch.float32, [3000, 64, 65, 1], None, 8, False),
 ])
-def test_noalloc_bit_identical_to_regular_entry_point(dev, dtype, lens, split, cluster, score):
-    _check(_case(dev, dtype, lens, split=split, cluster=cluster, score=score))
+def test_noalloc_bit_identical_to_regular_entry_point(dev, dtype, lens, sms, cluster, score):
+    _check(_case(dev, dtype, lens, sms=sms, cluster=cluster, score=score))
 
 
 def test_noalloc_clears_the_counters_each_call_uses(dev):
-    """Calls of growing and shrinking segment counts, alternating dtypes:
-    each starts from the counters the previous call left and must still
-    merge every segment's partials correctly."""
+    """Calls of growing and shrinking segment counts, alternating dtypes
+    (bf16 plans whose long segments go through cluster partials, fp32
+    cluster tables with arrival counters): each starts from the scratch the
+    previous call left and must still merge every segment's partials
+    correctly."""
     cases = [(torch.bfloat16, [9000, 17]), (torch.float32, [3000, 5, 1200, 2, 800, 64, 4000, 3]),
              (torch.bfloat16, [5000] * 12 + [130, 7]), (torch.float32, [2500]),
              (torch.bfloat16, [12000, 64, 3000, 1])]
     for i, (dtype, lens) in enumerate(cases):
-        _check(_case(dev, dtype, lens, cluster=2 if dtype == torch.bfloat16 else 4, seed=i))
+        _check(_case(dev, dtype, lens, sms=(5, 2) if dtype == torch.bfloat16 else None, cluster=4, seed=i))
 
 
 def test_noalloc_rejects_oversized_requests(dev):
@@ -134,10 +141,11 @@ def test_noalloc_rejects_oversized_requests(dev):
     t = _case(dev, torch.bfloat16, [100, 100])
     a = t["args"]
     a.q, a.out, a.err = t["q"].data_ptr(), t["q"].data_ptr(), t["err"].data_ptr()
-    a.n_clusters = (1 << 20) // (4 * 130) + 1  # one cluster more than the static partial buffer holds
+    parts = a.plan_parts
+    a.plan_parts = (1 << 20) // (4 * 130) + 1  # one partial more than the static partial buffer holds
     st = N.lib.wnw_decode_attn_noalloc(ctypes.byref(a), torch.cuda.current_stream().cuda_stream)
     assert st == 3 and b"static scratch holds" in N.lib.wnw_last_error()
-    a.n_clusters = t["work"].shape[0]
+    a.plan_parts = parts
     a.num_segs = (1 << 16) + 1
     st = N.lib.wnw_decode_attn_noalloc(ctypes.byref(a), torch.cuda.current_stream().cuda_stream)
     assert st == 3 and b"counters for" in N.lib.wnw_last_error()

@@ -210,6 +210,7 @@ class B200WnWCache(FlatVarlenCache):
         self.restore_meta = None
         self._pending = False
         self._decode_step = 0
+        self._rows_ready = [False] * self.num_layers
         self.prefilled = False
 
     # ------------------------------------------------------------ prefill
@@ -491,15 +492,13 @@ class B200WnWCache(FlatVarlenCache):
         self._seg_base = torch.from_numpy(self._base_host).to(dev)
         self._seg_cap = torch.from_numpy(self._cap_host.astype(np.int32)).to(dev)
         max_rows = int((self._len_host + self.max_decode_tokens).max()) if S else 0
-        self._work, self._shape = [], []
+        self._work = []
         n_max = 0
         for l in range(L):
-            # rows per CTA and cluster size fitted to this layer's capacities
-            split, cs = Kx.attn_launch_shape(self.dtype, D, self._cap_host[l])
-            self._shape.append((split, cs))
-            w = Kx.build_work_table(self._cap_host[l], split, cs)
-            self._work.append(torch.from_numpy(w).to(dev))
-            n_max = max(n_max, w.shape[0])
+            # the layer's launch layout, fitted to its capacities
+            w = Kx.AttnWork(self.dtype, D, self._cap_host[l], dev)
+            self._work.append(w)
+            n_max = max(n_max, w.slots)
         if getattr(self, "_scratch", None) is None or not self._scratch.fits(n_max, G, D, S):
             self._scratch = Kx.AttnScratch(dev, n_max, G, D, S)
             self._tail_args = None  # the step tail copies the scratch's error word
@@ -654,10 +653,16 @@ class B200WnWCache(FlatVarlenCache):
         Returns (k_store, v_store, seg_len, max_seqlen_k); seg_len counts the
         rows stored before this step's token (cache.py:487-515 contract)."""
         l = layer_idx
+        # rows and lengths of layer l stay as the last step left them (the
+        # host waited for that step's end) unless this step grows or rebuilds
+        # its slots
+        self._rows_ready[l] = self._decode_step > 0
         if self._grow_flags[l]:
             self._grow(l)
             self._grow_flags[l] = False
+            self._rows_ready[l] = False
         if self._pending and self._layer_chg[l]:
+            self._rows_ready[l] = False
             stream = self._raw_stream()
             st = N.lib.wnw_stream_wait_event(stream, self._event_handles[l])
             if st == 0:
@@ -753,23 +758,26 @@ class B200WnWCache(FlatVarlenCache):
                                                                           abs_tol=1e-12)
             S = self.batch_size * self.num_kv_heads
             args = Kx.make_attn_args(self.dtype, S, G, D, self.k_store[l], self.v_store[l], self._seg_base[l],
-                                     self._seg_len[l], self._work[l], self._shape[l][1], scale, self._scratch,
+                                     self._seg_len[l], self._work[l], scale, self._scratch,
                                      seg_cap=self._seg_cap[l], num_kv_heads=self.num_kv_heads,
-                                     score=None if sep else score, split=self._shape[l][0])
+                                     score=None if sep else score)
             cached = self._attn_args[l] = (scale, sep, args, C.byref(args))
         _, sep, args, ref = cached
+        # the kernel may read this layer's lengths and rows before it waits
+        # for the preceding kernel when nothing in this step has written them
+        args.flags = N.ATTN_ROWS_READY if self._rows_ready[l] else 0
         out = torch.empty_like(qf)
         st = N.lib.wnw_decode_attn_step(ref, qf.data_ptr(), nk.data_ptr(), nv.data_ptr(), out.data_ptr(),
                                         self._raw_stream())
         if st:
             N.check(st, "wnw_decode_attn_step")
-        Kx.LAUNCHES[0] += 1
+        Kx.LAUNCHES[0] += self._work[l].launches
         if sep:
             score = self._score_args(l)  # rescore with the reference's 1/sqrt(d) (the append is idempotent)
             Kx.decode_attention(qf, self.k_store[l], self.v_store[l], self._seg_base[l], self._seg_len[l],
-                                self._work[l], self._shape[l][1], D ** -0.5, self._scratch, new_k=nk, new_v=nv,
+                                self._work[l], D ** -0.5, self._scratch, new_k=nk, new_v=nv,
                                 seg_cap=self._seg_cap[l], num_kv_heads=self.num_kv_heads, score=score,
-                                out=torch.empty_like(qf), split=self._shape[l][0])
+                                out=torch.empty_like(qf))
         return out
 
     def decode_all_layers_done(self):

@@ -129,6 +129,12 @@ __device__ inline void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
                : "memory");
 }
 
+// Plain arrive (no transaction bytes): completes a phase of a barrier whose
+// expected arrival count is 1 without any copy.
+__device__ inline void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
 // 1-D bulk async copy global -> shared (this CTA), completion on `bar`.
 __device__ inline void bulk_g2s(void* dst_smem, const void* src_gmem, uint32_t bytes, uint64_t* bar) {
   asm volatile(

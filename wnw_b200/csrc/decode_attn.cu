@@ -1,6 +1,7 @@
 // C ABI of the decode-attention kernel: argument checks, dtype dispatch and
 // the host-side work-table builder.
 #include <algorithm>
+#include <cstdint>
 #include <map>
 #include <mutex>
 #include <tuple>
@@ -13,40 +14,17 @@ namespace wnw {
 int split_rows_for(int dtype, int head_dim) {
   const int esz = dtype == WNW_F32 ? 4 : 2;
   if (head_dim <= 0) return 0;
-  if (esz == 2 && (head_dim == 64 || head_dim == 128)) return 128;  // tensor-core kernel tile
+  if (esz == 2 && (head_dim == 64 || head_dim == 128)) return 0;  // tensor-core kernel: takes a plan
   return kAttnTileBytes / (2 * head_dim * esz);
 }
+
+bool uses_plan(int dtype, int head_dim) { return dtype != WNW_F32 && (head_dim == 64 || head_dim == 128); }
 
 }  // namespace wnw
 
 extern "C" int wnw_split_rows(int dtype, int head_dim) { return wnw::split_rows_for(dtype, head_dim); }
 
 namespace wnw {
-
-// Resident CTAs (clusters x size) of the tensor-core kernel, cached per
-// device, head_dim, cluster size and stage count.
-static wnw_status mma_slots(int head_dim, int cs, int nstages, int* slots) {
-  static std::mutex mu;
-  static std::map<std::tuple<int, int, int, int>, int> cache;
-  int dev = 0;
-  WNW_CUDA_TRY(cudaGetDevice(&dev));
-  const auto key = std::make_tuple(dev, head_dim, cs, nstages);
-  {
-    std::lock_guard<std::mutex> g(mu);
-    auto it = cache.find(key);
-    if (it != cache.end()) {
-      *slots = it->second;
-      return WNW_OK;
-    }
-  }
-  int n = 0;
-  const wnw_status st = attn_mma_active_clusters_any(head_dim, cs, nstages, &n);
-  if (st != WNW_OK) return st;
-  std::lock_guard<std::mutex> g(mu);
-  cache[key] = n * cs;
-  *slots = n * cs;
-  return WNW_OK;
-}
 
 }  // namespace wnw
 
@@ -55,6 +33,9 @@ extern "C" wnw_status wnw_attn_launch_shape(int dtype, int head_dim, const int32
   using namespace wnw;
   WNW_CHECK_ARG(seg_cap && split_rows && cluster_size, "null pointer argument");
   WNW_CHECK_ARG(num_segs >= 0, "num_segs < 0");
+  WNW_CHECK_ARG(!uses_plan(dtype, head_dim),
+                "16-bit K/V with head_dim %d take the tensor-core kernel, launched from a plan (wnw_attn_plan)",
+                head_dim);
   const int base = split_rows_for(dtype, head_dim);
   WNW_CHECK_ARG(base > 0, "unsupported head_dim %d", head_dim);
   std::vector<int64_t> units(num_segs);
@@ -64,78 +45,38 @@ extern "C" wnw_status wnw_attn_launch_shape(int dtype, int head_dim, const int32
     units[s] = (int64_t(seg_cap[s]) + 1 + base - 1) / base;
     maxu = std::max(maxu, units[s]);
   }
-  const bool mma = dtype != WNW_F32 && (head_dim == 64 || head_dim == 128);
-  if (!mma) {
-    // CUDA-core kernel: one tile per CTA, clusters of up to 8, smaller when
-    // even the longest segment needs fewer splits
-    int cs = 1;
-    while (cs < maxu && cs < 8) cs *= 2;
-    *split_rows = base;
-    *cluster_size = cs;
-    return WNW_OK;
-  }
-  int dev = 0, nsm = 0;
-  WNW_CUDA_TRY(cudaGetDevice(&dev));
-  WNW_CUDA_TRY(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev));
-  // Tiles per CTA T and cluster size cs.  Cost, in tile-stream times of one
-  // SM: every wave of resident CTAs pays a fixed latency (first copy issued
-  // only after the segment length is read, merge chain at the end: about
-  // kWaveFixed tiles) plus T tiles for each CTA sharing an SM.  Then the
-  // fewest cross-cluster partials, then the smaller T.
-  constexpr int64_t kWaveFixed = 3;
-  int64_t best_cost = INT64_MAX, best_ncl = INT64_MAX;
-  int best_t = 1, best_cs = 1;
-  for (int64_t t = 1;; t = (t < 4) ? t + 1 : (t % 3 == 0 ? t / 3 * 4 : t / 2 * 3)) {
-    const int64_t max_ctas = (maxu + t - 1) / t;  // CTAs of the longest segment
-    for (int cs = 8; cs >= 1; cs /= 2) {
-      if (cs > 1 && cs / 2 >= max_ctas) continue;  // the longest segment would leave half a cluster idle
-      int64_t ctas = 0, ncl_max = 0;
-      for (int s = 0; s < num_segs; ++s) {
-        const int64_t ncl = std::max<int64_t>(1, ((units[s] + t - 1) / t + cs - 1) / cs);
-        ctas += ncl * cs;
-        ncl_max = std::max(ncl_max, ncl);
-      }
-      int slots = 0;
-      const wnw_status st = mma_slots(head_dim, cs, mma_stages(t), &slots);
-      if (st != WNW_OK) return st;
-      if (slots <= 0 || ctas == 0) continue;
-      const int64_t waves = (ctas + slots - 1) / slots;
-      const int64_t per_sm = (std::min<int64_t>(ctas, slots) + nsm - 1) / nsm;
-      const int64_t cost = waves * (kWaveFixed + t * per_sm);
-      if (cost < best_cost || (cost == best_cost && ncl_max < best_ncl)) {
-        best_cost = cost;
-        best_ncl = ncl_max;
-        best_t = static_cast<int>(t);
-        best_cs = cs;
-      }
-    }
-    if (t >= maxu || t * base >= (int64_t(1) << 30)) break;
-  }
-  *split_rows = best_t * base;
-  *cluster_size = best_cs;
+  // CUDA-core kernel: one tile per CTA, clusters of up to 8, smaller when
+  // even the longest segment needs fewer splits
+  int cs = 1;
+  while (cs < maxu && cs < 8) cs *= 2;
+  *split_rows = base;
+  *cluster_size = cs;
   return WNW_OK;
 }
 
 extern "C" wnw_status wnw_decode_attn(const wnw_decode_attn_args* a, void* stream) {
   using namespace wnw;
   WNW_CHECK_ARG(a != nullptr, "null args");
-  WNW_CHECK_ARG(a->q && a->k_store && a->v_store && a->seg_base && a->seg_len && a->work && a->out &&
-                    a->partials && a->counters && a->err,
+  WNW_CHECK_ARG(a->q && a->k_store && a->v_store && a->seg_base && a->seg_len && a->out && a->partials && a->err,
                 "null pointer argument");
   WNW_CHECK_ARG((a->new_k == nullptr) == (a->new_v == nullptr), "new_k and new_v must both be given or both null");
   WNW_CHECK_ARG(a->num_segs > 0 && a->num_kv_heads > 0, "bad segment counts");
-  WNW_CHECK_ARG(a->cluster_size == 1 || a->cluster_size == 2 || a->cluster_size == 4 || a->cluster_size == 8 ||
-                    a->cluster_size == 16,
-                "cluster_size must be 1, 2, 4, 8 or 16");
-  WNW_CHECK_ARG(a->n_clusters >= 0, "n_clusters < 0");
   WNW_CHECK_ARG(aligned16(a->q) && aligned16(a->k_store) && aligned16(a->v_store) && aligned16(a->out) &&
                     aligned16(a->partials) &&
                     (a->new_k == nullptr || (aligned16(a->new_k) && aligned16(a->new_v))),
                 "q, stores, out, partials and new rows must be 16-byte aligned");
+  WNW_CHECK_ARG((a->flags & ~WNW_ATTN_ROWS_READY) == 0, "unknown flags 0x%x", a->flags);
   if (a->score_slot != nullptr)
     WNW_CHECK_ARG(a->audio_start && a->audio_end && a->logits && a->logits_off,
                   "scoring needs audio ranges, logits and offsets");
-  if (a->n_clusters == 0) return WNW_OK;
+  if (!uses_plan(a->dtype, a->head_dim)) {
+    WNW_CHECK_ARG(a->work && a->counters, "the CUDA-core path needs a work table and counters");
+    WNW_CHECK_ARG(a->cluster_size == 1 || a->cluster_size == 2 || a->cluster_size == 4 || a->cluster_size == 8 ||
+                      a->cluster_size == 16,
+                  "cluster_size must be 1, 2, 4, 8 or 16");
+    WNW_CHECK_ARG(a->n_clusters >= 0, "n_clusters < 0");
+    if (a->n_clusters == 0) return WNW_OK;
+  }
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   switch (a->dtype) {
     case WNW_F32: return dispatch_dtype<float>(a, s);
@@ -192,5 +133,140 @@ extern "C" wnw_status wnw_build_work_table(const int32_t* seg_cap, int num_segs,
       work[2 * k + 1] = static_cast<int32_t>(j);
     }
   }
+  return WNW_OK;
+}
+
+extern "C" wnw_status wnw_attn_plan(const int32_t* seg_cap, int num_segs, int sm_count, int max_cluster,
+                                    int32_t* plan, int64_t max_ints, wnw_attn_plan_info* info) {
+  using namespace wnw;
+  constexpr int64_t kUnit = 32;           // rows: one TMA box pair of two warps
+  constexpr int64_t kMaxShareUnits = 48;  // 1,536 rows: most a CTA takes to keep a segment in one cluster
+  WNW_CHECK_ARG(seg_cap && info && (plan || max_ints == 0), "null pointer argument");
+  WNW_CHECK_ARG(num_segs > 0, "num_segs must be positive");
+  WNW_CHECK_ARG(max_cluster <= 16, "max_cluster must be in 1..16 (or <= 0 for the device's)");
+  if (sm_count <= 0) {
+    int dev = 0;
+    WNW_CUDA_TRY(cudaGetDevice(&dev));
+    WNW_CUDA_TRY(cudaDeviceGetAttribute(&sm_count, cudaDevAttrMultiProcessorCount, dev));
+  }
+  if (max_cluster <= 0) {  // the largest cluster of the kernel the device can hold
+    max_cluster = 8;
+    int n = 0;
+    if (attn_mma_active_clusters_any(128, 16, &n) == WNW_OK && n > 0) max_cluster = 16;
+  }
+  std::vector<int64_t> units(num_segs);
+  int64_t total = 0, umax = 1;
+  for (int s = 0; s < num_segs; ++s) {
+    WNW_CHECK_ARG(seg_cap[s] >= 0 && seg_cap[s] < (1 << 30), "capacity of segment %d out of range", s);
+    units[s] = (int64_t(seg_cap[s]) + 1 + kUnit - 1) / kUnit;  // capacity + the step's token
+    total += units[s];
+    umax = std::max(umax, units[s]);
+  }
+  // units per CTA: an equal share of the device, raised so the longest
+  // segment fits one cluster as long as that keeps shares <= kMaxShareUnits
+  const int64_t share = std::max<int64_t>((total + sm_count - 1) / sm_count,
+                                          std::min<int64_t>(kMaxShareUnits, (umax + max_cluster - 1) / max_cluster));
+  std::vector<int64_t> k(num_segs);
+  int64_t kmax = 1;
+  for (int s = 0; s < num_segs; ++s) {
+    k[s] = std::max<int64_t>(1, (units[s] + share - 1) / share);
+    kmax = std::max(kmax, k[s]);
+  }
+  int C = 1;
+  while (C < std::min<int64_t>(kmax, max_cluster)) C *= 2;
+
+  struct Slot {
+    int32_t seg, r0, r1, meta;
+  };
+  std::vector<Slot> slots;       // clusters x C
+  std::vector<int32_t> part_r0;  // first row of each cluster partial
+  std::vector<int32_t> comb;     // seg, first part, parts, 0
+  auto new_cluster = [&]() {
+    const size_t at = slots.size();
+    slots.resize(at + C, Slot{-1, 0, 0, 0});
+    return at;
+  };
+  // ranks [r, r + n) of the cluster at `at` attend units [u0, u1) of segment
+  // s, split evenly (the first ranks take the extra units)
+  auto place = [&](size_t at, int r, int n, int s, int64_t u0, int64_t u1, bool to_part, int64_t part) {
+    const int64_t nu = u1 - u0;
+    int64_t u = u0;
+    for (int i = 0; i < n; ++i) {
+      const int64_t take = nu / n + (i < nu % n ? 1 : 0);
+      const uint32_t meta = static_cast<uint32_t>(r) | (static_cast<uint32_t>(n) << 5) |
+                            ((to_part ? 1u : 0u) << 10) | (static_cast<uint32_t>(part) << 11);
+      slots[at + r + i] = Slot{s, static_cast<int32_t>(u * kUnit), static_cast<int32_t>((u + take) * kUnit),
+                               static_cast<int32_t>(meta)};
+      u += take;
+    }
+  };
+  // segments needing more CTAs than a cluster holds: whole clusters, each
+  // an even share of the segment's units, merged by the combine kernel
+  for (int s = 0; s < num_segs; ++s) {
+    if (k[s] <= C) continue;
+    const int64_t ncl = (k[s] + C - 1) / C;
+    comb.insert(comb.end(), {s, static_cast<int32_t>(part_r0.size()), static_cast<int32_t>(ncl), 0});
+    for (int64_t j = 0; j < ncl; ++j) {
+      const int64_t u0 = units[s] * j / ncl, u1 = units[s] * (j + 1) / ncl;
+      WNW_CHECK_ARG(part_r0.size() < (size_t(1) << 21), "too many cluster partials");
+      const size_t at = new_cluster();
+      place(at, 0, C, s, u0, u1, true, static_cast<int64_t>(part_r0.size()));
+      part_r0.push_back(static_cast<int32_t>(u0 * kUnit));
+    }
+  }
+  // the others: packed into clusters, largest first, each into the cluster
+  // with the fewest free ranks that still hold it
+  std::vector<int> order;
+  for (int s = 0; s < num_segs; ++s)
+    if (k[s] <= C) order.push_back(s);
+  std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return k[a] > k[b]; });
+  std::vector<std::vector<size_t>> by_free(C + 1);  // clusters by free ranks
+  std::vector<int> used;                            // ranks taken per cluster (index: at / C)
+  for (int s : order) {
+    const int need = static_cast<int>(k[s]);
+    size_t at = SIZE_MAX;
+    for (int f = need; f < C && at == SIZE_MAX; ++f) {
+      if (!by_free[f].empty()) {
+        at = by_free[f].back();
+        by_free[f].pop_back();
+      }
+    }
+    if (at == SIZE_MAX) {
+      at = new_cluster();
+      used.resize(slots.size() / C, 0);
+    }
+    int& r = used[at / C];
+    place(at, r, need, s, 0, units[s], false, 0);
+    r += need;
+    if (r < C) by_free[C - r].push_back(at);
+  }
+  const int64_t ctas = static_cast<int64_t>(slots.size());
+  const int64_t parts = static_cast<int64_t>(part_r0.size());
+  const int64_t ints = 8 + 4 * ctas + (parts + 3) / 4 * 4 + static_cast<int64_t>(comb.size());
+  WNW_CHECK_ARG(ctas < INT32_MAX && ints < INT32_MAX, "plan too large");
+  info->ctas = static_cast<int>(ctas);
+  info->cluster = C;
+  info->parts = static_cast<int>(parts);
+  info->combine = static_cast<int>(comb.size() / 4);
+  info->ints = ints;
+  if (plan == nullptr) return WNW_OK;
+  if (max_ints < ints) {
+    set_error("the plan needs %lld ints, capacity %lld", static_cast<long long>(ints),
+              static_cast<long long>(max_ints));
+    return WNW_ERR_CAPACITY;
+  }
+  std::fill(plan, plan + ints, 0);
+  plan[0] = info->ctas;
+  plan[1] = C;
+  plan[2] = info->parts;
+  plan[3] = info->combine;
+  for (int64_t c = 0; c < ctas; ++c) {
+    plan[8 + 4 * c] = slots[c].seg;
+    plan[8 + 4 * c + 1] = slots[c].r0;
+    plan[8 + 4 * c + 2] = slots[c].r1;
+    plan[8 + 4 * c + 3] = slots[c].meta;
+  }
+  std::copy(part_r0.begin(), part_r0.end(), plan + 8 + 4 * ctas);
+  std::copy(comb.begin(), comb.end(), plan + 8 + 4 * ctas + (parts + 3) / 4 * 4);
   return WNW_OK;
 }

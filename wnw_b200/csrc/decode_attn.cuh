@@ -38,8 +38,6 @@ constexpr int kAttnThreads = 128;
 constexpr int kAttnWarps = 4;
 constexpr int kAttnTileBytes = 64 * 1024;  // K + V rows staged per CTA
 constexpr int kMaxCluster = 16;             // CTAs per cluster (16 needs the non-portable opt-in)
-constexpr int kMmaMaxStages = 3;            // tensor-core kernel: shared-memory stages per CTA
-inline int mma_stages(int64_t tiles) { return static_cast<int>(tiles < kMmaMaxStages ? tiles : kMmaMaxStages); }
 constexpr float kLog2e = 1.4426950408889634f;
 
 template <typename T, int D, int G>
@@ -77,6 +75,7 @@ struct AttnParams {
   void* out;
   float scale_log2;
   int num_kv_heads;
+  int num_segs;
   const int32_t* score_slot;
   const int32_t* audio_start;
   const int32_t* audio_end;
@@ -609,6 +608,7 @@ inline AttnParams make_params(const wnw_decode_attn_args* a) {
   p.out = a->out;
   p.scale_log2 = a->scale * kLog2e;
   p.num_kv_heads = a->num_kv_heads;
+  p.num_segs = a->num_segs;
   p.score_slot = a->score_slot;
   p.audio_start = a->audio_start;
   p.audio_end = a->audio_end;
@@ -655,8 +655,7 @@ wnw_status launch_attn(const wnw_decode_attn_args* a, cudaStream_t stream) {
 template <typename T>
 wnw_status dispatch_dtype(const wnw_decode_attn_args* a, cudaStream_t s);
 
-// co-resident clusters of `cs` CTAs of the tensor-core kernel with `nstages`
-// shared-memory stages (decode_attn_bf16.cu)
-wnw_status attn_mma_active_clusters_any(int head_dim, int cs, int nstages, int* n);
+// co-resident clusters of `cs` CTAs of the tensor-core kernel (decode_attn_bf16.cu)
+wnw_status attn_mma_active_clusters_any(int head_dim, int cs, int* n);
 
 }  // namespace wnw

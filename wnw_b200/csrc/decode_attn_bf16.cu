@@ -49,13 +49,13 @@ wnw_status dispatch_dtype<__nv_bfloat16>(const wnw_decode_attn_args* a, cudaStre
 
 namespace wnw {
 
-// Residency of the tensor-core kernel for the launch-shape chooser.  The f16
-// and bf16 instantiations (and every group size) use the same registers and
-// shared memory, so the bf16, group-4 one stands for all of them.
-wnw_status attn_mma_active_clusters_any(int head_dim, int cs, int nstages, int* n) {
+// Residency of the tensor-core kernel for the plan builder.  The f16 and
+// bf16 instantiations (and every group size) use the same resources per CTA,
+// so the bf16, group-4 one stands for all of them.
+wnw_status attn_mma_active_clusters_any(int head_dim, int cs, int* n) {
   switch (head_dim) {
-    case 64: return attn_mma_active_clusters<__nv_bfloat16, 64, 4>(cs, nstages, n);
-    case 128: return attn_mma_active_clusters<__nv_bfloat16, 128, 4>(cs, nstages, n);
+    case 64: return attn_mma_active_clusters<__nv_bfloat16, 64, 4>(cs, n);
+    case 128: return attn_mma_active_clusters<__nv_bfloat16, 128, 4>(cs, n);
     default: set_error("head_dim %d has no tensor-core kernel", head_dim); return WNW_ERR_UNSUPPORTED;
   }
 }

@@ -1,18 +1,30 @@
-// Tensor-core variant of the decode-attention kernel for 16-bit K/V
-// (bf16 / fp16, head_dim 64 or 128).
+// Tensor-core decode attention for 16-bit K/V (bf16 / fp16, head_dim 64 or
+// 128), launched from a work plan (wnw_attn_plan).
 //
-// Same work decomposition, fused append, class-A logits and merge tail as the
-// CUDA-core kernel (decode_attn.cuh), but the two products run on the tensor
-// cores with fp32 accumulation:
-//   S^T[rows x g] = K[rows x D] . q^T[D x g]      (mma m16n8k16, A = K via ldmatrix)
-//   O^T[D x g]   += V^T[D x rows] . P^T[rows x g]  (A = V^T via ldmatrix.trans,
-//                                                   B = P^T via movmatrix.trans)
-// with the GQA group (<= 8 heads) as the n = 8 dimension.  K / V tiles of 128
-// rows are staged by 2-D TMA with 128-byte swizzle (conflict-free ldmatrix);
-// a CTA streams `split_rows / 128` consecutive tiles of its segment through
-// up to three stages, each warp owning 32 rows of every tile: it waits for
-// its rows, keeps an online softmax across tiles and refills its rows of the
-// stage with a later tile as soon as it is done with them.
+// Work decomposition: every CTA attends one row range of one segment.  A
+// segment's CTAs sit in consecutive ranks of one thread-block cluster (up to
+// 16 CTAs), so their partial softmax states merge through distributed shared
+// memory -- no global-memory round trip; only a segment too long for one
+// cluster's CTAs spans several clusters, whose cluster partials a second
+// small kernel merges in order.  The plan gives each CTA about the same rows
+// (capped so a long segment fits one cluster) and packs short segments into
+// shared clusters.
+//
+// A CTA streams its rows as 128-row tiles through three shared-memory stages
+// (2-D TMA, 128-byte swizzle).  Its eight warps own 16 rows of every tile
+// each (two warps per scheduler, so one warp's latency hides behind the
+// other's): a warp waits for its rows, runs the two products on the tensor
+// cores with fp32 accumulation,
+//   S^T[16 x g] = K[16 x D] . q^T[D x g]       (mma m16n8k16, A = K via ldmatrix)
+//   O^T[D x g] += V^T[D x 16] . P^T[16 x g]    (A = V^T via ldmatrix.trans,
+//                                               B = P^T via movmatrix.trans)
+// with the GQA group (<= 8 heads) as the n = 8 dimension, keeps an online
+// softmax (base 2, MUFU ex2; the running sum stays per lane until the end)
+// and refills its rows of the stage with a later tile as soon as it is done.
+//
+// Programmatic dependent launch: the prologue overlaps the preceding kernel;
+// with WNW_ATTN_ROWS_READY the lengths are read and the first stages' loads
+// issued before the dependency wait as well.
 #pragma once
 
 #include "decode_attn.cuh"
@@ -20,8 +32,12 @@
 
 namespace wnw {
 
-constexpr int kMmaTileRows = 128;  // rows per CTA = 4 warps x 32
-constexpr int kMmaWarpRows = 32;
+constexpr int kTcThreads = 256;    // 8 warps
+constexpr int kTcWarps = 8;
+constexpr int kTcWarpRows = 16;    // one m16 block per warp and tile
+constexpr int kTcTileRows = 128;   // 8 warps x 16 rows
+constexpr int kTcStages = 3;
+constexpr int kTcMaxCluster = 16;
 
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
@@ -80,110 +96,146 @@ __device__ __forceinline__ uint32_t swz(int row, int chunk) {
   return uint32_t(row) * 128u + (uint32_t(chunk ^ (row & 7)) << 4);
 }
 
+
+// Device view of a wnw_attn_plan blob.
+//   cta[c]   = {segment (-1: an idle rank), row_begin, row_end, meta}
+//   meta     = leader rank (bits 0-4) | ranks of the segment in this cluster
+//              (bits 5-9) | writes a cluster partial (bit 10) | partial slot
+//              (bits 11-31)
+//   part_r0  = first row of each cluster partial's range
+//   comb[e]  = {segment, first partial, partials, 0}
+struct AttnPlanView {
+  const int4* cta;
+  const int32_t* part_r0;
+  const int4* comb;
+  int parts;
+  int ready;  // WNW_ATTN_ROWS_READY given
+};
+
+// rows of a segment attended at this launch: stored rows + the step's token
+__device__ __forceinline__ int seg_total(const AttnParams& p, int seg) {
+  return p.seg_len[seg] + (p.new_k != nullptr ? 1 : 0);
+}
+
 template <typename T, int D, int G>
-__global__ void __launch_bounds__(kAttnThreads)
-    decode_attn_mma_kernel(const AttnParams p, const __grid_constant__ CUtensorMap tmK,
-                           const __grid_constant__ CUtensorMap tmV, const int tiles, const int nstages) {
+__global__ void __launch_bounds__(kTcThreads, 1)
+    decode_attn_mma_kernel(const AttnParams p, const AttnPlanView pv, const __grid_constant__ CUtensorMap tmK,
+                           const __grid_constant__ CUtensorMap tmV) {
   static_assert(D == 64 || D == 128, "tensor-core path covers head_dim 64 and 128");
   static_assert(G >= 1 && G <= 8, "GQA group is the mma n=8 dimension");
-  constexpr int NH = D / 64;                   // 128-byte halves per row
-  constexpr int HALF = kMmaTileRows * 128;     // bytes of one half tile
-  constexpr int STAGE = 2 * NH * HALF;         // K + V of one 128-row tile
-  constexpr int NS = D / 16;                   // k-steps over D / m-tiles of O^T
+  constexpr int NH = D / 64;                // 128-byte halves per row
+  constexpr int HALF = kTcTileRows * 128;   // bytes of one half tile
+  constexpr int STAGE = 2 * NH * HALF;      // K + V of one 128-row tile
+  constexpr int NS = D / 16;                // k-steps over D / m-tiles of O^T
+  constexpr int NW = kTcWarps;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  __shared__ __align__(8) uint64_t bars[kMmaMaxStages][kAttnWarps];
+  __shared__ __align__(8) uint64_t bars[kTcStages][NW];
 
   cg::cluster_group cluster = cg::this_cluster();
   const int cs = static_cast<int>(cluster.num_blocks());
-  const int rank = static_cast<int>(cluster.block_rank());
-  const int cid = blockIdx.x / cs;
-  // prologue that does not depend on the preceding kernel (work table and
-  // slot bases are fixed per layout) overlaps its tail under PDL
-  const int seg = __ldg(p.work + 2 * cid);
-  const int j = __ldg(p.work + 2 * cid + 1);
-  const int64_t base = __ldg(p.seg_base + seg);
-  // L2 prefetch of this CTA's first tiles (up to the slot capacity): it needs
-  // only layout constants, so it runs before the dependency wait and the rows
-  // stream into L2 while the preceding kernel finishes.  L2 is the point of
-  // coherence and nothing lands in shared memory, so rows the preceding
-  // kernel still writes are read correctly after the wait.
-  if (p.seg_cap != nullptr && threadIdx.x < 2 * kMmaMaxStages) {
-    const int cap = __ldg(p.seg_cap + seg);
-    const int i = threadIdx.x >> 1;
-    const int r0 = (j * cs + rank) * tiles * kMmaTileRows + i * kMmaTileRows;
-    const int r1 = min(min(r0 + kMmaTileRows, cap), (j * cs + rank + 1) * tiles * kMmaTileRows);
-    if (i < tiles && r1 > r0) {
-      const T* src = reinterpret_cast<const T*>((threadIdx.x & 1) ? p.v_store : p.k_store) + (base + r0) * D;
-      prefetch_l2(src, uint32_t(r1 - r0) * D * sizeof(T));
-    }
-  }
-  if (threadIdx.x == 0) {
-#pragma unroll
-    for (int st = 0; st < kMmaMaxStages; ++st)
-#pragma unroll
-      for (int w = 0; w < kAttnWarps; ++w) mbar_init(&bars[st][w], 1);
-    fence_mbar_init();
-  }
-  pdl_wait();  // seg_len, K/V rows and q may come from the preceding kernel
-  const int len = p.seg_len[seg];
-  const bool append = p.new_k != nullptr;
-  const int total = len + (append ? 1 : 0);
-  const int rows_per_cta = tiles * kMmaTileRows;
-  const int nsplit = (total + rows_per_cta - 1) / rows_per_cta;
-  const int ncl = max(1, (nsplit + cs - 1) / cs);
-  if (j >= ncl) return;  // the whole cluster is idle at this length (uniform)
-
-  const int row0 = (j * cs + rank) * rows_per_cta;
-  const int nrows = max(0, min(rows_per_cta, total - row0));
-  const int ntiles = (nrows + kMmaTileRows - 1) / kMmaTileRows;
+  const int crank = static_cast<int>(cluster.block_rank());
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
-  const int gid = lane >> 2;
-  const int tig = lane & 3;
+
+  // ---- this CTA's item (plan constants: read before the dependency wait)
+  const int4 it = __ldg(pv.cta + blockIdx.x);
+  const int leader = it.w & 31;
+  const int nranks = (it.w >> 5) & 31;
+  const bool to_part = ((it.w >> 10) & 1) != 0;
+  const int part = static_cast<int>(static_cast<uint32_t>(it.w) >> 11);
+  bool active = it.x >= 0;
+  if (active && (it.x >= p.num_segs || it.y < 0 || it.z < it.y || nranks < 1 || leader + nranks > cs ||
+                 crank < leader || crank >= leader + nranks || (to_part && part >= pv.parts))) {
+    if (tid == 0) atomicOr(p.err, WNW_DEVERR_BAD_INDEX);  // not a wnw_attn_plan: attend nothing
+    active = false;
+  }
+  const int seg = active ? it.x : 0;
+  const int64_t base = active ? __ldg(p.seg_base + seg) : 0;
+  if (tid == 0) {
+#pragma unroll
+    for (int st = 0; st < kTcStages; ++st)
+#pragma unroll
+      for (int w = 0; w < NW; ++w) mbar_init(&bars[st][w], 1);
+    fence_mbar_init();
+  }
   __syncthreads();
 
-  // ---- producer: warp w's 32 rows of tile i -> stage i % nstages, one 2-D
-  // TMA box (32 rows x 64 columns) per half and tensor; each warp refills its
-  // own rows of a stage as soon as it is done with them
-  auto issue = [&](int i, int w) {
-    const int st = i % nstages;
+  int total = 0, rows = 0, ntiles = 0;
+  auto schedule = [&]() {
+    if (!active) return;
+    total = seg_total(p, seg);
+    rows = max(0, min(it.z, total) - it.y);
+    ntiles = (rows + kTcTileRows - 1) / kTcTileRows;
+  };
+  // this warp's 16 rows of tile t -> stage t % kTcStages (lane 0); a warp
+  // with no rows in the tile still completes the barrier's phase
+  auto issue = [&](int t) {
+    const int st = t % kTcStages;
     uint8_t* sK = smem + st * STAGE;
     uint8_t* sV = sK + NH * HALF;
-    const int trow0 = row0 + i * kMmaTileRows;
-    const int lo = w * kMmaWarpRows;
-    if (lo >= total - trow0) return;  // rows past the segment's end: no copy, no wait
-    mbar_arrive_expect_tx(&bars[st][w], 2u * NH * kMmaWarpRows * 128u);
-    const int y = static_cast<int>(base + trow0 + lo);
+    const int trow = t * kTcTileRows;
+    const int lo = warp * kTcWarpRows;
+    if (lo >= rows - trow) {
+      mbar_arrive(&bars[st][warp]);
+      return;
+    }
+    mbar_arrive_expect_tx(&bars[st][warp], 2u * NH * kTcWarpRows * 128u);
+    const int y = static_cast<int>(base + it.y + trow + lo);
 #pragma unroll
     for (int h = 0; h < NH; ++h) {
-      tma_load_2d(sK + h * HALF + lo * 128, &tmK, h * 64, y, &bars[st][w]);
-      tma_load_2d(sV + h * HALF + lo * 128, &tmV, h * 64, y, &bars[st][w]);
+      tma_load_2d(sK + h * HALF + lo * 128, &tmK, h * 64, y, &bars[st][warp]);
+      tma_load_2d(sV + h * HALF + lo * 128, &tmV, h * 64, y, &bars[st][warp]);
     }
   };
-  if (tid == 0) {
-    for (int i = 0; i < min(ntiles, nstages); ++i)
-      for (int w = 0; w < kAttnWarps; ++w) issue(i, w);
+  if (pv.ready) {  // lengths and rows are final: start streaming before the wait
+    schedule();
+    if (lane == 0)
+      for (int t = 0; t < min(ntiles, kTcStages); ++t) issue(t);
+    pdl_wait();  // q, the new rows and the outputs may belong to the preceding kernel
+  } else {
+    // L2 prefetch of this CTA's first rows by capacity (layout constants
+    // only; L2 is the point of coherence, so rows the preceding kernel still
+    // writes are read correctly after the wait)
+    if (active && tid < 2 * kTcStages) {
+      const int r0 = it.y + (tid >> 1) * kTcTileRows;
+      const int r1 = min(r0 + kTcTileRows, it.z);
+      if (r1 > r0) {
+        const T* src = reinterpret_cast<const T*>((tid & 1) ? p.v_store : p.k_store) + (base + r0) * D;
+        prefetch_l2(src, uint32_t(r1 - r0) * D * sizeof(T));
+      }
+    }
+    pdl_wait();  // seg_len, K/V rows and q may come from the preceding kernel
+    schedule();
+    if (lane == 0)
+      for (int t = 0; t < min(ntiles, kTcStages); ++t) issue(t);
   }
   pdl_launch_dependents();  // the next kernel may start its own prologue now
 
-  // ---- q as the mma B operand: b[k = d][n = g], zero for padded heads
-  const T* qs = reinterpret_cast<const T*>(p.q) + int64_t(seg) * G * D;
+  const int gid = lane >> 2;
+  const int tig = lane & 3;
+  const int jm = lane >> 3;  // which 8x8 matrix this lane addresses in ldmatrix
+  const bool append = p.new_k != nullptr;
+  const int len = total - (append ? 1 : 0);
+
+  // q as the mma B operand: b[k = d][n = g], zero for padded heads
   uint32_t qb[NS][2];
+  {
+    const T* qs = reinterpret_cast<const T*>(p.q) + int64_t(seg) * G * D;
 #pragma unroll
-  for (int s = 0; s < NS; ++s) {
-    if (gid < G) {
-      qb[s][0] = *reinterpret_cast<const uint32_t*>(qs + gid * D + 16 * s + 2 * tig);
-      qb[s][1] = *reinterpret_cast<const uint32_t*>(qs + gid * D + 16 * s + 8 + 2 * tig);
-    } else {
-      qb[s][0] = qb[s][1] = 0u;
+    for (int s = 0; s < NS; ++s) {
+      if (active && gid < G) {
+        qb[s][0] = *reinterpret_cast<const uint32_t*>(qs + gid * D + 16 * s + 2 * tig);
+        qb[s][1] = *reinterpret_cast<const uint32_t*>(qs + gid * D + 16 * s + 8 + 2 * tig);
+      } else {
+        qb[s][0] = qb[s][1] = 0u;
+      }
     }
   }
-
   int a0 = 0, a1 = 0;
   float* lg = nullptr;
-  if (p.score_slot != nullptr) {
+  if (active && p.score_slot != nullptr) {
     const int slot = p.score_slot[seg];
     if (slot >= 0) {
       const int b = seg / p.num_kv_heads;
@@ -193,23 +245,23 @@ __global__ void __launch_bounds__(kAttnThreads)
     }
   }
 
-  // running softmax state of this warp; per lane heads g0 = 2*tig, g1 = 2*tig+1
+  // running softmax of this warp: per lane heads g0 = 2*tig, g1 = 2*tig+1;
+  // the maxima are warp-uniform, the sums stay per lane until the end
   float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
   float o[NS][4];
 #pragma unroll
-  for (int t = 0; t < NS; ++t) o[t][0] = o[t][1] = o[t][2] = o[t][3] = 0.f;
-  const int jm = lane >> 3;  // which 8x8 matrix this lane addresses in ldmatrix
+  for (int u = 0; u < NS; ++u) o[u][0] = o[u][1] = o[u][2] = o[u][3] = 0.f;
 
-  for (int i = 0; i < ntiles; ++i) {
-    const int st = i % nstages;
+  for (int t = 0; t < ntiles; ++t) {
+    const int st = t % kTcStages;
     uint8_t* sK = smem + st * STAGE;
     uint8_t* sV = sK + NH * HALF;
-    const int trow0 = row0 + i * kMmaTileRows;
-    const int tv = min(kMmaTileRows, total - trow0);
-    const int lo = warp * kMmaWarpRows;
-    const int hi = min(lo + kMmaWarpRows, tv);
+    const int trow0 = it.y + t * kTcTileRows;  // segment row of the tile's first row
+    const int tv = min(kTcTileRows, rows - t * kTcTileRows);
+    const int lo = warp * kTcWarpRows;
+    const int hi = min(lo + kTcWarpRows, tv);
     if (hi > lo) {
-      mbar_wait(&bars[st][warp], (i / nstages) & 1, p.err);
+      mbar_wait(&bars[st][warp], (t / kTcStages) & 1, p.err);
       const int new_local = append ? (len - trow0) : -1;
       if (append && new_local >= lo && new_local < hi) {
         // the step's token: into the tile (swizzled) and into its slot row
@@ -229,11 +281,11 @@ __global__ void __launch_bounds__(kAttnThreads)
         if (!fits && lane == 0) atomicOr(p.err, WNW_DEVERR_CAPACITY);
         __syncwarp();
       }
-      if (hi - lo < kMmaWarpRows) {
-        // rows past the segment's end are masked out of the softmax, but their
-        // V bytes still enter the mma: zero them so stale or non-finite memory
-        // (slack rows, a neighbouring slot) cannot reach the output
-        const int n0 = (lo + kMmaWarpRows - hi) * NH * 8;
+      if (hi - lo < kTcWarpRows) {
+        // rows past the range's end are masked out of the softmax, but their
+        // V bytes still enter the mma: zero them so stale or non-finite
+        // memory (slack rows, a neighbouring slot) cannot reach the output
+        const int n0 = (lo + kTcWarpRows - hi) * NH * 8;
         for (int idx = lane; idx < n0; idx += 32) {
           const int r = hi + idx / (NH * 8);
           const int rem = idx % (NH * 8);
@@ -243,45 +295,44 @@ __global__ void __launch_bounds__(kAttnThreads)
       }
       const uint32_t kbase = smem_u32(sK);
       const uint32_t vbase = smem_u32(sV);
-      // S^T for the two 16-row blocks of this warp's chunk
-      float sc[2][4];
-#pragma unroll
-      for (int b = 0; b < 2; ++b) {
-        sc[b][0] = sc[b][1] = sc[b][2] = sc[b][3] = 0.f;
-        const int row = lo + 16 * b + (lane & 7) + 8 * (jm & 1);
+      // S^T of the warp's 16 rows, as two independent accumulation chains
+      float sa[4] = {0.f, 0.f, 0.f, 0.f}, sb[4] = {0.f, 0.f, 0.f, 0.f};
+      {
+        const int row = lo + (lane & 7) + 8 * (jm & 1);
 #pragma unroll
         for (int s = 0; s < NS; ++s) {
           const int h = (16 * s) >> 6;
           const int c = ((16 * s) & 63) / 8 + (jm >> 1);
-          uint32_t r0, r1, r2, r3;
-          ldsm_x4(kbase + h * HALF + swz(row, c), r0, r1, r2, r3);
-          mma16816<T>(sc[b], r0, r1, r2, r3, qb[s][0], qb[s][1]);
+          uint32_t r0_, r1_, r2_, r3_;
+          ldsm_x4(kbase + h * HALF + swz(row, c), r0_, r1_, r2_, r3_);
+          if (s & 1)
+            mma16816<T>(sb, r0_, r1_, r2_, r3_, qb[s][0], qb[s][1]);
+          else
+            mma16816<T>(sa, r0_, r1_, r2_, r3_, qb[s][0], qb[s][1]);
         }
       }
+      float sc[4];
       // base-2 scaling, masking of rows past the end, class-A logits
 #pragma unroll
-      for (int b = 0; b < 2; ++b) {
-#pragma unroll
-        for (int hrow = 0; hrow < 2; ++hrow) {
-          const int rw = lo + 16 * b + gid + 8 * hrow;
-          const bool valid = rw < hi;
-          float& x0 = sc[b][2 * hrow];
-          float& x1 = sc[b][2 * hrow + 1];
-          x0 = valid ? x0 * p.scale_log2 : -INFINITY;
-          x1 = valid ? x1 * p.scale_log2 : -INFINITY;
-          if (lg != nullptr && valid) {
-            const int srow = trow0 + rw;
-            if (srow >= a0 && srow < a1) {
-              float* dst = lg + int64_t(srow - a0) * G;
-              if (2 * tig < G) dst[2 * tig] = x0;
-              if (2 * tig + 1 < G) dst[2 * tig + 1] = x1;
-            }
+      for (int hrow = 0; hrow < 2; ++hrow) {
+        const int rw = lo + gid + 8 * hrow;
+        const bool valid = rw < hi;
+        const float x0 = (sa[2 * hrow] + sb[2 * hrow]) * p.scale_log2;
+        const float x1 = (sa[2 * hrow + 1] + sb[2 * hrow + 1]) * p.scale_log2;
+        sc[2 * hrow] = valid ? x0 : -INFINITY;
+        sc[2 * hrow + 1] = valid ? x1 : -INFINITY;
+        if (lg != nullptr && valid) {
+          const int srow = trow0 + rw;
+          if (srow >= a0 && srow < a1) {
+            float* dst = lg + int64_t(srow - a0) * G;
+            if (2 * tig < G) dst[2 * tig] = x0;
+            if (2 * tig + 1 < G) dst[2 * tig + 1] = x1;
           }
         }
       }
-      // online softmax update over this chunk: lanes sharing tig hold the same heads
-      float mx0 = fmaxf(fmaxf(sc[0][0], sc[0][2]), fmaxf(sc[1][0], sc[1][2]));
-      float mx1 = fmaxf(fmaxf(sc[0][1], sc[0][3]), fmaxf(sc[1][1], sc[1][3]));
+      // online softmax: the 8 lanes sharing tig hold the same heads
+      float mx0 = fmaxf(sc[0], sc[2]);
+      float mx1 = fmaxf(sc[1], sc[3]);
 #pragma unroll
       for (int off = 4; off < 32; off <<= 1) {
         mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
@@ -292,58 +343,53 @@ __global__ void __launch_bounds__(kAttnThreads)
       const float b0s = (mx0 == -INFINITY) ? 0.f : mx0;
       const float b1s = (mx1 == -INFINITY) ? 0.f : mx1;
       const float al0 = ex2(m0 - b0s), al1 = ex2(m1 - b1s);
-      float s0 = 0.f, s1 = 0.f;
-#pragma unroll
-      for (int b = 0; b < 2; ++b) {
-        sc[b][0] = ex2(sc[b][0] - b0s);
-        sc[b][1] = ex2(sc[b][1] - b1s);
-        sc[b][2] = ex2(sc[b][2] - b0s);
-        sc[b][3] = ex2(sc[b][3] - b1s);
-        s0 += sc[b][0] + sc[b][2];
-        s1 += sc[b][1] + sc[b][3];
-      }
-#pragma unroll
-      for (int off = 4; off < 32; off <<= 1) {
-        s0 += __shfl_xor_sync(0xffffffffu, s0, off);
-        s1 += __shfl_xor_sync(0xffffffffu, s1, off);
-      }
+      sc[0] = ex2(sc[0] - b0s);
+      sc[1] = ex2(sc[1] - b1s);
+      sc[2] = ex2(sc[2] - b0s);
+      sc[3] = ex2(sc[3] - b1s);
       m0 = mx0;
       m1 = mx1;
-      l0 = l0 * al0 + s0;
-      l1 = l1 * al1 + s1;
+      l0 = l0 * al0 + (sc[0] + sc[2]);
+      l1 = l1 * al1 + (sc[1] + sc[3]);
 #pragma unroll
-      for (int t = 0; t < NS; ++t) {
-        o[t][0] *= al0;
-        o[t][2] *= al0;
-        o[t][1] *= al1;
-        o[t][3] *= al1;
+      for (int u = 0; u < NS; ++u) {
+        o[u][0] *= al0;
+        o[u][2] *= al0;
+        o[u][1] *= al1;
+        o[u][3] *= al1;
       }
       // O^T += V^T . P^T
+      const uint32_t pb0 = movm_t(pack2<T>(sc[0], sc[1]));  // rows 0-7 of the block
+      const uint32_t pb1 = movm_t(pack2<T>(sc[2], sc[3]));  // rows 8-15
+      const int row = lo + (lane & 7) + 8 * (jm >> 1);
 #pragma unroll
-      for (int b = 0; b < 2; ++b) {
-        const uint32_t pb0 = movm_t(pack2<T>(sc[b][0], sc[b][1]));  // rows 0-7 of the block
-        const uint32_t pb1 = movm_t(pack2<T>(sc[b][2], sc[b][3]));  // rows 8-15
-        const int row = lo + 16 * b + (lane & 7) + 8 * (jm >> 1);
-#pragma unroll
-        for (int t = 0; t < NS; ++t) {
-          const int h = (16 * t) >> 6;
-          const int c = ((16 * t) & 63) / 8 + (jm & 1);
-          uint32_t r0, r1, r2, r3;
-          ldsm_x4_t(vbase + h * HALF + swz(row, c), r0, r1, r2, r3);
-          mma16816<T>(o[t], r0, r1, r2, r3, pb0, pb1);
-        }
+      for (int u = 0; u < NS; ++u) {
+        const int h = (16 * u) >> 6;
+        const int c = ((16 * u) & 63) / 8 + (jm & 1);
+        uint32_t r0_, r1_, r2_, r3_;
+        ldsm_x4_t(vbase + h * HALF + swz(row, c), r0_, r1_, r2_, r3_);
+        mma16816<T>(o[u], r0_, r1_, r2_, r3_, pb0, pb1);
       }
     }
     __syncwarp();  // the warp is done with its rows of this stage
-    if (lane == 0 && i + nstages < ntiles) issue(i + nstages, warp);
+    if (lane == 0 && t + kTcStages < ntiles) issue(t + kTcStages);
+  }
+  // the lane-held sums over the warp's rows
+#pragma unroll
+  for (int off = 4; off < 32; off <<= 1) {
+    l0 += __shfl_xor_sync(0xffffffffu, l0, off);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, off);
   }
 
-  // ---- hand the warp partials to the shared merge (tile region reused once
-  // every warp is done with its last tile)
+  // ---- merge the eight warps (the stage region is free: every load issued
+  // has been waited for), then the segment's CTAs of this cluster
   __syncthreads();
   float* wm = reinterpret_cast<float*>(smem);
-  float* wl = wm + kAttnWarps * G;
-  float* wo = wl + kAttnWarps * G;
+  float* wl = wm + NW * G;
+  float* wo = wl + NW * G;
+  float* Po = wo + NW * G * D;  // this CTA's partial: Po [G*D], Pm, Pl [G]
+  float* Pm = Po + G * D;
+  float* Pl = Pm + G;
   const int g0 = 2 * tig, g1 = 2 * tig + 1;
   if (gid == 0) {
     if (g0 < G) {
@@ -356,50 +402,196 @@ __global__ void __launch_bounds__(kAttnThreads)
     }
   }
 #pragma unroll
-  for (int t = 0; t < NS; ++t) {
-    const int d0 = 16 * t + gid, d1 = d0 + 8;
+  for (int u = 0; u < NS; ++u) {
+    const int d0 = 16 * u + gid, d1 = d0 + 8;
     if (g0 < G) {
-      wo[(warp * G + g0) * D + d0] = o[t][0];
-      wo[(warp * G + g0) * D + d1] = o[t][2];
+      wo[(warp * G + g0) * D + d0] = o[u][0];
+      wo[(warp * G + g0) * D + d1] = o[u][2];
     }
     if (g1 < G) {
-      wo[(warp * G + g1) * D + d0] = o[t][1];
-      wo[(warp * G + g1) * D + d1] = o[t][3];
+      wo[(warp * G + g1) * D + d0] = o[u][1];
+      wo[(warp * G + g1) * D + d1] = o[u][3];
     }
   }
   __syncthreads();
-  attn_finish<T, D, G>(p, smem, seg, j, cid, ncl);
+  for (int i = 4 * tid; i < G * D; i += 4 * kTcThreads) {
+    const int g = i / D, d = i % D;
+    float mx = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) mx = fmaxf(mx, wm[w * G + g]);
+    const float bse = (mx == -INFINITY) ? 0.f : mx;
+    float ls = 0.f;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int w = 0; w < NW; ++w) {
+      const float f = ex2(wm[w * G + g] - bse);
+      fma4(acc, *reinterpret_cast<const float4*>(wo + (w * G + g) * D + d), f);
+      ls += wl[w * G + g] * f;
+    }
+    *reinterpret_cast<float4*>(Po + i) = acc;
+    if (d == 0) {
+      Pm[g] = mx;
+      Pl[g] = ls;
+    }
+  }
+  cluster_arrive();  // CTA partials visible to the cluster
+  cluster_wait();
+  if (active && crank == leader && !(to_part && it.y >= total && it.y > 0)) {
+    float* part_out = to_part ? p.partials + int64_t(part) * PartIO<D, G>::kStride : nullptr;
+    for (int i = 4 * tid; i < G * D; i += 4 * kTcThreads) {
+      const int g = i / D;
+      // every rank's (max, sum, o) first, so the remote loads overlap
+      float pm[kTcMaxCluster], pl[kTcMaxCluster];
+      float4 po[kTcMaxCluster];
+#pragma unroll
+      for (int r = 0; r < kTcMaxCluster; ++r) {
+        if (r < nranks) {
+          pm[r] = *cluster.map_shared_rank(Pm + g, leader + r);
+          pl[r] = *cluster.map_shared_rank(Pl + g, leader + r);
+          po[r] = *reinterpret_cast<const float4*>(cluster.map_shared_rank(Po + i, leader + r));
+        } else {
+          pm[r] = -INFINITY;
+          pl[r] = 0.f;
+          po[r] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+      }
+      float mx = -INFINITY;
+#pragma unroll
+      for (int r = 0; r < kTcMaxCluster; ++r) mx = fmaxf(mx, pm[r]);
+      const float bse = (mx == -INFINITY) ? 0.f : mx;
+      float ls = 0.f;
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int r = 0; r < kTcMaxCluster; ++r) {
+        const float f = ex2(pm[r] - bse);
+        fma4(acc, po[r], f);
+        ls += pl[r] * f;
+      }
+      if (!to_part) {
+        attn_store4<T, D, G>(p, seg, i, mx, ls, acc);
+      } else {
+        PartIO<D, G>::st(part_out + i, acc);
+        if (i % D == 0) {
+          part_out[G * D + g] = mx;
+          part_out[G * D + G + g] = ls;
+        }
+      }
+    }
+  }
+  cluster_arrive();  // keep this CTA's shared memory until its leader has read it
+  cluster_wait();
 }
 
-// one stage = K + V of one 128-row tile; a CTA streaming several tiles keeps
-// up to three stages (192 KB at head_dim 128) in flight
-constexpr int kMmaStageBytes(int D) { return 2 * (D / 64) * kMmaTileRows * 128; }
+// Merge of the cluster partials of a segment that spans several clusters
+// (plan combine entry blockIdx.x, head blockIdx.y), in order, after the
+// attention kernel has finished.  The threads form groups of D/4 (one float4
+// column each); group j takes partials j, j + groups, ... with all its loads
+// in flight at once, and the groups are combined in order in shared memory.
+template <typename T, int D, int G>
+__global__ void __launch_bounds__(kAttnThreads) decode_attn_combine_kernel(const AttnParams p,
+                                                                           const AttnPlanView pv) {
+  using IO = PartIO<D, G>;
+  constexpr int C4 = D / 4;                  // float4 columns of one head
+  constexpr int NG = kAttnThreads / C4;      // thread groups
+  constexpr int B = 16;                      // loads in flight per thread and round
+  __shared__ float sm[NG], sl[NG];
+  __shared__ float4 so[NG][C4];
+  pdl_launch_dependents();
+  pdl_wait();  // the attention kernel's partials are complete and visible
+  const int4 e = __ldg(pv.comb + blockIdx.x);
+  const int g = blockIdx.y;
+  const int seg = e.x, first = e.y, n = e.z;
+  if (seg < 0 || seg >= p.num_segs || first < 0 || n < 1 || first + n > pv.parts) {
+    if (threadIdx.x == 0) atomicOr(p.err, WNW_DEVERR_BAD_INDEX);
+    return;
+  }
+  const int total = seg_total(p, seg);
+  int n_act = 1;  // partials whose range starts below the row count (a prefix; the first always counts)
+  while (n_act < n && __ldg(pv.part_r0 + first + n_act) < total) ++n_act;
+  const int col = threadIdx.x % C4, grp = threadIdx.x / C4;
+  const float* base = p.partials + int64_t(first) * IO::kStride;
+  float mx = -INFINITY, ls = 0.f;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int c0 = grp; c0 < n_act; c0 += NG * B) {
+    float bm[B], bl[B];
+    float4 bo[B];
+#pragma unroll
+    for (int u = 0; u < B; ++u) {
+      const int c = c0 + u * NG;
+      if (c < n_act) {
+        const float* pc = base + int64_t(c) * IO::kStride;
+        bm[u] = __ldcg(pc + G * D + g);
+        bl[u] = __ldcg(pc + G * D + G + g);
+        bo[u] = IO::ld(pc + g * D + 4 * col);
+      } else {
+        bm[u] = -INFINITY;
+        bl[u] = 0.f;
+        bo[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+    float mn = mx;
+#pragma unroll
+    for (int u = 0; u < B; ++u) mn = fmaxf(mn, bm[u]);
+    const float bse = (mn == -INFINITY) ? 0.f : mn;
+    const float a = ex2(mx - bse);
+    scale4(acc, a);
+    ls *= a;
+#pragma unroll
+    for (int u = 0; u < B; ++u) {
+      const float f = ex2(bm[u] - bse);
+      fma4(acc, bo[u], f);
+      ls += bl[u] * f;
+    }
+    mx = mn;
+  }
+  if (col == 0) {
+    sm[grp] = mx;
+    sl[grp] = ls;
+  }
+  so[grp][col] = acc;
+  __syncthreads();
+  if (grp != 0) return;
+  float m = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < NG; ++j) m = fmaxf(m, sm[j]);
+  const float bse = (m == -INFINITY) ? 0.f : m;
+  float l = 0.f;
+  float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+  for (int j = 0; j < NG; ++j) {
+    const float f = ex2(sm[j] - bse);
+    fma4(o, so[j][col], f);
+    l += sl[j] * f;
+  }
+  attn_store4<T, D, G>(p, seg, g * D + 4 * col, m, l, o);
+}
 
-constexpr int mma_smem_bytes(int D, int nstages) { return nstages * kMmaStageBytes(D) + 1024; }
+// three stages of K + V 128-row tiles (192 KB at head_dim 128); the merge
+// reuses them
+constexpr int mma_smem_bytes(int D) { return kTcStages * 2 * (D / 64) * kTcTileRows * 128 + 1024; }
 
 template <typename T, int D, int G>
 wnw_status configure_attn_mma() {
-  auto kern = decode_attn_mma_kernel<T, D, G>;
   static bool configured = false;
   if (!configured) {
-    WNW_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      mma_smem_bytes(D, kMmaMaxStages)));
+    auto kern = decode_attn_mma_kernel<T, D, G>;
+    WNW_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, mma_smem_bytes(D)));
     WNW_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
     configured = true;
   }
   return WNW_OK;
 }
 
-// Clusters of `cs` CTAs of the kernel that can be resident at once with
-// `nstages` stages of shared memory (0 when none fit).
+// Clusters of `cs` CTAs of the tensor-core kernel that fit the device at
+// once (0 when none fit).
 template <typename T, int D, int G>
-wnw_status attn_mma_active_clusters(int cs, int nstages, int* n) {
+wnw_status attn_mma_active_clusters(int cs, int* n) {
   const wnw_status st = configure_attn_mma<T, D, G>();
   if (st != WNW_OK) return st;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(cs, 1, 1);
-  cfg.blockDim = dim3(kAttnThreads, 1, 1);
-  cfg.dynamicSmemBytes = mma_smem_bytes(D, nstages);
+  cfg.blockDim = dim3(kTcThreads, 1, 1);
+  cfg.dynamicSmemBytes = mma_smem_bytes(D);
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = cs;
@@ -413,38 +605,56 @@ wnw_status attn_mma_active_clusters(int cs, int nstages, int* n) {
 
 template <typename T, int D, int G>
 wnw_status launch_attn_mma(const wnw_decode_attn_args* a, cudaStream_t stream) {
-  auto kern = decode_attn_mma_kernel<T, D, G>;
   {
     const wnw_status st = configure_attn_mma<T, D, G>();
     if (st != WNW_OK) return st;
   }
-  WNW_CHECK_ARG(a->split_rows >= kMmaTileRows && a->split_rows % kMmaTileRows == 0,
-                "split_rows %d must be a positive multiple of the tensor-core tile (%d rows)", a->split_rows,
-                kMmaTileRows);
-  const int tiles = a->split_rows / kMmaTileRows;
-  const int nstages = mma_stages(tiles);
-  const int smem = mma_smem_bytes(D, nstages);
+  WNW_CHECK_ARG(a->plan != nullptr && a->plan_ctas > 0 && a->plan_parts >= 0 && a->plan_combine >= 0,
+                "the tensor-core path needs a work plan (wnw_attn_plan): plan, plan_ctas, plan_parts, "
+                "plan_combine");
+  WNW_CHECK_ARG(a->cluster_size >= 1 && a->cluster_size <= kTcMaxCluster && a->plan_ctas % a->cluster_size == 0,
+                "cluster_size %d must be the plan's (1..16, dividing its %d CTAs)", a->cluster_size, a->plan_ctas);
+  WNW_CHECK_ARG(a->plan_combine == 0 || a->plan_parts > 0, "a plan with combine entries has partials");
   WNW_CHECK_ARG(a->store_rows > 0 && a->store_rows < (int64_t(1) << 31), "store_rows must be in (0, 2^31)");
+  WNW_CHECK_ARG(aligned16(a->plan), "plan must be 16-byte aligned");
   CUtensorMap tk, tv;
-  if (!kv_tensor_map(&tk, a->k_store, a->store_rows, D, a->dtype, kMmaWarpRows) ||
-      !kv_tensor_map(&tv, a->v_store, a->store_rows, D, a->dtype, kMmaWarpRows))
+  if (!kv_tensor_map(&tk, a->k_store, a->store_rows, D, a->dtype, kTcWarpRows) ||
+      !kv_tensor_map(&tv, a->v_store, a->store_rows, D, a->dtype, kTcWarpRows))
     return WNW_ERR_CUDA;
   AttnParams p = make_params(a);
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(a->n_clusters * a->cluster_size, 1, 1);
-  cfg.blockDim = dim3(kAttnThreads, 1, 1);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = stream;
+  AttnPlanView pv;
+  const int64_t cta_at = 8;
+  const int64_t part_at = cta_at + 4 * int64_t(a->plan_ctas);
+  const int64_t comb_at = part_at + (int64_t(a->plan_parts) + 3) / 4 * 4;
+  pv.cta = reinterpret_cast<const int4*>(a->plan + cta_at);
+  pv.part_r0 = a->plan + part_at;
+  pv.comb = reinterpret_cast<const int4*>(a->plan + comb_at);
+  pv.parts = a->plan_parts;
+  pv.ready = (a->flags & WNW_ATTN_ROWS_READY) ? 1 : 0;
   cudaLaunchAttribute attr[2];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = a->cluster_size;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = a->cluster_size;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(a->plan_ctas, 1, 1);
+  cfg.blockDim = dim3(kTcThreads, 1, 1);
+  cfg.dynamicSmemBytes = mma_smem_bytes(D);
+  cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  WNW_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, p, tk, tv, tiles, nstages));
+  WNW_CUDA_TRY(cudaLaunchKernelEx(&cfg, decode_attn_mma_kernel<T, D, G>, p, pv, tk, tv));
+  if (a->plan_combine > 0) {
+    cudaLaunchConfig_t c2 = {};
+    c2.gridDim = dim3(a->plan_combine, G, 1);
+    c2.blockDim = dim3(kAttnThreads, 1, 1);
+    c2.stream = stream;
+    c2.attrs = attr;
+    c2.numAttrs = 1;
+    WNW_CUDA_TRY(cudaLaunchKernelEx(&c2, decode_attn_combine_kernel<T, D, G>, p, pv));
+  }
   return WNW_OK;
 }
 

@@ -91,11 +91,16 @@ extern "C" wnw_status wnw_decode_attn_noalloc(const wnw_decode_attn_args* a, voi
   using namespace wnw;
   WNW_CHECK_ARG(a != nullptr, "null args");
   WNW_CHECK_ARG(a->err != nullptr, "err (a device word the caller owns) is required");
-  WNW_CHECK_ARG(a->n_clusters >= 0 && a->group >= 1 && a->head_dim > 0 && a->num_segs >= 0, "bad sizes");
-  const int64_t need = int64_t(a->n_clusters) * a->group * (a->head_dim + 2);
+  WNW_CHECK_ARG(a->n_clusters >= 0 && a->plan_parts >= 0 && a->group >= 1 && a->head_dim > 0 && a->num_segs >= 0,
+                "bad sizes");
+  // partial slots: the plan's cluster partials (tensor-core path) or one per cluster
+  const bool plan = a->plan != nullptr;
+  const int slots = plan ? a->plan_parts : a->n_clusters;
+  const int64_t need = int64_t(slots) * a->group * (a->head_dim + 2);
   if (need > WNW_NOALLOC_MAX_PARTIAL_FLOATS) {
-    set_error("%lld partial floats needed (%d clusters x group %d x (head_dim %d + 2)); the static scratch holds %d",
-              static_cast<long long>(need), a->n_clusters, a->group, a->head_dim, WNW_NOALLOC_MAX_PARTIAL_FLOATS);
+    set_error("%lld partial floats needed (%d %s x group %d x (head_dim %d + 2)); the static scratch holds %d",
+              static_cast<long long>(need), slots, plan ? "plan partials" : "clusters", a->group, a->head_dim,
+              WNW_NOALLOC_MAX_PARTIAL_FLOATS);
     return WNW_ERR_CAPACITY;
   }
   if (a->num_segs > WNW_NOALLOC_MAX_SEGS) {
@@ -108,7 +113,7 @@ extern "C" wnw_status wnw_decode_attn_noalloc(const wnw_decode_attn_args* a, voi
   wnw_decode_attn_args b = *a;
   b.partials = static_cast<float*>(base);
   b.counters = reinterpret_cast<int32_t*>(static_cast<unsigned char*>(base) + kPartialBytes);
-  if (b.num_segs > 0)
+  if (!plan && b.num_segs > 0)  // the cluster path's arrival counters start at zero
     WNW_CUDA_TRY(cudaMemsetAsync(b.counters, 0, size_t(b.num_segs) * 4, static_cast<cudaStream_t>(stream)));
   return wnw_decode_attn(&b, stream);
 }

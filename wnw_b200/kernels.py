@@ -19,12 +19,19 @@ def _count(n=1):
 
 
 def split_rows(dtype, head_dim):
+    """Rows per CTA of the CUDA-core kernel (0 for the tensor-core path)."""
     return N.lib.wnw_split_rows(N.dtype_code(dtype), int(head_dim))
 
 
+def uses_plan(dtype, head_dim):
+    """True when 16-bit K/V with this head_dim take the tensor-core kernel,
+    which is launched from a work plan (``attn_plan``)."""
+    return dtype in (torch.bfloat16, torch.float16) and int(head_dim) in (64, 128)
+
+
 def attn_launch_shape(dtype, head_dim, seg_cap):
-    """(split_rows, cluster_size) for one layer's capacities
-    (``wnw_attn_launch_shape``; needs the CUDA device for 16-bit head_dim 64/128)."""
+    """(split_rows, cluster_size) of the CUDA-core kernel for one layer's
+    capacities (``wnw_attn_launch_shape``)."""
     cap = np.ascontiguousarray(np.asarray(seg_cap, dtype=np.int32))
     split, cs = C.c_int(), C.c_int()
     N.call("wnw_attn_launch_shape", N.dtype_code(dtype), int(head_dim), N.ptr(cap), cap.size, C.byref(split),
@@ -52,6 +59,61 @@ def build_work_table(seg_cap, split, cluster_size):
     return work[:n.value]
 
 
+def attn_plan(seg_cap, sm_count=None, max_cluster=None):
+    """(numpy int32 plan, info) of the tensor-core kernel for one layer's
+    capacities (``wnw_attn_plan``; None: the current device's SMs and
+    largest cluster).  info = dict(ctas, cluster, parts, combine)."""
+    cap = np.ascontiguousarray(np.asarray(seg_cap, dtype=np.int32))
+    info = N.AttnPlanInfo()
+    args = (N.ptr(cap), cap.size, int(sm_count or 0), int(max_cluster or 0))
+    N.call("wnw_attn_plan", *args, None, 0, C.byref(info))
+    plan = np.zeros(int(info.ints), np.int32)
+    N.call("wnw_attn_plan", *args, N.ptr(plan), plan.size, C.byref(info))
+    return plan, dict(ctas=info.ctas, cluster=info.cluster, parts=info.parts, combine=info.combine)
+
+
+class AttnWork:
+    """Launch layout of one layer's decode attention, from its slot
+    capacities: the work plan of the tensor-core kernel, or the cluster work
+    table (rows per CTA ``split``, ``cluster_size``) of the CUDA-core kernel.
+    ``slots`` = partial states the layout can write (the scratch size),
+    ``table`` = the device tensor the launch reads."""
+
+    def __init__(self, dtype, head_dim, seg_cap, device, sm_count=None, max_cluster=None, split=None,
+                 cluster_size=None):
+        self.plan = uses_plan(dtype, head_dim)
+        if self.plan:
+            p, info = attn_plan(seg_cap, sm_count, max_cluster)
+            self.table = torch.from_numpy(p).to(device)
+            self.ctas, self.cluster_size = info["ctas"], info["cluster"]
+            self.parts, self.combine = info["parts"], info["combine"]
+            self.slots, self.split = max(1, self.parts), 0
+        else:
+            if split is None or cluster_size is None:
+                split, cluster_size = attn_launch_shape(dtype, head_dim, seg_cap)
+            w = build_work_table(seg_cap, split, cluster_size)
+            self.table = torch.from_numpy(w).to(device)
+            self.split, self.cluster_size = split, cluster_size
+            self.slots = self.n_clusters = w.shape[0]
+            self.ctas, self.parts, self.combine = 0, 0, 0
+
+    @property
+    def launches(self):
+        """Kernel launches of one attention call with this layout."""
+        return 1 + int(self.plan and self.combine > 0)
+
+    def fill(self, a):
+        """Write the layout fields of a ``DecodeAttnArgs``."""
+        if self.plan:
+            a.plan = self.table.data_ptr()
+            a.plan_ctas, a.plan_parts, a.plan_combine = self.ctas, self.parts, self.combine
+            a.work, a.n_clusters, a.cluster_size, a.split_rows = None, 0, self.cluster_size, 0
+        else:
+            a.plan, a.plan_ctas, a.plan_parts, a.plan_combine = None, 0, 0, 0
+            a.work = self.table.data_ptr()
+            a.n_clusters, a.cluster_size, a.split_rows = self.slots, self.cluster_size, self.split
+
+
 class AttnScratch:
     """Scratch of the decode-attention kernel: per-cluster partial states and
     per-segment arrival counters (zeroed once; the kernel leaves them zero),
@@ -68,12 +130,13 @@ class AttnScratch:
         return (n_clusters * group * (head_dim + 2) <= self.partials.numel() and num_segs <= self.counters.numel())
 
 
-def make_attn_args(dtype, S, G, D, k_store, v_store, seg_base, seg_len, work, cluster_size, scale, scratch,
-                   seg_cap=None, num_kv_heads=None, score=None, split=None):
+def make_attn_args(dtype, S, G, D, k_store, v_store, seg_base, seg_len, work, scale, scratch,
+                   seg_cap=None, num_kv_heads=None, score=None, flags=0):
     """A reusable ``wnw_decode_attn_args`` with everything but q / new rows /
-    out filled in (the per-layer constant part of a decode step).  The struct
-    keeps references to every tensor it points at, so temporaries passed in
-    stay alive as long as the arguments do."""
+    out filled in (the per-layer constant part of a decode step); ``work`` is
+    the layer's ``AttnWork``.  The struct keeps references to every tensor it
+    points at, so temporaries passed in stay alive as long as the arguments
+    do."""
     a = N.DecodeAttnArgs()
     a._keep = (k_store, v_store, seg_base, seg_len, work, scratch, seg_cap, score)
     a.dtype = N.dtype_code(dtype)
@@ -82,10 +145,7 @@ def make_attn_args(dtype, S, G, D, k_store, v_store, seg_base, seg_len, work, cl
     a.k_store, a.v_store = k_store.data_ptr(), v_store.data_ptr()
     a.seg_base, a.seg_len = seg_base.data_ptr(), seg_len.data_ptr()
     a.seg_cap = seg_cap.data_ptr() if seg_cap is not None else None
-    a.work = work.data_ptr()
-    a.n_clusters = work.shape[0]
-    a.cluster_size = cluster_size
-    a.split_rows = split or split_rows(dtype, D)
+    work.fill(a)
     a.scale = float(scale)
     if score is not None:
         a.score_slot = score["slot"].data_ptr()
@@ -98,6 +158,7 @@ def make_attn_args(dtype, S, G, D, k_store, v_store, seg_base, seg_len, work, cl
     a.counters = scratch.counters.data_ptr()
     a.err = scratch.err.data_ptr()
     a.store_rows = k_store.shape[0]
+    a.flags = int(flags)
     return a
 
 
@@ -110,7 +171,7 @@ def launch_attn(args, q, new_k, new_v, out, stream_handle):
     st = N.lib.wnw_decode_attn(C.byref(args), stream_handle)
     if st:
         N.check(st, "wnw_decode_attn")
-    LAUNCHES[0] += 1
+    LAUNCHES[0] += 1 + int(bool(args.plan) and args.plan_combine > 0)
     return out
 
 
@@ -131,45 +192,24 @@ def host_device_pointer(t):
     return out.value
 
 
-def decode_attention(q, k_store, v_store, seg_base, seg_len, work, cluster_size, scale, scratch,
+def decode_attention(q, k_store, v_store, seg_base, seg_len, work, scale, scratch,
                      new_k=None, new_v=None, seg_cap=None, out=None, num_kv_heads=None, score=None,
-                     stream=None, split=None):
-    """Launch ``wnw_decode_attn``.  q: [S, G, D]; work: device int32 [n, 2]
-    built with the same ``split`` (rows per CTA; default ``split_rows``).
+                     stream=None, flags=0):
+    """Launch ``wnw_decode_attn``.  q: [S, G, D]; ``work``: the layer's
+    ``AttnWork`` (built from capacities >= every segment's rows).
     ``score`` (optional) = dict(slot=int32[S], audio_start=int32[B], audio_end=int32[B],
     logits=fp32 buffer, logits_off=int64[n_slots], stats=fp32 [S, 2, G])."""
     S, G, D = q.shape
     if out is None:
         out = torch.empty_like(q)
-    a = N.DecodeAttnArgs()
-    a.dtype = N.dtype_code(q.dtype)
-    a.head_dim, a.group, a.num_segs = D, G, S
-    a.num_kv_heads = num_kv_heads if num_kv_heads is not None else S
+    a = make_attn_args(q.dtype, S, G, D, k_store, v_store, seg_base, seg_len, work, scale, scratch,
+                       seg_cap=seg_cap, num_kv_heads=num_kv_heads, score=score, flags=flags)
     a.q = q.data_ptr()
     a.new_k = new_k.data_ptr() if new_k is not None else None
     a.new_v = new_v.data_ptr() if new_v is not None else None
-    a.k_store, a.v_store = k_store.data_ptr(), v_store.data_ptr()
-    a.seg_base, a.seg_len = seg_base.data_ptr(), seg_len.data_ptr()
-    a.seg_cap = seg_cap.data_ptr() if seg_cap is not None else None
-    a.work = work.data_ptr()
-    a.n_clusters = work.shape[0]
-    a.cluster_size = cluster_size
-    a.split_rows = split or split_rows(q.dtype, D)
     a.out = out.data_ptr()
-    a.scale = float(scale)
-    if score is not None:
-        a.score_slot = score["slot"].data_ptr()
-        a.audio_start = score["audio_start"].data_ptr()
-        a.audio_end = score["audio_end"].data_ptr()
-        a.logits = score["logits"].data_ptr()
-        a.logits_off = score["logits_off"].data_ptr()
-        a.stats = score["stats"].data_ptr() if score.get("stats") is not None else None
-    a.partials = scratch.partials.data_ptr()
-    a.counters = scratch.counters.data_ptr()
-    a.err = scratch.err.data_ptr()
-    a.store_rows = k_store.shape[0]
     N.check(N.lib.wnw_decode_attn(C.byref(a), N.stream_ptr(stream)), "wnw_decode_attn")
-    _count()
+    _count(work.launches)
     return out
 
 
@@ -286,21 +326,19 @@ def check_device_error(err_tensor):
                                   (N.DEVERR_LEN_MISMATCH, "segment length disagrees with the plan"),
                                   (N.DEVERR_CAPACITY, "segment exceeds its slot capacity"),
                                   (N.DEVERR_PEER_TIMEOUT, "tensor-parallel peer timed out"),
-                                  (N.DEVERR_BAD_INDEX, "device fetch plan: index out of range")) if v & bit]
+                                  (N.DEVERR_BAD_INDEX, "device plan or attention plan: index out of range")) if v & bit]
         raise N.WnwError(5 if v & N.DEVERR_MBAR_TIMEOUT else 4, "device", ", ".join(names))
 
 
-def packed_attention(q, k, v, cu, scale, scratch=None, cluster_size=None):
+def packed_attention(q, k, v, cu, scale, scratch=None):
     """Attention over a reference-layout packed buffer ([T, D] + cu): the slot
     kernel with seg_base = cu[:-1], seg_len = diff(cu) and no append."""
     S, G, D = q.shape
     cu64 = cu.to(torch.int64)
     lens = (cu64[1:] - cu64[:-1]).to(torch.int32)
     lens_host = lens.cpu().numpy()
-    split = split_rows(q.dtype, D)
-    cs = cluster_size or choose_cluster_size(int(lens_host.max()) if S else 0, split)
-    # capacity = length - 1 so that ceil((cap+1)/split) covers exactly len rows
-    work = torch.from_numpy(build_work_table(np.maximum(lens_host - 1, 0), split, cs)).to(q.device)
-    if scratch is None or not scratch.fits(work.shape[0], G, D, S):
-        scratch = AttnScratch(q.device, work.shape[0], G, D, S)
-    return decode_attention(q.contiguous(), k, v, cu64[:-1].contiguous(), lens, work, cs, scale, scratch)
+    # capacity = length - 1: the layout then covers exactly len rows
+    work = AttnWork(q.dtype, D, np.maximum(lens_host - 1, 0), q.device)
+    if scratch is None or not scratch.fits(work.slots, G, D, S):
+        scratch = AttnScratch(q.device, work.slots, G, D, S)
+    return decode_attention(q.contiguous(), k, v, cu64[:-1].contiguous(), lens, work, scale, scratch)

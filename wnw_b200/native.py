@@ -53,7 +53,17 @@ class DecodeAttnArgs(C.Structure):
         ("out", P), ("scale", C.c_float),
         ("score_slot", P), ("audio_start", P), ("audio_end", P), ("logits", P), ("logits_off", P),
         ("stats", P), ("partials", P), ("counters", P), ("err", P), ("store_rows", C.c_int64),
+        ("plan", P), ("plan_ctas", C.c_int), ("plan_parts", C.c_int), ("plan_combine", C.c_int),
+        ("flags", C.c_int),
     ]
+
+
+ATTN_ROWS_READY = 1
+
+
+class AttnPlanInfo(C.Structure):
+    _fields_ = [("ctas", C.c_int), ("cluster", C.c_int), ("parts", C.c_int), ("combine", C.c_int),
+                ("ints", C.c_int64)]
 
 
 TP_MAX_RANKS = 8
@@ -89,6 +99,7 @@ _sig("wnw_decode_attn_noalloc", _S, C.POINTER(DecodeAttnArgs), P)
 _sig("wnw_split_rows", C.c_int, C.c_int, C.c_int)
 _sig("wnw_attn_launch_shape", _S, C.c_int, C.c_int, P, C.c_int, C.POINTER(C.c_int), C.POINTER(C.c_int))
 _sig("wnw_build_work_table", _S, P, C.c_int, C.c_int, C.c_int, P, C.c_int, C.POINTER(C.c_int))
+_sig("wnw_attn_plan", _S, P, C.c_int, C.c_int, C.c_int, P, C.c_int64, C.POINTER(AttnPlanInfo))
 _sig("wnw_advance_lengths", _S, P, C.c_int64, P)
 _sig("wnw_score_finalize", _S, P, P, P, P, P, P, C.c_int, C.c_int, P, C.c_int, P, P)
 _sig("wnw_chunk_topk", _S, P, P, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, P, P, P, P)
@@ -140,7 +151,7 @@ _sig("wnw_fetch_layers", _S, P, P, C.c_int64, P, P, P, C.c_int, P, P, C.c_int, P
 EXPORTS = [
     "wnw_abi_version", "wnw_status_string", "wnw_last_error", "wnw_decode_attn", "wnw_decode_attn_noalloc",
     "wnw_split_rows", "wnw_attn_launch_shape",
-    "wnw_build_work_table", "wnw_advance_lengths", "wnw_score_finalize", "wnw_chunk_topk",
+    "wnw_build_work_table", "wnw_attn_plan", "wnw_advance_lengths", "wnw_score_finalize", "wnw_chunk_topk",
     "wnw_rebuild_segments", "wnw_copy_segments", "wnw_interleave_append", "wnw_planner_create",
     "wnw_planner_destroy", "wnw_planner_set_config", "wnw_planner_set_seg_count",
     "wnw_planner_set_chunk_to_segs", "wnw_planner_set_class_b", "wnw_planner_set_restore_meta",
