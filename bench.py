@@ -77,8 +77,8 @@ def parse():
 
 
 # ------------------------------------------------------------------ set-up
-def wnw_config():
-    from wnw_b200.config import WnWConfig
+def wnw_config_fields():
+    """The WnWConfig fields of the workload (the reference's config schema)."""
     L, H, Hq = MODEL["L"], MODEL["Hkv"], MODEL["Hq"]
     G = Hq // H
     rng = np.random.default_rng(WNW["seed"])
@@ -87,9 +87,14 @@ def wnw_config():
     class_a = [(g // H) * Hq + (g % H) * G + j for g in a_kv for j in range(G)]
     class_b = [g for g in range(L * H) if g not in set(a_kv)]
     ret = [None if g in set(a_kv) else WNW["retention"] for g in range(L * H)]
-    return WnWConfig(chunk_size_s=float(WNW["chunk"]), overlap_s=0.0, token_rate=1.0, class_a=class_a,
-                     class_b=class_b, retention_ratios=ret, top_k_chunks=WNW["top_k"], eviction_lag=WNW["lag"],
-                     prefill_score_mode="last", num_layers=L, num_kv_heads=H, num_q_heads=Hq)
+    return dict(chunk_size_s=float(WNW["chunk"]), overlap_s=0.0, token_rate=1.0, class_a=class_a,
+                class_b=class_b, retention_ratios=ret, top_k_chunks=WNW["top_k"], eviction_lag=WNW["lag"],
+                prefill_score_mode="last", num_layers=L, num_kv_heads=H, num_q_heads=Hq)
+
+
+def wnw_config():
+    from wnw_b200.config import WnWConfig
+    return WnWConfig(**wnw_config_fields())
 
 
 def make_model(dev, seed):
@@ -130,30 +135,106 @@ class Recorder:
         return super().fused_decode_attention(l, q_flat, q, k_flat, v_flat, cu_k, scale)
 
 
-def record(dev, n_steps, seed):
-    """Run the random-init decoder through the session: prefill + n_steps
-    greedy decode steps; return the recorded hook inputs and model timing."""
-    from wnw_b200.adapters import LlamaFamilyAdapter
-    from wnw_b200.cache import B200WnWCache
-    from wnw_b200.session import WnWSession
+def reference_modules():
+    """(session module, WnWCache, WnWConfig, BaseModelAdapter) of the
+    reference's offline install in baseline/_ref, its session in the fused
+    attention mode (WNW_FUSED_ATTN=1)."""
+    import importlib
+    ref = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref, "algorithms")):
+        raise RuntimeError("baseline/_ref (offline install of the reference) not present")
+    os.environ["WNW_FUSED_ATTN"] = "1"
+    if ref not in sys.path:
+        sys.path.insert(0, ref)
+    sess = importlib.import_module("algorithms.wnw.code.session")
+    sess._FUSED_ATTN = True  # read once, at the module's import
+    return (sess, importlib.import_module("algorithms.wnw.code.cache").WnWCache,
+            importlib.import_module("algorithms.wnw.code.config").WnWConfig,
+            importlib.import_module("common.adapters.base").BaseModelAdapter)
 
-    class RecCache(Recorder, B200WnWCache):
+
+def reference_adapter(base_cls, audio_start, audio_end):
+    """The reference's BaseModelAdapter completed for the random-init Llama
+    decoder, with the audio span given explicitly (no audio encoder)."""
+    from transformers.models.llama.modeling_llama import apply_rotary_pos_emb
+
+    class BenchLlamaAdapter(base_cls):
+        name = "bench_llama"
+
+        def load(self, *a, **k): raise NotImplementedError
+        def _build_inputs(self, *a, **k): raise NotImplementedError
+        def get_decoder_layers(self, model): return model.model.layers
+        def get_text_config(self, model): return model.config
+
+        def locate_audio_tokens(self, input_ids, attention_mask, processor):
+            B = input_ids.shape[0]
+            return (torch.full((B,), audio_start, dtype=torch.int64, device=input_ids.device),
+                    torch.full((B,), audio_end, dtype=torch.int64, device=input_ids.device))
+
+        def compute_qkv(self, attn, h):
+            B, S, _ = h.shape
+            hd = attn.head_dim
+            return (attn.q_proj(h).view(B, S, -1, hd).transpose(1, 2),
+                    attn.k_proj(h).view(B, S, -1, hd).transpose(1, 2),
+                    attn.v_proj(h).view(B, S, -1, hd).transpose(1, 2))
+
+        def apply_rope(self, q, k, pe, attn): return apply_rotary_pos_emb(q, k, *pe)
+
+        def attention_meta(self, attn):
+            c = attn.config
+            return {"head_dim": attn.head_dim, "num_kv_heads": c.num_key_value_heads,
+                    "num_kv_groups": c.num_attention_heads // c.num_key_value_heads,
+                    "scaling": attn.scaling, "layer_idx": attn.layer_idx}
+
+        def prepare_for_inference(self, model): return {}
+        def restore_after_inference(self, model, state): pass
+        def generate(self, model, inputs, **kw): return model.generate(**inputs, **kw)
+        def get_logits(self, model, outputs): return outputs.logits
+        def get_text_model(self, model): return model
+        def get_audio_token_id(self, model): return 0
+        def build_analysis_inputs(self, *a, **k): raise NotImplementedError
+
+    return BenchLlamaAdapter()
+
+
+def record(dev, n_steps, seed, reference=False):
+    """Run the random-init decoder through the session: prefill + n_steps
+    greedy decode steps; return the recorded hook inputs and model timing.
+    ``reference``: through the reference's own session and cache (its
+    offline install in baseline/_ref) instead of this package's, so that the
+    reference arm runs none of this package's code."""
+    if reference:
+        sess_mod, CacheCls, CfgCls, base = reference_modules()
+        cfg = CfgCls(**wnw_config_fields())
+        Session = sess_mod.WnWSession
+    else:
+        from wnw_b200.cache import B200WnWCache as CacheCls
+        from wnw_b200.session import WnWSession as Session
+        cfg = wnw_config()
+
+    class RecCache(Recorder, CacheCls):
         pass
 
-    cfg = wnw_config()
     model = make_model(dev, seed)
     S0 = PROMPT["sink"] + PROMPT["audio"] + PROMPT["tail"]
     a0, a1 = PROMPT["sink"], PROMPT["sink"] + PROMPT["audio"]
-    cache = RecCache(cfg, MODEL["L"], MODEL["Hkv"], MODEL["Hq"], MODEL["D"], dev, max_decode_tokens=n_steps + 8)
+    if reference:
+        cache = RecCache(cfg, MODEL["L"], MODEL["Hkv"], MODEL["Hq"], MODEL["D"], dev, None)
+    else:
+        cache = RecCache(cfg, MODEL["L"], MODEL["Hkv"], MODEL["Hq"], MODEL["D"], dev, max_decode_tokens=n_steps + 8)
     cache.rec_prefill, cache.rec_steps = [], []
     g = torch.Generator(device=dev).manual_seed(seed)
     ids = torch.randint(1, MODEL["vocab"], (1, S0), device=dev, generator=g)
     with torch.no_grad():
         emb = model.get_input_embeddings()(ids)
         emb[:, a0:a1] = (torch.randn(1, a1 - a0, MODEL["hidden"], device=dev, generator=g) * 0.02).to(emb.dtype)
-    adapter = LlamaFamilyAdapter(a0, a1)
+    if reference:
+        adapter = reference_adapter(base, a0, a1)
+    else:
+        from wnw_b200.adapters import LlamaFamilyAdapter
+        adapter = LlamaFamilyAdapter(a0, a1)
     times = []
-    with WnWSession(model, adapter, cache) as sess, torch.no_grad():
+    with Session(model, adapter, cache) as sess, torch.no_grad():
         sess.setup_audio(ids)
         out = model(inputs_embeds=emb, past_key_values=cache, use_cache=True, logits_to_keep=1)
         tok = out.logits[:, -1:].argmax(-1)
@@ -307,12 +388,15 @@ def run_value(rec, dev, K, W, shard=None, tier="host"):
     cache = fresh_cache(rec, dev, K + W, shard, tier)
     steps, scale, L = shard.step_inputs(rec["steps"]), rec["scale"], MODEL["L"]
 
+    selections = []  # per step: (top-k chunks, loaded segments) of sample 0
+
     def one(i):
         for l in range(L):
             q, k, v = steps[i][l]
             kk, vv, cu, _ = cache.decode_before_attn(l, k, v)
             shard.o_proj(l, cache.fused_decode_attention(l, q, None, kk, vv, cu, scale))
         cache.decode_all_layers_done()
+        selections.append((list(cache.last_topk[0]), sorted(cache.loaded_segments[0])))
 
     for i in range(W):
         one(i)
@@ -341,7 +425,7 @@ def run_value(rec, dev, K, W, shard=None, tier="host"):
     total_ms = t0.elapsed_time(t1)
     us, nbytes, n = attention_replay(cache, [steps[W + K - 1][l][0] for l in range(L)], reps=10)
     return dict(ms=total_ms, attn_us=us, attn_bytes=nbytes, attn_n=n, launches=launches, fetched_rows=fetched,
-                window=(wall0, wall1))
+                window=(wall0, wall1), selections=selections)
 
 
 def run_e2e(rec, dev, K, W, shard=None):
@@ -431,6 +515,29 @@ def run_reference_gpu(rec, dev, K, W):
                          prefill_global_topk=c0.prefill_global_topk, num_layers=c0.num_layers,
                          num_kv_heads=c0.num_kv_heads, num_q_heads=c0.num_q_heads)
         cache = RefCache(rcfg, MODEL["L"], MODEL["Hkv"], MODEL["Hq"], MODEL["D"], dev, None)
+        # the reference's own selection each step (cache.py:632-649): its
+        # chunk scores (fp32 cumsum on the GPU) and the top-k it takes
+        picks = []
+        orig = cache._compute_chunk_changes
+
+        def capture(b, scores):
+            if b == 0:  # its chunk scores, formed as it forms them (cache.py:636-640)
+                prefix = torch.zeros(scores.shape[0] + 1, dtype=torch.float32, device=scores.device)
+                torch.cumsum(scores, dim=0, out=prefix[1:])
+                cs = (prefix[cache._chunk_ends_t[b]] - prefix[cache._chunk_starts_t[b]]) / cache._chunk_lens_t[b]
+                picks.append((cs.float().cpu().numpy(), None))
+            return orig(b, scores)
+
+        orig_topk = cache._compute_chunk_changes_from_topk
+
+        def capture_topk(b, topk_chunks):
+            if b == 0 and picks and picks[-1][1] is None:
+                picks[-1] = (picks[-1][0], sorted(int(c) for c in topk_chunks))
+            return orig_topk(b, topk_chunks)
+
+        cache._compute_chunk_changes = capture
+        cache._compute_chunk_changes_from_topk = capture_topk
+        ref_loaded = []
         a0, a1 = rec["audio"]
         cache.setup_audio(torch.tensor([a0]), torch.tensor([a1]), None)
         torch.cuda.synchronize()
@@ -448,6 +555,7 @@ def run_reference_gpu(rec, dev, K, W):
                 kk, vv, cu, _ = cache.decode_before_attn(l, k, v)
                 cache.fused_decode_attention(l, q, None, kk, vv, cu, scale)
             cache.decode_all_layers_done()
+            ref_loaded.append(sorted(cache.loaded_segments[0]))
 
         for i in range(W):
             one(i)
@@ -460,11 +568,46 @@ def run_reference_gpu(rec, dev, K, W):
         e1.record()
         torch.cuda.synchronize()
         ms = e0.elapsed_time(e1) / n
+        for i in range(W + n, min(W + K, len(steps))):  # the rest of the replay, untimed, for the selections
+            one(i)
+        torch.cuda.synchronize()
         return {"value": 1e3 / ms, "unit": "tokens/s", "ms_per_step": ms, "steps": n, "prefill_compress_ms": pre,
                 "how": "the reference's WnWCache (Python planner, Triton kernels; fused attention + scoring) "
-                       "from baseline/_ref, same replay on this GPU; informational"}
+                       "from baseline/_ref, same replay on this GPU; informational",
+                "_picks": picks, "_loaded": ref_loaded}
     except Exception as e:  # report, never fail the bench on the comparison leg
         return {"unavailable": f"{type(e).__name__}: {e}"[:300]}
+
+
+def selection_agreement(ours, ref_picks, ref_loaded, top_k, tie_rel=1e-5):
+    """Step-by-step agreement of this cache's chunk selection with the
+    reference's own GPU cache on the same replay: top-k sets and loaded
+    segment sets, and, where the top-k differ, whether the reference's own
+    scores have a near tie at the k-th place (gap between its k-th and
+    (k+1)-th chunk score below tie_rel of its largest)."""
+    n = min(len(ours), len(ref_picks), len(ref_loaded))
+    eq_topk = eq_loaded = ties = 0
+    first_diff = None
+    for i in range(n):
+        o_top, o_loaded = ours[i]
+        r_scores, r_top = ref_picks[i]
+        if o_top == r_top:
+            eq_topk += 1
+        else:
+            srt = np.sort(np.asarray(r_scores, np.float64))[::-1]
+            gap = srt[top_k - 1] - srt[top_k] if len(srt) > top_k else np.inf
+            if gap <= tie_rel * max(abs(srt[0]), 1e-30):
+                ties += 1
+            elif first_diff is None:
+                first_diff = i
+        if o_loaded == ref_loaded[i]:
+            eq_loaded += 1
+    return {"steps": n, "topk_equal_steps": eq_topk, "loaded_equal_steps": eq_loaded,
+            "near_tie_steps": ties, "first_step_differing_beyond_ties": first_diff,
+            "how": "per decode step, sample 0: this cache's top-k chunks and loaded segments against the "
+                   "reference's own WnWCache (baseline/_ref, Triton + torch fp32 cumsum on the GPU) replaying "
+                   "the same recorded q/k/v; a differing top-k counts as a near tie when the reference's k-th "
+                   "and (k+1)-th chunk scores differ by < 1e-5 of its largest"}
 
 
 def h2d_link_probe(dev, mb=128, reps=5):
@@ -657,14 +800,16 @@ def main():
 
 
 def _main(a, rank, world, local, dist, dev, K, W, cfg_json, tp, clk):
-    # replicas record their own request; tensor-parallel ranks share one
-    rec = record(dev, W + K, seed=1000 + (0 if tp else rank))
-    shard = Shard(dev, rank, world, tp=tp, seed=2000, exchange=a.tp_exchange)
-    if tp:
-        cfg_json["parallelism"] += f", exchange {a.tp_exchange}"
-
     if a.impl == "reference":
-        n = max(1, min(a.cpu_steps, K))
+        # the reference arm runs none of this package's code: its inputs are
+        # recorded through the reference's own session and cache (on the
+        # GPU, untimed), then the CPU restatement replays them
+        n = max(1, K)
+        try:
+            rec = record(dev, W + n, seed=1000, reference=True)
+        except Exception as e:  # report, exit 0
+            print(json.dumps({"impl": "reference", "unavailable": f"{type(e).__name__}: {e}"[:300]}), flush=True)
+            return
         sec = cpu_replay(rec, n, start=W)
         v = 1.0 / sec
         line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s",
@@ -672,11 +817,18 @@ def _main(a, rank, world, local, dist, dev, K, W, cfg_json, tp, clk):
                 "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
                 "config": cfg_json,
                 "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
-                                 "sample": f"{n} decode steps (all 30 layers) replayed by the CPU oracle"},
+                                 "sample": f"{n} decode steps (all 30 layers, after {W} untimed) replayed by the "
+                                           "CPU oracle; inputs recorded through the reference's own session and "
+                                           "cache"},
                 "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
         print(json.dumps(line), flush=True)
         return
 
+    # replicas record their own request; tensor-parallel ranks share one
+    rec = record(dev, W + K, seed=1000 + (0 if tp else rank))
+    shard = Shard(dev, rank, world, tp=tp, seed=2000, exchange=a.tp_exchange)
+    if tp:
+        cfg_json["parallelism"] += f", exchange {a.tp_exchange}"
     val = run_value(rec, dev, K, W, shard)
     clk.__exit__(None, None, None)
     e2e = run_e2e(rec, dev, K, W, shard)
@@ -686,6 +838,10 @@ def _main(a, rank, world, local, dist, dev, K, W, cfg_json, tp, clk):
     # for comparison only: the reference offloads to host memory
     hbm = run_value(rec, dev, K, W, shard, tier="hbm") if not dist and not a.profile else None
     ref_gpu = run_reference_gpu(rec, dev, K, W) if not dist and not a.profile and not tp else None
+    agreement = None
+    if ref_gpu is not None and "_picks" in ref_gpu:
+        agreement = selection_agreement(val["selections"], ref_gpu.pop("_picks"), ref_gpu.pop("_loaded"),
+                                        WNW["top_k"])
     ms = val["ms"]
     if dist:
         t = torch.tensor([ms, e2e["ms"]], device=dev)
@@ -728,6 +884,7 @@ def _main(a, rank, world, local, dist, dev, K, W, cfg_json, tp, clk):
                              "ceiling), both measured in this run"},
         "model_decode_ms_per_token": rec["model_ms"],
         "reference_gpu": ref_gpu,
+        "selection_vs_reference_gpu": agreement,
         "offload_tier_hbm": ({"value": tokens / (hbm["ms"] * 1e-3), "ms_per_step": hbm["ms"] / K,
                               "how": "same replay with offload_tier='hbm' (class-B rows in device memory, no "
                                      "host-link traffic); not the headline, which offloads to host memory as "

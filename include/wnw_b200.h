@@ -75,6 +75,11 @@ const char* wnw_last_error(void);
  * [audio_start[b], audio_end[b]) into logits + logits_off[slot] ([t][g]) and
  * the merged per-head softmax statistics into stats[s] ([2][group]: max, sum),
  * from which wnw_score_finalize forms the class-A scores.
+ * The layout inputs -- seg_base, seg_cap, the plan or work table and the
+ * scoring tables (score_slot, audio_start / audio_end, logits_off) -- are
+ * read before the kernel waits for the preceding kernel in the stream
+ * (programmatic dependent launch): they must not be written by a kernel that
+ * may still run when the launch starts.
  * ------------------------------------------------------------------ */
 typedef struct wnw_decode_attn_args {
   int dtype;           /* wnw_dtype of q, k/v stores, new_k/new_v and out   */

@@ -162,6 +162,22 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   }
   __syncthreads();
 
+  // class-A scoring geometry: layout constants, read before the dependency wait
+  int a0 = 0, a1 = 0;
+  float* lg = nullptr;
+  if (active && p.score_slot != nullptr) {
+    const int slot = __ldg(p.score_slot + seg);
+    if (slot >= 0) {
+      const int b = seg / p.num_kv_heads;
+      a0 = __ldg(p.audio_start + b);
+      a1 = __ldg(p.audio_end + b);
+      lg = p.logits + __ldg(p.logits_off + slot);
+    }
+  }
+  // q comes from the preceding kernel: bring its lines into L2 now (L2 is the
+  // point of coherence, so the loads after the wait see the final values)
+  if (active && tid == 32) prefetch_l2(reinterpret_cast<const T*>(p.q) + int64_t(seg) * G * D, G * D * sizeof(T));
+
   int total = 0, rows = 0, ntiles = 0;
   auto schedule = [&]() {
     if (!active) return;
@@ -233,18 +249,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
     }
   }
-  int a0 = 0, a1 = 0;
-  float* lg = nullptr;
-  if (active && p.score_slot != nullptr) {
-    const int slot = p.score_slot[seg];
-    if (slot >= 0) {
-      const int b = seg / p.num_kv_heads;
-      a0 = p.audio_start[b];
-      a1 = p.audio_end[b];
-      lg = p.logits + p.logits_off[slot];
-    }
-  }
-
   // running softmax of this warp: per lane heads g0 = 2*tig, g1 = 2*tig+1;
   // the maxima are warp-uniform, the sums stay per lane until the end
   float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
