@@ -8,7 +8,8 @@
 //    summation order (8 interleaved partial sums over the layer-major /
 //    ascending-kv term list, combined in order);
 //  * wnw_chunk_topk computes the chunk means of cache.py:632-640 and the top-k
-//    of cache.py:648 (ties -> lower index) in one CTA per sample.  The prefix
+//    of cache.py:648 (ties -> lower index) in one CTA per sample, the top-k
+//    by ranking every chunk against all others in one pass.  The prefix
 //    sums are taken at segment boundaries only, accumulated in fp64 and rounded
 //    to fp32, which is what torch's CPU cumsum produces for an fp32 input.
 #include <algorithm>
@@ -33,14 +34,25 @@ __global__ void __launch_bounds__(kFinWarps * 32)
   const int i0 = term_off[b], i1 = term_off[b + 1];
   float sum = 0.f;
   if (t < n) {
-    for (int i = i0 + warp; i < i1; i += kFinWarps) {
-      const float* st = stats + stat_off[i];
-      const float* lg = logits + logit_off[i] + int64_t(t) * group;
-      const uint32_t mask = qmask[i];
-      float p = 0.f;
-      for (int g = 0; g < group; ++g)
-        if (mask & (1u << g)) p += ex2(lg[g] - __ldg(st + g)) / __ldg(st + group + g);
-      sum += p;
+    // terms w, w + 8, w + 16, ... added in that order; four terms' loads in
+    // flight at a time
+    constexpr int U = 4;
+    for (int i = i0 + warp; i < i1; i += U * kFinWarps) {
+      float p[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int ii = i + u * kFinWarps;
+        p[u] = 0.f;
+        if (ii < i1) {
+          const float* st = stats + __ldg(stat_off + ii);
+          const float* lg = logits + __ldg(logit_off + ii) + int64_t(t) * group;
+          const uint32_t mask = __ldg(qmask + ii);
+          for (int g = 0; g < group; ++g)
+            if (mask & (1u << g)) p[u] += ex2(__ldcs(lg + g) - __ldg(st + g)) / __ldg(st + group + g);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) sum += p[u];
     }
   }
   part[warp][lane] = sum;
@@ -73,9 +85,6 @@ __global__ void __launch_bounds__(kTopkThreads)
   const int nseg = (n + stride - 1) / stride;
   double* segsum = reinterpret_cast<double*>(smem);        // [nseg + 1], becomes the prefix
   float* cs = reinterpret_cast<float*>(segsum + nseg + 1);  // [nseg] chunk scores
-  uint8_t* taken = reinterpret_cast<uint8_t*>(cs + nseg);    // [nseg] selected flags
-  __shared__ float red_v[kTopkThreads / 32];
-  __shared__ int red_i[kTopkThreads / 32];
   __shared__ double carry;
   const float* a = acc + score_off[b];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -126,58 +135,21 @@ __global__ void __launch_bounds__(kTopkThreads)
     if (chunk_scores != nullptr) chunk_scores[chunk_off[b] + c] = v;
   }
   __syncthreads();
-  // 4. top-k by repeated block argmax over the untaken chunks; NaN ranks as -inf
-  for (int c = tid; c < nseg; c += kTopkThreads) taken[c] = 0;
-  __syncthreads();
+  // 4. top-k in one pass: a chunk's rank is the number of chunks that beat
+  // it (larger score, then lower index: a strict total order, so ranks are
+  // distinct); NaN ranks as -inf.  Chunks ranked below k write themselves.
   const int k = min(top_k, nseg);
-  for (int j = 0; j < top_k; ++j) {
-    if (j >= k) {
-      if (tid == 0) topk[b * top_k + j] = -1;
-      continue;
+  for (int j = k + tid; j < top_k; j += kTopkThreads) topk[b * top_k + j] = -1;
+  for (int c = tid; c < nseg; c += kTopkThreads) {
+    float v = cs[c];
+    if (isnan(v)) v = -INFINITY;
+    int rank = 0;
+    for (int o = 0; o < nseg && rank < k; ++o) {
+      float w = cs[o];
+      if (isnan(w)) w = -INFINITY;
+      rank += better(w, o, v, c) ? 1 : 0;
     }
-    float bv = -INFINITY;
-    int bi = 0x7fffffff;
-    for (int c = tid; c < nseg; c += kTopkThreads) {
-      if (taken[c]) continue;
-      float v = cs[c];
-      if (isnan(v)) v = -INFINITY;
-      if (better(v, c, bv, bi)) {
-        bv = v;
-        bi = c;
-      }
-    }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
-      const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
-      if (better(ov, oi, bv, bi)) {
-        bv = ov;
-        bi = oi;
-      }
-    }
-    if (lane == 0) {
-      red_v[warp] = bv;
-      red_i[warp] = bi;
-    }
-    __syncthreads();
-    if (warp == 0) {
-      bv = (lane < nwarps) ? red_v[lane] : -INFINITY;
-      bi = (lane < nwarps) ? red_i[lane] : 0x7fffffff;
-#pragma unroll
-      for (int off = 16; off > 0; off >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
-        const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
-        if (better(ov, oi, bv, bi)) {
-          bv = ov;
-          bi = oi;
-        }
-      }
-      if (lane == 0) {
-        topk[b * top_k + j] = bi;
-        taken[bi] = 1;
-      }
-    }
-    __syncthreads();
+    if (rank < k) topk[b * top_k + rank] = c;
   }
 }
 
@@ -204,7 +176,7 @@ namespace wnw {
 // shared memory needed for a sample with `max_audio` tokens
 inline size_t topk_smem(int max_audio, int stride) {
   const int nseg = (max_audio + stride - 1) / stride;
-  return size_t(nseg + 1) * sizeof(double) + size_t(nseg) * (sizeof(float) + 1) + 16;
+  return size_t(nseg + 1) * sizeof(double) + size_t(nseg) * sizeof(float) + 16;
 }
 }  // namespace wnw
 
