@@ -168,13 +168,17 @@ int wnw_split_rows(int dtype, int head_dim);
  * counterpart: the reference's kernels take one CTA per segment).  Segment s
  * may hold up to seg_cap[s] + 1 rows at a launch (its capacity plus the
  * step's token), counted in 32-row units.  Every CTA takes about the same
- * units -- an equal share of `sm_count` SMs, raised (to at most 1,536 rows)
- * so the longest segment fits one cluster of `max_cluster` CTAs -- and a
- * segment needing k CTAs gets k consecutive ranks of one cluster (clusters
- * hold the smallest power of two >= the largest such k, at most
- * max_cluster; short segments share clusters).  A segment needing more
- * CTAs than a cluster holds takes whole clusters, each writing a partial
- * that the combine kernel merges.  sm_count <= 0: the current device's;
+ * units -- an equal share of the CTA slots the device holds at once, raised
+ * (to at most 1,536 rows) so the longest segment fits one cluster of
+ * `max_cluster` CTAs -- and a segment needing k CTAs gets k consecutive
+ * ranks of one cluster (clusters hold the smallest power of two >= the
+ * largest such k, at most max_cluster; short segments share clusters).  When
+ * the longest segment does not fit one cluster that way, clusters hold at
+ * most 4 CTAs, the share grows until the plan fits the resident slots in one
+ * wave, and a segment needing more CTAs than a cluster holds takes whole
+ * clusters, each writing a partial that the combine kernel merges.
+ * sm_count <= 0: the current device's SMs and its resident clusters of the
+ * kernel (otherwise sm_count stands for the slots at every cluster size);
  * max_cluster <= 0: 16 when the device holds clusters of 16 of the kernel,
  * else 8.  Layout of `plan` (int32):
  *   [0..7]  ctas, cluster, parts, combine, 0, 0, 0, 0

@@ -221,6 +221,16 @@ def test_attn_plan_config2_layer_fits_one_cluster_per_segment():
         assert len(ranks) == (16 if seg < 2 else 3)
 
 
+@pytest.mark.parametrize("lens", [[120000] * 2 + [4000] * 6, [60000] * 8, [30000] * 2 + [3000] * 6])
+def test_attn_plan_long_segments_fit_one_wave(lens):
+    """Layers whose longest segment needs more CTAs than a cluster holds:
+    clusters of at most 4 and no more CTAs than the (148) slots, so the
+    launch runs in one wave; long segments are merged by the combine kernel."""
+    from wnw_b200.kernels import attn_plan
+    plan, info = attn_plan(np.array(lens, np.int32) + 64, 148, 16)
+    assert info["cluster"] <= 4 and info["ctas"] <= 148 and info["combine"] >= 1
+
+
 def test_attn_plan_checks_arguments():
     from wnw_b200.kernels import attn_plan
     with pytest.raises(N.WnwError, match="out of range"):

@@ -144,16 +144,21 @@ extern "C" wnw_status wnw_attn_plan(const int32_t* seg_cap, int num_segs, int sm
   WNW_CHECK_ARG(seg_cap && info && (plan || max_ints == 0), "null pointer argument");
   WNW_CHECK_ARG(num_segs > 0, "num_segs must be positive");
   WNW_CHECK_ARG(max_cluster <= 16, "max_cluster must be in 1..16 (or <= 0 for the device's)");
-  if (sm_count <= 0) {
+  // CTA slots the device holds at once in clusters of c (the SM count when
+  // the caller gives one)
+  const bool query = sm_count <= 0;
+  if (query) {
     int dev = 0;
     WNW_CUDA_TRY(cudaGetDevice(&dev));
     WNW_CUDA_TRY(cudaDeviceGetAttribute(&sm_count, cudaDevAttrMultiProcessorCount, dev));
   }
-  if (max_cluster <= 0) {  // the largest cluster of the kernel the device can hold
-    max_cluster = 8;
+  auto slots_for = [&](int c) -> int64_t {
+    if (!query) return sm_count;
     int n = 0;
-    if (attn_mma_active_clusters_any(128, 16, &n) == WNW_OK && n > 0) max_cluster = 16;
-  }
+    if (attn_mma_active_clusters_any(128, c, &n) != WNW_OK || n <= 0) return sm_count;
+    return std::min<int64_t>(sm_count, int64_t(n) * c);
+  };
+  if (max_cluster <= 0) max_cluster = slots_for(16) >= 16 ? 16 : 8;  // the largest cluster the device holds
   std::vector<int64_t> units(num_segs);
   int64_t total = 0, umax = 1;
   for (int s = 0; s < num_segs; ++s) {
@@ -162,10 +167,28 @@ extern "C" wnw_status wnw_attn_plan(const int32_t* seg_cap, int num_segs, int sm
     total += units[s];
     umax = std::max(umax, units[s]);
   }
-  // units per CTA: an equal share of the device, raised so the longest
-  // segment fits one cluster as long as that keeps shares <= kMaxShareUnits
-  const int64_t share = std::max<int64_t>((total + sm_count - 1) / sm_count,
-                                          std::min<int64_t>(kMaxShareUnits, (umax + max_cluster - 1) / max_cluster));
+  // Units per CTA: an equal share of the device's CTA slots, raised so the
+  // longest segment fits one cluster as long as that keeps shares <=
+  // kMaxShareUnits; every segment then merges in distributed shared memory.
+  // When a segment does not fit one cluster anyway, it spans several
+  // (merged by the combine kernel): then clusters of at most 4 -- large
+  // clusters tie a segment's CTAs to a few GPCs and stream long segments
+  // slower -- and a share large enough that the plan fits the resident CTA
+  // slots in one wave.
+  int cl = max_cluster;
+  int64_t share = std::max<int64_t>((total + slots_for(cl) - 1) / slots_for(cl),
+                                    std::min<int64_t>(kMaxShareUnits, (umax + cl - 1) / cl));
+  if ((umax + share - 1) / share > cl) {
+    cl = std::min(cl, 4);
+    const int64_t slots = slots_for(cl);
+    share = std::max<int64_t>(1, (total + slots - 1) / slots);
+    auto ctas_bound = [&](int64_t sh) {  // every segment rounded up to whole clusters
+      int64_t n = 0;
+      for (int s = 0; s < num_segs; ++s) n += ((std::max<int64_t>(1, (units[s] + sh - 1) / sh) + cl - 1) / cl) * cl;
+      return n;
+    };
+    for (int it = 0; it < 64 && ctas_bound(share) > slots; ++it) share += std::max<int64_t>(1, share / 16);
+  }
   std::vector<int64_t> k(num_segs);
   int64_t kmax = 1;
   for (int s = 0; s < num_segs; ++s) {
@@ -173,7 +196,7 @@ extern "C" wnw_status wnw_attn_plan(const int32_t* seg_cap, int num_segs, int sm
     kmax = std::max(kmax, k[s]);
   }
   int C = 1;
-  while (C < std::min<int64_t>(kmax, max_cluster)) C *= 2;
+  while (C < std::min<int64_t>(kmax, cl)) C *= 2;
 
   struct Slot {
     int32_t seg, r0, r1, meta;
