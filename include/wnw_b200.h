@@ -173,8 +173,8 @@ int wnw_split_rows(int dtype, int head_dim);
  * `max_cluster` CTAs -- and a segment needing k CTAs gets k consecutive
  * ranks of one cluster (clusters hold the smallest power of two >= the
  * largest such k, at most max_cluster; short segments share clusters).  When
- * the longest segment does not fit one cluster that way, clusters hold at
- * most 4 CTAs, the share grows until the plan fits the resident slots in one
+ * the longest segment does not fit one cluster that way, or the equal share
+ * itself exceeds 1,536 rows, clusters hold at most 4 CTAs, the share grows until the plan fits the resident slots in one
  * wave, and a segment needing more CTAs than a cluster holds takes whole
  * clusters, each writing a partial that the combine kernel merges.
  * sm_count <= 0: the current device's SMs and its resident clusters of the

@@ -170,15 +170,16 @@ extern "C" wnw_status wnw_attn_plan(const int32_t* seg_cap, int num_segs, int sm
   // Units per CTA: an equal share of the device's CTA slots, raised so the
   // longest segment fits one cluster as long as that keeps shares <=
   // kMaxShareUnits; every segment then merges in distributed shared memory.
-  // When a segment does not fit one cluster anyway, it spans several
-  // (merged by the combine kernel): then clusters of at most 4 -- large
-  // clusters tie a segment's CTAs to a few GPCs and stream long segments
-  // slower -- and a share large enough that the plan fits the resident CTA
-  // slots in one wave.
+  // When a segment does not fit one cluster anyway, or the equal share itself
+  // exceeds kMaxShareUnits (a large layer), segments may span several
+  // clusters (merged by the combine kernel): then clusters of at most 4 --
+  // large clusters tie a segment's CTAs to a few GPCs and stream long
+  // segments slower -- and a share large enough that the plan fits the
+  // resident CTA slots in one wave.
   int cl = max_cluster;
   int64_t share = std::max<int64_t>((total + slots_for(cl) - 1) / slots_for(cl),
                                     std::min<int64_t>(kMaxShareUnits, (umax + cl - 1) / cl));
-  if ((umax + share - 1) / share > cl) {
+  if ((umax + share - 1) / share > cl || share > kMaxShareUnits) {
     cl = std::min(cl, 4);
     const int64_t slots = slots_for(cl);
     share = std::max<int64_t>(1, (total + slots - 1) / slots);
