@@ -161,6 +161,7 @@ def test_oproj_allreduce_reports_missing_peer():
     err = torch.zeros(1, dtype=torch.int32, device=dev)
     a = N.OprojAllReduceArgs()
     a.dtype, a.batch, a.n_out, a.k_in, a.rank, a.world = N.BF16, B, Nout, K, 0, world
+    a.recv_batch = B
     for p in range(world):
         a.recv[p] = bufs[p].data_ptr()
         a.flags[p] = bufs[p].data_ptr() + 4 * 2 * world * B * Nout
