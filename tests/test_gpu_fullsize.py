@@ -310,3 +310,118 @@ def test_config1_matches_oracle_fp32(dev):
         assert [sorted(s) for s in cache.loaded_segments] == [sorted(s) for s in orc.loaded_segments], t
         loads += sum(len(x) for x in orc.last_to_load)
     assert loads > 0
+
+
+def _stream_full_shape(dev, sc, steps, max_follow=1):
+    """Prefill and ``steps`` decode steps of scenario ``sc`` through
+    ``B200WnWCache`` and the oracle side by side, with the inputs drawn one
+    layer at a time (torch generator, bf16) and freed after use, so that the
+    full-size prompt never sits in host memory as a whole.  Checks per layer
+    and step: packed K layout and cu_seqlens bit for bit, attention within
+    bf16 tolerance; per step: class-A scores, top-k and loaded sets.  At most
+    ``max_follow`` steps may follow the GPU's selection on a near tie."""
+    from tests.follow_oracle import FollowOracle, sync_selection
+    from tests.golden.scenario import make_config_dict
+    from tests.test_gpu_cache import _packed_with_token
+    from wnw_b200.cache import B200WnWCache
+    from wnw_b200.config import WnWConfig
+
+    cfg = WnWConfig(**make_config_dict(sc))
+    L, H, Hq, D, B, S = sc["L"], sc["Hkv"], sc["Hq"], sc["D"], sc["B"], sc["S"]
+    G = Hq // H
+    g = torch.Generator().manual_seed(sc["seed"])
+    mask = torch.ones(B, S, dtype=torch.int64)
+    for b in range(B):
+        mask[b, :sc["pad"][b]] = 0
+    n_audio = [e - s for s, e in zip(sc["audio_starts"], sc["audio_ends"])]
+
+    def distinct(n):
+        # prefill scores without exact ties: which of two equal scores the
+        # reference keeps is unspecified (torch.topk), so tied inputs would
+        # make the expected layout ambiguous (uniform floats on a 2^-24 grid
+        # tie often at this size)
+        return torch.randperm(n, generator=g).to(torch.float32) / n
+
+    cache = B200WnWCache(cfg, L, H, Hq, D, dev, max_decode_tokens=steps + 2)
+    orc = FollowOracle(cfg, L, H, Hq, D)
+    cache.setup_audio(torch.tensor(sc["audio_starts"]), torch.tensor(sc["audio_ends"]), mask)
+    orc.setup_audio(sc["audio_starts"], sc["audio_ends"], sc["pad"])
+    for l in range(L):
+        k = torch.randn(B, H, S, D, generator=g).to(torch.bfloat16)
+        v = torch.randn(B, H, S, D, generator=g).to(torch.bfloat16)
+        ca_kv = bool(cfg.get_layer_class_a(l))
+        ca = [distinct(n_audio[b]) if ca_kv else None for b in range(B)]
+        ph = [[None if cfg.is_class_a_kv_head(l, h) else distinct(n_audio[b]) for h in range(H)] for b in range(B)]
+        cache.prefill_after_attn(l, [x.to(dev) if x is not None else None for x in ca],
+                                 [[x.to(dev) if x is not None else None for x in r] for r in ph], k.to(dev), v.to(dev))
+        orc.prefill_after_attn(l, ca, ph, k, v)
+        del k, v
+    cache.prefill_all_layers_done()
+    orc.prefill_all_layers_done()
+    assert cache._dplan is not None
+    assert [sorted(s) for s in cache.loaded_segments] == [sorted(s) for s in orc.loaded_segments]
+    loads = follows = 0
+    for t in range(steps):
+        for l in range(L):
+            q = torch.randn(B, Hq, 1, D, generator=g).to(torch.bfloat16)
+            k = torch.randn(B, H, 1, D, generator=g).to(torch.bfloat16)
+            v = torch.randn(B, H, 1, D, generator=g).to(torch.bfloat16)
+            kk, vv, cu, _ = cache.decode_before_attn(l, k.to(dev), v.to(dev))
+            orc.decode_before_attn(l, k, v)
+            qf = q.squeeze(2).reshape(B, H, G, D).reshape(-1, G, D)
+            out = cache.fused_decode_attention(l, qf.to(dev), q.to(dev), kk, vv, cu, D ** -0.5)
+            orc.fused_decode_attention(l, qf, scale=D ** -0.5)
+            np.testing.assert_allclose(out.float().cpu().numpy(), orc.last_out64, atol=2e-2, rtol=2e-2)
+            pk, _, pcu = _packed_with_token(cache, l)
+            assert np.array_equal(pcu, orc.cu(l)), (t, l)
+            assert torch.equal(pk.cpu(), orc.layer_k[l]), (t, l)
+        cache.decode_all_layers_done()
+        follows += bool(sync_selection(orc, cache.last_topk))
+        orc.decode_all_layers_done()
+        np.testing.assert_allclose(cache.score_accumulator.cpu().numpy(), orc.last_scores, atol=1e-4, rtol=1e-3)
+        assert cache.last_topk == orc.last_topk, t
+        assert [sorted(s) for s in cache.loaded_segments] == [sorted(s) for s in orc.loaded_segments], t
+        loads += sum(len(x) for x in orc.last_to_load)
+    assert loads > 0
+    assert follows <= max_follow
+
+
+def test_config3_full_shape_matches_oracle(dev):
+    """BASELINE config 3 at its shape: 28 layers, Qwen2.5-Omni-7B heads (4 kv
+    / 28 q, GQA 7, head_dim 128), batch 32 with seeded lognormal prompt
+    lengths (median 6k, sigma 0.5, clipped to [1k, 30k]) left-padded to the
+    longest, 50 % class-A kv heads, class-B retention 0.25, chunks of 128
+    tokens, top-8, lag 1; two decode steps."""
+    rng = np.random.default_rng(33)
+    B, L, H, Hq = 32, 28, 4, 28
+    lens = np.clip(np.round(np.exp(rng.normal(np.log(6000), 0.5, B))), 1000, 30000).astype(int)
+    S = int(lens.max())
+    pad = [int(S - n) for n in lens]
+    G = Hq // H
+    sc = dict(seed=33, L=L, Hkv=H, Hq=Hq, D=128, B=B, S=S, pad=pad,
+              audio_starts=[p + 4 for p in pad], audio_ends=[S - 30] * B,
+              chunk_size_s=128.0, overlap_s=0.0, token_rate=1.0,
+              class_a=[l * Hq + q for l in range(L) for q in range(2 * G)],
+              class_b=[l * H + h for l in range(L) for h in (2, 3)],
+              retention={(l, h): 0.25 for l in range(L) for h in (2, 3)},
+              top_k=8, lag=1, prefill_mode="last")
+    _stream_full_shape(dev, sc, steps=2)
+
+
+def test_config4_full_depth_matches_oracle(dev):
+    """BASELINE config 4 at its depth: 40 layers of Voxtral-Small-24B heads
+    (8 kv / 32 q, head_dim 128), batch 2 at a 120,064-token context, class-B
+    chunks of 128 tokens offloaded to pinned host memory, top-32; a quarter
+    of the kv heads class A (full context, scored), the rest at retention
+    0.05; two decode steps."""
+    B, L, H, Hq = 2, 40, 8, 32
+    S = 120064
+    G = Hq // H
+    sc = dict(seed=44, L=L, Hkv=H, Hq=Hq, D=128, B=B, S=S, pad=[0, 0],
+              audio_starts=[4, 4], audio_ends=[S - 160, S - 160],
+              chunk_size_s=128.0, overlap_s=0.0, token_rate=1.0,
+              class_a=[l * Hq + q for l in range(L) for q in range(2 * G)],
+              class_b=[l * H + h for l in range(L) for h in range(2, H)],
+              retention={(l, h): 0.05 for l in range(L) for h in range(2, H)},
+              top_k=32, lag=1, prefill_mode="last")
+    _stream_full_shape(dev, sc, steps=2)
