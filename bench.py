@@ -73,6 +73,21 @@ def parse():
                     help="N>1: independent per-request replicas, or one request sharded by kv head")
     ap.add_argument("--tp-exchange", default="fused", choices=["fused", "nccl"],
                     help="tensor parallel: o_proj GEMV + all-reduce as one NVLink kernel, or cuBLAS + NCCL")
+    ap.add_argument("--mode", default="step", choices=["step", "attn", "sweep"],
+                    help="step: the decode hot path (the default line); attn: decode attention alone on "
+                         "--class-a / --class-b segment lengths; sweep: the BASELINE config-5 kernel grid")
+    ap.add_argument("--class-a", type=int, default=15100, help="attn mode: rows of each class-A segment")
+    ap.add_argument("--class-b", type=int, default=2300, help="attn mode: rows of each class-B segment")
+    ap.add_argument("--n-class-a", type=int, default=2, help="attn mode: class-A segments of the 8 kv heads")
+    ap.add_argument("--layers", type=int, default=8, help="attn mode: distinct layers launched round-robin")
+    ap.add_argument("--reps", type=int, default=20, help="attn / sweep modes: timed passes over the layers")
+    ap.add_argument("--batch", default="1,16,64,256", help="sweep mode: batch sizes")
+    ap.add_argument("--ctx", default="1024,8192,32768,131072", help="sweep mode: context lengths")
+    ap.add_argument("--frac-a", default="0.1,0.3,0.5,1.0", help="sweep mode: class-A fractions of the kv heads")
+    ap.add_argument("--retained", default="0.1,0.25,0.5,1.0", help="sweep mode: class-B retained fractions")
+    ap.add_argument("--max-gb", type=float, default=48.0, help="sweep mode: skip cells above this many GB per GPU")
+    ap.add_argument("--check", action="store_true", help="attn / sweep modes: compare sampled segments with "
+                                                          "a torch fp32 reference")
     return ap.parse_args()
 
 
@@ -678,6 +693,185 @@ def _cpu_step(c, step, scale):
     c.decode_all_layers_done()
 
 
+# ------------------------------------------------------------------ kernel modes
+L2_BYTES = 126 << 20
+
+
+def attn_layer(dev, lens, G, D, seed, n_score=0, a0=4, a1=None):
+    """One layer of decode attention over segments of ``lens`` rows, laid
+    out as the cache lays a layer out (16-row aligned slots with slack),
+    with the library's plan; the first ``n_score`` segments are class A with
+    their audio rows [a0, a1) scored.  Returns the launch arguments and what
+    they point at."""
+    from wnw_b200 import kernels as Kx
+    from wnw_b200 import native as N
+    S = len(lens)
+    dtype = torch.bfloat16
+    g = torch.Generator(device=dev).manual_seed(seed)
+    cap = np.asarray(lens, np.int64) + 16
+    cap_al = (cap + 15) // 16 * 16
+    base = np.concatenate([[0], np.cumsum(cap_al)[:-1]]).astype(np.int64)
+    rows = int(cap_al.sum())
+    ks = torch.randn(rows, D, device=dev, generator=g, dtype=dtype)
+    vs = torch.randn(rows, D, device=dev, generator=g, dtype=dtype)
+    q = torch.randn(S, G, D, device=dev, generator=g, dtype=dtype)
+    work = Kx.AttnWork(dtype, D, cap, dev)
+    scratch = Kx.AttnScratch(dev, work.slots, G, D, S)
+    score = None
+    a1 = min(lens) if a1 is None else a1
+    n_audio = max(0, a1 - a0)
+    if n_score and n_audio:
+        slot = torch.full((S,), -1, dtype=torch.int32)
+        slot[:n_score] = torch.arange(n_score, dtype=torch.int32)
+        score = dict(slot=slot.to(dev), audio_start=torch.tensor([a0], dtype=torch.int32, device=dev),
+                     audio_end=torch.tensor([a1], dtype=torch.int32, device=dev),
+                     logits=torch.zeros(n_score * n_audio * G, device=dev),
+                     logits_off=torch.arange(0, n_score * n_audio * G, n_audio * G, dtype=torch.int64, device=dev),
+                     stats=torch.zeros(S * 2 * G, device=dev))
+    args = Kx.make_attn_args(dtype, S, G, D, ks, vs, torch.from_numpy(base).to(dev),
+                             torch.tensor(lens, dtype=torch.int32, device=dev), work, D ** -0.5, scratch,
+                             seg_cap=torch.from_numpy(cap.astype(np.int32)).to(dev), num_kv_heads=S, score=score,
+                             flags=N.ATTN_ROWS_READY)
+    nbytes = int(np.sum(lens)) * D * 2 * 2 + S * G * D * 2 * 2 + 8 * (n_score if score else 0) * n_audio
+    return dict(args=args, q=q, out=torch.empty_like(q), bytes=nbytes, work=work, lens=list(lens), base=base,
+                ks=ks, vs=vs, keep=(scratch, score))
+
+
+def time_attn(layers, reps):
+    """us per launch of the layers' decode attention, launched round-robin
+    back to back (nothing between them writes a layer's rows, so each may
+    load its rows before its dependency wait): replayed from a CUDA graph
+    (the kernels' own time) and launched from the host."""
+    from wnw_b200 import kernels as Kx
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for x in layers:
+            Kx.launch_attn(x["args"], x["q"], None, None, x["out"], side.cuda_stream)
+        torch.cuda.synchronize()
+        per = max(1, math.ceil(32 / len(layers)))
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, stream=side):
+            for _ in range(per):
+                for x in layers:
+                    Kx.launch_attn(x["args"], x["q"], None, None, x["out"], side.cuda_stream)
+    torch.cuda.synchronize()
+    gr.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        gr.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    graph_us = e0.elapsed_time(e1) * 1e3 / (reps * per * len(layers))
+    st = torch.cuda.current_stream().cuda_stream
+    e0.record()
+    for _ in range(reps):
+        for x in layers:
+            Kx.launch_attn(x["args"], x["q"], None, None, x["out"], st)
+    e1.record()
+    torch.cuda.synchronize()
+    host_us = e0.elapsed_time(e1) * 1e3 / (reps * len(layers))
+    del gr
+    return graph_us, host_us
+
+
+def check_attn(x, n=4):
+    """Max |error| of up to ``n`` segments of a launched layer against
+    softmax(q K^T / sqrt(d)) V in fp32 (torch)."""
+    lens, base = x["lens"], x["base"]
+    S, D = len(lens), x["ks"].shape[1]
+    pick = sorted({0, S - 1, S // 2, max(0, S // 3)})[:n]
+    err = 0.0
+    for s in pick:
+        if lens[s] == 0:
+            continue
+        k = x["ks"][base[s]:base[s] + lens[s]].float()
+        v = x["vs"][base[s]:base[s] + lens[s]].float()
+        p = torch.softmax(x["q"][s].float() @ k.t() * D ** -0.5, dim=-1)
+        err = max(err, float((p @ v - x["out"][s].float()).abs().max()))
+    return err
+
+
+def mode_attn(a, dev):
+    """Decode attention alone on one layer geometry (config 2's by default:
+    two class-A segments of 15,100 rows, scored, and six class-B ones of
+    2,300), ``--layers`` distinct layers launched round-robin so the working
+    set exceeds L2."""
+    H, G, D = MODEL["Hkv"], MODEL["Hq"] // MODEL["Hkv"], MODEL["D"]
+    lens = [a.class_a] * a.n_class_a + [a.class_b] * (H - a.n_class_a)
+    layers = [attn_layer(dev, lens, G, D, seed=l, n_score=a.n_class_a, a1=min(a.class_a, 15004))
+              for l in range(a.layers)]
+    graph_us, host_us = time_attn(layers, a.reps)
+    peak, kind = peaks()
+    nb = layers[0]["bytes"]
+    w = layers[0]["work"]
+    line = {"mode": "attn", "lens": lens, "bytes_per_launch": nb, "us_per_launch": graph_us,
+            "gbs": nb / (graph_us * 1e-6) / 1e9, "frac": nb / (graph_us * 1e-6) / 1e9 / peak, "peak_gbs": peak,
+            "peak_source": kind, "host_launched_us": host_us, "ctas": w.ctas, "cluster": w.cluster_size,
+            "partials": w.parts, "layers": len(layers),
+            "how": "CUDA-graph replay of the layers' launches back to back, CUDA events"}
+    if a.check:
+        line["max_abs_err"] = max(check_attn(x) for x in layers[:2])
+    print(json.dumps(line), flush=True)
+
+
+def mode_sweep(a, dev, rank, world):
+    """random bf16 K/V/q, 8 kv heads x head_dim 128, GQA
+    4; per cell of batch x context x class-A fraction x retained fraction,
+    the first round(frac_a * 8) kv heads of every sample are class A (the
+    whole context) and the rest class B (retained * context rows).  Under
+    torchrun the kv heads are sharded over the ranks (rank r attends heads
+    [r*8/N, (r+1)*8/N) of every sample); value = all ranks' bytes / the
+    slowest rank's time.  One JSON line per cell from rank 0."""
+    from wnw_b200.tp import head_range
+    H, G, D = MODEL["Hkv"], 4, MODEL["D"]
+    h0, h1 = head_range(rank, world, H)
+    ints = lambda t: [int(x) for x in t.split(",")]  # noqa: E731
+    flts = lambda t: [float(x) for x in t.split(",")]  # noqa: E731
+    peak, kind = peaks()
+    for b in ints(a.batch):
+        for c in ints(a.ctx):
+            for fa in flts(a.frac_a):
+                for r in flts(a.retained):
+                    n_a = min(H, max(0, round(fa * H)))
+                    lb = max(1, int(r * c))
+                    lens = [c if h < n_a else lb for _ in range(b) for h in range(h0, h1)]
+                    store = (sum(lens) + 16 * len(lens)) * D * 2 * 2
+                    cell = {"mode": "sweep", "batch": b, "ctx": c, "frac_a": fa, "retained": r, "n_gpus": world}
+                    t = torch.tensor([float(store > a.max_gb * 1e9)], device=dev)
+                    if world > 1:
+                        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+                    if t.item() > 0:
+                        if rank == 0:
+                            print(json.dumps(dict(cell, skipped=f"above --max-gb {a.max_gb} per GPU")), flush=True)
+                        continue
+                    n_layers = 1 if store > 8 * L2_BYTES else max(2, math.ceil(2 * L2_BYTES / store))
+                    layers = [attn_layer(dev, lens, G, D, seed=l) for l in range(n_layers)]
+                    if world > 1:
+                        torch.distributed.barrier()
+                    us, _ = time_attn(layers, max(2, a.reps // n_layers))
+                    err = check_attn(layers[0]) if a.check else None
+                    v = torch.tensor([us, layers[0]["bytes"], err or 0.0], device=dev, dtype=torch.float64)
+                    if world > 1:
+                        mx = v.clone()
+                        torch.distributed.all_reduce(mx, op=torch.distributed.ReduceOp.MAX)
+                        torch.distributed.all_reduce(v, op=torch.distributed.ReduceOp.SUM)
+                        us, nb, err = float(mx[0]), float(v[1]), float(mx[2])
+                    else:
+                        nb = float(v[1])
+                    if rank == 0:
+                        gbs = nb / (us * 1e-6) / 1e9
+                        cell.update(bytes=nb, us=us, gbs=gbs, frac=gbs / (peak * world), peak_gbs_per_gpu=peak,
+                                    ctas=layers[0]["work"].ctas, cluster=layers[0]["work"].cluster_size)
+                        if a.check:
+                            cell["max_abs_err"] = err
+                        print(json.dumps(cell), flush=True)
+                    del layers
+                    torch.cuda.empty_cache()
+
+
 # ------------------------------------------------------------------ clocks
 class Clocks:
     """nvidia-smi sampling during the timed region."""
@@ -777,6 +971,17 @@ def main():
         import datetime
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
                                              device_id=dev)
+    if a.mode != "step" and a.impl == "b200":
+        try:
+            if a.mode == "attn":
+                if rank == 0:
+                    mode_attn(a, dev)
+            else:
+                mode_sweep(a, dev, rank, world)
+        finally:
+            if dist:
+                torch.distributed.destroy_process_group()
+        return
     K, W = a.steps, a.warmup
     workload = "voxtral-mini-3b wnw decode hot path, B=1, 15064-token prompt (15000 audio), 30 layers"
     cfg_json = {"workload": workload, "batch": 1, "prompt_tokens": 15064, "audio_tokens": 15000,
