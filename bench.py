@@ -562,6 +562,7 @@ def run_reference_gpu(rec, dev, K, W):
         cache.prefill_all_layers_done()
         torch.cuda.synchronize()
         pre = (time.perf_counter() - t) * 1e3
+        picks.clear()  # the prefill's own selection; decode steps from here
         steps, scale, L = rec["steps"], rec["scale"], MODEL["L"]
 
         def one(i):
