@@ -76,6 +76,9 @@ def parse():
     ap.add_argument("--config", type=int, default=2, choices=[2, 3, 4],
                     help="BASELINE config of the step: 2 (the default line; q/k/v recorded from the random-init "
                          "decoder), 3 or 4 (their shapes with seeded synthetic q/k/v)")
+    ap.add_argument("--synthetic", action="store_true",
+                    help="config 2 with seeded synthetic inputs instead of the model run (as configs 3 and 4)")
+    ap.add_argument("--depth", type=int, default=None, help="synthetic configs: only this many layers")
     ap.add_argument("--mode", default="step", choices=["step", "attn", "sweep"],
                     help="step: the decode hot path (the default line); attn: decode attention alone on "
                          "--class-a / --class-b segment lengths; sweep: the BASELINE config-5 kernel grid")
@@ -279,6 +282,9 @@ SYNTH = {
             sigma=0.5, clip=(1000, 30000), class_a_kv=(0, 1), retention=0.25, chunk=128, top_k=8, lag=1, seed=33,
             note="batch 32, lognormal prompts (median 6k, sigma 0.5, clipped [1k, 30k]) left-padded, 50 % class-A kv "
                  "heads, class-B retention 0.25"),
+    2: dict(name="voxtral-mini-3b-shaped", L=30, Hkv=8, Hq=32, D=128, hidden=3072, B=1, S=15064, tail=60,
+            class_a_kv=(0, 1), retention=0.0, chunk=128, top_k=16, lag=1, seed=22,
+            note="batch 1, 15,064-token prompt (15,000 audio), 25 % class-A kv heads, class-B retention 0"),
     4: dict(name="voxtral-small-24b-shaped", L=40, Hkv=8, Hq=32, D=128, hidden=5120, B=2, S=120064,
             class_a_kv=(0, 1), retention=0.05, chunk=128, top_k=32, lag=1, seed=44,
             note="batch 2 at a 120,064-token context, 25 % class-A kv heads, class-B retention 0.05, class-B "
@@ -286,9 +292,13 @@ SYNTH = {
 }
 
 
-def use_config(n):
-    """Point the workload globals at BASELINE config ``n``."""
-    if n in SYNTH:
+def use_config(n, synthetic=False, layers=None):
+    """Point the workload globals at BASELINE config ``n`` (config 2 with
+    ``synthetic``: its shapes with seeded inputs instead of a model run);
+    ``layers`` shortens a synthetic config to that many layers."""
+    if n in SYNTH and layers:
+        SYNTH[n]["L"] = min(SYNTH[n]["L"], layers)
+    if n in SYNTH and (n != 2 or synthetic):
         c = SYNTH[n]
         MODEL.update(L=c["L"], Hkv=c["Hkv"], Hq=c["Hq"], D=c["D"], hidden=c["hidden"])
         WNW.update(chunk=c["chunk"], top_k=c["top_k"], lag=c["lag"], retention=c["retention"])
@@ -313,7 +323,7 @@ def synthetic_record(dev, n_steps, n, cfg_cls=None):
         starts, ends = [p + 4 for p in pad], [S - 30] * B
     else:
         S, pad = c["S"], [0] * B
-        starts, ends = [4] * B, [S - 160] * B
+        starts, ends = [4] * B, [S - c.get("tail", 160)] * B
     cfg = WnWConfig(chunk_size_s=float(c["chunk"]), overlap_s=0.0, token_rate=1.0,
                     class_a=[l * Hq + h * G + j for l in range(L) for h in c["class_a_kv"] for j in range(G)],
                     class_b=[l * H + h for l in range(L) for h in range(H) if h not in c["class_a_kv"]],
@@ -1043,7 +1053,8 @@ def traffic_per_launch(algorithmic_bytes):
 # ------------------------------------------------------------------ main
 def main():
     a = parse()
-    use_config(a.config)
+    use_config(a.config, a.synthetic, a.depth)
+    a.synth = a.config in SYNTH and (a.config != 2 or a.synthetic)
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -1068,7 +1079,7 @@ def main():
                 torch.distributed.destroy_process_group()
         return
     K, W = a.steps, a.warmup
-    if a.config in SYNTH:
+    if a.synth:
         c = SYNTH[a.config]
         cfg_json = {"workload": f"{c['name']} wnw decode hot path (BASELINE config {a.config}): {c['note']}, "
                                 f"{c['L']} layers", "config": a.config, "batch": c["B"], "layers": c["L"],
@@ -1106,14 +1117,14 @@ def _main(a, rank, world, local, dist, dev, K, W, cfg_json, tp, clk):
         # GPU, untimed), then the CPU restatement replays them
         n = max(1, K)
         try:
-            if a.config in SYNTH:
+            if a.synth:
                 rec = synthetic_record(dev, 1, a.config, cfg_cls=reference_modules()[2])
             else:
                 rec = record(dev, W + n, seed=1000, reference=True)
         except Exception as e:  # report, exit 0
             print(json.dumps({"impl": "reference", "unavailable": f"{type(e).__name__}: {e}"[:300]}), flush=True)
             return
-        if a.config in SYNTH:  # a deep workload: one step of the first few layers, scaled to the full depth
+        if a.synth:  # a deep workload: one step of the first few layers, scaled to the full depth
             nl = min(MODEL["L"], 2 if a.config == 4 else 3)
             n, W = 1, 0
             sec = cpu_replay(rec, 1, start=0, layers=nl) * MODEL["L"] / nl
@@ -1134,7 +1145,7 @@ def _main(a, rank, world, local, dist, dev, K, W, cfg_json, tp, clk):
         return
 
     # replicas record their own request; tensor-parallel ranks share one
-    if a.config in SYNTH:
+    if a.synth:
         rec = synthetic_record(dev, W + K, a.config)
     else:
         rec = record(dev, W + K, seed=1000 + (0 if tp else rank))
@@ -1150,7 +1161,7 @@ def _main(a, rank, world, local, dist, dev, K, W, cfg_json, tp, clk):
     # the same step with the offloaded rows kept in HBM (offload_tier="hbm"),
     # for comparison only: the reference offloads to host memory
     hbm = run_value(rec, dev, K, W, shard, tier="hbm") if not dist and not a.profile else None
-    ref_gpu = (run_reference_gpu(rec, dev, K, W) if not dist and not a.profile and not tp and a.config == 2
+    ref_gpu = (run_reference_gpu(rec, dev, K, W) if not dist and not a.profile and not tp and not a.synth
                else None)
     agreement = None
     if ref_gpu is not None and "_picks" in ref_gpu:
@@ -1173,7 +1184,7 @@ def _main(a, rank, world, local, dist, dev, K, W, cfg_json, tp, clk):
         "metric": METRIC, "value": tokens / (ms * 1e-3),
         "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": ms / K,
         "higher_is_better": True, "scaling": "strong" if tp else "weak", "vs_baseline": None, "dtype": "bf16",
-        "data": ("synthetic (seeded N(0,1) K/V and q/k/v at the config's shapes)" if a.config in SYNTH
+        "data": ("synthetic (seeded N(0,1) K/V and q/k/v at the config's shapes)" if a.synth
                  else "synthetic (random-init decoder, N(0,0.02) audio embeddings)"), "config": cfg_json,
         "e2e": {"value": tokens / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": e2e["in_bytes"],
                 "d2h_bytes_per_step": e2e["out_bytes"]},
@@ -1183,7 +1194,7 @@ def _main(a, rank, world, local, dist, dev, K, W, cfg_json, tp, clk):
                      "kernel": f"wnw::decode_attn_mma_kernel<bf16,128,{MODEL['Hq'] // MODEL['Hkv']}>",
                      "bytes_per_launch": val["attn_bytes"], "us_per_launch": val["attn_us"],
                      "launches_timed": val["attn_n"],
-                     "how": "all 30 layers' launches back to back on the timed run's final state, CUDA events"},
+                     "how": f"all {MODEL['L']} layers' launches back to back on the timed run's final state, CUDA events"},
         "gpu_launches": val["launches"],
         "clocks": clk.summary(val["window"]),
         "fetched_rows_per_step": val["fetched_rows"] / K,
@@ -1211,7 +1222,7 @@ def _main(a, rank, world, local, dist, dev, K, W, cfg_json, tp, clk):
                                        "allocation of the host store"},
     }
     if rank == 0 and not a.no_cpu and not a.profile:
-        if a.config in SYNTH:  # a deep workload: one step of the first few layers, scaled to the full depth
+        if a.synth:  # a deep workload: one step of the first few layers, scaled to the full depth
             nl = min(MODEL["L"], 2 if a.config == 4 else 3)
             sec = cpu_replay(rec, 1, start=0, layers=nl) * MODEL["L"] / nl
             sample = f"1 decode step of the first {nl} of {MODEL['L']} layers replayed by the CPU oracle, scaled"
