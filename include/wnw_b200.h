@@ -174,9 +174,11 @@ int wnw_split_rows(int dtype, int head_dim);
  * ranks of one cluster (clusters hold the smallest power of two >= the
  * largest such k, at most max_cluster; short segments share clusters).  When
  * the longest segment does not fit one cluster that way, or the equal share
- * itself exceeds 1,536 rows, clusters hold at most 4 CTAs, the share grows until the plan fits the resident slots in one
- * wave, and a segment needing more CTAs than a cluster holds takes whole
- * clusters, each writing a partial that the combine kernel merges.
+ * itself exceeds 1,536 rows, clusters hold at most 4 CTAs, the share is
+ * sized to whole waves of the resident slots (of 1 to 4 waves, the count
+ * whose waves x (share + 512 rows of fixed cost) is least), and a segment needing more CTAs than a
+ * cluster holds takes whole clusters, each writing a partial that the
+ * combine kernel merges.
  * sm_count <= 0: the current device's SMs and its resident clusters of the
  * kernel (otherwise sm_count stands for the slots at every cluster size);
  * max_cluster <= 0: 16 when the device holds clusters of 16 of the kernel,

@@ -231,6 +231,18 @@ def test_attn_plan_long_segments_fit_one_wave(lens):
     assert info["cluster"] <= 4 and info["ctas"] <= 148 and info["combine"] >= 1
 
 
+def test_attn_plan_balances_long_segments_among_many_short_ones():
+    """16 long segments beside 112 short ones (batch 16, one class-A kv head
+    of 8 at 131k rows): the plan spreads the long ones over several CTAs in
+    a few waves rather than one lopsided wave."""
+    from wnw_b200.kernels import attn_plan
+    lens = [131072 if h == 0 else 13107 for _ in range(16) for h in range(8)]
+    plan, info = attn_plan(np.array(lens, np.int32) + 16, 148, 16)
+    C, cta, _, _ = _parse_plan(plan)
+    per_seg = np.bincount(cta[cta[:, 0] >= 0, 0], minlength=128)
+    assert per_seg[::8].min() >= 4 and info["ctas"] <= 4 * 148
+
+
 def test_attn_plan_checks_arguments():
     from wnw_b200.kernels import attn_plan
     with pytest.raises(N.WnwError, match="out of range"):

@@ -141,6 +141,7 @@ extern "C" wnw_status wnw_attn_plan(const int32_t* seg_cap, int num_segs, int sm
   using namespace wnw;
   constexpr int64_t kUnit = 32;           // rows: one TMA box pair of two warps
   constexpr int64_t kMaxShareUnits = 48;  // 1,536 rows: most a CTA takes to keep a segment in one cluster
+  constexpr int64_t kWaveOverheadUnits = 16;  // a CTA's fixed cost (prologue, merge) ~ streaming 512 rows
   WNW_CHECK_ARG(seg_cap && info && (plan || max_ints == 0), "null pointer argument");
   WNW_CHECK_ARG(num_segs > 0, "num_segs must be positive");
   WNW_CHECK_ARG(max_cluster <= 16, "max_cluster must be in 1..16 (or <= 0 for the device's)");
@@ -152,11 +153,16 @@ extern "C" wnw_status wnw_attn_plan(const int32_t* seg_cap, int num_segs, int sm
     WNW_CUDA_TRY(cudaGetDevice(&dev));
     WNW_CUDA_TRY(cudaDeviceGetAttribute(&sm_count, cudaDevAttrMultiProcessorCount, dev));
   }
+  int64_t slot_c[17] = {};
   auto slots_for = [&](int c) -> int64_t {
     if (!query) return sm_count;
-    int n = 0;
-    if (attn_mma_active_clusters_any(128, c, &n) != WNW_OK || n <= 0) return sm_count;
-    return std::min<int64_t>(sm_count, int64_t(n) * c);
+    if (slot_c[c] == 0) {
+      int n = 0;
+      slot_c[c] = attn_mma_active_clusters_any(128, c, &n) != WNW_OK || n <= 0
+                      ? sm_count
+                      : std::min<int64_t>(sm_count, int64_t(n) * c);
+    }
+    return slot_c[c];
   };
   if (max_cluster <= 0) max_cluster = slots_for(16) >= 16 ? 16 : 8;  // the largest cluster the device holds
   std::vector<int64_t> units(num_segs);
@@ -174,21 +180,56 @@ extern "C" wnw_status wnw_attn_plan(const int32_t* seg_cap, int num_segs, int sm
   // exceeds kMaxShareUnits (a large layer), segments may span several
   // clusters (merged by the combine kernel): then clusters of at most 4 --
   // large clusters tie a segment's CTAs to a few GPCs and stream long
-  // segments slower -- and a share large enough that the plan fits the
-  // resident CTA slots in one wave.
+  // segments slower -- and a share sized to whole waves of resident CTAs.
   int cl = max_cluster;
   int64_t share = std::max<int64_t>((total + slots_for(cl) - 1) / slots_for(cl),
                                     std::min<int64_t>(kMaxShareUnits, (umax + cl - 1) / cl));
   if ((umax + share - 1) / share > cl || share > kMaxShareUnits) {
     cl = std::min(cl, 4);
-    const int64_t slots = slots_for(cl);
-    share = std::max<int64_t>(1, (total + slots - 1) / slots);
-    auto ctas_bound = [&](int64_t sh) {  // every segment rounded up to whole clusters
-      int64_t n = 0;
-      for (int s = 0; s < num_segs; ++s) n += ((std::max<int64_t>(1, (units[s] + sh - 1) / sh) + cl - 1) / cl) * cl;
-      return n;
+    int c = 1;  // the cluster size of the plan at share sh (set by ctas_at)
+    auto ctas_at = [&](int64_t sh) {  // the CTAs the packing below makes at share sh
+      int64_t km = 1;
+      for (int s = 0; s < num_segs; ++s) km = std::max(km, (units[s] + sh - 1) / sh);
+      c = 1;
+      while (c < std::min<int64_t>(km, cl)) c *= 2;
+      int64_t n = 0, clusters = 0;
+      std::vector<int64_t> need(c + 1, 0), free(c + 1, 0);  // segments by CTAs; clusters by free ranks
+      for (int s = 0; s < num_segs; ++s) {
+        const int64_t k = std::max<int64_t>(1, (units[s] + sh - 1) / sh);
+        if (k > c)
+          n += (k + c - 1) / c * c;
+        else
+          ++need[k];
+      }
+      for (int k = c; k >= 1; --k) {
+        for (; need[k] > 0; --need[k]) {
+          int f = k;
+          while (f < c && free[f] == 0) ++f;
+          if (f == c) ++clusters;
+          else --free[f];
+          if (f - k > 0) ++free[f - k];
+        }
+      }
+      return n + clusters * c;
     };
-    for (int it = 0; it < 64 && ctas_bound(share) > slots; ++it) share += std::max<int64_t>(1, share / 16);
+    // for w = 1..4 waves: the smallest share whose CTAs fit w waves of the
+    // resident slots (or every segment down to one CTA); then the w whose
+    // waves x (share + a CTA's fixed cost) -- the busiest SM's time -- is
+    // least.  One wave avoids a short tail wave; a few waves balance layers
+    // of many short segments beside a few long ones.
+    int64_t best = INT64_MAX;
+    for (int64_t w = 1; w <= 4; ++w) {
+      const int64_t slots1 = slots_for(cl);
+      int64_t sh = std::max<int64_t>(1, (total + w * slots1 - 1) / (w * slots1));
+      for (int it = 0; it < 256 && ctas_at(sh) > w * slots_for(c) && sh < umax; ++it)
+        sh = std::min(umax, sh + std::max<int64_t>(1, sh / 16));
+      const int64_t slots = slots_for(c);
+      const int64_t cost = (ctas_at(sh) + slots - 1) / slots * (sh + kWaveOverheadUnits);
+      if (cost < best) {
+        best = cost;
+        share = sh;
+      }
+    }
   }
   std::vector<int64_t> k(num_segs);
   int64_t kmax = 1;
