@@ -94,6 +94,12 @@ def parse():
     ap.add_argument("--max-gb", type=float, default=48.0, help="sweep mode: skip cells above this many GB per GPU")
     ap.add_argument("--check", action="store_true", help="attn / sweep modes: compare sampled segments with "
                                                           "a torch fp32 reference")
+    ap.add_argument("--max-cluster", type=int, default=None,
+                    help="attn mode: plan with clusters of at most this many CTAs (default: the device's largest)")
+    ap.add_argument("--sm-count", type=int, default=None,
+                    help="attn mode: plan for this many CTA slots (default: the device's resident clusters)")
+    ap.add_argument("--vs-reference", action="store_true",
+                    help="attn mode: also time the reference's own GPU kernels (baseline/_ref) on the same layers")
     return ap.parse_args()
 
 
@@ -791,7 +797,7 @@ def _cpu_step(c, step, scale):
 L2_BYTES = 126 << 20
 
 
-def attn_layer(dev, lens, G, D, seed, n_score=0, a0=4, a1=None):
+def attn_layer(dev, lens, G, D, seed, n_score=0, a0=4, a1=None, sm_count=None, max_cluster=None):
     """One layer of decode attention over segments of ``lens`` rows, laid
     out as the cache lays a layer out (16-row aligned slots with slack),
     with the library's plan; the first ``n_score`` segments are class A with
@@ -809,7 +815,7 @@ def attn_layer(dev, lens, G, D, seed, n_score=0, a0=4, a1=None):
     ks = torch.randn(rows, D, device=dev, generator=g, dtype=dtype)
     vs = torch.randn(rows, D, device=dev, generator=g, dtype=dtype)
     q = torch.randn(S, G, D, device=dev, generator=g, dtype=dtype)
-    work = Kx.AttnWork(dtype, D, cap, dev)
+    work = Kx.AttnWork(dtype, D, cap, dev, sm_count=sm_count, max_cluster=max_cluster)
     scratch = Kx.AttnScratch(dev, work.slots, G, D, S)
     score = None
     a1 = min(lens) if a1 is None else a1
@@ -828,7 +834,7 @@ def attn_layer(dev, lens, G, D, seed, n_score=0, a0=4, a1=None):
                              flags=N.ATTN_ROWS_READY)
     nbytes = int(np.sum(lens)) * D * 2 * 2 + S * G * D * 2 * 2 + 8 * (n_score if score else 0) * n_audio
     return dict(args=args, q=q, out=torch.empty_like(q), bytes=nbytes, work=work, lens=list(lens), base=base,
-                ks=ks, vs=vs, keep=(scratch, score))
+                ks=ks, vs=vs, n_score=n_score if score else 0, keep=(scratch, score))
 
 
 def time_attn(layers, reps):
@@ -888,6 +894,68 @@ def check_attn(x, n=4):
     return err
 
 
+def reference_kernels(layers, a0, a1, reps):
+    """The reference's own decode-attention GPU kernels from its offline
+    install, on the same layers packed into its flat layout (``cu_seqlens``):
+    ``q1_decode_attn_score`` (attention + class-A score accumulation,
+    src/common/kv/fused_attn.py:124-156, what its session calls with
+    WNW_FUSED_ATTN=1), ``q1_decode_attn`` (attention only, fused_attn.py:47-65)
+    and torch's ``varlen_attn`` as its default session path calls it
+    (src/algorithms/wnw/code/session.py:90-106).  us per launch, round-robin
+    over the layers, CUDA events."""
+    reference_modules()  # puts baseline/_ref on the path, or raises
+    from common.kv.fused_attn import q1_decode_attn, q1_decode_attn_score
+    from torch.nn.attention.varlen import varlen_attn
+    x0 = layers[0]
+    lens, dev = x0["lens"], x0["q"].device
+    S, G, D = x0["q"].shape
+    n_score = x0["n_score"]
+    cu = torch.tensor(np.concatenate([[0], np.cumsum(lens)]), dtype=torch.int32, device=dev)
+    ca_mask = torch.tensor([1 if s < n_score else 0 for s in range(S)], dtype=torch.int32, device=dev)
+    a_s = torch.tensor([a0], dtype=torch.int32, device=dev)
+    a_e = torch.tensor([a1], dtype=torch.int32, device=dev)
+    acc = torch.zeros(max(1, a1 - a0), dtype=torch.float32, device=dev)
+    offs = torch.tensor([0, a1 - a0], dtype=torch.int32, device=dev)
+    packed = []
+    for x in layers:
+        pk = torch.cat([x["ks"][int(b):int(b) + n] for b, n in zip(x["base"], lens)])
+        pv = torch.cat([x["vs"][int(b):int(b) + n] for b, n in zip(x["base"], lens)])
+        packed.append((x["q"], pk, pv))
+    scale = D ** -0.5
+    cu_q = torch.arange(S + 1, dtype=torch.int32, device=dev)
+
+    def varlen(q, pk, pv):  # the session's call: K/V heads broadcast to the query heads
+        T = pk.shape[0]
+        ke = pk.unsqueeze(1).as_strided((T, G, D), (D, 0, 1))
+        ve = pv.unsqueeze(1).as_strided((T, G, D), (D, 0, 1))
+        return varlen_attn(q, ke, ve, cu_q, cu, max_q=1, max_k=int(max(lens)), scale=scale)
+
+    def timed(fns):
+        for f in fns:
+            f()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            for f in fns:
+                f()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) * 1e3 / (reps * len(fns))
+
+    out = {"q1_decode_attn_score_us": timed([lambda p=p: q1_decode_attn_score(
+               p[0], p[1], p[2], cu, scale, ca_mask, S, a_s, a_e, acc, offs) for p in packed]),
+           "q1_decode_attn_us": timed([lambda p=p: q1_decode_attn(p[0], p[1], p[2], cu, scale) for p in packed])}
+    try:
+        out["varlen_attn_us"] = timed([lambda p=p: varlen(*p) for p in packed])
+    except Exception as e:  # the library kernel may not take this layout
+        out["varlen_attn_us"] = f"failed: {type(e).__name__}: {e}"[:200]
+    # both compute the same attention: ours (launched last by the timing) vs the reference's, layer 0
+    ref_o = q1_decode_attn(packed[0][0], packed[0][1], packed[0][2], cu, scale)
+    out["max_abs_diff_vs_ours"] = float((ref_o.float() - x0["out"].float()).abs().max())
+    return out
+
+
 def mode_attn(a, dev):
     """Decode attention alone on one layer geometry (config 2's by default:
     two class-A segments of 15,100 rows, scored, and six class-B ones of
@@ -895,8 +963,8 @@ def mode_attn(a, dev):
     set exceeds L2."""
     H, G, D = MODEL["Hkv"], MODEL["Hq"] // MODEL["Hkv"], MODEL["D"]
     lens = [a.class_a] * a.n_class_a + [a.class_b] * (H - a.n_class_a)
-    layers = [attn_layer(dev, lens, G, D, seed=l, n_score=a.n_class_a, a1=min(a.class_a, 15004))
-              for l in range(a.layers)]
+    layers = [attn_layer(dev, lens, G, D, seed=l, n_score=a.n_class_a, a1=min(a.class_a, 15004),
+                         sm_count=a.sm_count, max_cluster=a.max_cluster) for l in range(a.layers)]
     graph_us, host_us = time_attn(layers, a.reps)
     peak, kind = peaks()
     nb = layers[0]["bytes"]
@@ -908,6 +976,12 @@ def mode_attn(a, dev):
             "how": "CUDA-graph replay of the layers' launches back to back, CUDA events"}
     if a.check:
         line["max_abs_err"] = max(check_attn(x) for x in layers[:2])
+    if a.vs_reference:
+        try:
+            line["reference_kernels"] = reference_kernels(layers, 4, min(a.class_a, 15004),
+                                                          max(1, a.reps // 4))
+        except Exception as e:  # report, keep the line
+            line["reference_kernels"] = {"unavailable": f"{type(e).__name__}: {e}"[:300]}
     print(json.dumps(line), flush=True)
 
 

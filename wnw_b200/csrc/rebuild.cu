@@ -204,7 +204,24 @@ __global__ void copy_segments_kernel(const uint4* src_k, const uint4* src_v, con
   const int64_t n = int64_t(len[seg]) * chunks_per_row;
   const int64_t s0 = src_base[seg] * chunks_per_row;
   const int64_t d0 = dst_base[seg] * chunks_per_row;
-  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x) {
+  const int64_t stride = int64_t(gridDim.x) * blockDim.x;
+  int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  // four rows' chunks of K and V in flight per thread: the loads of a
+  // round are issued before its stores
+  for (; i + 3 * stride < n; i += 4 * stride) {
+    uint4 k[4], v[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      k[j] = src_k[s0 + i + j * stride];
+      v[j] = src_v[s0 + i + j * stride];
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      dst_k[d0 + i + j * stride] = k[j];
+      dst_v[d0 + i + j * stride] = v[j];
+    }
+  }
+  for (; i < n; i += stride) {
     dst_k[d0 + i] = src_k[s0 + i];
     dst_v[d0 + i] = src_v[s0 + i];
   }
@@ -278,7 +295,8 @@ extern "C" wnw_status wnw_copy_segments(int dtype, int head_dim, const void* src
   WNW_CHECK_ARG(rb > 0 && rb % 16 == 0, "row size must be a positive multiple of 16 bytes");
   if (num_segs <= 0) return WNW_OK;
   WNW_CHECK_ARG(num_segs <= 65535, "at most 65535 segments per call");
-  dim3 grid(8, num_segs);
+  // about four CTAs per SM over all segments (148 SMs), at least one per segment
+  dim3 grid(std::min(64, std::max(1, (4 * 148 + num_segs - 1) / num_segs)), num_segs);
   copy_segments_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const uint4*>(src_k), static_cast<const uint4*>(src_v), src_base, static_cast<uint4*>(dst_k),
       static_cast<uint4*>(dst_v), dst_base, len, rb / 16);

@@ -65,21 +65,30 @@ class ScoreReducer:
     ``all_gather`` then ``acc = x_0 + x_1 + ... + x_{P-1}`` elementwise, so
     the result is bit-identical on every rank (an all-reduce may sum in a
     different order per rank or per algorithm, and a one-ulp difference can
-    flip a near-tie in the top-k)."""
+    flip a near-tie in the top-k).  The gather buffer and the result are
+    allocated once per shape; the returned tensor is valid until the next
+    call."""
 
     def __init__(self, group=None):
         self.group = group
         self.world = torch.distributed.get_world_size(group)
+        self._buf = None  # [world, n] gather buffer and [n] result, kept from call to call
 
     def __call__(self, acc):
         if self.world == 1:
             return acc
-        parts = [torch.empty_like(acc) for _ in range(self.world)]
-        torch.distributed.all_gather(parts, acc.contiguous(), group=self.group)
-        out = parts[0].clone()
-        for p in parts[1:]:
-            out += p
-        return out
+        x = acc.contiguous().reshape(-1)
+        if self._buf is None or self._buf[1].numel() != x.numel() or self._buf[1].dtype != x.dtype \
+                or self._buf[1].device != x.device:
+            self._buf = (torch.empty(self.world * x.numel(), dtype=x.dtype, device=x.device),
+                         torch.empty(x.numel(), dtype=x.dtype, device=x.device))
+        flat, out = self._buf
+        torch.distributed.all_gather_into_tensor(flat, x, group=self.group)
+        parts = flat.view(self.world, -1)
+        torch.add(parts[0], parts[1], out=out)
+        for r in range(2, self.world):
+            out += parts[r]
+        return out.reshape(acc.shape)
 
 
 def slice_kv(x, h0, h1):
