@@ -38,7 +38,7 @@ typedef enum wnw_dtype { WNW_F32 = 0, WNW_F16 = 1, WNW_BF16 = 2 } wnw_dtype;
 #define WNW_DEVERR_LEN_MISMATCH 2   /* rebuild plan disagrees with seg_len   */
 #define WNW_DEVERR_CAPACITY 4       /* a segment would exceed its slot       */
 #define WNW_DEVERR_PEER_TIMEOUT 8   /* a tensor-parallel peer's partials did not arrive */
-#define WNW_DEVERR_BAD_INDEX 16     /* device fetch plan: top-k chunk or segment index out of range */
+#define WNW_DEVERR_BAD_INDEX 16     /* a device-side table index out of range (device fetch plan, prefill score task) */
 
 int wnw_abi_version(void);
 const char* wnw_status_string(wnw_status s);
@@ -504,6 +504,64 @@ int wnw_oproj_allreduce_chunks(int n_out);
 wnw_status wnw_ipc_alloc(int64_t bytes, void** ptr, void* handle);
 wnw_status wnw_ipc_open(const void* handle, void** ptr);
 wnw_status wnw_ipc_close(void* ptr, int owned);
+
+/* ------------------------------------------------------------------------
+ * Prefill audio scores (replaces _compute_prefill_scores and
+ * _compute_head_scores, src/algorithms/wnw/code/session.py:121-201).
+ *
+ * Per task: the query rows are (head, position) pairs -- n_heads query heads
+ * heads[head_off ...] at positions row0 .. row0 + n_rows - 1 of sample
+ * `batch` -- scored against every key of kv head `kv_head`:
+ *   x = rnd(rnd(rnd(q . k) * scaling) [+ mask])
+ * with rnd the rounding to the model dtype (the reference's bf16 / fp16
+ * matmul output, its scale and its mask add), then a softmax over all
+ * seq_len keys in fp32, and
+ *   out[out_off + j - audio_start] = sum over heads of the mean over
+ *                                    positions of softmax[j]
+ * for the audio keys j in [audio_start, audio_end).  The session's class-A
+ * score is one task (the class-A query heads, the last position, the first
+ * class-A head's kv head); each class-B kv head's score is one task (its
+ * group of query heads, the last position or the post-audio text
+ * positions).  Two launches: per-chunk row statistics, then the audio
+ * columns.  Sums are taken in a fixed order, so results repeat bit for bit.
+ * A task whose indices fall outside the given sizes sets
+ * WNW_DEVERR_BAD_INDEX in *err and writes nothing. */
+#define WNW_MASK_NONE 0      /* no mask added                              */
+#define WNW_MASK_CAUSAL 1    /* keys after the query position get -inf     */
+#define WNW_MASK_ADDITIVE 2  /* mask[b, position, key] added (model dtype) */
+typedef struct {
+  int32_t batch, kv_head;
+  int32_t head_off, n_heads;      /* query heads: heads[head_off .. + n_heads) */
+  int32_t row0, n_rows;           /* query positions                           */
+  int32_t audio_start, audio_end; /* key columns written                       */
+  int64_t out_off;
+} wnw_prefill_task;
+typedef struct {
+  int dtype, head_dim;                  /* WNW_BF16 / WNW_F16; 64 or 128    */
+  int batch, num_q_heads, num_kv_heads, seq_len;
+  int num_tasks;                        /* <= 65535                         */
+  int num_heads;                        /* entries of `heads`               */
+  int max_rows;                         /* >= n_heads * n_rows of any task  */
+  int max_audio;                        /* >= audio_end - audio_start       */
+  const void* q;                        /* [B, Hq, S, D] by the strides     */
+  int64_t q_stride_b, q_stride_h, q_stride_s;   /* elements, multiples of 8 */
+  const void* k;                        /* [B, Hkv, S, D]                   */
+  int64_t k_stride_b, k_stride_h, k_stride_s;
+  int mask_kind;                        /* WNW_MASK_*                       */
+  const void* mask;                     /* [B, S, S], keys contiguous       */
+  int64_t mask_stride_b, mask_stride_s;
+  float scaling;
+  const wnw_prefill_task* tasks;        /* device                           */
+  const int32_t* heads;                 /* device                           */
+  float* out;                           /* device                           */
+  int64_t out_len;                      /* floats at out                    */
+  void* scratch;                        /* device, >= scratch_bytes         */
+  int64_t scratch_bytes;
+  int32_t* err;                         /* device error word                */
+} wnw_prefill_scores_args;
+wnw_status wnw_prefill_scores(const wnw_prefill_scores_args* a, void* stream);
+/* Scratch bytes wnw_prefill_scores needs (per-chunk row statistics). */
+wnw_status wnw_prefill_scores_scratch_bytes(int num_tasks, int max_rows, int seq_len, int64_t* bytes);
 
 #ifdef __cplusplus
 }

@@ -54,6 +54,7 @@ def test_degqa_keeps_the_model_function():
 
 def test_mha_session_matches_reference(ref):
     from tests.oracle_hf import OracleHFCache, TracingMixin
+    from oracle.prefill_scores import compute_prefill_scores
     from wnw_b200.session import WnWSession
     model = _tiny_llama()
     adapter = LlamaFamilyAdapter(ss["audio_start"], ss["audio_end"])
@@ -67,7 +68,7 @@ def test_mha_session_matches_reference(ref):
 
     cache = Tracing(cfg, ss["L"], ss["Hq"], ss["Hq"], ss["D"])
     ids = session_inputs(ss)
-    with WnWSession(model, adapter, cache) as sess:
+    with WnWSession(model, adapter, cache, prefill_scores=compute_prefill_scores) as sess:
         sess.setup_audio(ids)
         with torch.no_grad():
             out = sess.generate({"input_ids": ids}, max_new_tokens=ss["new_tokens"], do_sample=False)

@@ -27,6 +27,37 @@ def test_library_exports_every_header_symbol():
     assert N.lib.wnw_split_rows(N.BF16, 128) == 0 and N.lib.wnw_split_rows(N.F32, 128) == 64
 
 
+def test_ctypes_structs_match_the_header(tmp_path):
+    """Every argument struct the ctypes binding declares has the C layout:
+    size and each field's offset, from a program compiled against the
+    header."""
+    import shutil
+    import subprocess
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    structs = {"wnw_decode_attn_args": N.DecodeAttnArgs, "wnw_attn_plan_info": N.AttnPlanInfo,
+               "wnw_oproj_allreduce_args": N.OprojAllReduceArgs, "wnw_fetch_info": N.FetchInfo,
+               "wnw_prefill_task": N.PrefillTask, "wnw_prefill_scores_args": N.PrefillScoresArgs}
+    lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "wnw_b200.h"', "int main(void) {"]
+    for cname, py in structs.items():
+        lines.append(f'  printf("{cname} %zu\\n", sizeof({cname}));')
+        for f, _ in py._fields_:
+            lines.append(f'  printf("{cname}.{f} %zu\\n", offsetof({cname}, {f}));')
+    lines += ["  return 0;", "}"]
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines))
+    exe = tmp_path / "layout"
+    subprocess.run([cc, "-I", os.path.join(root, "include"), str(src), "-o", str(exe)], check=True)
+    got = dict(line.rsplit(" ", 1) for line in subprocess.run([str(exe)], check=True, capture_output=True,
+                                                                 text=True).stdout.splitlines())
+    for cname, py in structs.items():
+        assert int(got[cname]) == ctypes.sizeof(py), cname
+        for f, _ in py._fields_:
+            assert int(got[f"{cname}.{f}"]) == getattr(py, f).offset, f"{cname}.{f}"
+
+
 def test_status_and_error_reporting():
     from wnw_b200.planner import Planner
     assert N.lib.wnw_status_string(3) == b"capacity exceeded"

@@ -326,7 +326,8 @@ def check_device_error(err_tensor):
                                   (N.DEVERR_LEN_MISMATCH, "segment length disagrees with the plan"),
                                   (N.DEVERR_CAPACITY, "segment exceeds its slot capacity"),
                                   (N.DEVERR_PEER_TIMEOUT, "tensor-parallel peer timed out"),
-                                  (N.DEVERR_BAD_INDEX, "device plan or attention plan: index out of range")) if v & bit]
+                                  (N.DEVERR_BAD_INDEX, "device plan, attention plan or prefill score task: "
+                                                       "index out of range")) if v & bit]
         raise N.WnwError(5 if v & N.DEVERR_MBAR_TIMEOUT else 4, "device", ", ".join(names))
 
 
@@ -342,3 +343,71 @@ def packed_attention(q, k, v, cu, scale, scratch=None):
     if scratch is None or not scratch.fits(work.slots, G, D, S):
         scratch = AttnScratch(q.device, work.slots, G, D, S)
     return decode_attention(q.contiguous(), k, v, cu64[:-1].contiguous(), lens, work, scale, scratch)
+
+
+class PrefillScorer:
+    """``wnw_prefill_scores`` for one device: the audio-token scores of a
+    prefill layer for a list of tasks (see the header), with the scratch
+    (per-chunk row statistics) grown on demand and a device error word that
+    ``check()`` reads back (a sync point; call it once, after the last
+    layer)."""
+
+    def __init__(self, device):
+        self.device = torch.device(device)
+        self.err = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self.scratch = torch.empty(0, dtype=torch.uint8, device=self.device)
+
+    def __call__(self, q, k, tasks, heads, scaling, out_len, mask_kind, mask=None, stream=None):
+        """q [B, Hq, S, D] and k [B, Hkv, S, D] (bf16 / fp16, head dims
+        contiguous); tasks: (batch, kv_head, head_off, n_heads, row0, n_rows,
+        audio_start, audio_end, out_off) tuples; heads: query head indices;
+        mask: [B, S, S] additive (mask_kind MASK_ADDITIVE), keys contiguous.
+        Returns the fp32 scores [out_len]."""
+        if q.device != self.device or k.device != self.device or q.device.type != "cuda":
+            raise ValueError(f"q and k must be on {self.device} (a CUDA device)")
+        if q.dim() != 4 or k.dim() != 4 or q.dtype != k.dtype or q.shape[0] != k.shape[0] \
+                or q.shape[2] != k.shape[2] or q.shape[3] != k.shape[3]:
+            raise ValueError(f"q {tuple(q.shape)} / k {tuple(k.shape)}: expected [B, Hq, S, D] and [B, Hkv, S, D] "
+                             "of one dtype")
+        if q.stride(3) != 1 or k.stride(3) != 1:
+            raise ValueError("q and k need contiguous head dimensions")
+        B, Hq, S, D = q.shape
+        out = torch.zeros(max(1, int(out_len)), dtype=torch.float32, device=self.device)
+        if not tasks:
+            return out[:out_len]
+        n = len(tasks)
+        tab = np.zeros((n, 10), np.int32)
+        tab[:, :8] = np.asarray([t[:8] for t in tasks], np.int32)
+        tab.view(np.int64)[:, 4] = np.asarray([t[8] for t in tasks], np.int64)
+        blob = np.concatenate([tab.reshape(-1), np.asarray(heads, np.int32)])
+        dev_blob = torch.from_numpy(blob).pin_memory().to(self.device, non_blocking=True)
+        max_rows = int(max(t[3] * t[5] for t in tasks))
+        max_audio = int(max(t[7] - t[6] for t in tasks))
+        need = C.c_int64()
+        N.call("wnw_prefill_scores_scratch_bytes", n, max_rows, S, C.byref(need))
+        if self.scratch.numel() < need.value:
+            self.scratch = torch.empty(need.value, dtype=torch.uint8, device=self.device)
+        if mask_kind == N.MASK_ADDITIVE:
+            if mask is None or mask.dtype != q.dtype or mask.dim() != 3 or mask.stride(2) != 1:
+                raise ValueError("an additive mask must be [B, S, S] in q's dtype with contiguous keys")
+        a = N.PrefillScoresArgs(
+            dtype=N.dtype_code(q.dtype), head_dim=D, batch=B, num_q_heads=Hq, num_kv_heads=k.shape[1], seq_len=S,
+            num_tasks=n, num_heads=len(heads), max_rows=max_rows, max_audio=max_audio,
+            q=q.data_ptr(), q_stride_b=q.stride(0), q_stride_h=q.stride(1), q_stride_s=q.stride(2),
+            k=k.data_ptr(), k_stride_b=k.stride(0), k_stride_h=k.stride(1), k_stride_s=k.stride(2),
+            mask_kind=int(mask_kind), mask=mask.data_ptr() if mask_kind == N.MASK_ADDITIVE else None,
+            mask_stride_b=mask.stride(0) if mask_kind == N.MASK_ADDITIVE else 0,
+            mask_stride_s=mask.stride(1) if mask_kind == N.MASK_ADDITIVE else 0,
+            scaling=float(scaling), tasks=dev_blob.data_ptr(), heads=dev_blob.data_ptr() + tab.nbytes,
+            out=out.data_ptr(), out_len=out.numel(), scratch=self.scratch.data_ptr(), scratch_bytes=self.scratch.numel(),
+            err=self.err.data_ptr())
+        N.check(N.lib.wnw_prefill_scores(C.byref(a), N.stream_ptr(stream)), "wnw_prefill_scores")
+        _count(2)
+        if stream is not None:  # buffers freed on the current stream must outlive the launches on `stream`
+            for t in (dev_blob, out, self.scratch):
+                t.record_stream(stream)
+        self._keep = dev_blob  # alive until the launches have read it (stream order)
+        return out[:out_len]
+
+    def check(self):
+        check_device_error(self.err)

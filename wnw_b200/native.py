@@ -78,6 +78,28 @@ class OprojAllReduceArgs(C.Structure):
     ]
 
 
+MASK_NONE, MASK_CAUSAL, MASK_ADDITIVE = 0, 1, 2
+
+
+class PrefillTask(C.Structure):
+    _fields_ = [("batch", C.c_int32), ("kv_head", C.c_int32), ("head_off", C.c_int32), ("n_heads", C.c_int32),
+                ("row0", C.c_int32), ("n_rows", C.c_int32), ("audio_start", C.c_int32), ("audio_end", C.c_int32),
+                ("out_off", C.c_int64)]
+
+
+class PrefillScoresArgs(C.Structure):
+    _fields_ = [
+        ("dtype", C.c_int), ("head_dim", C.c_int), ("batch", C.c_int), ("num_q_heads", C.c_int),
+        ("num_kv_heads", C.c_int), ("seq_len", C.c_int), ("num_tasks", C.c_int), ("num_heads", C.c_int),
+        ("max_rows", C.c_int), ("max_audio", C.c_int),
+        ("q", P), ("q_stride_b", C.c_int64), ("q_stride_h", C.c_int64), ("q_stride_s", C.c_int64),
+        ("k", P), ("k_stride_b", C.c_int64), ("k_stride_h", C.c_int64), ("k_stride_s", C.c_int64),
+        ("mask_kind", C.c_int), ("mask", P), ("mask_stride_b", C.c_int64), ("mask_stride_s", C.c_int64),
+        ("scaling", C.c_float), ("tasks", P), ("heads", P), ("out", P), ("out_len", C.c_int64), ("scratch", P),
+        ("scratch_bytes", C.c_int64), ("err", P),
+    ]
+
+
 class FetchInfo(C.Structure):
     _fields_ = [("plan_ints", C.c_int64), ("total_rows", C.c_int64), ("n_ranges", C.c_int64),
                 ("max_moved_rows", C.c_int64), ("fetch_launches", C.c_int64), ("layer_changed", P)]
@@ -146,6 +168,8 @@ _sig("wnw_ipc_close", _S, P, C.c_int)
 _sig("wnw_host_device_pointer", _S, P, C.POINTER(P))
 _sig("wnw_fetch_rows", _S, P, P, C.c_int64, P, P, C.c_int, P, P, C.c_int, P)
 _sig("wnw_fetch_layers", _S, P, P, C.c_int64, P, P, P, C.c_int, P, P, C.c_int, P, P)
+_sig("wnw_prefill_scores", _S, C.POINTER(PrefillScoresArgs), P)
+_sig("wnw_prefill_scores_scratch_bytes", _S, C.c_int, C.c_int, C.c_int, C.POINTER(C.c_int64))
 
 #: every symbol the header declares (checked by the CPU test suite)
 EXPORTS = [
@@ -161,7 +185,7 @@ EXPORTS = [
     "wnw_gather_rows", "wnw_h2d_async", "wnw_stream_wait_event", "wnw_planner_issue_fetch", "wnw_copy_async", "wnw_copy_mapped", "wnw_decode_attn_step", "wnw_oproj_allreduce",
     "wnw_oproj_allreduce_chunks", "wnw_ipc_alloc", "wnw_ipc_open", "wnw_ipc_close", "wnw_host_device_pointer", "wnw_fetch_rows",
     "wnw_fetch_layers", "wnw_planner_upload_plan", "wnw_dplan_create", "wnw_dplan_destroy", "wnw_dplan_step",
-    "wnw_dplan_verify",
+    "wnw_dplan_verify", "wnw_prefill_scores", "wnw_prefill_scores_scratch_bytes",
 ]
 
 

@@ -4,9 +4,9 @@ Mirrors the reference session (src/common/session.py:15-90 and
 src/algorithms/wnw/code/session.py:21-201) call for call, so either session
 can drive either cache:
 
-* prefill: SDPA over the GQA-expanded K/V, per-head audio scores,
-  ``cache.prefill_after_attn``, and ``prefill_all_layers_done`` after the last
-  layer;
+* prefill: SDPA over the GQA-expanded K/V, per-head audio scores
+  (``wnw_prefill_scores`` on the GPU), ``cache.prefill_after_attn``, and
+  ``prefill_all_layers_done`` after the last layer;
 * decode: ``cache.update`` -> ``decode_before_attn`` -> ``fused_decode_attention``
   -> ``o_proj``, and ``decode_all_layers_done`` after the last layer.
 
@@ -20,13 +20,19 @@ import types
 import torch
 import torch.nn.functional as F
 
+from wnw_b200 import native as N
+from wnw_b200.kernels import PrefillScorer
+
 
 class AlgorithmSession:
     """Context manager that installs and removes the patched attention forwards
     (src/common/session.py:15-90); the model is untouched outside the block."""
 
-    def __init__(self, model, adapter, cache, processor=None):
+    def __init__(self, model, adapter, cache, processor=None, prefill_scores=None):
         self.model, self.adapter, self.cache, self.processor = model, adapter, cache, processor
+        # prefill audio scores: the GPU kernel by default; a callable with the
+        # signature of compute_prefill_scores minus ``scorer`` replaces it
+        self.prefill_scores = prefill_scores
         self._state = None
         self._orig = []
 
@@ -70,6 +76,12 @@ class WnWSession(AlgorithmSession):
         H, G, D = meta["num_kv_heads"], meta["num_kv_groups"], meta["head_dim"]
         scaling, layer_idx = meta["scaling"], meta["layer_idx"]
         last = layer_idx == cache.num_layers - 1
+        scores_fn, scorer = self.prefill_scores, None
+        if scores_fn is None:
+            scorer = self._scorer = getattr(self, "_scorer", None) or PrefillScorer(cache.device)
+
+            def scores_fn(*args):
+                return compute_prefill_scores(*args, scorer=scorer)
 
         def patched_forward(self_attn, hidden_states, position_embeddings=None, attention_mask=None,
                             past_key_values=None, **kwargs):
@@ -84,9 +96,11 @@ class WnWSession(AlgorithmSession):
                 out = F.scaled_dot_product_attention(q, kg, vg, attn_mask=attention_mask, scale=scaling,
                                                      is_causal=attention_mask is None)
                 del kg, vg
-                ca, ph = compute_prefill_scores(q, k, attention_mask, cache, layer_idx, B, S, H, G, scaling)
+                ca, ph = scores_fn(q, k, attention_mask, cache, layer_idx, B, S, H, G, scaling)
                 cache.prefill_after_attn(layer_idx, ca, ph, k, v)
                 if last:
+                    if scorer is not None:
+                        scorer.check()  # the score tasks' device error word, once per prefill
                     cache.prefill_all_layers_done()
                 out = out.transpose(1, 2).reshape(B, S, -1).contiguous()
                 return self_attn.o_proj(out), None
@@ -102,73 +116,63 @@ class WnWSession(AlgorithmSession):
         return patched_forward
 
 
-def compute_prefill_scores(q, k, attention_mask, cache, layer_idx, B, S, H, G, scaling):
+def compute_prefill_scores(q, k, attention_mask, cache, layer_idx, B, S, H, G, scaling, scorer):
     """Per-sample class-A audio scores and per-kv-head audio scores from the
     last prefill query (or the mean over the post-audio text queries), as in
     src/algorithms/wnw/code/session.py:121-201 -- including the reference's
     choice of the FIRST class-A q head's kv head for all class-A heads of the
-    layer (session.py:144-147)."""
-    if attention_mask is not None and attention_mask.dim() == 4 and attention_mask.dtype == torch.bool:
-        attention_mask = torch.where(attention_mask, 0.0, float("-inf")).to(q.dtype)
-    if attention_mask is None:
-        # the causal mask's rows the scores read -- the last query, or the
-        # post-audio text queries -- instead of the whole S x S matrix
-        attention_mask = _CausalRows(S, q.device, q.dtype)
+    layer (session.py:144-147) -- in one ``wnw_prefill_scores`` call (two
+    launches) per layer.  Returns views of one fp32 buffer."""
+    mask_kind, mask = _score_mask(attention_mask, q.dtype)
     cfg = cache.config
-    ca_heads = cfg.get_layer_class_a(layer_idx)
-    class_a, per_head = [], []
+    ca_heads = list(cfg.get_layer_class_a(layer_idx))
+    mode = cfg.prefill_score_mode
+    if mode not in ("last", "mean_text"):
+        raise ValueError(f"unknown prefill_score_mode {mode!r}")
+    tasks, heads, spans, off = [], [], [], 0
     for b in range(B):
-        a0, a1 = cache._raw_audio_starts[b], cache._raw_audio_ends[b]
-        if ca_heads:
-            kv = ca_heads[0] // G
-            s = torch.matmul(q[b, ca_heads, -1:, :], k[b, kv:kv + 1].transpose(-1, -2)) * scaling
-            if attention_mask.dim() == 4:
-                s = s + attention_mask[b, :, -1:, :]
-            class_a.append(s.float().softmax(dim=-1)[:, 0, a0:a1].sum(dim=0).detach())
-        else:
-            class_a.append(None)
-        heads = []
+        a0, a1 = int(cache._raw_audio_starts[b]), int(cache._raw_audio_ends[b])
+        n = a1 - a0
+        ca = None
+        if ca_heads:  # the class-A query heads against the first one's kv head, last query
+            tasks.append((b, ca_heads[0] // G, len(heads), len(ca_heads), S - 1, 1, a0, a1, off))
+            heads.extend(ca_heads)
+            ca, off = (off, n), off + n
+        hs = []
         for h in range(H):
             if cfg.is_class_a_kv_head(layer_idx, h):
-                heads.append(None)
+                hs.append(None)
                 continue
-            heads.append(_head_scores(q[b], k[b, h], attention_mask, b, S, h * G, h * G + G, a0, a1, scaling,
-                                      cfg.prefill_score_mode))
-        per_head.append(heads)
+            if mode == "last":
+                row0, rows = S - 1, 1
+            elif S - a1 == 0:  # no text after the audio: zero scores
+                hs.append((off, n))
+                off += n
+                continue
+            else:
+                row0, rows = a1, S - a1
+            tasks.append((b, h, len(heads), G, row0, rows, a0, a1, off))
+            heads.extend(range(h * G, h * G + G))
+            hs.append((off, n))
+            off += n
+        spans.append((ca, hs))
+    out = scorer(q, k, [t for t in tasks if t[7] > t[6]], heads, scaling, off, mask_kind, mask)
+    class_a = [out[s[0]:s[0] + s[1]] if s is not None else None for s, _ in spans]
+    per_head = [[out[s[0]:s[0] + s[1]] if s is not None else None for s in hs] for _, hs in spans]
     return class_a, per_head
 
 
-class _CausalRows:
-    """Stand-in for a [B, 1, S, S] causal mask: indexing [b, :, rows, :]
-    builds only the requested rows (0 on and below the diagonal, -inf above)."""
-
-    def __init__(self, S, device, dtype):
-        self.S, self.device, self.dtype = S, device, dtype
-
-    def dim(self):
-        return 4
-
-    def __getitem__(self, idx):
-        _, _, rows, _ = idx
-        r = torch.arange(self.S, device=self.device)[rows]
-        cols = torch.arange(self.S, device=self.device)
-        m = torch.zeros(r.numel(), self.S, device=self.device, dtype=self.dtype)
-        m.masked_fill_(cols.unsqueeze(0) > r.unsqueeze(1), float("-inf"))
-        return m.unsqueeze(0)
-
-
-def _head_scores(q_all, k_one, mask, b, S, q0, q1, a0, a1, scaling, mode):
-    k = k_one.unsqueeze(0)
-    if mode == "last":
-        s = torch.matmul(q_all[q0:q1, -1:, :], k.transpose(-1, -2)) * scaling
-        if mask is not None and mask.dim() == 4:
-            s = s + mask[b, :, -1:, :]
-        return s.float().softmax(dim=-1)[:, 0, a0:a1].sum(dim=0)
-    if mode == "mean_text":
-        if S - a1 == 0:
-            return torch.zeros(a1 - a0, device=q_all.device, dtype=torch.float32)
-        s = torch.matmul(q_all[q0:q1, a1:, :], k.transpose(-1, -2)) * scaling
-        if mask is not None and mask.dim() == 4:
-            s = s + mask[b, :, a1:, :]
-        return s.float().softmax(dim=-1)[:, :, a0:a1].mean(dim=1).sum(dim=0)
-    raise ValueError(f"unknown prefill_score_mode {mode!r}")
+def _score_mask(attention_mask, dtype):
+    """(mask kind, [B, S, S] additive mask) the reference's score path uses:
+    a causal mask when none is given, nothing for a mask that is not 4-D,
+    else the mask (a boolean one turned into 0 / -inf in the model dtype)."""
+    if attention_mask is None:
+        return N.MASK_CAUSAL, None
+    if attention_mask.dim() != 4:
+        return N.MASK_NONE, None
+    if attention_mask.dtype == torch.bool:
+        attention_mask = torch.where(attention_mask, 0.0, float("-inf")).to(dtype)
+    m = attention_mask[:, 0]
+    if m.dtype != dtype or m.stride(2) != 1:
+        m = m.to(dtype).contiguous()
+    return N.MASK_ADDITIVE, m
