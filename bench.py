@@ -98,6 +98,9 @@ def parse():
                     help="attn mode: plan with clusters of at most this many CTAs (default: the device's largest)")
     ap.add_argument("--sm-count", type=int, default=None,
                     help="attn mode: plan for this many CTA slots (default: the device's resident clusters)")
+    ap.add_argument("--trace", action="store_true",
+                    help="attn mode: load libwnw_b200_trace.so (python -m wnw_b200.build --trace) and report the "
+                         "kernel's per-CTA phase timestamps")
     ap.add_argument("--vs-reference", action="store_true",
                     help="attn mode: also time the reference's own GPU kernels (baseline/_ref) on the same layers")
     return ap.parse_args()
@@ -956,6 +959,52 @@ def reference_kernels(layers, a0, a1, reps):
     return out
 
 
+def trace_phases(layers, reps=3):
+    """Per-CTA phase timestamps (%globaltimer, ns) of ``reps`` passes of the
+    layers' launches back to back, from the trace build: per launch, the
+    first CTA's start, the dependency wait's release, the last CTA's last
+    tile, CTA merge, cluster merge and exit; medians over the launches after
+    the first pass, in us relative to the launch's first CTA start."""
+    import ctypes as C
+    from wnw_b200 import kernels as Kx
+    from wnw_b200 import native as N
+    N.lib.wnw_attn_trace_reset.restype = C.c_int
+    N.lib.wnw_attn_trace_read.restype = C.c_int
+    N.check(N.lib.wnw_attn_trace_reset(), "wnw_attn_trace_reset")
+    st = torch.cuda.current_stream().cuda_stream
+    torch.cuda.synchronize()
+    for _ in range(reps):
+        for x in layers:
+            Kx.launch_attn(x["args"], x["q"], None, None, x["out"], st)
+    torch.cuda.synchronize()
+    buf = np.zeros((16384, 8), np.uint64)
+    n = C.c_int()
+    N.check(N.lib.wnw_attn_trace_read(C.c_void_p(buf.ctypes.data), 16384, C.byref(n)), "wnw_attn_trace_read")
+    rec = buf[:n.value].astype(np.int64)
+    ctas = layers[0]["work"].ctas
+    launches = []
+    for pp in np.unique(rec[:, 1]):  # one plan (pointer) per layer
+        r = rec[rec[:, 1] == pp]
+        r = r[np.argsort(r[:, 2])]
+        for k in range(len(r) // ctas):
+            launches.append(r[k * ctas:(k + 1) * ctas])
+    launches.sort(key=lambda r: r[:, 2].min())
+    rows = []
+    for i, r in enumerate(launches):
+        t0 = r[:, 2].min()
+        ph = [(r[:, 3].min() - t0), (r[:, 3].max() - t0), (r[:, 4].max() - t0), (r[:, 5].max() - t0),
+              (r[:, 6].max() - t0), (r[:, 7].max() - t0)]
+        gap = (r[:, 3].min() - launches[i - 1][:, 7].max()) if i else None
+        rows.append(ph + [gap, t0 - (launches[i - 1][:, 2].min() if i else t0)])
+    rows = rows[len(layers):] or rows
+    med = lambda j: float(np.median([x[j] for x in rows if x[j] is not None])) / 1e3  # noqa: E731
+    names = ["first_wait_release", "last_wait_release", "last_tile_done", "cta_merge_done", "cluster_barrier_done",
+             "last_exit", "release_after_prev_exit", "launch_to_launch"]
+    return {"launches": len(rows), "ctas_per_launch": ctas, "median_us": {nm: med(j) for j, nm in enumerate(names)},
+            "how": "%globaltimer per CTA (trace build), times from the launch's first CTA start; "
+                   "release_after_prev_exit = this launch's first wait release - the previous launch's last exit"}
+
+
 def mode_attn(a, dev):
     """Decode attention alone on one layer geometry (config 2's by default:
     two class-A segments of 15,100 rows, scored, and six class-B ones of
@@ -976,6 +1025,8 @@ def mode_attn(a, dev):
             "how": "CUDA-graph replay of the layers' launches back to back, CUDA events"}
     if a.check:
         line["max_abs_err"] = max(check_attn(x) for x in layers[:2])
+    if a.trace:
+        line["trace"] = trace_phases(layers)
     if a.vs_reference:
         try:
             line["reference_kernels"] = reference_kernels(layers, 4, min(a.class_a, 15004),
@@ -1127,6 +1178,8 @@ def traffic_per_launch(algorithmic_bytes):
 # ------------------------------------------------------------------ main
 def main():
     a = parse()
+    if a.trace:  # before anything loads the library
+        os.environ.setdefault("WNW_B200_LIB", os.path.join(ROOT, "wnw_b200", "libwnw_b200_trace.so"))
     use_config(a.config, a.synthetic, a.depth)
     a.synth = a.config in SYNTH and (a.config != 2 or a.synthetic)
     rank = int(os.environ.get("RANK", "0"))

@@ -172,13 +172,14 @@ int wnw_split_rows(int dtype, int head_dim);
  * (to at most 1,536 rows) so the longest segment fits one cluster of
  * `max_cluster` CTAs -- and a segment needing k CTAs gets k consecutive
  * ranks of one cluster (clusters hold the smallest power of two >= the
- * largest such k, at most max_cluster; short segments share clusters).  When
- * the longest segment does not fit one cluster that way, or the equal share
- * itself exceeds 1,536 rows, clusters hold at most 4 CTAs, the share is
- * sized to whole waves of the resident slots (of 1 to 4 waves, the count
- * whose waves x (share + 512 rows of fixed cost) is least), and a segment needing more CTAs than a
- * cluster holds takes whole clusters, each writing a partial that the
- * combine kernel merges.
+ * largest such k, at most max_cluster; short segments share clusters), the
+ * share raised further if needed so the clusters fit one wave of those the
+ * device holds at once.  When the longest segment does not fit one cluster
+ * that way, or the equal share itself exceeds 1,536 rows, clusters hold at
+ * most 4 CTAs, the share is sized to whole waves of the resident slots (of 1
+ * to 4 waves, the count whose waves x (share + 512 rows of fixed cost) is
+ * least), and a segment needing more CTAs than a cluster holds takes whole
+ * clusters, each writing a partial that the combine kernel merges.
  * sm_count <= 0: the current device's SMs and its resident clusters of the
  * kernel (otherwise sm_count stands for the slots at every cluster size);
  * max_cluster <= 0: 16 when the device holds clusters of 16 of the kernel,
@@ -198,6 +199,10 @@ typedef struct {
 } wnw_attn_plan_info;
 wnw_status wnw_attn_plan(const int32_t* seg_cap, int num_segs, int sm_count, int max_cluster, int32_t* plan,
                          int64_t max_ints, wnw_attn_plan_info* info);
+/* Clusters of `cluster` CTAs (1..16) of the tensor-core decode-attention
+ * kernel (head_dim 64 or 128) the current device holds at once
+ * (cudaOccupancyMaxActiveClusters); wnw_attn_plan sizes its waves by it. */
+wnw_status wnw_attn_resident_clusters(int head_dim, int cluster, int* n);
 
 /* Launch shape for one layer (no reference counterpart: the reference's
  * kernels take one CTA per segment).  From the per-segment row capacities,

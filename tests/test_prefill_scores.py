@@ -7,8 +7,9 @@ is executed task by task in torch and must equal the oracle bit for bit --
 this pins what each task means (query heads, positions, kv head, audio
 columns, mask) without a GPU.  GPU: the kernel against the oracle run on the
 same GPU tensors, in both score modes, with causal, boolean and additive
-masks, left-padded batches, GQA groups 4 and 8, head_dim 64 and 128, bf16 and
-fp16, row counts above one shared-memory block; results repeat bit for bit,
+masks, left-padded batches, GQA groups 4 and 8, head_dim 16 to 128, fp32,
+bf16 and fp16, row counts above one shared-memory block; results repeat bit
+for bit,
 and a task with an out-of-range index raises instead of writing.
 """
 import numpy as np
@@ -143,6 +144,36 @@ def test_prefill_scores_kernel_matches_oracle(dev, dtype, p):
         assert float(rel.max()) < 2e-2, float(rel.max())
         assert float((rel < 1e-4).float().mean()) > 0.99
         torch.testing.assert_close(x.sum(), y.sum(), rtol=1e-4, atol=1e-6)
+
+
+CC_CASES = [(torch.float32, dict(mode="last", D=16)), (torch.float32, dict(mode="mean_text", D=16, mask="bool")),
+            (torch.float32, dict(mode="mean_text", D=64)), (torch.float32, dict(mode="last", D=128, mask="additive")),
+            (torch.bfloat16, dict(mode="mean_text", D=32)), (torch.float16, dict(mode="last", D=16, class_a=()))]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype,p", CC_CASES)
+def test_prefill_scores_cuda_core_path(dev, dtype, p):
+    """fp32 q / k (the tiny session models) and 16-bit ones with head_dim
+    16 / 32 take the CUDA-core kernels: fp32 logits agree with the oracle to
+    summation order; 16-bit ones as on the tensor-core path."""
+    from wnw_b200.kernels import PrefillScorer
+    from wnw_b200.session import compute_prefill_scores
+    scorer = PrefillScorer(dev)
+    got = _flat(_run(compute_prefill_scores, dev, dtype, p, scorer=scorer))
+    again = _flat(_run(compute_prefill_scores, dev, dtype, p, scorer=scorer))
+    want = _flat(_run(oracle_scores, dev, dtype, p))
+    scorer.check()
+    for x, x2, y in zip(got, again, want):
+        assert (x is None) == (y is None)
+        if x is None or x.numel() == 0:
+            continue
+        assert torch.equal(x, x2)
+        rel = (x - y.float()).abs() / y.float().abs().clamp_min(1e-30)
+        if dtype == torch.float32:
+            assert float(rel.max()) < 1e-4, float(rel.max())
+        else:
+            assert float(rel.max()) < 2e-2 and float((rel < 1e-4).float().mean()) > 0.99
 
 
 @pytest.mark.gpu

@@ -136,6 +136,13 @@ extern "C" wnw_status wnw_build_work_table(const int32_t* seg_cap, int num_segs,
   return WNW_OK;
 }
 
+extern "C" wnw_status wnw_attn_resident_clusters(int head_dim, int cluster, int* n) {
+  using namespace wnw;
+  WNW_CHECK_ARG(n, "null pointer argument");
+  WNW_CHECK_ARG(cluster >= 1 && cluster <= 16, "cluster must be in 1..16");
+  return attn_mma_active_clusters_any(head_dim, cluster, n);
+}
+
 extern "C" wnw_status wnw_attn_plan(const int32_t* seg_cap, int num_segs, int sm_count, int max_cluster,
                                     int32_t* plan, int64_t max_ints, wnw_attn_plan_info* info) {
   using namespace wnw;
@@ -182,36 +189,42 @@ extern "C" wnw_status wnw_attn_plan(const int32_t* seg_cap, int num_segs, int sm
   // large clusters tie a segment's CTAs to a few GPCs and stream long
   // segments slower -- and a share sized to whole waves of resident CTAs.
   int cl = max_cluster;
+  int c = 1;  // the cluster size of the plan at share sh (set by ctas_at)
+  auto ctas_at = [&](int64_t sh) {  // the CTAs the packing below makes at share sh
+    int64_t km = 1;
+    for (int s = 0; s < num_segs; ++s) km = std::max(km, (units[s] + sh - 1) / sh);
+    c = 1;
+    while (c < std::min<int64_t>(km, cl)) c *= 2;
+    int64_t n = 0, clusters = 0;
+    std::vector<int64_t> need(c + 1, 0), free(c + 1, 0);  // segments by CTAs; clusters by free ranks
+    for (int s = 0; s < num_segs; ++s) {
+      const int64_t k = std::max<int64_t>(1, (units[s] + sh - 1) / sh);
+      if (k > c)
+        n += (k + c - 1) / c * c;
+      else
+        ++need[k];
+    }
+    for (int k = c; k >= 1; --k) {
+      for (; need[k] > 0; --need[k]) {
+        int f = k;
+        while (f < c && free[f] == 0) ++f;
+        if (f == c) ++clusters;
+        else --free[f];
+        if (f - k > 0) ++free[f - k];
+      }
+    }
+    return n + clusters * c;
+  };
   int64_t share = std::max<int64_t>((total + slots_for(cl) - 1) / slots_for(cl),
                                     std::min<int64_t>(kMaxShareUnits, (umax + cl - 1) / cl));
-  if ((umax + share - 1) / share > cl || share > kMaxShareUnits) {
+  if ((umax + share - 1) / share <= cl && share <= kMaxShareUnits) {
+    // one cluster per segment: keep the launch to one wave of the clusters
+    // the device holds at once (a larger share means fewer CTAs per segment
+    // and smaller clusters)
+    for (int it = 0; it < 256 && ctas_at(share) > slots_for(c) && share < umax; ++it)
+      share = std::min(umax, share + std::max<int64_t>(1, share / 16));
+  } else {
     cl = std::min(cl, 4);
-    int c = 1;  // the cluster size of the plan at share sh (set by ctas_at)
-    auto ctas_at = [&](int64_t sh) {  // the CTAs the packing below makes at share sh
-      int64_t km = 1;
-      for (int s = 0; s < num_segs; ++s) km = std::max(km, (units[s] + sh - 1) / sh);
-      c = 1;
-      while (c < std::min<int64_t>(km, cl)) c *= 2;
-      int64_t n = 0, clusters = 0;
-      std::vector<int64_t> need(c + 1, 0), free(c + 1, 0);  // segments by CTAs; clusters by free ranks
-      for (int s = 0; s < num_segs; ++s) {
-        const int64_t k = std::max<int64_t>(1, (units[s] + sh - 1) / sh);
-        if (k > c)
-          n += (k + c - 1) / c * c;
-        else
-          ++need[k];
-      }
-      for (int k = c; k >= 1; --k) {
-        for (; need[k] > 0; --need[k]) {
-          int f = k;
-          while (f < c && free[f] == 0) ++f;
-          if (f == c) ++clusters;
-          else --free[f];
-          if (f - k > 0) ++free[f - k];
-        }
-      }
-      return n + clusters * c;
-    };
     // for w = 1..4 waves: the smallest share whose CTAs fit w waves of the
     // resident slots (or every segment down to one CTA); then the w whose
     // waves x (share + a CTA's fixed cost) -- the busiest SM's time -- is

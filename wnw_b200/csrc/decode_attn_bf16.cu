@@ -1,5 +1,7 @@
 // Instantiations of the decode-attention kernel for one dtype (split per
 // dtype so the three translation units compile in parallel).
+#include <algorithm>
+
 #include "decode_attn_mma.cuh"
 
 namespace wnw {
@@ -61,3 +63,24 @@ wnw_status attn_mma_active_clusters_any(int head_dim, int cs, int* n) {
 }
 
 }  // namespace wnw
+
+#ifdef WNW_ATTN_TRACE
+// Trace build only (not part of the product ABI): clear and read the bf16
+// tensor-core kernel's phase records.
+extern "C" wnw_status wnw_attn_trace_reset(void) {
+  using namespace wnw;
+  const int zero = 0;
+  WNW_CUDA_TRY(cudaMemcpyToSymbol(g_attn_trace_n, &zero, sizeof(int)));
+  return WNW_OK;
+}
+extern "C" wnw_status wnw_attn_trace_read(unsigned long long* out, int max_records, int* n) {
+  using namespace wnw;
+  WNW_CHECK_ARG(out && n && max_records >= 0, "null pointer argument");
+  int cnt = 0;
+  WNW_CUDA_TRY(cudaMemcpyFromSymbol(&cnt, g_attn_trace_n, sizeof(int)));
+  cnt = std::min(std::min(cnt, kTraceCap), max_records);
+  if (cnt > 0) WNW_CUDA_TRY(cudaMemcpyFromSymbol(out, g_attn_trace, size_t(cnt) * 8 * sizeof(unsigned long long)));
+  *n = cnt;
+  return WNW_OK;
+}
+#endif

@@ -40,6 +40,30 @@ constexpr int kTcTileRows = 128;   // 8 warps x 16 rows
 constexpr int kTcStages = 3;
 constexpr int kTcMaxCluster = 16;
 
+#ifdef WNW_ATTN_TRACE
+// Phase timestamps of every CTA (the trace build only: python -m
+// wnw_b200.build --trace).  Per record: meta (block | smid << 16 | cluster
+// rank << 24 | rows << 32), the plan pointer (which layer), and %globaltimer
+// at kernel entry, after the dependency wait, after the last tile, after the
+// CTA merge, after the first cluster barrier and at exit.
+constexpr int kTraceCap = 16384;
+static __device__ unsigned long long g_attn_trace[kTraceCap][8];
+static __device__ int g_attn_trace_n;
+__device__ __forceinline__ unsigned long long gtimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+#define WNW_TR(i)                   \
+  do {                              \
+    if (tid == 0) tr_[i] = gtimer(); \
+  } while (0)
+#else
+#define WNW_TR(i) \
+  do {            \
+  } while (0)
+#endif
+
 // byte offset of (row, 16-byte chunk) inside a 128-byte-swizzled tile whose
 // base is 1024-byte aligned
 __device__ __forceinline__ uint32_t swz(int row, int chunk) {
@@ -88,6 +112,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
+#ifdef WNW_ATTN_TRACE
+  unsigned long long tr_[6] = {0, 0, 0, 0, 0, 0};
+#endif
+  WNW_TR(0);
 
   // ---- this CTA's item (plan constants: read before the dependency wait)
   const int4 it = __ldg(pv.cta + blockIdx.x);
@@ -160,6 +188,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     if (lane == 0)
       for (int t = 0; t < min(ntiles, kTcStages); ++t) issue(t);
     pdl_wait();  // q, the new rows and the outputs may belong to the preceding kernel
+    WNW_TR(1);
   } else {
     // L2 prefetch of this CTA's first rows by capacity (layout constants
     // only; L2 is the point of coherence, so rows the preceding kernel still
@@ -173,6 +202,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
     }
     pdl_wait();  // seg_len, K/V rows and q may come from the preceding kernel
+    WNW_TR(1);
     schedule();
     if (lane == 0)
       for (int t = 0; t < min(ntiles, kTcStages); ++t) issue(t);
@@ -328,6 +358,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     __syncwarp();  // the warp is done with its rows of this stage
     if (lane == 0 && t + kTcStages < ntiles) issue(t + kTcStages);
   }
+  WNW_TR(2);
   // the lane-held sums over the warp's rows
 #pragma unroll
   for (int off = 4; off < 32; off <<= 1) {
@@ -388,8 +419,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       Pl[g] = ls;
     }
   }
+  WNW_TR(3);
   cluster_arrive();  // CTA partials visible to the cluster
   cluster_wait();
+  WNW_TR(4);
   if (active && crank == leader && !(to_part && it.y >= total && it.y > 0)) {
     float* part_out = to_part ? p.partials + int64_t(part) * PartIO<D, G>::kStride : nullptr;
     for (int i = 4 * tid; i < G * D; i += 4 * kTcThreads) {
@@ -434,6 +467,20 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   }
   cluster_arrive();  // keep this CTA's shared memory until its leader has read it
   cluster_wait();
+#ifdef WNW_ATTN_TRACE
+  WNW_TR(5);
+  if (tid == 0) {
+    const int k = atomicAdd(&g_attn_trace_n, 1);
+    if (k < kTraceCap) {
+      unsigned smid;
+      asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+      g_attn_trace[k][0] = uint64_t(blockIdx.x) | (uint64_t(smid) << 16) | (uint64_t(crank) << 24) |
+                           (uint64_t(uint32_t(rows)) << 32);
+      g_attn_trace[k][1] = reinterpret_cast<uint64_t>(pv.cta);
+      for (int i = 0; i < 6; ++i) g_attn_trace[k][2 + i] = tr_[i];
+    }
+  }
+#endif
 }
 
 // Merge of the cluster partials of a segment that spans several clusters

@@ -9,9 +9,10 @@
 // chunk's keys.  Pass 2, one CTA per (task, 1,024 audio keys): merges the
 // chunks' statistics of every row (in chunk order), recomputes the audio
 // keys' logits and adds exp(x - max) / sum over the rows, in a fixed order.
-// Logits come from the tensor cores (mma m16n8k16, keys as m, query rows as
-// n, fp32 accumulation) and are rounded to the model dtype exactly where the
-// reference rounds them.
+// Logits of 16-bit q / k with head_dim 64 or 128 come from the tensor cores
+// (mma m16n8k16, keys as m, query rows as n, fp32 accumulation); fp32 ones
+// and small head dims from CUDA-core FMAs.  They are rounded to the model
+// dtype exactly where the reference rounds them (not at all for fp32).
 #include <algorithm>
 #include <cmath>
 
@@ -275,6 +276,137 @@ __global__ void __launch_bounds__(kPfThreads) prefill_colsum_kernel(PfParams p) 
   }
 }
 
+// ---- CUDA-core variant: fp32 q / k, or 16-bit ones with head_dim 16 / 32.
+// Same two passes, same statistics layout; dot products in fp32 FMAs, one key
+// per lane, the 8 query rows of a tile (pass 1) or a block of rows (pass 2)
+// staged in shared memory as fp32.
+constexpr int kPfCcRows = 32;  // query rows staged at a time in pass 2
+
+template <typename T, int D>
+__device__ __forceinline__ void load_row_f(const T* src, float (&x)[D]) {
+  constexpr int E = 16 / sizeof(T);  // elements per 16-byte load
+#pragma unroll
+  for (int c = 0; c < D / E; ++c) unpack16<T>(__ldg(reinterpret_cast<const uint4*>(src) + c), x + c * E);
+}
+
+template <typename T, int D>
+__global__ void __launch_bounds__(kPfThreads) prefill_stats_cc_kernel(PfParams p) {
+  const wnw_prefill_task t = p.tasks[blockIdx.y];
+  if (!task_ok(t, p)) {
+    if (blockIdx.x == 0 && threadIdx.x == 0) atomicOr(p.err, WNW_DEVERR_BAD_INDEX);
+    return;
+  }
+  const int k0 = blockIdx.x * kPfChunk;
+  if (k0 >= p.S) return;
+  const int k1 = min(p.S, k0 + kPfChunk);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int R = t.n_heads * t.n_rows;
+  const T* kb = static_cast<const T*>(p.k) + t.batch * p.ksb + t.kv_head * p.ksh;
+  __shared__ float qs[8][D];
+  __shared__ float2 red[kPfWarps][8];
+  for (int rt = 0; rt < R; rt += 8) {
+    __syncthreads();  // the previous tile's rows and partials are no longer read
+    for (int i = threadIdx.x; i < 8 * D; i += kPfThreads) {
+      const T* qr = q_row<T>(p, t, rt + i / D, R);
+      qs[i / D][i % D] = qr ? DT<T>::to_f(qr[i % D]) : 0.f;
+    }
+    __syncthreads();
+    float m[8], l[8];
+#pragma unroll
+    for (int r = 0; r < 8; ++r) m[r] = -INFINITY, l[r] = 0.f;
+    for (int j = k0 + warp * 32 + lane; j < k1; j += kPfThreads) {
+      float kv[D];
+      load_row_f<T, D>(kb + int64_t(j) * p.kss, kv);
+#pragma unroll
+      for (int r = 0; r < 8; ++r) {
+        float dot = 0.f;
+#pragma unroll
+        for (int d = 0; d < D; ++d) dot = fmaf(qs[r][d], kv[d], dot);
+        online(m[r], l[r], logit<T>(p, t, dot, row_pos(t, rt + r, R), j));
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const float m2 = __shfl_xor_sync(0xffffffffu, m[r], o), l2 = __shfl_xor_sync(0xffffffffu, l[r], o);
+        merge(m[r], l[r], m2, l2);
+      }
+      if (lane == 0) red[warp][r] = make_float2(m[r], l[r]);
+    }
+    __syncthreads();
+    if (threadIdx.x < 8 && rt + int(threadIdx.x) < R) {
+      float mm = -INFINITY, ll = 0.f;
+      for (int w = 0; w < kPfWarps; ++w) merge(mm, ll, red[w][threadIdx.x].x, red[w][threadIdx.x].y);
+      p.stats[(int64_t(blockIdx.y) * p.max_rows + rt + threadIdx.x) * p.n_chunks + blockIdx.x] = make_float2(mm, ll);
+    }
+  }
+}
+
+template <typename T, int D>
+__global__ void __launch_bounds__(kPfThreads) prefill_colsum_cc_kernel(PfParams p) {
+  const wnw_prefill_task t = p.tasks[blockIdx.y];
+  if (!task_ok(t, p)) return;  // flagged by pass 1
+  const int j = t.audio_start + blockIdx.x * kPfThreads + threadIdx.x;
+  if (t.audio_start + int(blockIdx.x) * kPfThreads >= t.audio_end) return;  // CTA-uniform
+  const bool valid = j < t.audio_end;
+  const int R = t.n_heads * t.n_rows;
+  const T* kb = static_cast<const T*>(p.k) + t.batch * p.ksb + t.kv_head * p.ksh;
+  __shared__ float qs[kPfCcRows][D];
+  __shared__ float2 st[kPfCcRows];
+  float kv[D];
+  if (valid) load_row_f<T, D>(kb + int64_t(j) * p.kss, kv);
+  float acc = 0.f;
+  for (int rb = 0; rb < R; rb += kPfCcRows) {
+    const int nr = min(kPfCcRows, R - rb);
+    __syncthreads();
+    for (int i = threadIdx.x; i < kPfCcRows * D; i += kPfThreads) {
+      const T* qr = q_row<T>(p, t, rb + i / D, R);
+      qs[i / D][i % D] = qr ? DT<T>::to_f(qr[i % D]) : 0.f;
+    }
+    for (int r = threadIdx.x; r < nr; r += kPfThreads) {
+      float m = -INFINITY, l = 0.f;
+      const float2* sp = p.stats + (int64_t(blockIdx.y) * p.max_rows + rb + r) * p.n_chunks;
+      for (int c = 0; c < p.n_chunks; ++c) {
+        const float2 v = sp[c];
+        merge(m, l, v.x, v.y);
+      }
+      st[r] = make_float2(m, l);
+    }
+    __syncthreads();
+    if (valid) {
+      for (int r = 0; r < nr; ++r) {
+        float dot = 0.f;
+#pragma unroll
+        for (int d = 0; d < D; ++d) dot = fmaf(qs[r][d], kv[d], dot);
+        const float x = logit<T>(p, t, dot, row_pos(t, rb + r, R), j);
+        if (x > -INFINITY) acc += expf(x - st[r].x) / st[r].y;
+      }
+    }
+  }
+  if (valid) p.out[t.out_off + j - t.audio_start] = t.n_rows > 1 ? acc / float(t.n_rows) : acc;
+}
+
+template <typename T, int D>
+wnw_status launch_pf_cc(const PfParams& p, int num_tasks, cudaStream_t s) {
+  prefill_stats_cc_kernel<T, D><<<dim3(p.n_chunks, num_tasks), kPfThreads, 0, s>>>(p);
+  WNW_CUDA_TRY(cudaGetLastError());
+  const int ax = std::max(1, (p.max_audio + kPfThreads - 1) / kPfThreads);
+  prefill_colsum_cc_kernel<T, D><<<dim3(ax, num_tasks), kPfThreads, 0, s>>>(p);
+  WNW_CUDA_TRY(cudaGetLastError());
+  return WNW_OK;
+}
+
+template <typename T>
+wnw_status launch_pf_cc_any(const PfParams& p, int head_dim, int num_tasks, cudaStream_t s) {
+  switch (head_dim) {
+    case 16: return launch_pf_cc<T, 16>(p, num_tasks, s);
+    case 32: return launch_pf_cc<T, 32>(p, num_tasks, s);
+    case 64: return launch_pf_cc<T, 64>(p, num_tasks, s);
+    default: return launch_pf_cc<T, 128>(p, num_tasks, s);
+  }
+}
+
 template <typename T, int D>
 wnw_status launch_pf(const PfParams& p, int num_tasks, cudaStream_t s) {
   static bool configured = false;  // the dynamic shared memory opt-in, once per instantiation
@@ -305,8 +437,9 @@ extern "C" wnw_status wnw_prefill_scores_scratch_bytes(int num_tasks, int max_ro
 extern "C" wnw_status wnw_prefill_scores(const wnw_prefill_scores_args* a, void* stream) {
   using namespace wnw;
   WNW_CHECK_ARG(a, "null pointer argument");
-  WNW_CHECK_ARG(a->dtype == WNW_BF16 || a->dtype == WNW_F16, "prefill scores take bf16 or fp16 q/k");
-  WNW_CHECK_ARG(a->head_dim == 64 || a->head_dim == 128, "head_dim must be 64 or 128");
+  WNW_CHECK_ARG(a->dtype == WNW_BF16 || a->dtype == WNW_F16 || a->dtype == WNW_F32, "unknown dtype %d", a->dtype);
+  WNW_CHECK_ARG(a->head_dim == 16 || a->head_dim == 32 || a->head_dim == 64 || a->head_dim == 128,
+                "head_dim must be 16, 32, 64 or 128");
   WNW_CHECK_ARG(a->num_tasks >= 0 && a->num_tasks <= 65535, "num_tasks must be in 0..65535");
   if (a->num_tasks == 0) return WNW_OK;
   WNW_CHECK_ARG(a->batch > 0 && a->num_q_heads > 0 && a->num_kv_heads > 0 && a->seq_len > 0 && a->num_heads > 0 &&
@@ -317,9 +450,10 @@ extern "C" wnw_status wnw_prefill_scores(const wnw_prefill_scores_args* a, void*
                 "unknown mask kind %d", a->mask_kind);
   WNW_CHECK_ARG(a->mask_kind != WNW_MASK_ADDITIVE || a->mask, "an additive mask needs its pointer");
   WNW_CHECK_ARG(aligned16(a->q) && aligned16(a->k), "q and k must be 16-byte aligned");
-  WNW_CHECK_ARG(a->q_stride_b % 8 == 0 && a->q_stride_h % 8 == 0 && a->q_stride_s % 8 == 0 &&
-                    a->k_stride_b % 8 == 0 && a->k_stride_h % 8 == 0 && a->k_stride_s % 8 == 0,
-                "q / k strides must be multiples of 8 elements (16-byte rows)");
+  const int epc = a->dtype == WNW_F32 ? 4 : 8;  // elements per 16 bytes
+  WNW_CHECK_ARG(a->q_stride_b % epc == 0 && a->q_stride_h % epc == 0 && a->q_stride_s % epc == 0 &&
+                    a->k_stride_b % epc == 0 && a->k_stride_h % epc == 0 && a->k_stride_s % epc == 0,
+                "q / k strides must be multiples of 16 bytes");
   int64_t need = 0;
   wnw_status st = wnw_prefill_scores_scratch_bytes(a->num_tasks, a->max_rows, a->seq_len, &need);
   if (st != WNW_OK) return st;
@@ -357,6 +491,10 @@ extern "C" wnw_status wnw_prefill_scores(const wnw_prefill_scores_args* a, void*
   p.n_chunks = (a->seq_len + kPfChunk - 1) / kPfChunk;
   p.err = a->err;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (a->dtype == WNW_F32) return launch_pf_cc_any<float>(p, a->head_dim, a->num_tasks, s);
+  if (a->head_dim < 64)  // tensor-core tiles cover head_dim 64 and 128
+    return a->dtype == WNW_BF16 ? launch_pf_cc_any<__nv_bfloat16>(p, a->head_dim, a->num_tasks, s)
+                                : launch_pf_cc_any<__half>(p, a->head_dim, a->num_tasks, s);
   if (a->dtype == WNW_BF16)
     return a->head_dim == 128 ? launch_pf<__nv_bfloat16, 128>(p, a->num_tasks, s)
                               : launch_pf<__nv_bfloat16, 64>(p, a->num_tasks, s);

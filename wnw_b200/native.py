@@ -169,6 +169,7 @@ _sig("wnw_host_device_pointer", _S, P, C.POINTER(P))
 _sig("wnw_fetch_rows", _S, P, P, C.c_int64, P, P, C.c_int, P, P, C.c_int, P)
 _sig("wnw_fetch_layers", _S, P, P, C.c_int64, P, P, P, C.c_int, P, P, C.c_int, P, P)
 _sig("wnw_prefill_scores", _S, C.POINTER(PrefillScoresArgs), P)
+_sig("wnw_attn_resident_clusters", _S, C.c_int, C.c_int, C.POINTER(C.c_int))
 _sig("wnw_prefill_scores_scratch_bytes", _S, C.c_int, C.c_int, C.c_int, C.POINTER(C.c_int64))
 
 #: every symbol the header declares (checked by the CPU test suite)
@@ -185,7 +186,7 @@ EXPORTS = [
     "wnw_gather_rows", "wnw_h2d_async", "wnw_stream_wait_event", "wnw_planner_issue_fetch", "wnw_copy_async", "wnw_copy_mapped", "wnw_decode_attn_step", "wnw_oproj_allreduce",
     "wnw_oproj_allreduce_chunks", "wnw_ipc_alloc", "wnw_ipc_open", "wnw_ipc_close", "wnw_host_device_pointer", "wnw_fetch_rows",
     "wnw_fetch_layers", "wnw_planner_upload_plan", "wnw_dplan_create", "wnw_dplan_destroy", "wnw_dplan_step",
-    "wnw_dplan_verify", "wnw_prefill_scores", "wnw_prefill_scores_scratch_bytes",
+    "wnw_dplan_verify", "wnw_prefill_scores", "wnw_prefill_scores_scratch_bytes", "wnw_attn_resident_clusters",
 ]
 
 
