@@ -60,11 +60,11 @@ const char* wnw_last_error(void);
  *    the layer's work plan from wnw_attn_plan -- every CTA attends one row
  *    range of one segment, a segment's CTAs share one thread-block cluster of
  *    `cluster_size` CTAs and merge through distributed shared memory, and a
- *    segment too long for one cluster spans several whose partials a second
- *    kernel (launched here, after the first) merges in order -- with
- *    plan_ctas / cluster_size / plan_parts / plan_combine copied from its
- *    wnw_attn_plan_info.  work / n_clusters / split_rows / counters are not
- *    used.
+ *    segment too long for one cluster spans several: each writes its partial,
+ *    arrives at the segment's counter, and the last to arrive merges the
+ *    partials in order -- with plan_ctas / cluster_size / plan_parts /
+ *    plan_combine copied from its wnw_attn_plan_info.  work / n_clusters /
+ *    split_rows are not used; counters only when plan_combine > 0.
  *  - CUDA-core path (fp32, or head_dim 16 / 32): work is split into
  *    `split_rows`-row pieces grouped into clusters of `cluster_size` CTAs;
  *    `work` lists (segment, cluster index within the segment) pairs covering
@@ -110,8 +110,8 @@ typedef struct wnw_decode_attn_args {
   const int64_t* logits_off;     /* [n_slots] element offset of each slot    */
   float* stats;                  /* [num_segs][2][group] or NULL             */
   /* scratch: partials [n_clusters, or plan_parts][group][head_dim + 2]
-     fp32, counters [num_segs] int32 (CUDA-core path; zero before first use,
-     kernels leave them zero) */
+     fp32, counters [num_segs] int32 (CUDA-core path, and plans with combine
+     entries; zero before first use, kernels leave them zero) */
   float* partials;
   int32_t* counters;
   int32_t* err;                  /* device error word (WNW_DEVERR_* bits)    */
@@ -179,7 +179,7 @@ int wnw_split_rows(int dtype, int head_dim);
  * most 4 CTAs, the share is sized to whole waves of the resident slots (of 1
  * to 4 waves, the count whose waves x (share + 512 rows of fixed cost) is
  * least), and a segment needing more CTAs than a cluster holds takes whole
- * clusters, each writing a partial that the combine kernel merges.
+ * clusters, each writing a partial that the last of them to finish merges.
  * sm_count <= 0: the current device's SMs and its resident clusters of the
  * kernel (otherwise sm_count stands for the slots at every cluster size);
  * max_cluster <= 0: 16 when the device holds clusters of 16 of the kernel,

@@ -185,7 +185,7 @@ extern "C" wnw_status wnw_attn_plan(const int32_t* seg_cap, int num_segs, int sm
   // kMaxShareUnits; every segment then merges in distributed shared memory.
   // When a segment does not fit one cluster anyway, or the equal share itself
   // exceeds kMaxShareUnits (a large layer), segments may span several
-  // clusters (merged by the combine kernel): then clusters of at most 4 --
+  // clusters (merged by the last of them to finish): then clusters of at most 4 --
   // large clusters tie a segment's CTAs to a few GPCs and stream long
   // segments slower -- and a share sized to whole waves of resident CTAs.
   int cl = max_cluster;
@@ -279,7 +279,7 @@ extern "C" wnw_status wnw_attn_plan(const int32_t* seg_cap, int num_segs, int sm
     }
   };
   // segments needing more CTAs than a cluster holds: whole clusters, each
-  // an even share of the segment's units, merged by the combine kernel
+  // an even share of the segment's units; the last cluster to finish merges them
   for (int s = 0; s < num_segs; ++s) {
     if (k[s] <= C) continue;
     const int64_t ncl = (k[s] + C - 1) / C;

@@ -83,7 +83,8 @@ struct AttnPlanView {
   const int32_t* part_r0;
   const int4* comb;
   int parts;
-  int ready;  // WNW_ATTN_ROWS_READY given
+  int combine;  // entries of comb
+  int ready;    // WNW_ATTN_ROWS_READY given
 };
 
 // rows of a segment attended at this launch: stored rows + the step's token
@@ -467,6 +468,80 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   }
   cluster_arrive();  // keep this CTA's shared memory until its leader has read it
   cluster_wait();
+  // ---- a segment spanning several clusters: each cluster's leader arrives
+  // at the segment's counter once its partial is out; the last to arrive
+  // merges the segment's partials in order (no second kernel, no wait)
+  if (active && to_part && crank == leader) {
+    __shared__ int s_last, s_first, s_n;
+    __syncthreads();  // this CTA's partial stores are issued (CTA scope) ...
+    if (tid == 0) {
+      int lo = 0, hi = pv.combine;  // the combine entry holding `part` (entries ordered by first partial)
+      while (hi - lo > 1) {
+        const int mid = (lo + hi) >> 1;
+        if (__ldg(&pv.comb[mid].y) <= part) lo = mid; else hi = mid;
+      }
+      const int4 e = pv.combine > 0 ? __ldg(pv.comb + lo) : make_int4(-1, 0, 0, 0);
+      int last = 0;
+      if (e.x == seg && e.y <= part && part < e.y + e.z && e.y + e.z <= pv.parts) {
+        fence_acq_rel_gpu();  // ... and released at gpu scope before the arrival
+        last = (atomicAdd(p.counters + seg, 1) == e.z - 1) ? 1 : 0;
+        if (last) {
+          p.counters[seg] = 0;  // every partial of this launch has arrived
+          fence_acq_rel_gpu();  // acquire the others' partials
+        }
+      } else {
+        atomicOr(p.err, WNW_DEVERR_BAD_INDEX);
+      }
+      s_last = last;
+      s_first = e.y;
+      s_n = e.z;
+    }
+    __syncthreads();
+    if (s_last) {
+      // partials whose range starts below the row count (a prefix; the first always counts)
+      int n_act = 1;
+      while (n_act < s_n && __ldg(pv.part_r0 + s_first + n_act) < total) ++n_act;
+      const float* base = p.partials + int64_t(s_first) * PartIO<D, G>::kStride;
+      for (int i = 4 * tid; i < G * D; i += 4 * kTcThreads) {
+        const int g = i / D;
+        float mx = -INFINITY, ls = 0.f;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int c0 = 0; c0 < n_act; c0 += kTcMaxCluster) {
+          float bm[kTcMaxCluster], bl[kTcMaxCluster];
+          float4 bo[kTcMaxCluster];
+#pragma unroll
+          for (int u = 0; u < kTcMaxCluster; ++u) {
+            const int c = c0 + u;
+            if (c < n_act) {
+              const float* pc = base + int64_t(c) * PartIO<D, G>::kStride;
+              bm[u] = __ldcg(pc + G * D + g);
+              bl[u] = __ldcg(pc + G * D + G + g);
+              bo[u] = PartIO<D, G>::ld(pc + i);
+            } else {
+              bm[u] = -INFINITY;
+              bl[u] = 0.f;
+              bo[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+          }
+          float mn = mx;
+#pragma unroll
+          for (int u = 0; u < kTcMaxCluster; ++u) mn = fmaxf(mn, bm[u]);
+          const float bse = (mn == -INFINITY) ? 0.f : mn;
+          const float a = ex2(mx - bse);
+          scale4(acc, a);
+          ls *= a;
+#pragma unroll
+          for (int u = 0; u < kTcMaxCluster; ++u) {
+            const float f = ex2(bm[u] - bse);
+            fma4(acc, bo[u], f);
+            ls += bl[u] * f;
+          }
+          mx = mn;
+        }
+        attn_store4<T, D, G>(p, seg, i, mx, ls, acc);
+      }
+    }
+  }
 #ifdef WNW_ATTN_TRACE
   WNW_TR(5);
   if (tid == 0) {
@@ -481,90 +556,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
   }
 #endif
-}
-
-// Merge of the cluster partials of a segment that spans several clusters
-// (plan combine entry blockIdx.x, head blockIdx.y), in order, after the
-// attention kernel has finished.  The threads form groups of D/4 (one float4
-// column each); group j takes partials j, j + groups, ... with all its loads
-// in flight at once, and the groups are combined in order in shared memory.
-template <typename T, int D, int G>
-__global__ void __launch_bounds__(kAttnThreads) decode_attn_combine_kernel(const AttnParams p,
-                                                                           const AttnPlanView pv) {
-  using IO = PartIO<D, G>;
-  constexpr int C4 = D / 4;                  // float4 columns of one head
-  constexpr int NG = kAttnThreads / C4;      // thread groups
-  constexpr int B = 16;                      // loads in flight per thread and round
-  __shared__ float sm[NG], sl[NG];
-  __shared__ float4 so[NG][C4];
-  pdl_launch_dependents();
-  pdl_wait();  // the attention kernel's partials are complete and visible
-  const int4 e = __ldg(pv.comb + blockIdx.x);
-  const int g = blockIdx.y;
-  const int seg = e.x, first = e.y, n = e.z;
-  if (seg < 0 || seg >= p.num_segs || first < 0 || n < 1 || first + n > pv.parts) {
-    if (threadIdx.x == 0) atomicOr(p.err, WNW_DEVERR_BAD_INDEX);
-    return;
-  }
-  const int total = seg_total(p, seg);
-  int n_act = 1;  // partials whose range starts below the row count (a prefix; the first always counts)
-  while (n_act < n && __ldg(pv.part_r0 + first + n_act) < total) ++n_act;
-  const int col = threadIdx.x % C4, grp = threadIdx.x / C4;
-  const float* base = p.partials + int64_t(first) * IO::kStride;
-  float mx = -INFINITY, ls = 0.f;
-  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int c0 = grp; c0 < n_act; c0 += NG * B) {
-    float bm[B], bl[B];
-    float4 bo[B];
-#pragma unroll
-    for (int u = 0; u < B; ++u) {
-      const int c = c0 + u * NG;
-      if (c < n_act) {
-        const float* pc = base + int64_t(c) * IO::kStride;
-        bm[u] = __ldcg(pc + G * D + g);
-        bl[u] = __ldcg(pc + G * D + G + g);
-        bo[u] = IO::ld(pc + g * D + 4 * col);
-      } else {
-        bm[u] = -INFINITY;
-        bl[u] = 0.f;
-        bo[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-      }
-    }
-    float mn = mx;
-#pragma unroll
-    for (int u = 0; u < B; ++u) mn = fmaxf(mn, bm[u]);
-    const float bse = (mn == -INFINITY) ? 0.f : mn;
-    const float a = ex2(mx - bse);
-    scale4(acc, a);
-    ls *= a;
-#pragma unroll
-    for (int u = 0; u < B; ++u) {
-      const float f = ex2(bm[u] - bse);
-      fma4(acc, bo[u], f);
-      ls += bl[u] * f;
-    }
-    mx = mn;
-  }
-  if (col == 0) {
-    sm[grp] = mx;
-    sl[grp] = ls;
-  }
-  so[grp][col] = acc;
-  __syncthreads();
-  if (grp != 0) return;
-  float m = -INFINITY;
-#pragma unroll
-  for (int j = 0; j < NG; ++j) m = fmaxf(m, sm[j]);
-  const float bse = (m == -INFINITY) ? 0.f : m;
-  float l = 0.f;
-  float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-  for (int j = 0; j < NG; ++j) {
-    const float f = ex2(sm[j] - bse);
-    fma4(o, so[j][col], f);
-    l += sl[j] * f;
-  }
-  attn_store4<T, D, G>(p, seg, g * D + 4 * col, m, l, o);
 }
 
 // three stages of K + V 128-row tiles (192 KB at head_dim 128); the merge
@@ -615,7 +606,8 @@ wnw_status launch_attn_mma(const wnw_decode_attn_args* a, cudaStream_t stream) {
                 "plan_combine");
   WNW_CHECK_ARG(a->cluster_size >= 1 && a->cluster_size <= kTcMaxCluster && a->plan_ctas % a->cluster_size == 0,
                 "cluster_size %d must be the plan's (1..16, dividing its %d CTAs)", a->cluster_size, a->plan_ctas);
-  WNW_CHECK_ARG(a->plan_combine == 0 || a->plan_parts > 0, "a plan with combine entries has partials");
+  WNW_CHECK_ARG(a->plan_combine == 0 || (a->plan_parts > 0 && a->partials && a->counters),
+                "a plan with combine entries needs partials and per-segment counters (zero before first use)");
   WNW_CHECK_ARG(a->store_rows > 0 && a->store_rows < (int64_t(1) << 31), "store_rows must be in (0, 2^31)");
   WNW_CHECK_ARG(aligned16(a->plan), "plan must be 16-byte aligned");
   CUtensorMap tk, tv;
@@ -631,6 +623,7 @@ wnw_status launch_attn_mma(const wnw_decode_attn_args* a, cudaStream_t stream) {
   pv.part_r0 = a->plan + part_at;
   pv.comb = reinterpret_cast<const int4*>(a->plan + comb_at);
   pv.parts = a->plan_parts;
+  pv.combine = a->plan_combine;
   pv.ready = (a->flags & WNW_ATTN_ROWS_READY) ? 1 : 0;
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -647,15 +640,6 @@ wnw_status launch_attn_mma(const wnw_decode_attn_args* a, cudaStream_t stream) {
   cfg.attrs = attr;
   cfg.numAttrs = 2;
   WNW_CUDA_TRY(cudaLaunchKernelEx(&cfg, decode_attn_mma_kernel<T, D, G>, p, pv, tk, tv));
-  if (a->plan_combine > 0) {
-    cudaLaunchConfig_t c2 = {};
-    c2.gridDim = dim3(a->plan_combine, G, 1);
-    c2.blockDim = dim3(kAttnThreads, 1, 1);
-    c2.stream = stream;
-    c2.attrs = attr;
-    c2.numAttrs = 1;
-    WNW_CUDA_TRY(cudaLaunchKernelEx(&c2, decode_attn_combine_kernel<T, D, G>, p, pv));
-  }
   return WNW_OK;
 }
 

@@ -113,7 +113,7 @@ extern "C" wnw_status wnw_decode_attn_noalloc(const wnw_decode_attn_args* a, voi
   wnw_decode_attn_args b = *a;
   b.partials = static_cast<float*>(base);
   b.counters = reinterpret_cast<int32_t*>(static_cast<unsigned char*>(base) + kPartialBytes);
-  if (!plan && b.num_segs > 0)  // the cluster path's arrival counters start at zero
+  if ((!plan || a->plan_combine > 0) && b.num_segs > 0)  // arrival counters start at zero
     WNW_CUDA_TRY(cudaMemsetAsync(b.counters, 0, size_t(b.num_segs) * 4, static_cast<cudaStream_t>(stream)));
   return wnw_decode_attn(&b, stream);
 }

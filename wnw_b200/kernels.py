@@ -100,7 +100,7 @@ class AttnWork:
     @property
     def launches(self):
         """Kernel launches of one attention call with this layout."""
-        return 1 + int(self.plan and self.combine > 0)
+        return 1
 
     def fill(self, a):
         """Write the layout fields of a ``DecodeAttnArgs``."""
@@ -171,7 +171,7 @@ def launch_attn(args, q, new_k, new_v, out, stream_handle):
     st = N.lib.wnw_decode_attn(C.byref(args), stream_handle)
     if st:
         N.check(st, "wnw_decode_attn")
-    LAUNCHES[0] += 1 + int(bool(args.plan) and args.plan_combine > 0)
+    LAUNCHES[0] += 1
     return out
 
 
