@@ -101,6 +101,7 @@ def parse():
     ap.add_argument("--trace", action="store_true",
                     help="attn mode: load libwnw_b200_trace.so (python -m wnw_b200.build --trace) and report the "
                          "kernel's per-CTA phase timestamps")
+    ap.add_argument("--isolated", action="store_true", help="attn mode --trace: one launch at a time")
     ap.add_argument("--vs-reference", action="store_true",
                     help="attn mode: also time the reference's own GPU kernels (baseline/_ref) on the same layers")
     return ap.parse_args()
@@ -959,9 +960,10 @@ def reference_kernels(layers, a0, a1, reps):
     return out
 
 
-def trace_phases(layers, reps=3):
+def trace_phases(layers, reps=3, isolated=False):
     """Per-CTA phase timestamps (%globaltimer, ns) of ``reps`` passes of the
-    layers' launches back to back, from the trace build: per launch, the
+    layers' launches -- back to back, or (``isolated``) one launch at a time
+    with the GPU idle before each -- from the trace build: per launch, the
     first CTA's start, the dependency wait's release, the last CTA's last
     tile, CTA merge, cluster merge and exit; medians over the launches after
     the first pass, in us relative to the launch's first CTA start."""
@@ -970,17 +972,32 @@ def trace_phases(layers, reps=3):
     from wnw_b200 import native as N
     N.lib.wnw_attn_trace_reset.restype = C.c_int
     N.lib.wnw_attn_trace_read.restype = C.c_int
-    N.check(N.lib.wnw_attn_trace_reset(), "wnw_attn_trace_reset")
+
+    def read():
+        buf = np.zeros((16384, 8), np.uint64)
+        n = C.c_int()
+        N.check(N.lib.wnw_attn_trace_read(C.c_void_p(buf.ctypes.data), 16384, C.byref(n)), "wnw_attn_trace_read")
+        return buf[:n.value].astype(np.int64)
+
     st = torch.cuda.current_stream().cuda_stream
     torch.cuda.synchronize()
-    for _ in range(reps):
-        for x in layers:
-            Kx.launch_attn(x["args"], x["q"], None, None, x["out"], st)
-    torch.cuda.synchronize()
-    buf = np.zeros((16384, 8), np.uint64)
-    n = C.c_int()
-    N.check(N.lib.wnw_attn_trace_read(C.c_void_p(buf.ctypes.data), 16384, C.byref(n)), "wnw_attn_trace_read")
-    rec = buf[:n.value].astype(np.int64)
+    if isolated:
+        parts = []
+        for _ in range(reps):
+            for x in layers:
+                N.check(N.lib.wnw_attn_trace_reset(), "wnw_attn_trace_reset")
+                torch.cuda.synchronize()
+                Kx.launch_attn(x["args"], x["q"], None, None, x["out"], st)
+                torch.cuda.synchronize()
+                parts.append(read())
+        rec = np.concatenate(parts)
+    else:
+        N.check(N.lib.wnw_attn_trace_reset(), "wnw_attn_trace_reset")
+        for _ in range(reps):
+            for x in layers:
+                Kx.launch_attn(x["args"], x["q"], None, None, x["out"], st)
+        torch.cuda.synchronize()
+        rec = read()
     ctas = layers[0]["work"].ctas
     launches = []
     for pp in np.unique(rec[:, 1]):  # one plan (pointer) per layer
@@ -1000,7 +1017,10 @@ def trace_phases(layers, reps=3):
     med = lambda j: float(np.median([x[j] for x in rows if x[j] is not None])) / 1e3  # noqa: E731
     names = ["first_wait_release", "last_wait_release", "last_tile_done", "cta_merge_done", "cluster_barrier_done",
              "last_exit", "release_after_prev_exit", "launch_to_launch"]
-    return {"launches": len(rows), "ctas_per_launch": ctas, "median_us": {nm: med(j) for j, nm in enumerate(names)},
+    if isolated:
+        names = names[:6]
+    return {"launches": len(rows), "ctas_per_launch": ctas, "isolated": isolated,
+            "median_us": {nm: med(j) for j, nm in enumerate(names)},
             "how": "%globaltimer per CTA (trace build), times from the launch's first CTA start; "
                    "release_after_prev_exit = this launch's first wait release - the previous launch's last exit"}
 
@@ -1026,7 +1046,7 @@ def mode_attn(a, dev):
     if a.check:
         line["max_abs_err"] = max(check_attn(x) for x in layers[:2])
     if a.trace:
-        line["trace"] = trace_phases(layers)
+        line["trace"] = trace_phases(layers, isolated=a.isolated)
     if a.vs_reference:
         try:
             line["reference_kernels"] = reference_kernels(layers, 4, min(a.class_a, 15004),
