@@ -155,21 +155,26 @@ extern "C" wnw_status wnw_attn_plan(const int32_t* seg_cap, int num_segs, int sm
   // CTA slots the device holds at once in clusters of c (the SM count when
   // the caller gives one)
   const bool query = sm_count <= 0;
+  int dev = 0;
   if (query) {
-    int dev = 0;
     WNW_CUDA_TRY(cudaGetDevice(&dev));
     WNW_CUDA_TRY(cudaDeviceGetAttribute(&sm_count, cudaDevAttrMultiProcessorCount, dev));
   }
-  int64_t slot_c[17] = {};
+  // residency queries take a while and never change for a device: kept per
+  // (device, cluster size) for the life of the process
+  static std::mutex slot_mu;
+  static std::map<std::pair<int, int>, int64_t> slot_cache;
   auto slots_for = [&](int c) -> int64_t {
     if (!query) return sm_count;
-    if (slot_c[c] == 0) {
-      int n = 0;
-      slot_c[c] = attn_mma_active_clusters_any(128, c, &n) != WNW_OK || n <= 0
-                      ? sm_count
-                      : std::min<int64_t>(sm_count, int64_t(n) * c);
-    }
-    return slot_c[c];
+    std::lock_guard<std::mutex> lock(slot_mu);
+    auto it = slot_cache.find({dev, c});
+    if (it != slot_cache.end()) return it->second;
+    int n = 0;
+    const int64_t v = attn_mma_active_clusters_any(128, c, &n) != WNW_OK || n <= 0
+                          ? sm_count
+                          : std::min<int64_t>(sm_count, int64_t(n) * c);
+    slot_cache[{dev, c}] = v;
+    return v;
   };
   if (max_cluster <= 0) max_cluster = slots_for(16) >= 16 ? 16 : 8;  // the largest cluster the device holds
   std::vector<int64_t> units(num_segs);

@@ -4,9 +4,9 @@
 // scale and a mask add in the model dtype, then an fp32 softmax over all
 // keys).
 //
-// Two launches per layer.  Pass 1, one CTA per (task, 1,024-key chunk): for
-// every query row of the task, the running max and sum of exp over the
-// chunk's keys.  Pass 2, one CTA per (task, 1,024 audio keys): merges the
+// Two launches per layer.  Pass 1, one CTA per (task, 1,024-key chunk, 64
+// query rows): for each of its rows, the running max and sum of exp over the
+// chunk's keys (each K fragment loaded once for the 64 rows).  Pass 2, one CTA per (task, 1,024 audio keys): merges the
 // chunks' statistics of every row (in chunk order), recomputes the audio
 // keys' logits and adds exp(x - max) / sum over the rows, in a fixed order.
 // Logits of 16-bit q / k with head_dim 64 or 128 come from the tensor cores
@@ -28,6 +28,7 @@ constexpr int kPfChunk = 1024;        // keys per pass-1 CTA
 constexpr int kPfAudioChunk = 1024;   // audio keys per pass-2 CTA
 constexpr int kPfTilesPerWarp = kPfAudioChunk / (16 * kPfWarps);
 constexpr int kPfRowsBlock = 256;     // query rows staged in shared memory at a time (pass 2)
+constexpr int kPfRowTiles = 8;        // 8-row query tiles per pass-1 CTA (64 rows)
 
 struct PfParams {
   const void* q;
@@ -89,13 +90,18 @@ __device__ __forceinline__ float logit(const PfParams& p, const wnw_prefill_task
   return x;
 }
 
+// The softmax runs in base 2 on x * log2(e) (MUFU ex2): row statistics are
+// (max, sum of 2^(x' - max)) of the scaled logits x'.
+constexpr float kLog2e = 1.4426950408889634f;
+
 __device__ __forceinline__ void online(float& m, float& l, float x) {
   if (!(x > -INFINITY)) return;
+  x *= kLog2e;
   if (x > m) {
-    l = l * expf(m - x) + 1.f;
+    l = l * ex2(m - x) + 1.f;
     m = x;
   } else {
-    l += expf(x - m);
+    l += ex2(x - m);
   }
 }
 
@@ -107,9 +113,12 @@ __device__ __forceinline__ void merge(float& m, float& l, float m2, float l2) {
     return;
   }
   const float mx = fmaxf(m, m2);
-  l = l * expf(m - mx) + l2 * expf(m2 - mx);
+  l = l * ex2(m - mx) + l2 * ex2(m2 - mx);
   m = mx;
 }
+
+// softmax probability of logit x (natural units) under row statistics s
+__device__ __forceinline__ float prob(float x, float2 s) { return x > -INFINITY ? ex2(x * kLog2e - s.x) / s.y : 0.f; }
 
 // K fragment (A operand, keys j0 + g and j0 + g + 8, head dims [16 kk, 16 kk + 16))
 template <typename T, int D>
@@ -131,61 +140,77 @@ template <typename T, int D>
 __global__ void __launch_bounds__(kPfThreads) prefill_stats_kernel(PfParams p) {
   const wnw_prefill_task t = p.tasks[blockIdx.y];
   if (!task_ok(t, p)) {
-    if (blockIdx.x == 0 && threadIdx.x == 0) atomicOr(p.err, WNW_DEVERR_BAD_INDEX);
+    if (blockIdx.x == 0 && blockIdx.z == 0 && threadIdx.x == 0) atomicOr(p.err, WNW_DEVERR_BAD_INDEX);
     return;
   }
   const int k0 = blockIdx.x * kPfChunk;
-  if (k0 >= p.S) return;
-  const int k1 = min(p.S, k0 + kPfChunk);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, tq = lane & 3;
   const int R = t.n_heads * t.n_rows;
+  const int rb = blockIdx.z * 8 * kPfRowTiles;  // this CTA's query rows: [rb, rb + 64)
+  if (k0 >= p.S || rb >= R) return;
+  const int k1 = min(p.S, k0 + kPfChunk);
+  const int nt = min(kPfRowTiles, (R - rb + 7) / 8);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, tq = lane & 3;
   const T* kb = static_cast<const T*>(p.k) + t.batch * p.ksb + t.kv_head * p.ksh;
-  __shared__ float2 red[kPfWarps][8];
-  for (int rt = 0; rt < R; rt += 8) {
-    // B fragment: query row rt + g, head dims (2 tq, 2 tq + 1) and (+8) of each k-step
-    uint32_t bq[D / 16][2];
-    const T* qr = q_row<T>(p, t, rt + g, R);
+  constexpr int QS = D + 8;  // padded row: a fragment load's 8 rows fall in distinct banks
+  __shared__ __align__(16) T qs[8 * kPfRowTiles][QS];
+  __shared__ float2 red[kPfWarps][8 * kPfRowTiles];
+  for (int i = threadIdx.x; i < 8 * kPfRowTiles * (D / 8); i += kPfThreads) {
+    const int r = i / (D / 8), c = i % (D / 8);
+    const T* qr = q_row<T>(p, t, rb + r, R);
+    *reinterpret_cast<uint4*>(&qs[r][c * 8]) =
+        qr ? __ldg(reinterpret_cast<const uint4*>(qr + c * 8)) : make_uint4(0u, 0u, 0u, 0u);
+  }
+  __syncthreads();
+  // per lane: rows 8 ti + 2 tq (a) and + 1 (b) of each row tile, over this warp's keys
+  float ma[kPfRowTiles], la[kPfRowTiles], mb[kPfRowTiles], lb[kPfRowTiles];
 #pragma unroll
-    for (int kk = 0; kk < D / 16; ++kk) {
-      bq[kk][0] = qr ? ld32(qr + 16 * kk + 2 * tq) : 0u;
-      bq[kk][1] = qr ? ld32(qr + 16 * kk + 2 * tq + 8) : 0u;
-    }
-    const int pa = row_pos(t, rt + 2 * tq, R), pb = row_pos(t, rt + 2 * tq + 1, R);
-    float ma = -INFINITY, la = 0.f, mb = -INFINITY, lb = 0.f;
-    for (int j = k0 + warp * 16; j < k1; j += kPfWarps * 16) {
-      uint32_t a[D / 16][4];
-      load_k<T, D>(kb, p.kss, j, k1, g, tq, a);
-      float c[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int ti = 0; ti < kPfRowTiles; ++ti) ma[ti] = mb[ti] = -INFINITY, la[ti] = lb[ti] = 0.f;
+  for (int j = k0 + warp * 16; j < k1; j += kPfWarps * 16) {
+    uint32_t a[D / 16][4];  // the K fragment of keys j .. j + 15, reused by every row tile
+    load_k<T, D>(kb, p.kss, j, k1, g, tq, a);
 #pragma unroll
-      for (int kk = 0; kk < D / 16; ++kk) mma16816<T>(c, a[kk][0], a[kk][1], a[kk][2], a[kk][3], bq[kk][0], bq[kk][1]);
-      // c[0]: (key j+g, row 2tq), c[1]: (key j+g, row 2tq+1), c[2] / c[3]: key j+g+8
-      if (j + g < k1) {
-        online(ma, la, logit<T>(p, t, c[0], pa, j + g));
-        online(mb, lb, logit<T>(p, t, c[1], pb, j + g));
+    for (int ti = 0; ti < kPfRowTiles; ++ti) {
+      if (ti < nt) {
+        const T* qr = &qs[8 * ti + g][2 * tq];
+        float c[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk)
+          mma16816<T>(c, a[kk][0], a[kk][1], a[kk][2], a[kk][3], *reinterpret_cast<const uint32_t*>(qr + 16 * kk),
+                      *reinterpret_cast<const uint32_t*>(qr + 16 * kk + 8));
+        // c[0]: (key j+g, row 2tq), c[1]: (key j+g, row 2tq+1), c[2] / c[3]: key j+g+8
+        const int pa = row_pos(t, rb + 8 * ti + 2 * tq, R), pb = row_pos(t, rb + 8 * ti + 2 * tq + 1, R);
+        if (j + g < k1) {
+          online(ma[ti], la[ti], logit<T>(p, t, c[0], pa, j + g));
+          online(mb[ti], lb[ti], logit<T>(p, t, c[1], pb, j + g));
+        }
+        if (j + g + 8 < k1) {
+          online(ma[ti], la[ti], logit<T>(p, t, c[2], pa, j + g + 8));
+          online(mb[ti], lb[ti], logit<T>(p, t, c[3], pb, j + g + 8));
+        }
       }
-      if (j + g + 8 < k1) {
-        online(ma, la, logit<T>(p, t, c[2], pa, j + g + 8));
-        online(mb, lb, logit<T>(p, t, c[3], pb, j + g + 8));
+    }
+  }
+#pragma unroll
+  for (int ti = 0; ti < kPfRowTiles; ++ti) {
+    if (ti < nt) {
+#pragma unroll
+      for (int o = 4; o < 32; o <<= 1) {
+        const float m2a = __shfl_xor_sync(0xffffffffu, ma[ti], o), l2a = __shfl_xor_sync(0xffffffffu, la[ti], o);
+        const float m2b = __shfl_xor_sync(0xffffffffu, mb[ti], o), l2b = __shfl_xor_sync(0xffffffffu, lb[ti], o);
+        merge(ma[ti], la[ti], m2a, l2a);
+        merge(mb[ti], lb[ti], m2b, l2b);
+      }
+      if (g == 0) {
+        red[warp][8 * ti + 2 * tq] = make_float2(ma[ti], la[ti]);
+        red[warp][8 * ti + 2 * tq + 1] = make_float2(mb[ti], lb[ti]);
       }
     }
-#pragma unroll
-    for (int o = 4; o < 32; o <<= 1) {
-      const float m2a = __shfl_xor_sync(0xffffffffu, ma, o), l2a = __shfl_xor_sync(0xffffffffu, la, o);
-      const float m2b = __shfl_xor_sync(0xffffffffu, mb, o), l2b = __shfl_xor_sync(0xffffffffu, lb, o);
-      merge(ma, la, m2a, l2a);
-      merge(mb, lb, m2b, l2b);
-    }
-    if (g == 0) {
-      red[warp][2 * tq] = make_float2(ma, la);
-      red[warp][2 * tq + 1] = make_float2(mb, lb);
-    }
-    __syncthreads();
-    if (threadIdx.x < 8 && rt + int(threadIdx.x) < R) {
-      float m = -INFINITY, l = 0.f;
-      for (int w = 0; w < kPfWarps; ++w) merge(m, l, red[w][threadIdx.x].x, red[w][threadIdx.x].y);
-      p.stats[(int64_t(blockIdx.y) * p.max_rows + rt + threadIdx.x) * p.n_chunks + blockIdx.x] = make_float2(m, l);
-    }
-    __syncthreads();
+  }
+  __syncthreads();
+  for (int r = threadIdx.x; r < min(8 * kPfRowTiles, R - rb); r += kPfThreads) {
+    float m = -INFINITY, l = 0.f;
+    for (int w = 0; w < kPfWarps; ++w) merge(m, l, red[w][r].x, red[w][r].y);
+    p.stats[(int64_t(blockIdx.y) * p.max_rows + rb + r) * p.n_chunks + blockIdx.x] = make_float2(m, l);
   }
 }
 
@@ -252,8 +277,8 @@ __global__ void __launch_bounds__(kPfThreads) prefill_colsum_kernel(PfParams p) 
               const float2 s = st[r];
               const float x0 = logit<T>(p, t, c[e], pos, j + g);
               const float x1 = logit<T>(p, t, c[2 + e], pos, j + g + 8);
-              if (x0 > -INFINITY) acc[ti][0] += expf(x0 - s.x) / s.y;
-              if (x1 > -INFINITY) acc[ti][1] += expf(x1 - s.x) / s.y;
+              acc[ti][0] += prob(x0, s);
+              acc[ti][1] += prob(x1, s);
             }
           }
         }
@@ -380,7 +405,7 @@ __global__ void __launch_bounds__(kPfThreads) prefill_colsum_cc_kernel(PfParams 
 #pragma unroll
         for (int d = 0; d < D; ++d) dot = fmaf(qs[r][d], kv[d], dot);
         const float x = logit<T>(p, t, dot, row_pos(t, rb + r, R), j);
-        if (x > -INFINITY) acc += expf(x - st[r].x) / st[r].y;
+        acc += prob(x, st[r]);
       }
     }
   }
@@ -415,7 +440,8 @@ wnw_status launch_pf(const PfParams& p, int num_tasks, cudaStream_t s) {
                                       pf_smem_bytes<D>()));
     configured = true;
   }
-  prefill_stats_kernel<T, D><<<dim3(p.n_chunks, num_tasks), kPfThreads, 0, s>>>(p);
+  prefill_stats_kernel<T, D><<<dim3(p.n_chunks, num_tasks, (p.max_rows + 8 * kPfRowTiles - 1) / (8 * kPfRowTiles)),
+                                kPfThreads, 0, s>>>(p);
   WNW_CUDA_TRY(cudaGetLastError());
   const int ax = std::max(1, (p.max_audio + kPfAudioChunk - 1) / kPfAudioChunk);
   prefill_colsum_kernel<T, D><<<dim3(ax, num_tasks), kPfThreads, pf_smem_bytes<D>(), s>>>(p);
@@ -445,6 +471,7 @@ extern "C" wnw_status wnw_prefill_scores(const wnw_prefill_scores_args* a, void*
   WNW_CHECK_ARG(a->batch > 0 && a->num_q_heads > 0 && a->num_kv_heads > 0 && a->seq_len > 0 && a->num_heads > 0 &&
                     a->max_rows > 0 && a->max_audio >= 0 && a->out_len >= 0,
                 "sizes must be positive");
+  WNW_CHECK_ARG(a->max_rows <= 65535 * 8 * kPfRowTiles, "max_rows above %d", 65535 * 8 * kPfRowTiles);
   WNW_CHECK_ARG(a->q && a->k && a->tasks && a->heads && a->out && a->scratch && a->err, "null pointer argument");
   WNW_CHECK_ARG(a->mask_kind == WNW_MASK_NONE || a->mask_kind == WNW_MASK_CAUSAL || a->mask_kind == WNW_MASK_ADDITIVE,
                 "unknown mask kind %d", a->mask_kind);
