@@ -701,6 +701,7 @@ def selection_agreement(ours, ref_picks, ref_loaded, top_k, tie_rel=1e-5):
     n = min(len(ours), len(ref_picks), len(ref_loaded))
     eq_topk = eq_loaded = ties = 0
     first_diff = None
+    diffs = []  # (step, the reference's k-th / (k+1)-th score gap relative to its largest score)
     for i in range(n):
         o_top, o_loaded = ours[i]
         r_scores, r_top = ref_picks[i]
@@ -709,7 +710,9 @@ def selection_agreement(ours, ref_picks, ref_loaded, top_k, tie_rel=1e-5):
         else:
             srt = np.sort(np.asarray(r_scores, np.float64))[::-1]
             gap = srt[top_k - 1] - srt[top_k] if len(srt) > top_k else np.inf
-            if gap <= tie_rel * max(abs(srt[0]), 1e-30):
+            rel = float(gap / max(abs(srt[0]), 1e-30))
+            diffs.append([i, rel, len(set(o_top) ^ set(r_top)) // 2])
+            if rel <= tie_rel:
                 ties += 1
             elif first_diff is None:
                 first_diff = i
@@ -717,6 +720,7 @@ def selection_agreement(ours, ref_picks, ref_loaded, top_k, tie_rel=1e-5):
             eq_loaded += 1
     return {"steps": n, "topk_equal_steps": eq_topk, "loaded_equal_steps": eq_loaded,
             "near_tie_steps": ties, "first_step_differing_beyond_ties": first_diff,
+            "differing_steps": diffs[:8],  # [step, relative k-th gap, chunks swapped]
             "how": "per decode step, sample 0: this cache's top-k chunks and loaded segments against the "
                    "reference's own WnWCache (baseline/_ref, Triton + torch fp32 cumsum on the GPU) replaying "
                    "the same recorded q/k/v; a differing top-k counts as a near tie when the reference's k-th "

@@ -135,6 +135,7 @@ def test_prefill_scores_kernel_matches_oracle(dev, dtype, p):
         assert (x is None) == (y is None)
         if x is None:
             continue
+        assert bool(torch.isfinite(x).all())
         assert torch.equal(x, x2)  # fixed summation order
         y = y.float()
         assert x.shape == y.shape
@@ -168,6 +169,7 @@ def test_prefill_scores_cuda_core_path(dev, dtype, p):
         assert (x is None) == (y is None)
         if x is None or x.numel() == 0:
             continue
+        assert bool(torch.isfinite(x).all())
         assert torch.equal(x, x2)
         rel = (x - y.float()).abs() / y.float().abs().clamp_min(1e-30)
         if dtype == torch.float32:

@@ -6,9 +6,10 @@
 //
 // Two launches per layer.  Pass 1, one CTA per (task, 1,024-key chunk, 64
 // query rows): for each of its rows, the running max and sum of exp over the
-// chunk's keys (each K fragment loaded once for the 64 rows).  Pass 2, one CTA per (task, 1,024 audio keys): merges the
-// chunks' statistics of every row (in chunk order), recomputes the audio
-// keys' logits and adds exp(x - max) / sum over the rows, in a fixed order.
+// chunk's keys (each K fragment loaded once for the 64 rows).  Pass 2, one
+// CTA per (task, 256 audio keys): merges the chunks' statistics of every row
+// (in chunk order), recomputes the audio keys' logits and adds
+// exp(x - max) / sum over the rows, in a fixed order.
 // Logits of 16-bit q / k with head_dim 64 or 128 come from the tensor cores
 // (mma m16n8k16, keys as m, query rows as n, fp32 accumulation); fp32 ones
 // and small head dims from CUDA-core FMAs.  They are rounded to the model
@@ -25,7 +26,7 @@ namespace {
 constexpr int kPfThreads = 256;
 constexpr int kPfWarps = 8;
 constexpr int kPfChunk = 1024;        // keys per pass-1 CTA
-constexpr int kPfAudioChunk = 1024;   // audio keys per pass-2 CTA
+constexpr int kPfAudioChunk = 256;    // audio keys per pass-2 CTA
 constexpr int kPfTilesPerWarp = kPfAudioChunk / (16 * kPfWarps);
 constexpr int kPfRowsBlock = 256;     // query rows staged in shared memory at a time (pass 2)
 constexpr int kPfRowTiles = 8;        // 8-row query tiles per pass-1 CTA (64 rows)
@@ -95,8 +96,8 @@ __device__ __forceinline__ float logit(const PfParams& p, const wnw_prefill_task
 constexpr float kLog2e = 1.4426950408889634f;
 
 __device__ __forceinline__ void online(float& m, float& l, float x) {
+  x *= kLog2e;  // a masked logit near -FLT_MAX becomes -inf here
   if (!(x > -INFINITY)) return;
-  x *= kLog2e;
   if (x > m) {
     l = l * ex2(m - x) + 1.f;
     m = x;
@@ -117,8 +118,23 @@ __device__ __forceinline__ void merge(float& m, float& l, float m2, float l2) {
   m = mx;
 }
 
-// softmax probability of logit x (natural units) under row statistics s
-__device__ __forceinline__ float prob(float x, float2 s) { return x > -INFINITY ? ex2(x * kLog2e - s.x) / s.y : 0.f; }
+// two logits (natural units) into a row's statistics, without branches
+// (ex2 of -inf is 0, so masked logits and a first update need no case)
+__device__ __forceinline__ void online2(float& m, float& l, float x0, float x1) {
+  x0 *= kLog2e;  // a masked logit near -FLT_MAX becomes -inf here
+  x1 *= kLog2e;
+  const float mn = fmaxf(m, fmaxf(x0, x1));
+  if (mn == -INFINITY) return;
+  l = l * ex2(m - mn) + ex2(x0 - mn) + ex2(x1 - mn);
+  m = mn;
+}
+
+// softmax probability of logit x (natural units) under row statistics
+// s = (max, 1 / sum)
+__device__ __forceinline__ float prob(float x, float2 s) {
+  x *= kLog2e;
+  return x > -INFINITY ? ex2(x - s.x) * s.y : 0.f;
+}
 
 // K fragment (A operand, keys j0 + g and j0 + g + 8, head dims [16 kk, 16 kk + 16))
 template <typename T, int D>
@@ -179,14 +195,11 @@ __global__ void __launch_bounds__(kPfThreads) prefill_stats_kernel(PfParams p) {
                       *reinterpret_cast<const uint32_t*>(qr + 16 * kk + 8));
         // c[0]: (key j+g, row 2tq), c[1]: (key j+g, row 2tq+1), c[2] / c[3]: key j+g+8
         const int pa = row_pos(t, rb + 8 * ti + 2 * tq, R), pb = row_pos(t, rb + 8 * ti + 2 * tq + 1, R);
-        if (j + g < k1) {
-          online(ma[ti], la[ti], logit<T>(p, t, c[0], pa, j + g));
-          online(mb[ti], lb[ti], logit<T>(p, t, c[1], pb, j + g));
-        }
-        if (j + g + 8 < k1) {
-          online(ma[ti], la[ti], logit<T>(p, t, c[2], pa, j + g + 8));
-          online(mb[ti], lb[ti], logit<T>(p, t, c[3], pb, j + g + 8));
-        }
+        const bool v0 = j + g < k1, v1 = j + g + 8 < k1;
+        online2(ma[ti], la[ti], v0 ? logit<T>(p, t, c[0], pa, j + g) : -INFINITY,
+                v1 ? logit<T>(p, t, c[2], pa, j + g + 8) : -INFINITY);
+        online2(mb[ti], lb[ti], v0 ? logit<T>(p, t, c[1], pb, j + g) : -INFINITY,
+                v1 ? logit<T>(p, t, c[3], pb, j + g + 8) : -INFINITY);
       }
     }
   }
@@ -253,7 +266,7 @@ __global__ void __launch_bounds__(kPfThreads) prefill_colsum_kernel(PfParams p) 
         const float2 v = s[c];
         merge(m, l, v.x, v.y);
       }
-      st[r] = make_float2(m, l);
+      st[r] = make_float2(m, l > 0.f ? 1.f / l : 0.f);
     }
     __syncthreads();
 #pragma unroll
@@ -396,7 +409,7 @@ __global__ void __launch_bounds__(kPfThreads) prefill_colsum_cc_kernel(PfParams 
         const float2 v = sp[c];
         merge(m, l, v.x, v.y);
       }
-      st[r] = make_float2(m, l);
+      st[r] = make_float2(m, l > 0.f ? 1.f / l : 0.f);
     }
     __syncthreads();
     if (valid) {

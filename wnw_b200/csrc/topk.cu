@@ -94,7 +94,15 @@ __global__ void __launch_bounds__(kTopkThreads)
   for (int s = warp; s < nseg; s += nwarps) {
     const int lo = s * stride, hi = min(n, lo + stride);
     double x = 0.0;
-    for (int t = lo + lane; t < hi; t += 32) x += double(a[t]);
+    int t = lo + lane;
+    for (; t + 96 < hi; t += 128) {  // four loads in flight, added in the same order
+      const float v0 = a[t], v1 = a[t + 32], v2 = a[t + 64], v3 = a[t + 96];
+      x += double(v0);
+      x += double(v1);
+      x += double(v2);
+      x += double(v3);
+    }
+    for (; t < hi; t += 32) x += double(a[t]);
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) x += __shfl_xor_sync(0xffffffffu, x, off);
     if (lane == 0) segsum[s] = x;
