@@ -974,6 +974,9 @@ def trace_phases(layers, reps=3, isolated=False):
     import ctypes as C
     from wnw_b200 import kernels as Kx
     from wnw_b200 import native as N
+    if not hasattr(N.lib, "wnw_attn_trace_reset"):
+        raise RuntimeError(f"{N.LIB_PATH} has no phase trace: build libwnw_b200_trace.so with "
+                           "`python -m wnw_b200.build --trace`")
     N.lib.wnw_attn_trace_reset.restype = C.c_int
     N.lib.wnw_attn_trace_read.restype = C.c_int
 

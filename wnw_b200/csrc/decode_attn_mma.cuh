@@ -424,9 +424,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   cluster_arrive();  // CTA partials visible to the cluster
   cluster_wait();
   WNW_TR(4);
-  if (active && crank == leader && !(to_part && it.y >= total && it.y > 0)) {
+  // every rank of the segment merges a slice of the output -- float4 group q
+  // of the G*D/4 goes to rank q % nranks -- from all the ranks' partials over
+  // DSMEM; a cluster partial whose range starts past the rows is not written
+  const int range0 = to_part ? __ldg(pv.part_r0 + part) : 0;
+  if (active && !(to_part && range0 >= total && range0 > 0)) {
     float* part_out = to_part ? p.partials + int64_t(part) * PartIO<D, G>::kStride : nullptr;
-    for (int i = 4 * tid; i < G * D; i += 4 * kTcThreads) {
+    for (int q = (crank - leader) + nranks * tid; q < G * D / 4; q += nranks * kTcThreads) {
+      const int i = 4 * q;
       const int g = i / D;
       // every rank's (max, sum, o) first, so the remote loads overlap
       float pm[kTcMaxCluster], pl[kTcMaxCluster];
@@ -466,7 +471,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
     }
   }
-  cluster_arrive();  // keep this CTA's shared memory until its leader has read it
+  cluster_arrive();  // keep this CTA's shared memory until every rank has read it
   cluster_wait();
   // ---- a segment spanning several clusters: each cluster's leader arrives
   // at the segment's counter once its partial is out; the last to arrive

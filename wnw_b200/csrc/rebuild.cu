@@ -105,6 +105,7 @@ __global__ void __launch_bounds__(kRbThreads)
                           const int32_t* seg_cap, const int32_t* blob, int64_t blob_ints, int layer, int num_segs,
                           int64_t land_rows, uint4* k_move, uint4* v_move, int64_t move_rows, int32_t* status,
                           int32_t* err, int cpr) {
+  pdl_launch_dependents();  // the scatter may start validating its record now
   if (!cta_record_ok(blob, blob_ints, layer, num_segs, err)) return;
   const RbRec r(blob, layer);
   const int64_t gtid = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -166,7 +167,8 @@ __global__ void __launch_bounds__(kRbThreads)
   // may start its layout-only prologue now; it waits for this grid to finish
   // before it reads anything written here
   pdl_launch_dependents();
-  if (!cta_record_ok(blob, blob_ints, layer, num_segs, err)) return;
+  if (!cta_record_ok(blob, blob_ints, layer, num_segs, err)) return;  // reads the plan blob only
+  pdl_wait();  // the gather's status words and moved rows are complete
   const RbRec r(blob, layer);
   if (r.moved_total > move_rows) return;  // refused by the gather (error bit set there)
   const int64_t gtid = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -274,12 +276,23 @@ extern "C" wnw_status wnw_rebuild_segments(int dtype, int head_dim, void* k_stor
       blob_ints, layer, num_segs, k_landing ? land_rows : 0, static_cast<uint4*>(k_move),
       static_cast<uint4*>(v_move), move_rows, status, err, rb / 16);
   WNW_CUDA_TRY(cudaGetLastError());
-  rebuild_scatter_kernel<<<kRbMaxBlocks, kRbThreads, 0, s>>>(
-      static_cast<uint4*>(k_store), static_cast<uint4*>(v_store), seg_base, seg_len, seg_cap,
-      static_cast<const uint4*>(k_landing), static_cast<const uint4*>(v_landing), plan_blob, blob_ints, layer,
-      num_segs, move_rows, static_cast<const uint4*>(k_move), static_cast<const uint4*>(v_move), status, err,
-      rb / 16);
-  WNW_CUDA_TRY(cudaGetLastError());
+  // programmatic dependent launch: the scatter's CTAs validate their record
+  // while the gather finishes, then wait for it (griddepcontrol.wait)
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(kRbMaxBlocks, 1, 1);
+  cfg.blockDim = dim3(kRbThreads, 1, 1);
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  WNW_CUDA_TRY(cudaLaunchKernelEx(&cfg, rebuild_scatter_kernel, static_cast<uint4*>(k_store),
+                                  static_cast<uint4*>(v_store), seg_base, seg_len, seg_cap,
+                                  static_cast<const uint4*>(k_landing), static_cast<const uint4*>(v_landing),
+                                  plan_blob, blob_ints, layer, num_segs, move_rows,
+                                  static_cast<const uint4*>(k_move), static_cast<const uint4*>(v_move),
+                                  static_cast<const int32_t*>(status), err, rb / 16));
   return WNW_OK;
 }
 
