@@ -427,7 +427,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   // every rank of the segment merges a slice of the output -- float4 group q
   // of the G*D/4 goes to rank q % nranks -- from all the ranks' partials over
   // DSMEM; a cluster partial whose range starts past the rows is not written
-  const int range0 = to_part ? __ldg(pv.part_r0 + part) : 0;
+  const int range0 = (active && to_part) ? __ldg(pv.part_r0 + part) : 0;  // part < parts when active
   if (active && !(to_part && range0 >= total && range0 > 0)) {
     float* part_out = to_part ? p.partials + int64_t(part) * PartIO<D, G>::kStride : nullptr;
     for (int q = (crank - leader) + nranks * tid; q < G * D / 4; q += nranks * kTcThreads) {
