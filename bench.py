@@ -102,6 +102,9 @@ def parse():
                     help="attn mode: load libwnw_b200_trace.so (python -m wnw_b200.build --trace) and report the "
                          "kernel's per-CTA phase timestamps")
     ap.add_argument("--isolated", action="store_true", help="attn mode --trace: one launch at a time")
+    ap.add_argument("--no-rebuild-ahead", action="store_true",
+                    help="rebuild each changed layer on the compute stream before its attention "
+                         "(B200WnWCache(rebuild_ahead=False)) instead of ahead on its own stream")
     ap.add_argument("--vs-reference", action="store_true",
                     help="attn mode: also time the reference's own GPU kernels (baseline/_ref) on the same layers")
     return ap.parse_args()
@@ -429,13 +432,15 @@ class Shard:
 
 
 PREFILL_MS = []  # prefill-side compression time of every cache built (ms)
+REBUILD_AHEAD = [True]  # B200WnWCache(rebuild_ahead=...); --no-rebuild-ahead for comparison
 
 
 def fresh_cache(rec, dev, n_steps, shard=None, tier="host"):
     from wnw_b200.cache import B200WnWCache
     shard = shard or Shard(dev)
     c = B200WnWCache(shard.cfg(rec["cfg"]), MODEL["L"], shard.Hkv, shard.Hq, MODEL["D"], dev,
-                     max_decode_tokens=n_steps + 8, score_reduce=shard.score_reduce(), offload_tier=tier)
+                     max_decode_tokens=n_steps + 8, score_reduce=shard.score_reduce(), offload_tier=tier,
+                     rebuild_ahead=REBUILD_AHEAD[0])
     if len(rec["audio"]) == 2:
         a0, a1 = rec["audio"]
         c.setup_audio(torch.tensor([a0]), torch.tensor([a1]), None)
@@ -472,6 +477,7 @@ def attention_replay(cache, qs, reps):
     from wnw_b200 import kernels as Kx
     from wnw_b200 import native as N
     L = cache.num_layers
+    torch.cuda.synchronize()  # the fetch and rebuilds issued ahead for the next step are done
     st = torch.cuda.current_stream()
     outs = [torch.empty_like(q) for q in qs]
     args = [cache._attn_args[l][2] for l in range(L)]
@@ -525,7 +531,7 @@ def run_value(rec, dev, K, W, shard=None, tier="host"):
     torch.cuda.nvtx.range_push("wnw_timed")
     for i in range(W, W + K):
         one(i)
-        fetched += cache._fetched_rows if cache._pending else 0
+        fetched += cache._fetched_rows
     torch.cuda.nvtx.range_pop()
     t1.record()
     torch.cuda.synchronize()
@@ -1205,6 +1211,7 @@ def traffic_per_launch(algorithmic_bytes):
 # ------------------------------------------------------------------ main
 def main():
     a = parse()
+    REBUILD_AHEAD[0] = not a.no_rebuild_ahead
     if a.trace:  # before anything loads the library
         os.environ.setdefault("WNW_B200_LIB", os.path.join(ROOT, "wnw_b200", "libwnw_b200_trace.so"))
     use_config(a.config, a.synthetic, a.depth)

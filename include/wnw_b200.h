@@ -278,6 +278,23 @@ wnw_status wnw_rebuild_segments(int dtype, int head_dim, void* k_store, void* v_
                                 int64_t land_rows, const int32_t* plan_blob, int64_t blob_ints,
                                 int layer, void* k_move, void* v_move, int64_t move_rows,
                                 int32_t* status, int32_t* err, void* stream);
+/* The rebuilds of one step's changed layers in one call (no reference
+ * counterpart: the per-layer issue loop of wnw_rebuild_segments done
+ * natively, so the host spends microseconds, not tens of them, per layer).
+ * For each l < num_layers with layer_changed[l] != 0 (a host array): the
+ * stream waits for wait_events[l] (cudaEvent_t; NULL entries or a NULL
+ * array: no wait), layer l's rebuild runs with k_store[l], v_store[l],
+ * seg_base[l], seg_len[l], seg_cap[l], num_segs[l] and the shared landing,
+ * plan, move, status and error buffers, then record_events[l] is recorded
+ * (same NULL rules).  Stops at the first failing call and returns its
+ * status. */
+wnw_status wnw_rebuild_layers(int dtype, int head_dim, int num_layers, const int32_t* layer_changed,
+                              void* const* k_store, void* const* v_store, const int64_t* const* seg_base,
+                              int32_t* const* seg_len, const int32_t* const* seg_cap, const int32_t* num_segs,
+                              const void* k_landing, const void* v_landing, int64_t land_rows,
+                              const int32_t* plan_blob, int64_t blob_ints, void* k_move, void* v_move,
+                              int64_t move_rows, int32_t* status, int32_t* err, void* const* wait_events,
+                              void* const* record_events, void* stream);
 
 /* Copy rows [0, len[s]) of every segment from src (+src_base[s]) to dst
  * (+dst_base[s]); src and dst must not overlap.  Used to pack a slot layout

@@ -135,7 +135,7 @@ class B200WnWCache(FlatVarlenCache):
 
     def __init__(self, config, num_layers, num_kv_heads, num_q_heads, head_dim, device, adapter=None, *,
                  max_decode_tokens=256, fetch_mode="zerocopy", fetch_threads=8, fetch_ctas=12, score_reduce=None,
-                 offload_tier="host", wait_timeout_s=60.0, fetch_plan="device"):
+                 offload_tier="host", wait_timeout_s=60.0, fetch_plan="device", rebuild_ahead=True):
         super().__init__(num_layers, num_kv_heads, num_q_heads, head_dim, device, adapter)
         if self.device.type != "cuda":
             raise RuntimeError("B200WnWCache needs a CUDA device; the CPU oracle lives in the test suite")
@@ -156,6 +156,13 @@ class B200WnWCache(FlatVarlenCache):
         if fetch_plan not in ("device", "host"):
             raise ValueError(f"fetch_plan must be 'device' or 'host', not {fetch_plan!r}")
         self.fetch_plan = fetch_plan
+        # rebuild every changed layer on its own stream as soon as its rows
+        # land (the next step's attention of layer l waits for layer l only),
+        # instead of on the compute stream right before layer l's attention
+        self.rebuild_ahead = bool(rebuild_ahead)
+        self._rb_stream = None
+        self._rb_events = None
+        self._rebuilt = None
         self._dplan = None
         self._dplan_args = None
         self.wait_timeout_s = float(wait_timeout_s)
@@ -177,6 +184,8 @@ class B200WnWCache(FlatVarlenCache):
             # the previous request's last step fetched ahead for a step that
             # never came: let it land before its buffers and plan go away
             self._copy_stream.synchronize()
+        if self._rb_stream is not None:  # likewise its rebuilds issued ahead
+            self._rb_stream.synchronize()
         self._dplan = self._dplan_args = None
         self._seg_rows = None
         super().setup_audio(audio_starts, audio_ends, attention_mask)
@@ -209,6 +218,7 @@ class B200WnWCache(FlatVarlenCache):
         self._nonaudio = {}
         self.restore_meta = None
         self._pending = False
+        self._rebuilt = [False] * self.num_layers
         self._decode_step = 0
         self._rows_ready = [False] * self.num_layers
         self.prefilled = False
@@ -661,6 +671,16 @@ class B200WnWCache(FlatVarlenCache):
             self._grow(l)
             self._grow_flags[l] = False
             self._rows_ready[l] = False
+        if self._rebuilt[l]:
+            # rebuilt ahead on the rebuild stream: the compute stream waits
+            # for this layer's rebuild (and the kernel reads the rebuilt
+            # lengths only after its dependency wait, as after an in-stream
+            # rebuild)
+            self._rebuilt[l] = False
+            self._rows_ready[l] = False
+            st = N.lib.wnw_stream_wait_event(self._raw_stream(), self._rb_events[l].cuda_event)
+            if st:
+                N.check(st, "wnw_stream_wait_event")
         if self._pending and self._layer_chg[l]:
             self._rows_ready[l] = False
             stream = self._raw_stream()
@@ -783,6 +803,7 @@ class B200WnWCache(FlatVarlenCache):
     def decode_all_layers_done(self):
         """cache.py:568-600: advance lengths, score, select, plan, prefetch."""
         self._decode_step += 1
+        self._fetched_rows = 0  # rows this step's plan fetches (set when it changes anything)
         self.stats.flush_decode_step(self._decode_step)
         if self.stats.enabled and self._decode_step % self.stats.interval == 0:
             self.stats.record_decode(self._decode_step, self._snapshot_cache_stats)
@@ -840,6 +861,65 @@ class B200WnWCache(FlatVarlenCache):
                     self.stats.record_cpu_gpu_transfer(b, c2g_tokens=n, c2g_bytes=n * row_bytes * 2)
             self.loaded_segments[b] = now
         self._plan_layer_checks()
+        if self.rebuild_ahead and self._pending:
+            self._issue_rebuilds()
+
+    def _issue_rebuilds(self):
+        """The step's rebuilds, issued now on the rebuild stream: after
+        everything issued so far on the compute stream (the step's tail and
+        the plan upload, and any slot growth, done here first), layer l's
+        rebuild waits for layer l's fetched rows and records its own event,
+        which the compute stream waits for before layer l's attention.  The
+        next step's fetch reuses the landing rows only after the top-k,
+        which comes after every attention, hence after every rebuild."""
+        L = self.num_layers
+        for l in range(L):  # growth copies the layer's rows into larger slots: before its rebuild
+            if self._grow_flags[l]:
+                self._grow(l)
+                self._grow_flags[l] = False
+        if self._rb_stream is None:
+            self._rb_stream = torch.cuda.Stream(device=self.device)
+            self._rb_events = [torch.cuda.Event() for _ in range(L)]
+            for e in self._rb_events:  # create the CUDA events now: their handles are passed down
+                e.record(self._rb_stream)
+        rs = self._rb_stream
+        start = torch.cuda.Event()
+        start.record()
+        rs.wait_event(start)
+        b = self._rebuild_batch()
+        chg = np.ascontiguousarray(self._layer_chg, np.int32)
+        st = N.lib.wnw_rebuild_layers(*b["head"], chg.ctypes.data, *b["layers"], *b["shared"], self._event_handles,
+                                      b["record"], rs.cuda_stream)
+        if st:
+            N.check(st, "wnw_rebuild_layers")
+        for l in np.nonzero(chg)[0].tolist():
+            Kx.LAUNCHES[0] += 2
+            self._len_host[l] = self._next_lens[l]
+            self._rebuilt[l] = True
+        self._pending = False
+
+    def _rebuild_batch(self):
+        """wnw_rebuild_layers arguments: per-layer pointer arrays and the
+        shared buffers, from the per-layer rebuild arguments (rebuilt when
+        those are: every invalidation assigns a new _rb_args list)."""
+        if getattr(self, "_rb_batch_key", None) is self._rb_args:
+            return self._rb_batch
+        L = self.num_layers
+        args = [self._rebuild_args(l) for l in range(L)]
+        P = C.c_void_p
+        arr = lambda i: (P * L)(*[a[i] for a in args])  # noqa: E731
+        a0 = args[0]
+        self._rb_batch = {
+            "head": (a0[0], a0[1], L),
+            "layers": (arr(2), arr(3), arr(4), arr(5), arr(6), (C.c_int32 * L)(*[a[7] for a in args])),
+            # landing k / v, rows, plan blob, ints, move k / v, rows, status, err (layer index a[13] dropped)
+            "shared": (a0[8], a0[9], a0[10], a0[11], a0[12], a0[14], a0[15], a0[16], a0[17], a0[18]),
+            "record": (P * L)(*[e.cuda_event for e in self._rb_events]),
+        }
+        if not all(b for b in self._rb_batch["record"]):
+            raise RuntimeError("rebuild events have no CUDA handle")
+        self._rb_batch_key = self._rb_args
+        return self._rb_batch
 
     def _tail_call(self, name, args, stream):
         st = getattr(N.lib, name)(*args, stream)

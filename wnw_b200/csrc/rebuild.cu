@@ -296,6 +296,33 @@ extern "C" wnw_status wnw_rebuild_segments(int dtype, int head_dim, void* k_stor
   return WNW_OK;
 }
 
+extern "C" wnw_status wnw_rebuild_layers(int dtype, int head_dim, int num_layers, const int32_t* layer_changed,
+                                         void* const* k_store, void* const* v_store,
+                                         const int64_t* const* seg_base, int32_t* const* seg_len,
+                                         const int32_t* const* seg_cap, const int32_t* num_segs,
+                                         const void* k_landing, const void* v_landing, int64_t land_rows,
+                                         const int32_t* plan_blob, int64_t blob_ints, void* k_move, void* v_move,
+                                         int64_t move_rows, int32_t* status, int32_t* err,
+                                         void* const* wait_events, void* const* record_events, void* stream) {
+  using namespace wnw;
+  WNW_CHECK_ARG(num_layers >= 0, "num_layers < 0");
+  WNW_CHECK_ARG(num_layers == 0 || (layer_changed && k_store && v_store && seg_base && seg_len && seg_cap &&
+                                    num_segs),
+                "null pointer argument");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  for (int l = 0; l < num_layers; ++l) {
+    if (!layer_changed[l]) continue;
+    if (wait_events && wait_events[l]) WNW_CUDA_TRY(cudaStreamWaitEvent(s, static_cast<cudaEvent_t>(wait_events[l]), 0));
+    const wnw_status st = wnw_rebuild_segments(dtype, head_dim, k_store[l], v_store[l], seg_base[l], seg_len[l],
+                                               seg_cap[l], num_segs[l], k_landing, v_landing, land_rows, plan_blob,
+                                               blob_ints, l, k_move, v_move, move_rows, status, err, stream);
+    if (st != WNW_OK) return st;
+    if (record_events && record_events[l])
+      WNW_CUDA_TRY(cudaEventRecord(static_cast<cudaEvent_t>(record_events[l]), s));
+  }
+  return WNW_OK;
+}
+
 extern "C" wnw_status wnw_copy_segments(int dtype, int head_dim, const void* src_k, const void* src_v,
                                         const int64_t* src_base, void* dst_k, void* dst_v,
                                         const int64_t* dst_base, const int32_t* len, int num_segs,
