@@ -673,11 +673,10 @@ class B200WnWCache(FlatVarlenCache):
             self._rows_ready[l] = False
         if self._rebuilt[l]:
             # rebuilt ahead on the rebuild stream: the compute stream waits
-            # for this layer's rebuild (and the kernel reads the rebuilt
-            # lengths only after its dependency wait, as after an in-stream
-            # rebuild)
+            # for this layer's rebuild, so its rows and lengths are final
+            # before the attention launches (a stream wait holds back every
+            # later launch, whatever its programmatic-dependency attribute)
             self._rebuilt[l] = False
-            self._rows_ready[l] = False
             st = N.lib.wnw_stream_wait_event(self._raw_stream(), self._rb_events[l].cuda_event)
             if st:
                 N.check(st, "wnw_stream_wait_event")
