@@ -104,6 +104,15 @@ __device__ inline void fence_mbar_init() {
 // acquire-release fence at gpu scope (cheaper than the sequentially
 // consistent __threadfence)
 __device__ inline void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+// atomic add with acquire-release semantics at gpu scope: releases what this
+// thread has observed (cumulative) and acquires what earlier releasers of the
+// same location published, in one memory round trip instead of fence + atomic
+// + fence; returns the old value
+__device__ inline int atom_add_acq_rel_gpu(int* addr, int v) {
+  int old;
+  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(addr), "r"(v) : "memory");
+  return old;
+}
 // split cluster barrier: arrive (release) now, wait (acquire) later; every
 // thread of every CTA of the cluster executes both, in this order
 __device__ inline void cluster_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }

@@ -5,8 +5,9 @@
 // segment's CTAs sit in consecutive ranks of one thread-block cluster (up to
 // 16 CTAs), so their partial softmax states merge through distributed shared
 // memory -- no global-memory round trip; only a segment too long for one
-// cluster's CTAs spans several clusters, whose cluster partials a second
-// small kernel merges in order.  The plan gives each CTA about the same rows
+// cluster's CTAs spans several clusters, whose cluster partials the last
+// cluster to arrive at the segment's counter merges in order (one atomic,
+// then the partials' loads).  The plan gives each CTA about the same rows
 // (capped so a long segment fits one cluster) and packs short segments into
 // shared clusters.
 //
@@ -184,13 +185,49 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       tma_load_2d(sV + h * HALF + lo * 128, &tmV, h * 64, y, &bars[st][warp]);
     }
   };
+  // A leader CTA of a segment spanning clusters looks up, in the prologue,
+  // the combine entry of its partial (cfirst, cn; cok: the entry checks out)
+  // and how many of the segment's partials cover rows at this launch (nact),
+  // so that the tail after its arrival is one atomic and the partials' loads.
+  // Warp 0 holds the values; everything it reads is a plan constant but the
+  // row count.
+  const bool spans = active && to_part && crank == leader;
+  int cfirst = 0, cn = 0, nact = 1;
+  bool cok = false;
+  auto find_entry = [&]() {
+    if (!spans || warp != 0) return;
+    int4 e = make_int4(-1, 0, 0, 0);
+    if (lane == 0 && pv.combine > 0) {  // entries are ordered by first partial
+      int lo = 0, hi = pv.combine;
+      while (hi - lo > 1) {
+        const int mid = (lo + hi) >> 1;
+        if (__ldg(&pv.comb[mid].y) <= part) lo = mid; else hi = mid;
+      }
+      e = __ldg(pv.comb + lo);
+    }
+    e.x = __shfl_sync(0xffffffffu, e.x, 0);
+    e.y = __shfl_sync(0xffffffffu, e.y, 0);
+    e.z = __shfl_sync(0xffffffffu, e.z, 0);
+    cok = e.x == seg && e.y <= part && part < e.y + e.z && e.y + e.z <= pv.parts;
+    cfirst = e.y;
+    cn = e.z;
+  };
+  auto count_active = [&]() {  // partials whose range starts below the row count (the first always counts)
+    if (!cok) return;          // warp-uniform
+    int n = 0;
+    for (int c = 1 + lane; c < cn; c += 32) n += __ldg(pv.part_r0 + cfirst + c) < total ? 1 : 0;
+    nact = 1 + __reduce_add_sync(0xffffffffu, n);
+  };
   if (pv.ready) {  // lengths and rows are final: start streaming before the wait
     schedule();
     if (lane == 0)
       for (int t = 0; t < min(ntiles, kTcStages); ++t) issue(t);
+    find_entry();
+    count_active();
     pdl_wait();  // q, the new rows and the outputs may belong to the preceding kernel
     WNW_TR(1);
   } else {
+    find_entry();
     // L2 prefetch of this CTA's first rows by capacity (layout constants
     // only; L2 is the point of coherence, so rows the preceding kernel still
     // writes are read correctly after the wait)
@@ -207,6 +244,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     schedule();
     if (lane == 0)
       for (int t = 0; t < min(ntiles, kTcStages); ++t) issue(t);
+    count_active();
   }
   pdl_launch_dependents();  // the next kernel may start its own prologue now
 
@@ -476,36 +514,26 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   // ---- a segment spanning several clusters: each cluster's leader arrives
   // at the segment's counter once its partial is out; the last to arrive
   // merges the segment's partials in order (no second kernel, no wait)
-  if (active && to_part && crank == leader) {
+  if (spans) {
     __shared__ int s_last, s_first, s_n;
-    __syncthreads();  // this CTA's partial stores are issued (CTA scope) ...
+    __syncthreads();  // this cluster's partial stores are ordered before (cluster barrier, CTA barrier) ...
     if (tid == 0) {
-      int lo = 0, hi = pv.combine;  // the combine entry holding `part` (entries ordered by first partial)
-      while (hi - lo > 1) {
-        const int mid = (lo + hi) >> 1;
-        if (__ldg(&pv.comb[mid].y) <= part) lo = mid; else hi = mid;
-      }
-      const int4 e = pv.combine > 0 ? __ldg(pv.comb + lo) : make_int4(-1, 0, 0, 0);
       int last = 0;
-      if (e.x == seg && e.y <= part && part < e.y + e.z && e.y + e.z <= pv.parts) {
-        fence_acq_rel_gpu();  // ... and released at gpu scope before the arrival
-        last = (atomicAdd(p.counters + seg, 1) == e.z - 1) ? 1 : 0;
-        if (last) {
-          p.counters[seg] = 0;  // every partial of this launch has arrived
-          fence_acq_rel_gpu();  // acquire the others' partials
-        }
+      if (cok) {
+        // ... and released at gpu scope by the arrival, which acquires the
+        // earlier arrivals' partials for the last one
+        last = (atom_add_acq_rel_gpu(p.counters + seg, 1) == cn - 1) ? 1 : 0;
+        if (last) p.counters[seg] = 0;  // every partial of this launch has arrived; the next use is a later launch
       } else {
         atomicOr(p.err, WNW_DEVERR_BAD_INDEX);
       }
       s_last = last;
-      s_first = e.y;
-      s_n = e.z;
+      s_first = cfirst;
+      s_n = nact;
     }
     __syncthreads();
     if (s_last) {
-      // partials whose range starts below the row count (a prefix; the first always counts)
-      int n_act = 1;
-      while (n_act < s_n && __ldg(pv.part_r0 + s_first + n_act) < total) ++n_act;
+      const int n_act = s_n;
       const float* base = p.partials + int64_t(s_first) * PartIO<D, G>::kStride;
       for (int i = 4 * tid; i < G * D; i += 4 * kTcThreads) {
         const int g = i / D;
