@@ -238,18 +238,31 @@ def test_attn_plan_properties_random(seed):
         assert list(part_r0[first:first + n]) == sorted(part_r0[first:first + n]) and part_r0[first] == 0
 
 
-def test_attn_plan_config2_layer_fits_one_cluster_per_segment():
+def test_attn_plan_config2_layer_spreads_over_half_the_sms():
     """The config-2 layer (two 15,100-row class-A and six 2,300-row class-B
-    segments) on a 148-SM device with clusters of 16: every segment merges
-    inside its cluster (no partials, no combine kernel)."""
+    segments) on a 148-SM device with clusters of up to 16: one cluster of 16
+    per class-A segment would stream each at one GPC's rate, so the plan
+    takes clusters of 4 on at most half the SMs (the next layer's CTAs run
+    beside it): the class-A segments span several clusters, merged through
+    their partials, and each class-B segment stays inside one cluster."""
     from wnw_b200.kernels import attn_plan
     cap = np.array([15100 + 40] * 2 + [2300 + 40] * 6, np.int32)
     plan, info = attn_plan(cap, 148, 16)
-    assert info["cluster"] == 16 and info["parts"] == 0 and info["combine"] == 0
-    C, cta, _, _ = _parse_plan(plan)
-    for seg in range(8):
+    assert info["cluster"] == 4 and 64 <= info["ctas"] <= 74 and info["combine"] == 2
+    C, cta, _, comb = _parse_plan(plan)
+    assert sorted(int(e[0]) for e in comb) == [0, 1]
+    for seg in range(2, 8):
         ranks = cta[cta[:, 0] == seg]
-        assert len(ranks) == (16 if seg < 2 else 3)
+        assert len(ranks) <= 4 and all(_meta(m)[2] == 0 for m in ranks[:, 3])
+
+
+@pytest.mark.parametrize("lens", [[2300] * 8, [1, 2, 3, 300], [7000] * 4])
+def test_attn_plan_short_shares_keep_one_cluster_per_segment(lens):
+    """Layers whose one-cluster shares are at most 512 rows keep every
+    segment inside one cluster (no partials)."""
+    from wnw_b200.kernels import attn_plan
+    plan, info = attn_plan(np.array(lens, np.int32) + 40, 148, 16)
+    assert info["parts"] == 0 and info["combine"] == 0
 
 
 @pytest.mark.parametrize("lens", [[120000] * 2 + [4000] * 6, [60000] * 8, [30000] * 2 + [3000] * 6])

@@ -222,32 +222,66 @@ extern "C" wnw_status wnw_attn_plan(const int32_t* seg_cap, int num_segs, int sm
   };
   int64_t share = std::max<int64_t>((total + slots_for(cl) - 1) / slots_for(cl),
                                     std::min<int64_t>(kMaxShareUnits, (umax + cl - 1) / cl));
+  // half: plan for half the SMs.  Back-to-back layers then run side by side
+  // (one CTA per SM): the next layer's CTAs find free SMs and load their
+  // first stages while this layer's CTAs stream and merge.
+  bool half = false;
+  auto slots_of = [&](int x) {  // CTA slots a plan may fill per wave
+    return half ? std::max<int64_t>(1, std::min<int64_t>(slots_for(x), sm_count / 2)) : slots_for(x);
+  };
+  // Segments spanning clusters: clusters of at most 4; for w = 1..4 waves,
+  // the smallest share whose CTAs fit w waves of the resident slots (or
+  // every segment down to one CTA); then the w whose waves x (share + a
+  // CTA's fixed cost) -- the busiest SM's time -- is least.  One wave avoids
+  // a short tail wave; a few waves balance layers of many short segments
+  // beside a few long ones.  Sets cl; returns the share.
+  auto spread_share = [&]() {
+    cl = std::min(cl, 4);
+    int64_t best = INT64_MAX, best_sh = 1;
+    for (int64_t w = 1; w <= 4; ++w) {
+      const int64_t slots1 = slots_of(cl);
+      int64_t sh = std::max<int64_t>(1, (total + w * slots1 - 1) / (w * slots1));
+      for (int it = 0; it < 256 && ctas_at(sh) > w * slots_of(c) && sh < umax; ++it)
+        sh = std::min(umax, sh + std::max<int64_t>(1, sh / 16));
+      const int64_t slots = slots_of(c);
+      const int64_t cost = (ctas_at(sh) + slots - 1) / slots * (sh + kWaveOverheadUnits);
+      if (cost < best) {
+        best = cost;
+        best_sh = sh;
+      }
+    }
+    return best_sh;
+  };
   if ((umax + share - 1) / share <= cl && share <= kMaxShareUnits) {
     // one cluster per segment: keep the launch to one wave of the clusters
     // the device holds at once (a larger share means fewer CTAs per segment
     // and smaller clusters)
     for (int it = 0; it < 256 && ctas_at(share) > slots_for(c) && share < umax; ++it)
       share = std::min(umax, share + std::max<int64_t>(1, share / 16));
-  } else {
-    cl = std::min(cl, 4);
-    // for w = 1..4 waves: the smallest share whose CTAs fit w waves of the
-    // resident slots (or every segment down to one CTA); then the w whose
-    // waves x (share + a CTA's fixed cost) -- the busiest SM's time -- is
-    // least.  One wave avoids a short tail wave; a few waves balance layers
-    // of many short segments beside a few long ones.
-    int64_t best = INT64_MAX;
-    for (int64_t w = 1; w <= 4; ++w) {
-      const int64_t slots1 = slots_for(cl);
-      int64_t sh = std::max<int64_t>(1, (total + w * slots1 - 1) / (w * slots1));
-      for (int it = 0; it < 256 && ctas_at(sh) > w * slots_for(c) && sh < umax; ++it)
-        sh = std::min(umax, sh + std::max<int64_t>(1, sh / 16));
-      const int64_t slots = slots_for(c);
-      const int64_t cost = (ctas_at(sh) + slots - 1) / slots * (sh + kWaveOverheadUnits);
-      if (cost < best) {
-        best = cost;
+    // Clusters above 4 CTAs tie each long segment to one GPC, which streams
+    // it at about 1 TB/s.  When that makes a CTA's streaming outweigh its
+    // fixed cost (shares above kWaveOverheadUnits), the layer is planned
+    // again with segments spanning clusters of 4 on half the SMs, and that
+    // plan is taken if its share is smaller.  Back to back, the next layer's
+    // CTAs then find free SMs (one CTA per SM) and load their first stages
+    // while this layer's CTAs stream and merge.  Config 2's layer (two
+    // 15.1k-row and six 2.3k-row segments): 64 CTAs in clusters of 16 at
+    // 960-row shares, 9.95 us -> 72 CTAs in clusters of 4 at 640 rows,
+    // 9.36 us (B200).
+    const int64_t h = std::max<int64_t>(1, sm_count / 2);
+    if (c > 4 && share > kWaveOverheadUnits && (total + h - 1) / h <= kMaxShareUnits) {
+      const int keep_cl = cl;
+      half = true;
+      const int64_t sh = spread_share();
+      if (sh < share) {
         share = sh;
+      } else {
+        half = false;
+        cl = keep_cl;
       }
     }
+  } else {
+    share = spread_share();
   }
   std::vector<int64_t> k(num_segs);
   int64_t kmax = 1;
