@@ -222,12 +222,9 @@ extern "C" wnw_status wnw_attn_plan(const int32_t* seg_cap, int num_segs, int sm
   };
   int64_t share = std::max<int64_t>((total + slots_for(cl) - 1) / slots_for(cl),
                                     std::min<int64_t>(kMaxShareUnits, (umax + cl - 1) / cl));
-  // half: plan for half the SMs.  Back-to-back layers then run side by side
-  // (one CTA per SM): the next layer's CTAs find free SMs and load their
-  // first stages while this layer's CTAs stream and merge.
-  bool half = false;
+  int64_t limit = 0;  // > 0: plan for at most this many SMs (see below)
   auto slots_of = [&](int x) {  // CTA slots a plan may fill per wave
-    return half ? std::max<int64_t>(1, std::min<int64_t>(slots_for(x), sm_count / 2)) : slots_for(x);
+    return limit > 0 ? std::max<int64_t>(1, std::min<int64_t>(slots_for(x), limit)) : slots_for(x);
   };
   // Segments spanning clusters: clusters of at most 4; for w = 1..4 waves,
   // the smallest share whose CTAs fit w waves of the resident slots (or
@@ -261,22 +258,25 @@ extern "C" wnw_status wnw_attn_plan(const int32_t* seg_cap, int num_segs, int sm
     // Clusters above 4 CTAs tie each long segment to one GPC, which streams
     // it at about 1 TB/s.  When that makes a CTA's streaming outweigh its
     // fixed cost (shares above kWaveOverheadUnits), the layer is planned
-    // again with segments spanning clusters of 4 on half the SMs, and that
-    // plan is taken if its share is smaller.  Back to back, the next layer's
-    // CTAs then find free SMs (one CTA per SM) and load their first stages
-    // while this layer's CTAs stream and merge.  Config 2's layer (two
-    // 15.1k-row and six 2.3k-row segments): 64 CTAs in clusters of 16 at
-    // 960-row shares, 9.95 us -> 72 CTAs in clusters of 4 at 640 rows,
-    // 9.36 us (B200).
-    const int64_t h = std::max<int64_t>(1, sm_count / 2);
-    if (c > 4 && share > kWaveOverheadUnits && (total + h - 1) / h <= kMaxShareUnits) {
+    // again with segments spanning clusters of 4 on half, then two thirds of
+    // the SMs, and the first of those plans whose share is smaller is taken.
+    // Back to back, the next layer's CTAs then find free SMs (one CTA per
+    // SM) and load their first stages while this layer's CTAs stream and
+    // merge.  Measured on a B200, layers of 2-5 segments of 15.1k rows beside
+    // 2.3k-row ones, back to back: one class-A segment 9.80 -> 9.17 us (half),
+    // two 10.07 -> 9.38 (half), three 10.41 -> 9.91 and four 11.37 -> 10.76
+    // (two thirds); all the SMs (clusters of 4) gave 9.75-11.27 us.
+    if (c > 4 && share > kWaveOverheadUnits) {
       const int keep_cl = cl;
-      half = true;
-      const int64_t sh = spread_share();
-      if (sh < share) {
-        share = sh;
-      } else {
-        half = false;
+      for (const int64_t part : {int64_t(sm_count) / 2, int64_t(sm_count) * 2 / 3}) {
+        if (part < 1 || (total + part - 1) / part > kMaxShareUnits) continue;
+        limit = part;
+        const int64_t sh = spread_share();
+        if (sh < share) {
+          share = sh;
+          break;
+        }
+        limit = 0;
         cl = keep_cl;
       }
     }
