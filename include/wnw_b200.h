@@ -295,6 +295,28 @@ wnw_status wnw_rebuild_layers(int dtype, int head_dim, int num_layers, const int
                               const int32_t* plan_blob, int64_t blob_ints, void* k_move, void* v_move,
                               int64_t move_rows, int32_t* status, int32_t* err, void* const* wait_events,
                               void* const* record_events, void* stream);
+/* The same rebuilds as wnw_rebuild_layers in one gather and one scatter
+ * launch for all the changed layers (per 48 changed layers), for steps whose
+ * fetched rows are all in device memory before the first rebuild is needed
+ * (no reference counterpart; the reference rebuilds each layer in its own
+ * kernel, src/algorithms/wnw/code/cache.py:716-754).  The stream waits for
+ * every changed layer's wait_events[l] first, and every changed layer's
+ * record_events[l] is recorded after the last launch.  Layer l (the i-th
+ * changed layer of its launch) keeps its moved rows in the move buffers from
+ * the row that sums the moved-row totals of the launch's earlier changed
+ * layers (read from their plan records), so move_rows must cover the sum of
+ * the changed layers' moved rows; its status words start at the sum of the
+ * earlier changed layers' num_segs, so status_len must be at least the sum
+ * over all changed layers.  Every check of wnw_rebuild_segments applies per
+ * layer; a layer whose moved rows do not fit sets WNW_DEVERR_CAPACITY and
+ * moves nothing.  Layouts and lengths equal those of the per-layer calls. */
+wnw_status wnw_rebuild_layers_fused(int dtype, int head_dim, int num_layers, const int32_t* layer_changed,
+                                    void* const* k_store, void* const* v_store, const int64_t* const* seg_base,
+                                    int32_t* const* seg_len, const int32_t* const* seg_cap, const int32_t* num_segs,
+                                    const void* k_landing, const void* v_landing, int64_t land_rows,
+                                    const int32_t* plan_blob, int64_t blob_ints, void* k_move, void* v_move,
+                                    int64_t move_rows, int32_t* status, int64_t status_len, int32_t* err,
+                                    void* const* wait_events, void* const* record_events, void* stream);
 
 /* Copy rows [0, len[s]) of every segment from src (+src_base[s]) to dst
  * (+dst_base[s]); src and dst must not overlap.  Used to pack a slot layout

@@ -309,6 +309,81 @@ def test_rebuild_matches_oracle(dev):
     assert torch.equal(ks, snap)
 
 
+def _rebuild_case(dev, D, dtype, L, seed):
+    """L layers of six slots each with random changes (evictions, loads, some
+    layers unchanged); returns the layers' tensors, the plan blob, the landing
+    rows and the changed flags."""
+    rng = np.random.default_rng(seed)
+    layers, plans, changed = [], [], []
+    cur = 0
+    for l in range(L):
+        lens = [int(x) for x in rng.integers(0, 1500, 6)]
+        ks, vs, base, cap = _slots(lens, 1200, D, dtype, dev, seed=seed + l)
+        recs = []
+        if l % 4 != 3:  # every fourth layer unchanged
+            for s in rng.permutation(6)[:int(rng.integers(1, 6))].tolist():
+                n = lens[s]
+                cuts = sorted(set(int(x) for x in rng.integers(0, n + 1, 2 * int(rng.integers(0, 4))))) if n else []
+                ev = [(cuts[i], cuts[i + 1]) for i in range(0, len(cuts) - 1, 2) if cuts[i + 1] > cuts[i]]
+                nl = int(rng.integers(0, 300))
+                new = n - sum(b - a for a, b in ev) + nl
+                recs.append((s, n, new, cur, nl, ev))
+                cur += nl
+        plans.append(recs)
+        changed.append(1 if recs else 0)
+        layers.append((ks, vs, torch.from_numpy(base).to(dev), torch.tensor(lens, dtype=torch.int32, device=dev),
+                       torch.from_numpy(cap.astype(np.int32)).to(dev)))
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    land_k = torch.randn(max(1, cur), D, generator=g).to(dtype).to(dev)
+    land_v = torch.randn(max(1, cur), D, generator=g).to(dtype).to(dev)
+    from wnw_b200 import kernels as Kx
+    blob = Kx.pack_plan(plans)
+    moved = [Kx.plan_record(blob, l)["moved_total"] for l in range(L)]
+    return layers, torch.from_numpy(blob).to(dev), land_k, land_v, changed, moved
+
+
+def test_rebuild_layers_fused_equals_per_layer(dev):
+    """wnw_rebuild_layers_fused (one launch pair for every changed layer, each
+    with its own region of the move buffers) leaves every store and length
+    exactly as the per-layer wnw_rebuild_segments calls do; a move buffer too
+    small for the step's moved rows is refused with the capacity bit."""
+    from wnw_b200 import kernels as Kx
+    from wnw_b200 import native as N
+    D, dtype, L = 128, torch.bfloat16, 7
+    layers, blob, land_k, land_v, changed, moved = _rebuild_case(dev, D, dtype, L, seed=31)
+    assert sum(moved) > 0 and sum(changed) >= 4
+    ref = [tuple(t.clone() for t in lay) for lay in layers]
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    mk = torch.empty(max(moved) + 1, D, dtype=dtype, device=dev)
+    mv = torch.empty_like(mk)
+    status = torch.zeros(8, dtype=torch.int32, device=dev)
+    for l in range(L):
+        ks, vs, base, slen, cap = ref[l]
+        Kx.rebuild_layer(ks, vs, base, slen, cap, land_k, land_v, blob, l, mk, mv, status, err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    mk2 = torch.empty(sum(moved), D, dtype=dtype, device=dev)
+    mv2 = torch.empty_like(mk2)
+    status2 = torch.zeros(6 * L, dtype=torch.int32, device=dev)
+    Kx.rebuild_layers_fused(layers, changed, land_k, land_v, blob, mk2, mv2, status2, err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    for l in range(L):
+        for a, b in zip(layers[l], ref[l]):
+            assert torch.equal(a, b), l
+    # the same step again from the original stores, with one row too few to
+    # move: the last layer that moves rows does not fit and is left as it was
+    layers, blob, land_k, land_v, changed, moved = _rebuild_case(dev, D, dtype, L, seed=31)
+    last = max(l for l in range(L) if moved[l] > 0)
+    before = [t.clone() for t in layers[last]]
+    small = torch.empty(sum(moved) - 1, D, dtype=dtype, device=dev)
+    Kx.rebuild_layers_fused(layers, changed, land_k, land_v, blob, small, torch.empty_like(small), status2, err)
+    torch.cuda.synchronize()
+    assert int(err.item()) & N.DEVERR_CAPACITY
+    for a, b in zip(layers[last], before):
+        assert torch.equal(a, b)
+
+
 def test_rebuild_refuses_malformed_plans(dev):
     """Host-side fault injection: corrupted plan blobs (a layer offset past the
     blob, more records than segments, a segment number out of range, landing

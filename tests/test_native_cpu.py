@@ -429,6 +429,33 @@ def test_oproj_allreduce_rejects_bad_arguments():
     assert N.lib.wnw_oproj_allreduce(ctypes.byref(a), None) == 1
 
 
+def test_rebuild_layers_fused_rejects_bad_arguments():
+    """Argument checks of the one-launch-pair rebuild run before any launch:
+    null per-layer tables, misaligned stores, and a status buffer shorter than
+    the changed layers' segments."""
+    P = ctypes.c_void_p
+    buf = (ctypes.c_uint8 * 8192)()
+    base = (ctypes.addressof(buf) + 255) // 256 * 256
+    L = 3
+    ptrs = lambda off: (P * L)(*[base + off + 16 * i for i in range(L)])  # noqa: E731
+    chg = np.array([1, 0, 1], np.int32)
+    nsegs = (ctypes.c_int32 * L)(8, 8, 8)
+
+    def call(k_store, status_len, changed=chg):
+        return N.lib.wnw_rebuild_layers_fused(N.BF16, 128, L, changed.ctypes.data, k_store, ptrs(1024),
+                                              ptrs(2048), ptrs(3072), ptrs(4096), nsegs, None, None, 0, base,
+                                              64, None, None, 0, base + 5120, status_len, base + 6144, None, None,
+                                              None)
+
+    assert call(ptrs(0), 15) == 1 and b"status needs 16" in N.lib.wnw_last_error()
+    bad = (P * L)(base, base, base + 8)
+    assert call(bad, 16) == 1 and b"layer 2" in N.lib.wnw_last_error()
+    bad = (P * L)(None, base, base)
+    assert call(bad, 16) == 1 and b"layer 0" in N.lib.wnw_last_error()
+    assert N.lib.wnw_rebuild_layers_fused(N.BF16, 128, 0, None, None, None, None, None, None, None, None, None, 0,
+                                          None, 0, None, None, 0, None, 0, None, None, None, None) == 0
+
+
 def test_oproj_exchange_refuses_shapes_it_was_not_built_for():
     """OprojAllReduce checks every call's tensors against the receive
     buffers it was built for before it launches anything."""

@@ -112,10 +112,12 @@ class B200WnWCache(FlatVarlenCache):
                            memory; "dma": host threads gather them into pinned
                            staging and cudaMemcpyAsync copies each layer;
       fetch_threads     -- host threads of the "dma" gather;
-      fetch_ctas        -- CTAs of the zero-copy fetch: 12 (~0.8 MB of host
-                           reads in flight) keep the link saturated; more only
-                           queue requests in the memory system and slow the
-                           layer kernels running beside the fetch;
+      fetch_ctas        -- CTAs of the zero-copy fetch; by default 12 for
+                           the host tier (~0.8 MB of host reads in flight
+                           keep the link saturated; more only queue requests
+                           in the memory system and slow the layer kernels
+                           running beside the fetch) and 148 for the HBM tier
+                           (a device-memory gather, one range per CTA);
       fetch_plan        -- "device" (default): each step's fetch is planned
                            on the GPU from the device top-k and starts at
                            once, while the host planner plans the rebuild and
@@ -127,14 +129,16 @@ class B200WnWCache(FlatVarlenCache):
                            host memory, the reference's CPU offload; default)
                            or "hbm" (device memory, for deployments whose HBM
                            budget holds them: the same gather then reads HBM
-                           instead of crossing the host link);
+                           instead of crossing the host link, and with
+                           rebuild_ahead each step's rebuilds run as one
+                           launch pair for all layers);
       score_reduce      -- tensor parallelism by kv head (wnw_b200.tp): a
                            callable that sums the class-A score accumulator
                            over the ranks before every chunk selection.
     """
 
     def __init__(self, config, num_layers, num_kv_heads, num_q_heads, head_dim, device, adapter=None, *,
-                 max_decode_tokens=256, fetch_mode="zerocopy", fetch_threads=8, fetch_ctas=12, score_reduce=None,
+                 max_decode_tokens=256, fetch_mode="zerocopy", fetch_threads=8, fetch_ctas=None, score_reduce=None,
                  offload_tier="host", wait_timeout_s=60.0, fetch_plan="device", rebuild_ahead=True):
         super().__init__(num_layers, num_kv_heads, num_q_heads, head_dim, device, adapter)
         if self.device.type != "cuda":
@@ -160,6 +164,11 @@ class B200WnWCache(FlatVarlenCache):
         # land (the next step's attention of layer l waits for layer l only),
         # instead of on the compute stream right before layer l's attention
         self.rebuild_ahead = bool(rebuild_ahead)
+        # the HBM tier's fetch lands every layer's rows within microseconds:
+        # its rebuilds run as one launch pair for the whole step instead of a
+        # pair per layer (the host tier keeps per-layer rebuilds, each behind
+        # its own layer's fetch over the host link)
+        self._fused_rebuild = self.rebuild_ahead and offload_tier == "hbm"
         self._rb_stream = None
         self._rb_events = None
         self._rebuilt = None
@@ -167,7 +176,7 @@ class B200WnWCache(FlatVarlenCache):
         self._dplan_args = None
         self.wait_timeout_s = float(wait_timeout_s)
         self.fetch_threads = int(fetch_threads)
-        self.fetch_ctas = int(fetch_ctas)
+        self.fetch_ctas = int(fetch_ctas) if fetch_ctas is not None else (148 if offload_tier == "hbm" else 12)
         self.score_reduce = score_reduce
         self._dev_index = self.device.index if self.device.index is not None else torch.cuda.current_device()
         self._rb_args = [None] * num_layers
@@ -618,7 +627,10 @@ class B200WnWCache(FlatVarlenCache):
         self._restore_ptrs = None
         self._fetched_rows = 0
         self._move_k = self._move_v = None
-        self._rb_status = torch.zeros(max(1, S), dtype=torch.int32, device=self.device)
+        # status words: one layer's records, or every layer's for the fused
+        # rebuild of the HBM tier
+        self._rb_status = torch.zeros(max(1, S * (L if self._fused_rebuild else 1)), dtype=torch.int32,
+                                      device=self.device)
         self._layer_chg = [0] * L
         self._chg_buf = None
         self._layer_rows = np.zeros(L + 1, np.int64)
@@ -648,7 +660,9 @@ class B200WnWCache(FlatVarlenCache):
             return
         n_ranges = L * S * segs
         self._ensure_fetch_capacity(rows, n_ranges)
-        self._ensure_move_capacity(int((bound + self.max_decode_tokens * (bound > 0)).sum(axis=1).max()))
+        moved = (bound + self.max_decode_tokens * (bound > 0)).sum(axis=1)
+        # the fused rebuild keeps every changed layer's moved rows at once
+        self._ensure_move_capacity(int(moved.sum() if self._fused_rebuild else moved.max()))
         plan_ints = (L + 1) + L * (6 + 8 * S) + 2 * n_ranges
         if plan_ints > self._plan_host.numel():
             n = 1 << (plan_ints - 1).bit_length()
@@ -882,17 +896,29 @@ class B200WnWCache(FlatVarlenCache):
             for e in self._rb_events:  # create the CUDA events now: their handles are passed down
                 e.record(self._rb_stream)
         rs = self._rb_stream
+        chg = np.ascontiguousarray(self._layer_chg, np.int32)
+        if self._fused_rebuild:  # every changed layer's moved rows at once (presized; grows only past that)
+            ph = self._plan_host.numpy()
+            self._ensure_move_capacity(int(sum(int(ph[int(ph[l]) + 1]) for l in np.nonzero(chg)[0])))
         start = torch.cuda.Event()
         start.record()
         rs.wait_event(start)
         b = self._rebuild_batch()
-        chg = np.ascontiguousarray(self._layer_chg, np.int32)
-        st = N.lib.wnw_rebuild_layers(*b["head"], chg.ctypes.data, *b["layers"], *b["shared"], self._event_handles,
-                                      b["record"], rs.cuda_stream)
+        if self._fused_rebuild:
+            sh = b["shared"]  # ... status, then its length, then err
+            st = N.lib.wnw_rebuild_layers_fused(*b["head"], chg.ctypes.data, *b["layers"], *sh[:9],
+                                                int(self._rb_status.numel()), sh[9], self._event_handles,
+                                                b["record"], rs.cuda_stream)
+            name = "wnw_rebuild_layers_fused"
+        else:
+            st = N.lib.wnw_rebuild_layers(*b["head"], chg.ctypes.data, *b["layers"], *b["shared"],
+                                          self._event_handles, b["record"], rs.cuda_stream)
+            name = "wnw_rebuild_layers"
         if st:
-            N.check(st, "wnw_rebuild_layers")
-        for l in np.nonzero(chg)[0].tolist():
-            Kx.LAUNCHES[0] += 2
+            N.check(st, name)
+        changed = np.nonzero(chg)[0].tolist()
+        Kx.LAUNCHES[0] += 2 * ((len(changed) + 47) // 48 if self._fused_rebuild else len(changed))
+        for l in changed:
             self._len_host[l] = self._next_lens[l]
             self._rebuilt[l] = True
         self._pending = False

@@ -11,6 +11,7 @@
 // two grid-wide launches (gather, then scatter).  The step's new token is
 // appended afterwards by the decode-attention kernel.
 #include <algorithm>
+#include <vector>
 
 #include "common.cuh"
 
@@ -74,11 +75,12 @@ __device__ inline bool record_well_formed(const int32_t* blob, int64_t blob_ints
 
 // Every CTA checks the layer record once; on a malformed record the block 0
 // thread 0 raises the error bit and every CTA returns before reading it.
-__device__ inline bool cta_record_ok(const int32_t* blob, int64_t blob_ints, int layer, int num_segs, int32_t* err) {
+__device__ inline bool cta_record_ok(const int32_t* blob, int64_t blob_ints, int layer, int num_segs, int32_t* err,
+                                     bool first_cta) {
   __shared__ int s_ok;
   if (threadIdx.x == 0) {
     s_ok = record_well_formed(blob, blob_ints, layer, num_segs) ? 1 : 0;
-    if (!s_ok && blockIdx.x == 0) atomicOr(err, WNW_DEVERR_LEN_MISMATCH);
+    if (!s_ok && first_cta) atomicOr(err, WNW_DEVERR_LEN_MISMATCH);
   }
   __syncthreads();
   return s_ok != 0;
@@ -99,17 +101,16 @@ __device__ inline int kept_source_row(const RbRec& r, int i, int k) {
   return -1;
 }
 
-// Phase 1: validate every record, gather the moving kept rows into scratch.
-__global__ void __launch_bounds__(kRbThreads)
-    rebuild_gather_kernel(const uint4* k_store, const uint4* v_store, const int64_t* seg_base, const int32_t* seg_len,
-                          const int32_t* seg_cap, const int32_t* blob, int64_t blob_ints, int layer, int num_segs,
-                          int64_t land_rows, uint4* k_move, uint4* v_move, int64_t move_rows, int32_t* status,
-                          int32_t* err, int cpr) {
-  pdl_launch_dependents();  // the scatter may start validating its record now
-  if (!cta_record_ok(blob, blob_ints, layer, num_segs, err)) return;
+// Phase 1 of one layer, by CTA `cta` of `ncta`: validate every record,
+// gather the moving kept rows into scratch.
+__device__ void gather_layer(const uint4* k_store, const uint4* v_store, const int64_t* seg_base,
+                             const int32_t* seg_len, const int32_t* seg_cap, const int32_t* blob, int64_t blob_ints,
+                             int layer, int num_segs, int64_t land_rows, uint4* k_move, uint4* v_move,
+                             int64_t move_rows, int32_t* status, int32_t* err, int cpr, int cta, int ncta) {
+  if (!cta_record_ok(blob, blob_ints, layer, num_segs, err, cta == 0)) return;
   const RbRec r(blob, layer);
-  const int64_t gtid = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
-  const int64_t nthreads = int64_t(gridDim.x) * blockDim.x;
+  const int64_t gtid = int64_t(cta) * blockDim.x + threadIdx.x;
+  const int64_t nthreads = int64_t(ncta) * blockDim.x;
   for (int i = static_cast<int>(gtid); i < r.n; i += static_cast<int>(nthreads)) {
     const int seg = r.seg[i];
     const int e0 = r.ev_off[i], e1 = r.ev_off[i + 1];
@@ -157,22 +158,29 @@ __global__ void __launch_bounds__(kRbThreads)
   }
 }
 
-// Phase 2: write moved and fetched rows to their final slot rows; set seg_len.
 __global__ void __launch_bounds__(kRbThreads)
-    rebuild_scatter_kernel(uint4* k_store, uint4* v_store, const int64_t* seg_base, int32_t* seg_len,
-                           const int32_t* seg_cap, const uint4* k_land, const uint4* v_land, const int32_t* blob,
-                           int64_t blob_ints, int layer, int num_segs, int64_t move_rows, const uint4* k_move,
-                           const uint4* v_move, const int32_t* status, int32_t* err, int cpr) {
-  // the layer's decode attention (launched with programmatic dependent launch)
-  // may start its layout-only prologue now; it waits for this grid to finish
-  // before it reads anything written here
-  pdl_launch_dependents();
-  if (!cta_record_ok(blob, blob_ints, layer, num_segs, err)) return;  // reads the plan blob only
+    rebuild_gather_kernel(const uint4* k_store, const uint4* v_store, const int64_t* seg_base, const int32_t* seg_len,
+                          const int32_t* seg_cap, const int32_t* blob, int64_t blob_ints, int layer, int num_segs,
+                          int64_t land_rows, uint4* k_move, uint4* v_move, int64_t move_rows, int32_t* status,
+                          int32_t* err, int cpr) {
+  pdl_launch_dependents();  // the scatter may start validating its record now
+  gather_layer(k_store, v_store, seg_base, seg_len, seg_cap, blob, blob_ints, layer, num_segs, land_rows, k_move,
+               v_move, move_rows, status, err, cpr, blockIdx.x, gridDim.x);
+}
+
+// Phase 2 of one layer, by CTA `cta` of `ncta` of a launch dependent on the
+// gather's (it checks the layer's record, then waits for the gather): write
+// moved and fetched rows to their final slot rows; set seg_len.
+__device__ void scatter_layer(uint4* k_store, uint4* v_store, const int64_t* seg_base, int32_t* seg_len,
+                              const uint4* k_land, const uint4* v_land, const int32_t* blob, int64_t blob_ints,
+                              int layer, int num_segs, int64_t move_rows, const uint4* k_move, const uint4* v_move,
+                              const int32_t* status, int32_t* err, int cpr, int cta, int ncta) {
+  if (!cta_record_ok(blob, blob_ints, layer, num_segs, err, cta == 0)) return;  // reads the plan blob only
   pdl_wait();  // the gather's status words and moved rows are complete
   const RbRec r(blob, layer);
   if (r.moved_total > move_rows) return;  // refused by the gather (error bit set there)
-  const int64_t gtid = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
-  const int64_t nthreads = int64_t(gridDim.x) * blockDim.x;
+  const int64_t gtid = int64_t(cta) * blockDim.x + threadIdx.x;
+  const int64_t nthreads = int64_t(ncta) * blockDim.x;
   const int64_t total = int64_t(r.out_total) * cpr;
   for (int64_t x = gtid; x < total; x += nthreads) {
     const int row = static_cast<int>(x / cpr);
@@ -196,6 +204,86 @@ __global__ void __launch_bounds__(kRbThreads)
   }
   for (int i = static_cast<int>(gtid); i < r.n; i += static_cast<int>(nthreads))
     if (status[i]) seg_len[r.seg[i]] = r.new_len[i];
+}
+
+__global__ void __launch_bounds__(kRbThreads)
+    rebuild_scatter_kernel(uint4* k_store, uint4* v_store, const int64_t* seg_base, int32_t* seg_len,
+                           const int32_t* seg_cap, const uint4* k_land, const uint4* v_land, const int32_t* blob,
+                           int64_t blob_ints, int layer, int num_segs, int64_t move_rows, const uint4* k_move,
+                           const uint4* v_move, const int32_t* status, int32_t* err, int cpr) {
+  // the layer's decode attention (launched with programmatic dependent launch)
+  // may start its layout-only prologue now; it waits for this grid to finish
+  // before it reads anything written here
+  pdl_launch_dependents();
+  scatter_layer(k_store, v_store, seg_base, seg_len, k_land, v_land, blob, blob_ints, layer, num_segs, move_rows,
+                k_move, v_move, status, err, cpr, blockIdx.x, gridDim.x);
+}
+
+// ------------------------------------------------ every changed layer at once
+// One gather and one scatter launch for all the changed layers of a step:
+// blockIdx.y picks the layer, blockIdx.x / gridDim.x the CTA within it; each
+// layer does exactly what its own wnw_rebuild_segments pair would, with its
+// moved rows in a region of the move buffers of their own and its status
+// words at status_base.
+constexpr int kRbMultiMax = 48;  // layers per launch pair (by-value kernel argument, < 4 KB)
+struct RbLayer {
+  uint4* k_store;
+  uint4* v_store;
+  const int64_t* seg_base;
+  int32_t* seg_len;
+  const int32_t* seg_cap;
+  int layer, num_segs, status_base;
+};
+struct RbMulti {
+  RbLayer l[kRbMultiMax];
+  int n;
+};
+
+// First row of the i-th layer's moved rows in the move buffers: the moved-row
+// totals of the launch's earlier layers, read from their records (a record
+// outside the blob counts 0; its own layer refuses it).  Every thread of the
+// CTA returns the same value.
+__device__ int64_t move_base_of(const RbMulti& m, int i, const int32_t* blob, int64_t blob_ints) {
+  __shared__ unsigned long long s_base;
+  if (threadIdx.x == 0) s_base = 0;
+  __syncthreads();
+  for (int j = threadIdx.x; j < i; j += blockDim.x) {
+    const int l = m.l[j].layer;
+    if (l >= 0 && int64_t(l) < blob_ints) {
+      const int64_t o = blob[l];
+      if (o >= 0 && o + 3 <= blob_ints && blob[o + 1] > 0) atomicAdd(&s_base, static_cast<unsigned long long>(blob[o + 1]));
+    }
+  }
+  __syncthreads();
+  return static_cast<int64_t>(s_base);
+}
+
+__global__ void __launch_bounds__(kRbThreads)
+    rebuild_gather_multi_kernel(const RbMulti m, const int32_t* blob, int64_t blob_ints, int64_t land_rows,
+                                uint4* k_move, uint4* v_move, int64_t move_rows, int32_t* status, int32_t* err,
+                                int cpr) {
+  pdl_launch_dependents();  // the scatter may start validating its records now
+  const int i = blockIdx.y;
+  const RbLayer& L = m.l[i];
+  const int64_t mb = move_base_of(m, i, blob, blob_ints);
+  const int64_t room = mb <= move_rows ? move_rows - mb : -1;  // a negative room refuses every moved row
+  gather_layer(L.k_store, L.v_store, L.seg_base, L.seg_len, L.seg_cap, blob, blob_ints, L.layer, L.num_segs,
+               land_rows, k_move + (room >= 0 ? mb : 0) * cpr, v_move + (room >= 0 ? mb : 0) * cpr, room,
+               status + L.status_base, err, cpr, blockIdx.x, gridDim.x);
+}
+
+__global__ void __launch_bounds__(kRbThreads)
+    rebuild_scatter_multi_kernel(const RbMulti m, const uint4* k_land, const uint4* v_land, const int32_t* blob,
+                                 int64_t blob_ints, int64_t move_rows, const uint4* k_move, const uint4* v_move,
+                                 const int32_t* status, int32_t* err, int cpr) {
+  pdl_launch_dependents();
+  const int i = blockIdx.y;
+  const RbLayer& L = m.l[i];
+  const int64_t mb = move_base_of(m, i, blob, blob_ints);
+  const int64_t room = mb <= move_rows ? move_rows - mb : -1;
+  scatter_layer(L.k_store, L.v_store, L.seg_base, L.seg_len, k_land, v_land, blob, blob_ints, L.layer, L.num_segs,
+                room, k_move + (room >= 0 ? mb : 0) * cpr, v_move + (room >= 0 ? mb : 0) * cpr,
+                status + L.status_base, err, cpr, blockIdx.x, gridDim.x);
 }
 
 // ------------------------------------------------------------ segment copy
@@ -320,6 +408,86 @@ extern "C" wnw_status wnw_rebuild_layers(int dtype, int head_dim, int num_layers
     if (record_events && record_events[l])
       WNW_CUDA_TRY(cudaEventRecord(static_cast<cudaEvent_t>(record_events[l]), s));
   }
+  return WNW_OK;
+}
+
+extern "C" wnw_status wnw_rebuild_layers_fused(int dtype, int head_dim, int num_layers, const int32_t* layer_changed,
+                                               void* const* k_store, void* const* v_store,
+                                               const int64_t* const* seg_base, int32_t* const* seg_len,
+                                               const int32_t* const* seg_cap, const int32_t* num_segs,
+                                               const void* k_landing, const void* v_landing, int64_t land_rows,
+                                               const int32_t* plan_blob, int64_t blob_ints, void* k_move,
+                                               void* v_move, int64_t move_rows, int32_t* status,
+                                               int64_t status_len, int32_t* err, void* const* wait_events,
+                                               void* const* record_events, void* stream) {
+  using namespace wnw;
+  WNW_CHECK_ARG(num_layers >= 0, "num_layers < 0");
+  if (num_layers == 0) return WNW_OK;
+  WNW_CHECK_ARG(layer_changed && k_store && v_store && seg_base && seg_len && seg_cap && num_segs && plan_blob &&
+                    status && err,
+                "null pointer argument");
+  WNW_CHECK_ARG(land_rows >= 0 && move_rows >= 0 && status_len >= 0 && blob_ints > num_layers,
+                "negative sizes, or a blob too small for the layer table");
+  WNW_CHECK_ARG(k_landing == nullptr || (aligned16(k_landing) && aligned16(v_landing)),
+                "landing buffers must be 16-byte aligned");
+  WNW_CHECK_ARG(move_rows == 0 || (k_move && v_move && aligned16(k_move) && aligned16(v_move)),
+                "move buffers must be given and 16-byte aligned when move_rows > 0");
+  const int rb = row_bytes_of(dtype, head_dim);
+  WNW_CHECK_ARG(rb > 0 && rb % 16 == 0, "row size must be a positive multiple of 16 bytes");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // the changed layers, checked and cut into launch pairs of kRbMultiMax
+  std::vector<int> chg;
+  int64_t st_need = 0;
+  for (int l = 0; l < num_layers; ++l) {
+    if (!layer_changed[l]) continue;
+    WNW_CHECK_ARG(k_store[l] && v_store[l] && seg_base[l] && seg_len[l] && seg_cap[l] && num_segs[l] >= 0,
+                  "layer %d: null store or table, or negative num_segs", l);
+    WNW_CHECK_ARG(aligned16(k_store[l]) && aligned16(v_store[l]), "layer %d: stores must be 16-byte aligned", l);
+    chg.push_back(l);
+    st_need += num_segs[l];
+  }
+  WNW_CHECK_ARG(st_need <= status_len, "status needs %lld entries (the changed layers' num_segs), has %lld",
+                static_cast<long long>(st_need), static_cast<long long>(status_len));
+  if (chg.empty()) return WNW_OK;
+  // every launch reads rows any earlier fetch may land: wait for all of them
+  if (wait_events)
+    for (int l : chg)
+      if (wait_events[l]) WNW_CUDA_TRY(cudaStreamWaitEvent(s, static_cast<cudaEvent_t>(wait_events[l]), 0));
+  int64_t status_base = 0;
+  for (size_t c0 = 0; c0 < chg.size(); c0 += kRbMultiMax) {
+    const int n = static_cast<int>(std::min<size_t>(kRbMultiMax, chg.size() - c0));
+    RbMulti m = {};
+    m.n = n;
+    for (int i = 0; i < n; ++i) {
+      const int l = chg[c0 + i];
+      m.l[i] = RbLayer{static_cast<uint4*>(k_store[l]), static_cast<uint4*>(v_store[l]), seg_base[l], seg_len[l],
+                       seg_cap[l], l, num_segs[l], static_cast<int>(status_base)};
+      status_base += num_segs[l];
+    }
+    // about eight CTAs per SM over the launch's layers, at least 8 per layer
+    const dim3 grid(std::max(8, (2 * kRbMaxBlocks + n - 1) / n), n);
+    rebuild_gather_multi_kernel<<<grid, kRbThreads, 0, s>>>(m, plan_blob, blob_ints, k_landing ? land_rows : 0,
+                                                             static_cast<uint4*>(k_move),
+                                                             static_cast<uint4*>(v_move), move_rows, status, err,
+                                                             rb / 16);
+    WNW_CUDA_TRY(cudaGetLastError());
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(kRbThreads, 1, 1);
+    cfg.stream = s;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    WNW_CUDA_TRY(cudaLaunchKernelEx(&cfg, rebuild_scatter_multi_kernel, m, static_cast<const uint4*>(k_landing),
+                                    static_cast<const uint4*>(v_landing), plan_blob, blob_ints, move_rows,
+                                    static_cast<const uint4*>(k_move), static_cast<const uint4*>(v_move),
+                                    static_cast<const int32_t*>(status), err, rb / 16));
+  }
+  if (record_events)
+    for (int l : chg)
+      if (record_events[l]) WNW_CUDA_TRY(cudaEventRecord(static_cast<cudaEvent_t>(record_events[l]), s));
   return WNW_OK;
 }
 

@@ -252,6 +252,27 @@ def rebuild_layer(k_store, v_store, seg_base, seg_len, seg_cap, k_landing, v_lan
     _count(2)
 
 
+def rebuild_layers_fused(layers, changed, k_landing, v_landing, plan_blob, k_move, v_move, status, err,
+                         stream=None):
+    """Every changed layer's compaction + splice in one gather and one scatter
+    launch.  ``layers``: per layer (k_store, v_store, seg_base, seg_len,
+    seg_cap); ``changed``: per layer 0 / 1."""
+    L = len(layers)
+    P = C.c_void_p
+    arr = lambda i: (P * L)(*[t[i].data_ptr() for t in layers])  # noqa: E731
+    chg = np.ascontiguousarray(changed, np.int32)
+    nsegs = (C.c_int32 * L)(*[int(t[3].numel()) for t in layers])
+    k0 = layers[0][0]
+    N.call("wnw_rebuild_layers_fused", N.dtype_code(k0.dtype), k0.shape[1], L, chg.ctypes.data, arr(0), arr(1),
+           arr(2), arr(3), arr(4), nsegs, k_landing.data_ptr() if k_landing is not None else None,
+           v_landing.data_ptr() if v_landing is not None else None,
+           int(k_landing.shape[0]) if k_landing is not None else 0, plan_blob.data_ptr(), int(plan_blob.numel()),
+           k_move.data_ptr() if k_move is not None else None, v_move.data_ptr() if v_move is not None else None,
+           int(k_move.shape[0]) if k_move is not None else 0, status.data_ptr(), int(status.numel()),
+           err.data_ptr(), None, None, N.stream_ptr(stream))
+    _count(2 * ((int(chg.astype(bool).sum()) + 47) // 48))
+
+
 def plan_record(blob, layer):
     """Host-side view of one layer record of a device-plan blob (numpy int32)."""
     o = int(blob[layer])

@@ -172,6 +172,8 @@ _sig("wnw_prefill_scores", _S, C.POINTER(PrefillScoresArgs), P)
 _sig("wnw_attn_resident_clusters", _S, C.c_int, C.c_int, C.POINTER(C.c_int))
 _sig("wnw_rebuild_layers", _S, C.c_int, C.c_int, C.c_int, P, P, P, P, P, P, P, P, P, C.c_int64, P, C.c_int64,
      P, P, C.c_int64, P, P, P, P, P)
+_sig("wnw_rebuild_layers_fused", _S, C.c_int, C.c_int, C.c_int, P, P, P, P, P, P, P, P, P, C.c_int64, P,
+     C.c_int64, P, P, C.c_int64, P, C.c_int64, P, P, P, P)
 _sig("wnw_prefill_scores_scratch_bytes", _S, C.c_int, C.c_int, C.c_int, C.POINTER(C.c_int64))
 
 #: every symbol the header declares (checked by the CPU test suite)
@@ -189,7 +191,7 @@ EXPORTS = [
     "wnw_oproj_allreduce_chunks", "wnw_ipc_alloc", "wnw_ipc_open", "wnw_ipc_close", "wnw_host_device_pointer", "wnw_fetch_rows",
     "wnw_fetch_layers", "wnw_planner_upload_plan", "wnw_dplan_create", "wnw_dplan_destroy", "wnw_dplan_step",
     "wnw_dplan_verify", "wnw_prefill_scores", "wnw_prefill_scores_scratch_bytes", "wnw_attn_resident_clusters",
-    "wnw_rebuild_layers",
+    "wnw_rebuild_layers", "wnw_rebuild_layers_fused",
 ]
 
 
