@@ -33,11 +33,11 @@ class WnWConfig:
         self._class_a_set = set(self.class_a)
         self._class_b_set = set(self.class_b)
         if self.stride_tokens <= 0:
-            raise ValueError(f"stride must be positive: chunk_size_tokens={self.chunk_size_tokens} "
-                             f"<= overlap_tokens={self.overlap_tokens}")
+            raise ValueError(f"overlap_tokens {self.overlap_tokens} leaves no stride within chunks of "
+                             f"{self.chunk_size_tokens} tokens (the overlap must be smaller than the chunk)")
         if self.chunk_size_tokens % self.stride_tokens != 0:
-            raise ValueError(f"chunk_size_tokens ({self.chunk_size_tokens}) must be an integer multiple "
-                             f"of stride_tokens ({self.stride_tokens})")
+            raise ValueError(f"a chunk of {self.chunk_size_tokens} tokens is not a whole number of "
+                             f"{self.stride_tokens}-token segments (the stride must divide the chunk size)")
         if self.num_q_heads > 0 and self.num_kv_heads > 0:
             self._rebuild_class_a_kv_set()
 
