@@ -7,6 +7,8 @@ prefill / decode hooks are implemented by subclasses.
 """
 from __future__ import annotations
 
+from functools import partial
+
 import torch
 from transformers.cache_utils import Cache, CacheLayerMixin
 
@@ -44,16 +46,14 @@ class _SeqLengthStub(CacheLayerMixin):
         pass
 
     def reorder_cache(self, beam_idx):
-        raise NotImplementedError("Beam search not supported")
+        raise NotImplementedError("the flat varlen layout cannot be reordered for beam search")
 
 
 class FlatVarlenCache(Cache):
     is_compileable = False
 
     def __init__(self, num_layers, num_kv_heads, num_q_heads, head_dim, device, adapter=None):
-        stubs = [_SeqLengthStub(lambda i=i: self._seq_lengths[i] if i < len(self._seq_lengths) else 0)
-                 for i in range(num_layers)]
-        super().__init__(layers=stubs)
+        super().__init__(layers=[_SeqLengthStub(partial(self._layer_len, i)) for i in range(num_layers)])
         self.num_layers = num_layers
         self.num_kv_heads = num_kv_heads
         self.num_q_heads = num_q_heads
@@ -71,14 +71,19 @@ class FlatVarlenCache(Cache):
         self.prefilled = False
         self._seq_lengths = [0] * self.num_layers
         self.stats.reset(audio_starts.shape[0])
-        if attention_mask is not None:
-            pads = []
-            for row in attention_mask:
-                nz = (row == 1).nonzero(as_tuple=True)[0]
-                pads.append(int(nz[0].item()) if len(nz) else 0)
-            self.pad_lens = torch.tensor(pads, dtype=torch.int64, device=self.device)
-        else:
+        # left padding per sample: the first position whose mask is 1 (0 for
+        # a row without one, and without a mask)
+        if attention_mask is None:
             self.pad_lens = torch.zeros(audio_starts.shape[0], dtype=torch.int64, device=self.device)
+        else:
+            valid = attention_mask == 1
+            first = valid.to(torch.int8).argmax(dim=-1)  # the first maximum
+            self.pad_lens = torch.where(valid.any(dim=-1), first, 0).to(device=self.device, dtype=torch.int64)
+
+    def _layer_len(self, i):
+        """Tokens seen by layer i (0 before any), for the per-layer stubs."""
+        lens = getattr(self, "_seq_lengths", None)
+        return lens[i] if lens is not None and i < len(lens) else 0
 
     def update(self, key_states, value_states, layer_idx, *args, **kwargs):
         self._seq_lengths[layer_idx] += key_states.shape[-2]
@@ -100,17 +105,19 @@ class FlatVarlenCache(Cache):
         self.audio_starts = self.audio_ends = self.pad_lens = None
         self.stats.reset(0)
 
+    # the flat varlen layout keeps one ragged segment per (sample, kv head):
+    # HF's reordering and cropping operations have no meaning for it
     def reorder_cache(self, beam_idx):
-        raise NotImplementedError("FlatVarlenCache does not support beam search")
+        raise NotImplementedError("the flat varlen layout cannot be reordered for beam search")
 
     def crop(self, max_length):
-        raise NotImplementedError("FlatVarlenCache does not support assisted decoding crop")
+        raise NotImplementedError("the flat varlen layout cannot be cropped (assisted decoding)")
 
     def batch_repeat_interleave(self, repeats):
-        raise NotImplementedError("FlatVarlenCache does not support batch_repeat_interleave")
+        raise NotImplementedError("the flat varlen layout cannot repeat samples of its batch")
 
     def batch_select_indices(self, indices):
-        raise NotImplementedError("FlatVarlenCache does not support batch_select_indices")
+        raise NotImplementedError("the flat varlen layout cannot select samples of its batch")
 
     # WnW hooks (flat_cache.py:161-186)
     def prefill_before_attn(self, layer_idx):
@@ -123,7 +130,7 @@ class FlatVarlenCache(Cache):
         self.prefilled = True
 
     def decode_before_attn(self, layer_idx, k_new, v_new):
-        raise NotImplementedError("subclass must implement decode_before_attn")
+        raise NotImplementedError(f"{type(self).__name__} defines no decode_before_attn storage")
 
     def decode_after_attn(self, layer_idx, q):
         pass
@@ -132,4 +139,4 @@ class FlatVarlenCache(Cache):
         pass
 
     def _snapshot_cache_stats(self, step=-1):
-        raise NotImplementedError("subclass must implement _snapshot_cache_stats")
+        raise NotImplementedError(f"{type(self).__name__} defines no cache statistics snapshot")
