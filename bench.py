@@ -105,6 +105,9 @@ def parse():
     ap.add_argument("--no-rebuild-ahead", action="store_true",
                     help="rebuild each changed layer on the compute stream before its attention "
                          "(B200WnWCache(rebuild_ahead=False)) instead of ahead on its own stream")
+    ap.add_argument("--tier", default="host", choices=["host", "hbm"],
+                    help="step mode: where the timed legs keep the offloaded rows (host: pinned host memory, the "
+                         "headline; hbm: device memory, to profile that tier)")
     ap.add_argument("--vs-reference", action="store_true",
                     help="attn mode: also time the reference's own GPU kernels (baseline/_ref) on the same layers")
     return ap.parse_args()
@@ -546,12 +549,12 @@ def run_value(rec, dev, K, W, shard=None, tier="host"):
                 window=(wall0, wall1), selections=selections)
 
 
-def run_e2e(rec, dev, K, W, shard=None):
+def run_e2e(rec, dev, K, W, shard=None, tier="host"):
     """Hook API with host buffers: per step one H2D copy of all layers' q/k/v
     from pinned memory and one D2H copy of all layers' outputs (attention
     outputs; under tensor parallelism the all-reduced o_proj rows)."""
     shard = shard or Shard(dev)
-    cache = fresh_cache(rec, dev, K + W, shard)
+    cache = fresh_cache(rec, dev, K + W, shard, tier)
     steps, scale, L = shard.step_inputs(rec["steps"]), rec["scale"], MODEL["L"]
     shapes = [tuple(x.shape) for x in steps[0][0]]
     sizes = [math.prod(sh) for sh in shapes]
@@ -1260,6 +1263,8 @@ def main():
     tp = a.parallel == "tp" and a.impl == "b200"
     if tp:
         cfg_json["parallelism"] = f"tp{world} (kv heads sharded, o_proj all-reduce per layer)"
+    if a.tier != "host":
+        cfg_json["offload_tier"] = f"{a.tier} (class-B offloaded rows in device memory; not the headline)"
     # the clock sampler starts now so its start-up is long over by the timed
     # region; only the samples inside that region are reported
     clk = Clocks(local)
@@ -1314,14 +1319,15 @@ def _main(a, rank, world, local, dist, dev, K, W, cfg_json, tp, clk):
     shard = Shard(dev, rank, world, tp=tp, seed=2000, exchange=a.tp_exchange, batch=B)
     if tp:
         cfg_json["parallelism"] += f", exchange {a.tp_exchange}"
-    val = run_value(rec, dev, K, W, shard)
+    val = run_value(rec, dev, K, W, shard, tier=a.tier)
     clk.__exit__(None, None, None)
-    e2e = run_e2e(rec, dev, K, W, shard)
+    e2e = run_e2e(rec, dev, K, W, shard, tier=a.tier)
     if shard.ex is not None:
         shard.ex.check()
     # the same step with the offloaded rows kept in HBM (offload_tier="hbm"),
     # for comparison only: the reference offloads to host memory
-    hbm = run_value(rec, dev, K, W, shard, tier="hbm") if not dist and not a.profile else None
+    hbm = (run_value(rec, dev, K, W, shard, tier="hbm") if not dist and not a.profile and a.tier == "host"
+           else None)
     ref_gpu = (run_reference_gpu(rec, dev, K, W) if not dist and not a.profile and not tp and not a.synth
                else None)
     agreement = None
