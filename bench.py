@@ -523,6 +523,7 @@ def run_value(rec, dev, K, W, shard=None, tier="host"):
         one(i)
     fetched = 0
     launches0 = Kx.LAUNCHES[0]
+    wait0 = cache.host_wait_s
     torch.cuda.synchronize()
     if shard.world > 1:
         torch.distributed.barrier()
@@ -543,10 +544,11 @@ def run_value(rec, dev, K, W, shard=None, tier="host"):
         torch.distributed.barrier()
         torch.cuda.synchronize()
     launches = Kx.LAUNCHES[0] - launches0
+    host_wait_ms = (cache.host_wait_s - wait0) * 1e3
     total_ms = t0.elapsed_time(t1)
     us, nbytes, n = attention_replay(cache, [steps[W + K - 1][l][0] for l in range(L)], reps=10)
     return dict(ms=total_ms, attn_us=us, attn_bytes=nbytes, attn_n=n, launches=launches, fetched_rows=fetched,
-                window=(wall0, wall1), selections=selections)
+                window=(wall0, wall1), selections=selections, host_wait_ms=host_wait_ms)
 
 
 def run_e2e(rec, dev, K, W, shard=None, tier="host"):
@@ -1378,7 +1380,9 @@ def _main(a, rank, world, local, dist, dev, K, W, cfg_json, tp, clk):
         "model_decode_ms_per_token": rec["model_ms"],
         "reference_gpu": ref_gpu,
         "selection_vs_reference_gpu": agreement,
+        "host_wait_ms_per_step": val["host_wait_ms"] / K,
         "offload_tier_hbm": ({"value": tokens / (hbm["ms"] * 1e-3), "ms_per_step": hbm["ms"] / K,
+                              "host_wait_ms_per_step": hbm["host_wait_ms"] / K,
                               "how": "same replay with offload_tier='hbm' (class-B rows in device memory, no "
                                      "host-link traffic); not the headline, which offloads to host memory as "
                                      "the reference does"} if hbm else None),

@@ -175,6 +175,9 @@ class B200WnWCache(FlatVarlenCache):
         self._dplan = None
         self._dplan_args = None
         self.wait_timeout_s = float(wait_timeout_s)
+        # seconds the host spent blocked in the step's wait for its tail (a
+        # small total means the host, not the device, paces the steps)
+        self.host_wait_s = 0.0
         self.fetch_threads = int(fetch_threads)
         self.fetch_ctas = int(fetch_ctas) if fetch_ctas is not None else (148 if offload_tier == "hbm" else 12)
         self.score_reduce = score_reduce
@@ -842,7 +845,9 @@ class B200WnWCache(FlatVarlenCache):
         self._tail_call("wnw_copy_async", a["topk_d2h"], st)
         self._tail_call("wnw_copy_async", a["err_d2h"], st)
         self._ready.record()
+        t_wait = time.perf_counter()
         wait_event(self._ready, self.wait_timeout_s)
+        self.host_wait_s += time.perf_counter() - t_wait
         if int(a["err_np"][0]):
             Kx.check_device_error(self._scratch.err)
         if select:
