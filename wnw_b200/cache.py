@@ -171,6 +171,7 @@ class B200WnWCache(FlatVarlenCache):
         self._fused_rebuild = self.rebuild_ahead and offload_tier == "hbm"
         self._rb_stream = None
         self._rb_events = None
+        self._fused_ev = 0  # the rebuild event the fused rebuild records (its first changed layer's)
         self._rebuilt = None
         self._dplan = None
         self._dplan_args = None
@@ -692,9 +693,16 @@ class B200WnWCache(FlatVarlenCache):
             # rebuilt ahead on the rebuild stream: the compute stream waits
             # for this layer's rebuild, so its rows and lengths are final
             # before the attention launches (a stream wait holds back every
-            # later launch, whatever its programmatic-dependency attribute)
-            self._rebuilt[l] = False
-            st = N.lib.wnw_stream_wait_event(self._raw_stream(), self._rb_events[l].cuda_event)
+            # later launch, whatever its programmatic-dependency attribute).
+            # The fused rebuild finishes every layer at once and records one
+            # event: the first rebuilt layer's wait covers the step.
+            if self._fused_rebuild:
+                ev = self._rb_events[self._fused_ev]
+                self._rebuilt = [False] * self.num_layers
+            else:
+                ev = self._rb_events[l]
+                self._rebuilt[l] = False
+            st = N.lib.wnw_stream_wait_event(self._raw_stream(), ev.cuda_event)
             if st:
                 N.check(st, "wnw_stream_wait_event")
         if self._pending and self._layer_chg[l]:
@@ -910,10 +918,24 @@ class B200WnWCache(FlatVarlenCache):
         rs.wait_event(start)
         b = self._rebuild_batch()
         if self._fused_rebuild:
+            # the layers' fetch kernels run in order on the copy stream, so
+            # the last changed layer's fetch event covers every earlier one;
+            # one event, recorded in the first changed layer's slot, marks the
+            # end of the launch pair (decode_before_attn waits for it once)
+            idx = np.nonzero(chg)[0]
+            if idx.size == 0:  # nothing to rebuild this step
+                self._pending = False
+                return
+            first, last = int(idx[0]), int(idx[-1])
+            P = C.c_void_p
+            waits = (P * L)()
+            waits[last] = self._event_handles[last]
+            recs = (P * L)()
+            recs[first] = b["record"][first]
+            self._fused_ev = first
             sh = b["shared"]  # ... status, then its length, then err
             st = N.lib.wnw_rebuild_layers_fused(*b["head"], chg.ctypes.data, *b["layers"], *sh[:9],
-                                                int(self._rb_status.numel()), sh[9], self._event_handles,
-                                                b["record"], rs.cuda_stream)
+                                                int(self._rb_status.numel()), sh[9], waits, recs, rs.cuda_stream)
             name = "wnw_rebuild_layers_fused"
         else:
             st = N.lib.wnw_rebuild_layers(*b["head"], chg.ctypes.data, *b["layers"], *b["shared"],
