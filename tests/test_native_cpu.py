@@ -256,6 +256,22 @@ def test_attn_plan_config2_layer_spreads_over_half_the_sms():
         assert len(ranks) <= 4 and all(_meta(m)[2] == 0 for m in ranks[:, 3])
 
 
+@pytest.mark.parametrize("n_a,most", [(1, 74), (2, 74), (3, 98), (4, 98)])
+def test_attn_plan_spreads_over_a_fraction_of_the_sms(n_a, most):
+    """Layers of 1-4 long (15.1k-row) segments beside 2.3k-row ones: spread
+    over clusters of 4 on half the SMs (1-2 long segments) or two thirds of
+    them (3-4), the first fraction whose share is below the one-cluster
+    plan's 960 rows -- the plans measured fastest back to back."""
+    from wnw_b200.kernels import attn_plan
+    lens = [15100 + 296] * n_a + [2300] * (8 - n_a)
+    plan, info = attn_plan(np.array(lens, np.int32) + 40, 148, 16)
+    assert info["cluster"] == 4 and info["combine"] == n_a
+    assert most // 2 < info["ctas"] <= most
+    C, cta, _, _ = _parse_plan(plan)
+    rows = cta[cta[:, 0] >= 0, 2] - cta[cta[:, 0] >= 0, 1]
+    assert rows.max() < 960
+
+
 @pytest.mark.parametrize("lens", [[2300] * 8, [1, 2, 3, 300], [7000] * 4])
 def test_attn_plan_short_shares_keep_one_cluster_per_segment(lens):
     """Layers whose one-cluster shares are at most 512 rows keep every
